@@ -1,0 +1,457 @@
+"""Benchmark of the Qwen3-30B-A3B sparse-MoE block on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload prefill|decode]
+
+A step is one forward of the MoE block (router, softmax/top-8, permute,
+grouped gate/up GEMM + SwiGLU, grouped down GEMM + routing weight, combine)
+over one batch of synthetic tokens:
+  prefill (default): 8192 tokens per GPU (4 x 2048), seed 2;
+  decode:            64 tokens, seed 1 (also reported as a sub-object of the
+                     prefill line at N=1).
+Weights are random N(0, 0.02) with the layer's real shapes (hidden 2048, 128
+experts, top-8, intermediate 768); activations N(0, 1); bf16 storage, fp32
+router and accumulation.  At N > 1 the block runs expert-parallel (E/N
+experts per GPU, each GPU with its own 8192 tokens: weak scaling) with NCCL
+all-to-all dispatch and combine.
+
+Prints ONE JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+# Per-launch DRAM traffic (read + write bytes) of the dominant kernel, from
+# the ncu captures summarised in profiles/ (None until captured).
+NCU_TRAFFIC_BYTES = {"prefill": None, "decode": None}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement")
+    ap.add_argument("--profile-once", action="store_true", help="one warm step only (for ncu launch lists)")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t_start = self.t_end = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.gpu),
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        threading.Thread(target=self._read, daemon=True).start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, start: bool):
+        if start:
+            self.t_start = time.time()
+        else:
+            self.t_end = time.time()
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for t, line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((t, float(parts[1]), float(parts[2]), parts))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        inwin = [r for r in rows if self.t_start and self.t_end and self.t_start <= r[0] <= self.t_end]
+        use = inwin or rows
+        mhz = sorted(r[1] for r in use)
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in use:
+            for name, v in zip(names[1:], r[3][5:9]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(name)
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[2] for r in use), "reasons": sorted(reasons),
+                "samples": len(use), "samples_in_timed_region": len(inwin)}
+
+
+# ---------------------------------------------------------------- helpers
+def algorithmic(wl, idx_np=None):
+    """FLOPs and bytes of one block and of its GEMM-1 launch."""
+    import numpy as np
+    T, H, I, E, K = wl.tokens, wl.hidden, wl.intermediate, wl.experts, wl.top_k
+    R = T * K
+    u = len(np.unique(idx_np)) if idx_np is not None else E
+    return {
+        "block_flops": wl.flops,
+        "gemm1_flops": 2.0 * R * H * 2 * I,
+        "gemm2_flops": 2.0 * R * I * H,
+        # bytes that must move at least once: touched expert weights + activations in/out
+        "gemm1_bytes": u * 2 * I * H * 2 + R * H * 2 + R * I * 2,
+        "gemm2_bytes": u * H * I * 2 + R * I * 2 + R * H * 2,
+        "block_bytes": u * wl.expert_bytes + E * H * 4 + 2 * T * H * 2 + T * K * 8,
+        "unique_experts": int(u),
+    }
+
+
+def stage_events(torch):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    return evs
+
+
+def set_stage_events(evs):
+    import ctypes
+
+    from nki_moe_b200 import _lib
+    if evs is None:
+        _lib.call("nkimoe_set_stage_events", None, 0)
+        return
+    arr = (ctypes.c_void_p * len(evs))(*[ctypes.c_void_p(e.cuda_event) for e in evs])
+    _lib.call("nkimoe_set_stage_events", arr, len(evs))
+
+
+STAGES = ["router", "topk", "permute", "gather", "gemm1_swiglu", "gemm2_scale", "combine"]
+
+
+def cpu_oracle_tokens_per_s(inp_cpu, wl, sample_tokens, repeat=1):
+    """The oracle (numpy restatement of the reference CPU path) on a bounded
+    token sample: router + top-8 + grouped expert FFNs + combine."""
+    import numpy as np
+
+    import oracle
+    x = inp_cpu["x"][:sample_tokens]
+    t0 = time.perf_counter()
+    for _ in range(repeat):
+        lg = oracle.router_logits(x, inp_cpu["router"]) + inp_cpu["router_bias"]
+        idx, w = oracle.topk_softmax(lg, wl.top_k)
+        oracle.experts_forward(x, inp_cpu["gate_up"], inp_cpu["down"], idx, w)
+    dt = (time.perf_counter() - t0) / repeat
+    return sample_tokens / dt, dt
+
+
+def cpu_inputs(inp, torch):
+    return {k: v.to(torch.bfloat16).float().cpu().numpy() if k != "router" and k != "router_bias"
+            else v.float().cpu().numpy() for k, v in inp.items()}
+
+
+def cpu_threads():
+    import numpy as np  # noqa: F401
+    try:
+        from threadpoolctl import threadpool_info
+        n = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:
+        n = os.cpu_count()
+    return int(n or 1)
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the reference CPU path runs once, on rank 0
+    import numpy as np  # noqa: F401
+    import torch
+
+    from nki_moe_b200.workloads import WORKLOADS, make_moe_inputs
+    wl = WORKLOADS["c3" if args.workload == "prefill" else "c2"]
+    sample = 1024 if args.workload == "prefill" else wl.tokens
+    inp = make_moe_inputs(wl, tokens=sample)
+    cin = cpu_inputs(inp, torch)
+    for _ in range(max(args.warmup, 0)):
+        cpu_oracle_tokens_per_s(cin, wl, sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_oracle_tokens_per_s(cin, wl, sample)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    tps = sample / dt
+    cores = cpu_threads()
+    line = {
+        "impl": "reference", "metric": "moe_block_tokens_per_s", "value": tps, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_gpu": wl.tokens, "hidden": wl.hidden, "experts": wl.experts,
+                   "top_k": wl.top_k, "intermediate": wl.intermediate, "sample_tokens_per_step": sample},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens of the {wl.name} workload per step (numpy oracle, fp32)"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu": {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(),
+                "model": _cpu_model()},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------- B200 arm
+def time_steps(torch, fn, steps, warmup, stream, world, evs=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stage_ms = [0.0] * (len(STAGES))
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, stage_ms
+
+
+def measure_stages(torch, fn, steps, evs):
+    """Per-kernel durations from CUDA events recorded by the library between
+    its launches on the launching stream (averaged over `steps` steps)."""
+    set_stage_events(evs)
+    acc = [0.0] * len(STAGES)
+    for _ in range(steps):
+        fn()
+        evs[-1].synchronize()
+        for i in range(len(STAGES)):
+            acc[i] += evs[i].elapsed_time(evs[i + 1])
+    set_stage_events(None)
+    return [a / steps for a in acc]
+
+
+def run_b200(args):
+    import numpy as np
+    import torch
+
+    from nki_moe_b200 import _lib, ops
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+    from nki_moe_b200.workloads import WORKLOADS, make_moe_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    _lib.load()
+    hbm_gbs, tf_burst, tf_sus, peak_src = peaks()
+    sampler = ClockSampler(local)
+    sampler.start()
+
+    def setup(wl, seed_offset=0):
+        inp = make_moe_inputs(wl, device="cuda")
+        moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
+        with torch.no_grad():
+            moe.router.weight.copy_(inp["router"])
+            moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
+            moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+        x = inp["x"].to(torch.bfloat16)
+        return inp, moe, x
+
+    def graph_of(fn):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    result = {}
+    workloads = ["prefill"] if args.workload == "prefill" else ["decode"]
+    if args.workload == "prefill" and world == 1 and not args.no_decode:
+        workloads.append("decode")
+    for which in workloads:
+        wl = WORKLOADS["c3" if which == "prefill" else "c2"]
+        inp, moe, x = setup(wl)
+        if world > 1:
+            from nki_moe_b200.ep import ExpertParallelMoE
+            block = ExpertParallelMoE.from_dense(moe, torch.distributed.group.WORLD)
+            fwd = lambda: block(x)  # noqa: E731
+        else:
+            pe = moe.packed()
+            rw = moe.router.weight
+            fwd = lambda: ops.moe_block(x, rw, pe, wl.top_k)  # noqa: E731
+        stream = torch.cuda.current_stream()
+        # routing of this batch (for the algorithmic byte count) and warm-up
+        _, idx, _ = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k, return_routing=True)
+        alg = algorithmic(wl, idx.cpu().numpy())
+        if args.profile_once:
+            fwd()
+            torch.cuda.synchronize()
+            return
+        run = fwd
+        use_graph = world == 1
+        if use_graph:
+            g = graph_of(fwd)
+            run = g.replay
+        if which == "prefill":
+            sampler.mark(True)
+        ms, _ = time_steps(torch, run, args.steps, max(args.warmup, 3), stream, world)
+        if which == "prefill":
+            sampler.mark(False)
+        st = measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch)) if world == 1 else None
+        tokens_total = wl.tokens * world
+        r = {"ms_per_step": ms, "tokens_per_s": tokens_total / (ms * 1e-3),
+             "block_tflops": alg["block_flops"] * world / (ms * 1e-3) / 1e12,
+             "block_gbs": alg["block_bytes"] * world / (ms * 1e-3) / 1e9, "alg": alg, "stages_ms": None}
+        if st is not None:
+            r["stages_ms"] = dict(zip(STAGES, [round(v, 4) for v in st]))
+            if which == "prefill":
+                t = st[4] * 1e-3
+                r["roofline"] = {"bound": "tensor", "kernel": "grouped_gemm_rows (gate/up + SwiGLU)",
+                                 "achieved": alg["gemm1_flops"] / t / 1e12, "peak": tf_burst, "unit": "TFLOP/s",
+                                 "frac": alg["gemm1_flops"] / t / 1e12 / tf_burst,
+                                 "traffic": NCU_TRAFFIC_BYTES["prefill"],
+                                 "peak_source": f"{peak_src} bf16 burst"}
+                t2 = st[5] * 1e-3
+                r["roofline_gemm2"] = {"bound": "tensor", "achieved": alg["gemm2_flops"] / t2 / 1e12,
+                                       "frac": alg["gemm2_flops"] / t2 / 1e12 / tf_burst}
+            else:
+                t = st[4] * 1e-3
+                r["roofline"] = {"bound": "hbm", "kernel": "grouped_gemm_weights (gate/up + SwiGLU)",
+                                 "achieved": alg["gemm1_bytes"] / t / 1e9, "peak": hbm_gbs, "unit": "GB/s",
+                                 "frac": alg["gemm1_bytes"] / t / 1e9 / hbm_gbs,
+                                 "traffic": NCU_TRAFFIC_BYTES["decode"], "peak_source": f"{peak_src} HBM copy"}
+                blk = alg["block_bytes"] / (ms * 1e-3) / 1e9
+                r["roofline_block"] = {"bound": "hbm", "achieved": blk, "frac": blk / hbm_gbs, "unit": "GB/s"}
+        # e2e through the public module API with pinned host buffers
+        if not args.no_e2e:
+            xh = x.reshape(1, *x.shape).cpu().pin_memory()
+            outh = torch.empty_like(xh).pin_memory()
+
+            def e2e_step():
+                xd = xh.to("cuda", non_blocking=True)
+                y = moe(xd) if world == 1 else block(xd[0]).unsqueeze(0)
+                outh.copy_(y, non_blocking=True)
+
+            e_ms, _ = time_steps(torch, e2e_step, args.steps, max(args.warmup, 3), stream, world)
+            r["e2e"] = {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+                        "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+                        "d2h_bytes_per_step": outh.numel() * outh.element_size()}
+        if not args.no_cpu_baseline and rank == 0 and world == 1:
+            sample = 512 if which == "prefill" else wl.tokens
+            sub = {k: (v[:sample] if k == "x" else v) for k, v in inp.items()}
+            cin = cpu_inputs(sub, torch)
+            cpu_oracle_tokens_per_s(cin, wl, min(sample, 32))
+            tps, dt = cpu_oracle_tokens_per_s(cin, wl, sample)
+            r["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+                                 "sample": f"{sample} tokens of the {wl.name} workload (numpy oracle, fp32), "
+                                           f"{dt:.2f} s"}
+        result[which] = r
+        del moe, inp, x
+        torch.cuda.empty_cache()
+
+    sampler.stop()
+    clocks = sampler.summary()
+    main_key = workloads[0]
+    m = result[main_key]
+    wl = WORKLOADS["c3" if main_key == "prefill" else "c2"]
+    launches_per_step = 9
+    line = {
+        "metric": "moe_block_tokens_per_s", "value": m["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": m["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_gpu": wl.tokens, "hidden": wl.hidden, "experts": wl.experts,
+                   "top_k": wl.top_k, "intermediate": wl.intermediate,
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (1.21 GB of expert weights read per step)",
+                   "timing": "CUDA graph replay, CUDA events" if world == 1 else "eager, CUDA events, max over ranks"},
+        "roofline": m.get("roofline"),
+        "cpu_baseline": m.get("cpu_baseline"),
+        "e2e": m.get("e2e"),
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "block_tflops": m["block_tflops"],
+        "stages_ms": m["stages_ms"],
+    }
+    if "roofline_gemm2" in m:
+        line["roofline_gemm2"] = m["roofline_gemm2"]
+    if "decode" in result and main_key != "decode":
+        d = result["decode"]
+        line["decode"] = {"workload": WORKLOADS["c2"].name, "tokens_per_s": d["tokens_per_s"],
+                          "ms_per_step": d["ms_per_step"], "roofline": d.get("roofline"),
+                          "roofline_block": d.get("roofline_block"), "stages_ms": d["stages_ms"],
+                          "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline"),
+                          "unique_experts": d["alg"]["unique_experts"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * nkimoe.h - C ABI of the B200 (sm_100a) implementation of the Qwen3-30B-A3B
+ * sparse-MoE block and the norms that feed it.
+ *
+ * Plain pointers and sizes only.  All device pointers are CUDA global memory
+ * of the current device; `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  Every call is asynchronous and stream-ordered, allocates nothing,
+ * and returns NKIMOE_OK or an error code; nkimoe_last_error() gives the
+ * calling thread's last message.  Device-side faults that cannot be detected
+ * at launch (an expert id out of range, a bounded wait that ran out) are
+ * accumulated in a status word at the start of the caller's workspace and
+ * read with nkimoe_read_status().
+ *
+ * Reference interfaces (Goomelo/nki-moe, Python/NKI) replaced by each entry
+ * point are cited as file:line.
+ */
+#ifndef NKIMOE_H_
+#define NKIMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NKIMOE_API __attribute__((visibility("default")))
+#else
+#define NKIMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define NKIMOE_OK 0
+#define NKIMOE_ERR_INVALID_ARG 1   /* bad pointer, shape, dtype or alignment   */
+#define NKIMOE_ERR_UNSUPPORTED 2   /* shape outside what the kernels handle    */
+#define NKIMOE_ERR_WORKSPACE 3     /* workspace too small                      */
+#define NKIMOE_ERR_CUDA 4          /* a CUDA runtime/driver call failed        */
+#define NKIMOE_ERR_DEVICE 5        /* nkimoe_read_status: device flagged a fault */
+
+/* device status bits (nkimoe_read_status) */
+#define NKIMOE_DEV_TIMEOUT 1       /* a bounded device-side wait ran out       */
+#define NKIMOE_DEV_BAD_INDEX 2     /* an expert id outside [0, num_experts)    */
+
+/* dtype codes */
+#define NKIMOE_F32 0
+#define NKIMOE_BF16 1
+#define NKIMOE_I32 2
+#define NKIMOE_I64 3
+
+/* weight layouts accepted by the packing entry points */
+#define NKIMOE_LAYOUT_NXD 0        /* gate_up [E,H,2I], down [E,I,H] (qwen.py:164-226)          */
+#define NKIMOE_LAYOUT_HF 1         /* gate_up [E,2I,H], down [E,H,I] (HF Qwen3MoeExperts)       */
+
+NKIMOE_API int nkimoe_version(void);
+NKIMOE_API const char* nkimoe_last_error(void);
+/* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows, 2 weights),
+ * "weights_rows" (16, 32 or 64 rows per decode tile), "router" (0 auto,
+ * 1 CUDA-core fp32, 2 tensor-core split-fp32).  Returns NKIMOE_OK or
+ * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */
+NKIMOE_API int nkimoe_set_option(const char* name, long long value);
+
+/* Profiling hook: `events` is an array of `count` (<= 8) cudaEvent_t that the
+ * calling thread's later block calls record on their stream at the start of
+ * each stage: 0 router, 1 top-k, 2 permute, 3 gather, 4 GEMM-1 (SwiGLU),
+ * 5 GEMM-2 (routing weight), 6 combine, 7 end.  count = 0 turns it off.
+ * No reference counterpart (the reference times whole graphs, main.py:258-277). */
+NKIMOE_API int nkimoe_set_stage_events(void* const* events, int count);
+
+/* ---------------------------------------------------------------- norms */
+
+/* nki_rmsnorm_kernel(input_tensor[N,H], weight[H], eps) -> [N,H]
+ * (nki_custom_rmsnorm.py:8-70; module NKIRMSNorm.forward :96-123).
+ * x_dtype/out_dtype: F32 or BF16; w_dtype: F32 or BF16.  H % 8 == 0. */
+NKIMOE_API int nkimoe_rmsnorm(const void* x, int x_dtype, const void* weight, int w_dtype, void* out, int out_dtype,
+                   int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* residual_out = x + residual (bf16); out = rmsnorm(residual_out) (bf16).
+ * The decoder's residual add feeding post_attention_layernorm
+ * (qwen_with_nki.py:447-452).  residual_out may alias residual or x. */
+NKIMOE_API int nkimoe_add_rmsnorm(const void* x, const void* residual, void* residual_out, const void* weight, int w_dtype,
+                       void* out, int64_t rows, int64_t hidden, float eps, void* stream);
+
+/* Per-head q/k RMSNorm then rotate-half RoPE on a fused bf16 QKV row
+ * [T, (n_heads + 2*n_kv_heads) * head_dim] laid out [Q | K | V]
+ * (q_layernorm/k_layernorm qwen_with_nki.py:349-350, RotaryEmbedding
+ * :330-334; NKI counterpart nki_rope_kernel nki_attention.py:172-249, whose
+ * interleaved-pair convention is NOT followed).  positions: int64 [T].
+ * qkv_out may equal qkv_in.  head_dim must be 128. */
+NKIMOE_API int nkimoe_qk_norm_rope(const void* qkv_in, void* qkv_out, const void* q_weight, const void* k_weight, int w_dtype,
+                        const int64_t* positions, int64_t tokens, int n_heads, int n_kv_heads, int head_dim,
+                        float rope_theta, float eps, void* stream);
+
+/* ---------------------------------------------------------------- router */
+
+/* logits[T,E] (fp32) = x(bf16)[T,H] . router_w(fp32)[E,H]^T (+ router_bias[E])
+ * (NKIMoESimple.router, nki_moe_integrated.py:411-412, :437). */
+NKIMOE_API int nkimoe_router_logits(const void* x, const float* router_w, const float* router_bias, float* logits, int64_t T,
+                         int64_t H, int64_t E, void* stream);
+
+/* softmax -> top-k (descending; ties to the lower expert id) -> renormalise
+ * (nki_moe_integrated.py:438-443).  idx int32 [T,K], w fp32 [T,K]. */
+NKIMOE_API int nkimoe_topk_softmax(const float* logits, int64_t T, int64_t E, int64_t K, int32_t* topk_idx, float* topk_w,
+                        void* stream);
+
+/* ---------------------------------------------------------------- permutation */
+
+NKIMOE_API size_t nkimoe_permute_workspace_bytes(int64_t T, int64_t K, int64_t E);
+
+/* Stable grouping of the T*K assignments by expert, (k, t) order inside an
+ * expert (nki_moe_integrated.py:450-467).  topk_idx is [T,K] of idx_dtype
+ * (I32 or I64).  Outputs: row_token[T*K], row_slot[T*K] (= t*K + k),
+ * slot_row[T*K] (inverse; -1 for an out-of-range id), expert_offsets[E+1]. */
+NKIMOE_API int nkimoe_permute(const void* topk_idx, int idx_dtype, int64_t T, int64_t K, int64_t E, int32_t* row_token,
+                   int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- weights */
+
+/* Packs gate_up_proj into the GEMM layout W13 [E, 2I, H] bf16: K-major, row
+ * blocks of 128 = [gate 64 | up 64].  layout: NKIMOE_LAYOUT_NXD for the
+ * reference's [E,H,2I] (qwen.py:164-202), NKIMOE_LAYOUT_HF for [E,2I,H].
+ * I % 64 == 0, H % 64 == 0. */
+NKIMOE_API int nkimoe_pack_gate_up(const void* gate_up, int layout, void* w13, int64_t E, int64_t H, int64_t I, void* stream);
+
+/* Packs down_proj into W2 [E, H, I] bf16 (K-major).  layout NXD: [E,I,H]
+ * (qwen.py:204-226) is transposed; HF: [E,H,I] is copied. */
+NKIMOE_API int nkimoe_pack_down(const void* down, int layout, void* w2, int64_t E, int64_t H, int64_t I, void* stream);
+
+/* ---------------------------------------------------------------- MoE block */
+
+NKIMOE_API size_t nkimoe_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
+
+/* Expert stage given routing: out[T,H] (bf16) = sum_k w[t,k] *
+ * FFN_{idx[t,k]}(x[t]).  The whole-block kernels nki_moe_full_forward /
+ * nki_moe_optimized (nki_moe_kernel.py:185-423), nki_moe_expert_kernel /
+ * nki_moe_expert_fused_kernel_v2 (nki_moe_expert.py:21-355), all
+ * (hidden_states[T,H], gate_up_proj, down_proj, expert_indices[T,K],
+ * expert_weights[T,K]) -> [T,H].  x bf16 [T,H]; w13/w2 packed (above);
+ * topk_idx [T,K] of idx_dtype; topk_w fp32 [T,K]. */
+NKIMOE_API int nkimoe_moe_experts(const void* x, const void* w13, const void* w2, const void* topk_idx, int idx_dtype,
+                       const float* topk_w, void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Whole block, router included: NKIMoESimple.forward
+ * (nki_moe_integrated.py:428-475) and NKIMoEWrapper._nki_forward (:292-387).
+ * router_w fp32 [E,H]; router_bias fp32 [E] or NULL; topk_idx_out (int32
+ * [T,K]) and topk_w_out (fp32 [T,K]) may be NULL. */
+NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const float* router_bias, const void* w13, const void* w2,
+                     void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
+                     int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads and clears the device status word of a workspace (synchronises the
+ * stream).  Returns NKIMOE_OK, NKIMOE_ERR_DEVICE (status in *status_out), or
+ * NKIMOE_ERR_CUDA. */
+NKIMOE_API int nkimoe_read_status(void* workspace, void* stream, int* status_out);
+
+/* ---------------------------------------------------------------- pieces */
+
+/* Grouped GEMM over expert segments: for each expert e, rows
+ * [offsets[e], offsets[e+1]) of a (bf16 [M, Kd], K-major) times w_packed[e]
+ * (bf16 [N, Kd], K-major); out bf16 [M, N] (or [out_rows, N] through
+ * out_row_map).  nki_grouped_expert_gemm(input_tokens[M,H],
+ * expert_weights[E,H,N], expert_ids[M], num_experts) (nki_moe_expert.py:466-542)
+ * and nki_matmul_tiled(a[M,K], b[K,N]) (nki_moe_integrated.py:27-84, E = 1).
+ * expert_offsets is a device int32 [E+1]; status: device int or NULL. */
+NKIMOE_API int nkimoe_grouped_gemm(const void* a, const void* w_packed, const int32_t* expert_offsets, const int32_t* out_row_map,
+                        void* out, int64_t M, int64_t N, int64_t Kd, int64_t E, int* status, void* stream);
+
+/* silu(gate) * up over a bf16 [M, 2N] gate|up split (nki_swiglu,
+ * nki_moe_integrated.py:87-139). */
+NKIMOE_API int nkimoe_swiglu(const void* gate_up, void* out, int64_t M, int64_t N, void* stream);
+
+/* Sum over the leading top-k axis of bf16 [K, T, H] (nki_moe_aggregate,
+ * nki_moe_integrated.py:209-251). */
+NKIMOE_API int nkimoe_aggregate(const void* expert_outputs, void* out, int64_t K, int64_t T, int64_t H, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NKIMOE_H_ */

@@ -1,0 +1,462 @@
+// C ABI (include/nkimoe.h): argument checks, workspace carving, TMA
+// descriptors and the launch sequence of the MoE block.
+//
+// Launch sequence of one block (all on the caller's stream, no host sync):
+//   [router: logits -> softmax/top-k]  permute  gather  GEMM-1 (+SwiGLU)
+//   GEMM-2 (+routing weight)  combine
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "kernels.h"
+#include "nkimoe.h"
+
+namespace nkimoe {
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define NKI_CUDA(call)                                                                      \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return fail(NKIMOE_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define NKI_REQUIRE(cond, code, ...)         \
+  do {                                       \
+    if (!(cond)) return fail(code, __VA_ARGS__); \
+  } while (0)
+
+std::atomic<int> g_schedule{0};      // 0 auto, 1 rows, 2 weights
+// Optional CUDA events recorded between the stages of a block call (set by
+// nkimoe_set_stage_events, per calling thread): stage i starts at event i.
+thread_local cudaEvent_t g_stage_events[kNumStageEvents] = {};
+thread_local int g_num_stage_events = 0;
+
+inline void mark(int stage, cudaStream_t s) {
+  if (stage < g_num_stage_events && g_stage_events[stage]) cudaEventRecord(g_stage_events[stage], s);
+}
+std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+inline size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+struct WsLayout {
+  size_t status, logits, idx, w, offsets, row_token, row_slot, slot_row, scratch, xy, h, total;
+};
+
+WsLayout ws_layout(long long T, long long H, long long I, long long E, long long K) {
+  WsLayout L{};
+  size_t o = 0;
+  const long long TK = T * K;
+  L.status = o; o += 256;
+  L.logits = o; o += round256(sizeof(float) * T * E);
+  L.idx = o; o += round256(sizeof(int32_t) * TK);
+  L.w = o; o += round256(sizeof(float) * TK);
+  L.offsets = o; o += round256(sizeof(int32_t) * (E + 1));
+  L.row_token = o; o += round256(sizeof(int32_t) * TK);
+  L.row_slot = o; o += round256(sizeof(int32_t) * TK);
+  L.slot_row = o; o += round256(sizeof(int32_t) * TK);
+  L.scratch = o; o += round256(permute_scratch_bytes(T, static_cast<int>(K), static_cast<int>(E)));
+  L.xy = o; o += round256(sizeof(uint16_t) * TK * H);
+  L.h = o; o += round256(sizeof(uint16_t) * TK * I);
+  L.total = o;
+  return L;
+}
+
+int choose_variant(long long rows_total, long long E, long long N) {
+  const int sched = g_schedule.load();
+  const double avg = E > 0 ? static_cast<double>(rows_total) / static_cast<double>(E) : 0.0;
+  const bool weights = sched == 2 || (sched == 0 && avg <= 48.0);
+  if (weights) {
+    int r = g_weights_rows.load();
+    if (r == 0) r = avg <= 8.0 ? 16 : (avg <= 24.0 ? 32 : 64);
+    return r == 16 ? kWeightsT16 : (r == 32 ? kWeightsT32 : kWeightsT64);
+  }
+  return (N % 256 == 0) ? kRowsBN256 : kRowsBN128;
+}
+
+// One grouped GEMM: act [act_rows, kd] x w [E*N, kd]^T per expert segment.
+int run_gemm(const void* act, long long act_rows, const void* w, long long E, long long N, long long kd,
+             const int32_t* offsets, int epilogue, void* out, long long out_ld, const float* slot_w,
+             const int32_t* row_slot, const int32_t* out_row_map, const float* col_bias, int* status,
+             cudaStream_t s) {
+  if (act_rows == 0) return NKIMOE_OK;
+  const int variant = choose_variant(act_rows, E, N);
+  CUtensorMap ta, tw;
+  NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
+              "cuTensorMapEncodeTiled failed for the activation operand");
+  NKI_REQUIRE(make_tmap_bf16(&tw, w, E * N, kd, grouped_gemm_box_rows_w(variant)), NKIMOE_ERR_CUDA,
+              "cuTensorMapEncodeTiled failed for the weight operand");
+  GroupedGemmParams p{};
+  p.expert_offsets = offsets;
+  p.num_experts = static_cast<int>(E);
+  p.n = static_cast<int>(N);
+  p.k_blocks = static_cast<int>(kd / 64);
+  p.k_blocks_a = static_cast<int>(kd / 64);
+  p.epilogue = epilogue;
+  p.out = out;
+  p.out_ld = out_ld;
+  p.slot_weight = slot_w;
+  p.row_slot = row_slot;
+  p.out_row_map = out_row_map;
+  p.col_bias = col_bias;
+  p.status = status;
+  const bool rows = variant == kRowsBN256 || variant == kRowsBN128;
+  const long long rpt = grouped_gemm_box_rows_act(variant);
+  const long long fpt = rows ? grouped_gemm_box_rows_w(variant) : 128;
+  const long long max_tiles = (act_rows / rpt + E) * (N / fpt);
+  const long long grid = std::min<long long>(max_tiles, device_sm_count());
+  NKI_CUDA(grouped_gemm_launch(variant, ta, tw, p, static_cast<int>(std::max<long long>(grid, 1)), s));
+  return NKIMOE_OK;
+}
+
+int check_moe_shapes(long long T, long long H, long long I, long long E, long long K) {
+  NKI_REQUIRE(T >= 0 && H > 0 && I > 0 && E > 0 && K > 0, NKIMOE_ERR_INVALID_ARG, "non-positive dimension");
+  NKI_REQUIRE(E <= kMaxExperts, NKIMOE_ERR_UNSUPPORTED, "num_experts %lld > %d", E, kMaxExperts);
+  NKI_REQUIRE(K <= 32 && K <= E, NKIMOE_ERR_UNSUPPORTED, "top_k %lld must be <= 32 and <= num_experts", K);
+  NKI_REQUIRE(H % 128 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden %lld must be a multiple of 128", H);
+  NKI_REQUIRE(I % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "intermediate %lld must be a multiple of 64", I);
+  NKI_REQUIRE(T * K < (1LL << 31), NKIMOE_ERR_UNSUPPORTED, "T*K too large");
+  return NKIMOE_OK;
+}
+
+int experts_impl(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype, const float* topk_w,
+                 void* out, long long T, long long H, long long I, long long E, long long K, void* ws, size_t ws_bytes,
+                 cudaStream_t s) {
+  const WsLayout L = ws_layout(T, H, I, E, K);
+  char* base = static_cast<char*>(ws);
+  int* status = reinterpret_cast<int*>(base + L.status);
+  int32_t* offsets = reinterpret_cast<int32_t*>(base + L.offsets);
+  int32_t* row_token = reinterpret_cast<int32_t*>(base + L.row_token);
+  int32_t* row_slot = reinterpret_cast<int32_t*>(base + L.row_slot);
+  int32_t* slot_row = reinterpret_cast<int32_t*>(base + L.slot_row);
+  __nv_bfloat16* xy = reinterpret_cast<__nv_bfloat16*>(base + L.xy);
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(base + L.h);
+  const long long TK = T * K;
+  if (T == 0) return NKIMOE_OK;
+  mark(kStagePermute, s);
+  NKI_CUDA(permute_launch(idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
+                          row_slot, slot_row, offsets, base + L.scratch, status, s));
+  mark(kStageGather, s);
+  NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(E), xy, TK,
+                              static_cast<int>(H), s));
+  mark(kStageGemm1, s);
+  int rc = run_gemm(xy, TK, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s);
+  if (rc != NKIMOE_OK) return rc;
+  mark(kStageGemm2, s);
+  rc = run_gemm(h, TK, w2, E, H, I, offsets, kEpiScaleBf16, xy, H, topk_w, row_slot, nullptr, nullptr, status, s);
+  if (rc != NKIMOE_OK) return rc;
+  mark(kStageCombine, s);
+  NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
+                          static_cast<int>(K), static_cast<int>(H), s));
+  mark(kStageEnd, s);
+  return NKIMOE_OK;
+}
+
+}  // namespace
+
+bool make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn || rows <= 0 || cols <= 0 || (cols * 2) % 16 != 0 || !aligned16(base)) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int device_sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (counts[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    counts[dev] = n > 0 ? n : 148;
+  }
+  return counts[dev];
+}
+
+}  // namespace nkimoe
+
+using namespace nkimoe;
+
+extern "C" {
+
+int nkimoe_version(void) { return 1; }
+
+int nkimoe_set_stage_events(void* const* events, int count) {
+  if (count < 0 || count > kNumStageEvents || (count > 0 && !events))
+    return fail(NKIMOE_ERR_INVALID_ARG, "stage events: 0..%d events", kNumStageEvents);
+  for (int i = 0; i < kNumStageEvents; ++i)
+    g_stage_events[i] = i < count ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  g_num_stage_events = count;
+  return NKIMOE_OK;
+}
+
+const char* nkimoe_last_error(void) { return g_err.c_str(); }
+
+int nkimoe_set_option(const char* name, long long value) {
+  if (!name) return fail(NKIMOE_ERR_INVALID_ARG, "null option name");
+  const std::string n(name);
+  if (n == "gemm_schedule" && value >= 0 && value <= 2) {
+    g_schedule = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "weights_rows" && (value == 0 || value == 16 || value == 32 || value == 64)) {
+    g_weights_rows = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "router" && value >= 0 && value <= 2) return NKIMOE_OK;
+  return fail(NKIMOE_ERR_INVALID_ARG, "unknown option %s=%lld", name, value);
+}
+
+int nkimoe_rmsnorm(const void* x, int x_dtype, const void* weight, int w_dtype, void* out, int out_dtype,
+                   int64_t rows, int64_t hidden, float eps, void* stream) {
+  NKI_REQUIRE(rows >= 0 && hidden > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(hidden % 8 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden %lld must be a multiple of 8", (long long)hidden);
+  if (rows == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && weight && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out), NKIMOE_ERR_INVALID_ARG,
+              "pointers must be 16-byte aligned");
+  cudaError_t e = rmsnorm_launch(x, x_dtype, weight, w_dtype, out, out_dtype, rows, static_cast<int>(hidden), eps,
+                                 as_stream(stream));
+  NKI_REQUIRE(e != cudaErrorInvalidValue, NKIMOE_ERR_INVALID_ARG, "unsupported dtype combination %d/%d/%d", x_dtype,
+              w_dtype, out_dtype);
+  NKI_CUDA(e);
+  return NKIMOE_OK;
+}
+
+int nkimoe_add_rmsnorm(const void* x, const void* residual, void* residual_out, const void* weight, int w_dtype,
+                       void* out, int64_t rows, int64_t hidden, float eps, void* stream) {
+  NKI_REQUIRE(rows >= 0 && hidden > 0 && hidden % 8 == 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  if (rows == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && residual && residual_out && weight && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(residual) && aligned16(residual_out) && aligned16(weight) && aligned16(out),
+              NKIMOE_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  cudaError_t e = add_rmsnorm_launch(x, residual, residual_out, weight, w_dtype, out, rows, static_cast<int>(hidden),
+                                     eps, as_stream(stream));
+  NKI_REQUIRE(e != cudaErrorInvalidValue, NKIMOE_ERR_INVALID_ARG, "unsupported weight dtype %d", w_dtype);
+  NKI_CUDA(e);
+  return NKIMOE_OK;
+}
+
+int nkimoe_qk_norm_rope(const void* qkv_in, void* qkv_out, const void* q_weight, const void* k_weight, int w_dtype,
+                        const int64_t* positions, int64_t tokens, int n_heads, int n_kv_heads, int head_dim,
+                        float rope_theta, float eps, void* stream) {
+  NKI_REQUIRE(tokens >= 0 && n_heads > 0 && n_kv_heads >= 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(head_dim == 128, NKIMOE_ERR_UNSUPPORTED, "head_dim %d (only 128 is supported)", head_dim);
+  NKI_REQUIRE(w_dtype == NKIMOE_F32 || w_dtype == NKIMOE_BF16, NKIMOE_ERR_INVALID_ARG, "bad weight dtype");
+  if (tokens == 0) return NKIMOE_OK;
+  NKI_REQUIRE(qkv_in && qkv_out && q_weight && k_weight && positions, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(qkv_in) && aligned16(qkv_out), NKIMOE_ERR_INVALID_ARG, "qkv must be 16-byte aligned");
+  NKI_CUDA(qk_norm_rope_launch(qkv_in, qkv_out, q_weight, k_weight, w_dtype,
+                               reinterpret_cast<const long long*>(positions), tokens, n_heads, n_kv_heads, head_dim,
+                               rope_theta, eps, as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+int nkimoe_router_logits(const void* x, const float* router_w, const float* router_bias, float* logits, int64_t T,
+                         int64_t H, int64_t E, void* stream) {
+  NKI_REQUIRE(T >= 0 && H > 0 && E > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(H % 32 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden %lld must be a multiple of 32", (long long)H);
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && router_w && logits, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(router_w), NKIMOE_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  NKI_CUDA(router_logits_simt_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
+                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+int nkimoe_topk_softmax(const float* logits, int64_t T, int64_t E, int64_t K, int32_t* topk_idx, float* topk_w,
+                        void* stream) {
+  NKI_REQUIRE(T >= 0 && E > 0 && K > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(E <= 256 && K <= 32 && K <= E, NKIMOE_ERR_UNSUPPORTED, "E <= 256 and K <= min(32, E) required");
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(logits && topk_idx && topk_w, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_CUDA(topk_softmax_launch(logits, static_cast<int>(T), static_cast<int>(E), static_cast<int>(K), topk_idx, topk_w,
+                               as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+size_t nkimoe_permute_workspace_bytes(int64_t T, int64_t K, int64_t E) {
+  return 256 + permute_scratch_bytes(T, static_cast<int>(K), static_cast<int>(E));
+}
+
+int nkimoe_permute(const void* topk_idx, int idx_dtype, int64_t T, int64_t K, int64_t E, int32_t* row_token,
+                   int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  NKI_REQUIRE(T >= 0 && K > 0 && E > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(E <= kMaxExperts, NKIMOE_ERR_UNSUPPORTED, "num_experts > %d", kMaxExperts);
+  NKI_REQUIRE(idx_dtype == NKIMOE_I32 || idx_dtype == NKIMOE_I64, NKIMOE_ERR_INVALID_ARG, "idx dtype must be I32/I64");
+  NKI_REQUIRE(workspace_bytes >= nkimoe_permute_workspace_bytes(T, K, E), NKIMOE_ERR_WORKSPACE,
+              "workspace %zu < %zu", workspace_bytes, nkimoe_permute_workspace_bytes(T, K, E));
+  NKI_REQUIRE(expert_offsets && workspace, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  const cudaStream_t s = as_stream(stream);
+  int* status = static_cast<int*>(workspace);
+  NKI_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+  if (T > 0) NKI_REQUIRE(topk_idx && row_token && row_slot && slot_row, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_CUDA(permute_launch(topk_idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
+                          row_slot, slot_row, expert_offsets, static_cast<char*>(workspace) + 256, status, s));
+  return NKIMOE_OK;
+}
+
+int nkimoe_pack_gate_up(const void* gate_up, int layout, void* w13, int64_t E, int64_t H, int64_t I, void* stream) {
+  NKI_REQUIRE(gate_up && w13 && E > 0 && H > 0 && I > 0, NKIMOE_ERR_INVALID_ARG, "bad argument");
+  NKI_REQUIRE(I % 64 == 0 && H % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "I and H must be multiples of 64");
+  NKI_REQUIRE(aligned16(gate_up) && aligned16(w13), NKIMOE_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  const auto* in = static_cast<const __nv_bfloat16*>(gate_up);
+  auto* out = static_cast<__nv_bfloat16*>(w13);
+  if (layout == NKIMOE_LAYOUT_NXD) {
+    NKI_CUDA(pack_gate_up_nxd_launch(in, out, static_cast<int>(E), static_cast<int>(H), static_cast<int>(I),
+                                     as_stream(stream)));
+  } else if (layout == NKIMOE_LAYOUT_HF) {
+    NKI_CUDA(pack_gate_up_hf_launch(in, out, static_cast<int>(E), static_cast<int>(H), static_cast<int>(I),
+                                    as_stream(stream)));
+  } else {
+    return fail(NKIMOE_ERR_INVALID_ARG, "unknown layout %d", layout);
+  }
+  return NKIMOE_OK;
+}
+
+int nkimoe_pack_down(const void* down, int layout, void* w2, int64_t E, int64_t H, int64_t I, void* stream) {
+  NKI_REQUIRE(down && w2 && E > 0 && H > 0 && I > 0, NKIMOE_ERR_INVALID_ARG, "bad argument");
+  NKI_REQUIRE(I % 64 == 0 && H % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "I and H must be multiples of 64");
+  if (layout == NKIMOE_LAYOUT_NXD) {
+    NKI_CUDA(transpose_launch(static_cast<const __nv_bfloat16*>(down), static_cast<__nv_bfloat16*>(w2),
+                              static_cast<int>(E), static_cast<int>(I), static_cast<int>(H), as_stream(stream)));
+  } else if (layout == NKIMOE_LAYOUT_HF) {
+    NKI_CUDA(cudaMemcpyAsync(w2, down, sizeof(uint16_t) * E * H * I, cudaMemcpyDeviceToDevice, as_stream(stream)));
+  } else {
+    return fail(NKIMOE_ERR_INVALID_ARG, "unknown layout %d", layout);
+  }
+  return NKIMOE_OK;
+}
+
+size_t nkimoe_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K) {
+  return ws_layout(T, H, I, E, K).total;
+}
+
+int nkimoe_moe_experts(const void* x, const void* w13, const void* w2, const void* topk_idx, int idx_dtype,
+                       const float* topk_w, void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_moe_shapes(T, H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
+  NKI_REQUIRE(idx_dtype == NKIMOE_I32 || idx_dtype == NKIMOE_I64, NKIMOE_ERR_INVALID_ARG, "idx dtype must be I32/I64");
+  const size_t need = nkimoe_moe_workspace_bytes(T, H, I, E, K);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  const cudaStream_t s = as_stream(stream);
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && w13 && w2 && topk_idx && topk_w && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(w13) && aligned16(w2) && aligned16(out), NKIMOE_ERR_INVALID_ARG,
+              "x, weights and out must be 16-byte aligned");
+  return experts_impl(x, w13, w2, topk_idx, idx_dtype, topk_w, out, T, H, I, E, K, workspace, workspace_bytes, s);
+}
+
+int nkimoe_moe_block(const void* x, const float* router_w, const float* router_bias, const void* w13, const void* w2,
+                     void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
+                     int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_moe_shapes(T, H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
+  NKI_REQUIRE(E <= 256, NKIMOE_ERR_UNSUPPORTED, "router top-k supports up to 256 experts");
+  const size_t need = nkimoe_moe_workspace_bytes(T, H, I, E, K);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  const cudaStream_t s = as_stream(stream);
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && router_w && w13 && w2 && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(router_w) && aligned16(w13) && aligned16(w2) && aligned16(out),
+              NKIMOE_ERR_INVALID_ARG, "x, weights and out must be 16-byte aligned");
+  const WsLayout L = ws_layout(T, H, I, E, K);
+  char* base = static_cast<char*>(workspace);
+  float* logits = reinterpret_cast<float*>(base + L.logits);
+  int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(base + L.idx);
+  float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(base + L.w);
+  mark(kStageRouter, s);
+  NKI_CUDA(router_logits_simt_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
+                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s));
+  mark(kStageTopk, s);
+  NKI_CUDA(topk_softmax_launch(logits, static_cast<int>(T), static_cast<int>(E), static_cast<int>(K), idx, w, s));
+  return experts_impl(x, w13, w2, idx, NKIMOE_I32, w, out, T, H, I, E, K, workspace, workspace_bytes, s);
+}
+
+int nkimoe_read_status(void* workspace, void* stream, int* status_out) {
+  NKI_REQUIRE(workspace, NKIMOE_ERR_INVALID_ARG, "null workspace");
+  const cudaStream_t s = as_stream(stream);
+  int v = 0;
+  NKI_CUDA(cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, s));
+  NKI_CUDA(cudaStreamSynchronize(s));
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  if (status_out) *status_out = v;
+  if (v != 0) return fail(NKIMOE_ERR_DEVICE, "device status 0x%x (1 = wait timeout, 2 = expert id out of range)", v);
+  return NKIMOE_OK;
+}
+
+int nkimoe_grouped_gemm(const void* a, const void* w_packed, const int32_t* expert_offsets, const int32_t* out_row_map,
+                        void* out, int64_t M, int64_t N, int64_t Kd, int64_t E, int* status, void* stream) {
+  NKI_REQUIRE(M >= 0 && N > 0 && Kd > 0 && E > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(E <= kMaxExperts, NKIMOE_ERR_UNSUPPORTED, "num_experts > %d", kMaxExperts);
+  NKI_REQUIRE(N % 128 == 0 && Kd % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "N %% 128 == 0 and K %% 64 == 0 required");
+  if (M == 0) return NKIMOE_OK;
+  NKI_REQUIRE(a && w_packed && expert_offsets && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(a) && aligned16(w_packed) && aligned16(out), NKIMOE_ERR_INVALID_ARG,
+              "pointers must be 16-byte aligned");
+  return run_gemm(a, M, w_packed, E, N, Kd, expert_offsets, kEpiStoreBf16, out, N, nullptr, nullptr, out_row_map,
+                  nullptr, status, as_stream(stream));
+}
+
+int nkimoe_swiglu(const void* gate_up, void* out, int64_t M, int64_t N, void* stream) {
+  NKI_REQUIRE(M >= 0 && N > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  if (M == 0) return NKIMOE_OK;
+  NKI_REQUIRE(gate_up && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_CUDA(swiglu_launch(static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), M,
+                         static_cast<int>(N), as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+int nkimoe_aggregate(const void* expert_outputs, void* out, int64_t K, int64_t T, int64_t H, void* stream) {
+  NKI_REQUIRE(K > 0 && T >= 0 && H > 0 && H % 8 == 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(expert_outputs && out && aligned16(expert_outputs) && aligned16(out), NKIMOE_ERR_INVALID_ARG,
+              "null or unaligned pointer");
+  NKI_CUDA(aggregate_launch(static_cast<const __nv_bfloat16*>(expert_outputs), static_cast<__nv_bfloat16*>(out),
+                            static_cast<int>(K), T, static_cast<int>(H), as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,631 @@
+// K4/K5: grouped expert GEMMs on the 5th-generation tensor cores.
+//
+// Problem: for every expert e, rows [off[e], off[e+1]) of a permuted
+// activation matrix A (K-major, bf16) are multiplied by that expert's packed
+// weight W[e] (N x K, K-major, bf16):  C_e = A_e . W[e]^T, fp32 accumulate.
+// Used twice per MoE block (nki_moe_integrated.py:154-161):
+//   GEMM-1: A = gathered tokens [R, H], W13[e] = [2I, H] -> SwiGLU epilogue -> h [R, I]
+//   GEMM-2: A = h [R, I],               W2[e]  = [H, I]  -> routing-weight epilogue -> Y [R, H]
+//
+// Two tile schedules over the same machinery:
+//   rows    (prefill): tile = 128 rows x BN features; A is the MMA's A operand.
+//   weights (decode):  tile = 128 features x BT rows ("swap AB"); the weight
+//                      block is the MMA's A operand so a handful of tokens per
+//                      expert still fills the 128-wide M dimension, and every
+//                      CTA streams whole weight blocks at HBM speed.
+//
+// Structure (persistent, one CTA per SM, 192 threads):
+//   warp 0: TMA producer     — fills a STAGES-deep ring of smem stages
+//   warp 1: MMA issuer       — tcgen05.mma (M=128, K=16 per instruction) into
+//                              one of two TMEM accumulators; tcgen05.commit
+//                              releases smem stages and publishes accumulators
+//   warps 2-5: epilogue      — tcgen05.ld, fused SwiGLU / scale, bf16 stores
+// Tiles are enumerated on the device from expert_offsets (no host sync):
+// expert-major, then feature block, then row block, so concurrently running
+// CTAs share weight panels through L2.
+#include <algorithm>
+#include <atomic>
+
+#include "kernels.h"
+
+namespace nkimoe {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int BM = 128;  // MMA M (rows of the A operand per tile)
+constexpr int BK = 64;   // bf16 elements per 128-byte swizzled row
+constexpr int UK = 16;   // K per tcgen05.mma kind::f16
+
+struct SharedCtl {
+  uint64_t full[16];
+  uint64_t empty[16];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int seg[kMaxExperts + 1];         // expert row offsets
+  int tile_start[kMaxExperts + 1];  // first tile of each expert
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// Warp-wide: lane 0 waits, the result is broadcast (keeps the warp converged
+// for the .sync.aligned tcgen05 instructions that follow).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, SharedCtl& ctl, int* status) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, &ctl.abort_flag, status);
+  return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// Short bounded wait used only while tearing down after an abort.
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitBudgetCycles / 8) break;
+  }
+}
+
+// Per-expert tile table in smem.  tiles(e) = ceil(rows_e / rows_per_tile) * feat_tiles.
+__device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int E, int rows_per_tile, int feat_tiles) {
+  const int lane = threadIdx.x & 31;
+  int run = 0;
+  for (int b = 0; b < E; b += 32) {
+    const int e = b + lane;
+    int cnt = 0, s0 = 0;
+    if (e < E) {
+      s0 = offs[e];
+      cnt = offs[e + 1] - s0;
+    }
+    const int tiles = ((cnt + rows_per_tile - 1) / rows_per_tile) * feat_tiles;
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (e < E) {
+      ctl.tile_start[e] = run + incl - tiles;
+      ctl.seg[e] = s0;
+    }
+    run += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) {
+    ctl.tile_start[E] = run;
+    ctl.seg[E] = offs[E];
+  }
+}
+
+struct TileCoord {
+  int e;       // expert
+  int rblk;    // row block within the expert
+  int fblk;    // feature block within the expert
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const SharedCtl& ctl, int E, int tile, int rows_per_tile,
+                                                 int feat_tiles) {
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (ctl.tile_start[mid] <= tile) lo = mid;
+    else hi = mid - 1;
+  }
+  const int local = tile - ctl.tile_start[lo];
+  const int rtiles = (ctl.tile_start[lo + 1] - ctl.tile_start[lo]) / feat_tiles;
+  TileCoord c;
+  c.e = lo;
+  c.fblk = local / rtiles;
+  c.rblk = local % rtiles;
+  (void)rows_per_tile;
+  return c;
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float (&v)[N]) {
+  static_assert(N % 16 == 0, "column count");
+  if constexpr (N % 32 == 0) {
+#pragma unroll
+    for (int c = 0; c < N; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[c + j] = __uint_as_float(r[j]);
+    }
+  } else {
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(taddr, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+    u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+    u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+    u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    d[q] = u;
+  }
+}
+
+// ============================================================ rows schedule
+// Tile: 128 activation rows x BN packed features.  A = activations (box 64 x
+// 128), B = weights (box 64 x BN), D[row][feature] in TMEM lanes x columns.
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_rows_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
+                             const GroupedGemmParams p) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(STAGES <= 16, "stages");
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SharedCtl ctl;
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * A_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.num_experts;
+  const int feat_tiles = p.n / BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl.acc_full[a], 1);
+      mbar_init(&ctl.acc_empty[a], 4 * 32);
+    }
+    mbar_init(&ctl.drain, 1);
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_act);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, E, BM, feat_tiles);
+  tcgen05_fence_before();
+  __syncthreads();
+  tcgen05_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total_tiles = ctl.tile_start[E];
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, last_phase_mask = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
+      const int row0 = ctl.seg[tc.e] + tc.rblk * BM;
+      const int wrow0 = tc.e * p.n + tc.fblk * BN;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
+          tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, row0);
+          tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0);
+        }
+        issued_mask |= 1u << stage;
+        last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && lane == 0) {  // let copies in flight land before the CTA exits
+      for (int s = 0; s < STAGES; ++s)
+        if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true, issued = false;
+    int t_local = 0;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      if (!warp_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, ctl, p.status)) {
+        ok = false;
+        break;
+      }
+      tcgen05_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!warp_wait(&ctl.full[stage], phase, ctl, p.status)) {
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sb + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k) {
+            umma_bf16(d_tmem, umma_desc_sw128(a0 + k * UK * 2), umma_desc_sw128(b0 + k * UK * 2), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&ctl.empty[stage]);
+          issued = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&ctl.acc_full[acc]);
+      __syncwarp();
+    }
+    if (!ok && lane == 0 && issued) {  // wait for issued MMAs before TMEM is released
+      umma_commit(&ctl.drain);
+      drain_wait(&ctl.drain, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const int row_in_tile = quarter * 32 + lane;
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t_local) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      if (!warp_wait(&ctl.acc_full[acc], acc_phase, ctl, p.status)) break;
+      tcgen05_fence_after();
+      const int seg_end = ctl.seg[tc.e + 1];
+      const int r = ctl.seg[tc.e] + tc.rblk * BM + row_in_tile;
+      const bool valid = r < seg_end;
+      const long long orow = valid ? (p.out_row_map ? p.out_row_map[r] : r) : 0;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+
+      if (p.epilogue == kEpiSwiGLU) {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+        for (int blk = 0; blk < BN / 128; ++blk) {
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            float g[32], u[32];
+            tmem_ld_cols<32>(tbase + blk * 128 + half * 32, g);
+            tmem_ld_cols<32>(tbase + blk * 128 + 64 + half * 32, u);
+            if (valid) {
+              float h[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) h[j] = silu_f(g[j]) * u[j];
+              const long long col = static_cast<long long>(tc.fblk) * (BN / 2) + blk * 64 + half * 32;
+              store_bf16x32(out + orow * p.out_ld + col, h);
+            }
+          }
+        }
+      } else if (p.epilogue == kEpiScaleBf16 || p.epilogue == kEpiStoreBf16) {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+        const float scale = (p.epilogue == kEpiScaleBf16 && valid) ? p.slot_weight[p.row_slot[r]] : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld_cols<32>(tbase + c, v);
+          if (valid) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= scale;
+            store_bf16x32(out + orow * p.out_ld + static_cast<long long>(tc.fblk) * BN + c, v);
+          }
+        }
+      } else {  // kEpiStoreF32
+        float* out = static_cast<float*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld_cols<32>(tbase + c, v);
+          if (valid) {
+            const long long col0 = static_cast<long long>(tc.fblk) * BN + c;
+            float4* dst = reinterpret_cast<float4*>(out + orow * p.out_ld + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 f = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              if (p.col_bias) {
+                f.x += p.col_bias[col0 + 4 * q];
+                f.y += p.col_bias[col0 + 4 * q + 1];
+                f.z += p.col_bias[col0 + 4 * q + 2];
+                f.w += p.col_bias[col0 + 4 * q + 3];
+              }
+              dst[q] = f;
+            }
+          }
+        }
+      }
+      tcgen05_fence_before();
+      mbar_arrive(&ctl.acc_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tcgen05_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ============================================================ weights schedule
+// Tile: 128 packed features x BT activation rows.  A = weight block (box 64 x
+// 128), B = activation rows (box 64 x BT); D[feature][row].
+template <int BT, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_weights_kernel(const __grid_constant__ CUtensorMap tmap_act,
+                                const __grid_constant__ CUtensorMap tmap_w, const GroupedGemmParams p) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;  // weight block
+  constexpr uint32_t B_BYTES = BT * BK * 2;  // activation rows
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = (2 * BT < 32) ? 32 : 2 * BT;
+  static_assert(STAGES <= 16, "stages");
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SharedCtl ctl;
+  __shared__ float xch[64][BT + 1];  // up-projection values handed to the gate lanes
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * A_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = p.num_experts;
+  const int feat_tiles = p.n / BM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl.acc_full[a], 1);
+      mbar_init(&ctl.acc_empty[a], 4 * 32);
+    }
+    mbar_init(&ctl.drain, 1);
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_act);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, E, BT, feat_tiles);
+  tcgen05_fence_before();
+  __syncthreads();
+  tcgen05_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total_tiles = ctl.tile_start[E];
+
+  if (warp == 0) {
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, last_phase_mask = 0;
+    bool ok = true;
+    const uint64_t pol_w = policy_evict_first();
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
+      const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
+      const int wrow0 = tc.e * p.n + tc.fblk * BM;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
+          tma_load_2d_hint(sa + stage * A_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0, pol_w);
+          tma_load_2d(sb + stage * B_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, row0);
+        }
+        issued_mask |= 1u << stage;
+        last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      for (int s = 0; s < STAGES; ++s)
+        if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BT);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true, issued = false;
+    int t_local = 0;
+    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      if (!warp_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, ctl, p.status)) {
+        ok = false;
+        break;
+      }
+      tcgen05_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BT;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!warp_wait(&ctl.full[stage], phase, ctl, p.status)) {
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sb + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k) {
+            umma_bf16(d_tmem, umma_desc_sw128(a0 + k * UK * 2), umma_desc_sw128(b0 + k * UK * 2), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&ctl.empty[stage]);
+          issued = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&ctl.acc_full[acc]);
+      __syncwarp();
+    }
+    if (!ok && lane == 0 && issued) {
+      umma_commit(&ctl.drain);
+      drain_wait(&ctl.drain, 0);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int feat = quarter * 32 + lane;  // TMEM lane = feature row of the tile
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t_local) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      const bool ok = warp_wait(&ctl.acc_full[acc], acc_phase, ctl, p.status);
+      // the SwiGLU hand-off below uses a named barrier over all four warps:
+      // every epilogue warp must take the same path, so the stop decision is
+      // a vote over all 128 threads
+      if (named_bar_any(1, 128, !ok)) break;
+      tcgen05_fence_after();
+      const int r0 = ctl.seg[tc.e] + tc.rblk * BT;
+      const int nvalid = min(BT, ctl.seg[tc.e + 1] - r0);
+      float v[BT];
+      tmem_ld_cols<BT>(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BT, v);
+      tcgen05_fence_before();
+      mbar_arrive(&ctl.acc_empty[acc]);  // accumulator is in registers now
+
+      if (p.epilogue == kEpiSwiGLU) {
+        // lanes 0-63: gate of feature tc.fblk*64 + feat; lanes 64-127: up of feature - 64
+        if (feat >= 64) {
+#pragma unroll
+          for (int j = 0; j < BT; ++j) xch[feat - 64][j] = v[j];
+        }
+        named_bar_sync(1, 128);
+        if (feat < 64) {
+          __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+          const long long col = static_cast<long long>(tc.fblk) * 64 + feat;
+#pragma unroll
+          for (int j = 0; j < BT; ++j) {
+            if (j >= nvalid) break;
+            const long long r = r0 + j;
+            const long long orow = p.out_row_map ? p.out_row_map[r] : r;
+            out[orow * p.out_ld + col] = __float2bfloat16_rn(silu_f(v[j]) * xch[feat][j]);
+          }
+        }
+      } else if (p.epilogue == kEpiScaleBf16 || p.epilogue == kEpiStoreBf16) {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+        const long long col = static_cast<long long>(tc.fblk) * BM + feat;
+#pragma unroll
+        for (int j = 0; j < BT; ++j) {
+          if (j >= nvalid) break;
+          const long long r = r0 + j;
+          const float sc = p.epilogue == kEpiScaleBf16 ? p.slot_weight[p.row_slot[r]] : 1.f;
+          const long long orow = p.out_row_map ? p.out_row_map[r] : r;
+          out[orow * p.out_ld + col] = __float2bfloat16_rn(sc * v[j]);
+        }
+      } else {
+        float* out = static_cast<float*>(p.out);
+        const long long col = static_cast<long long>(tc.fblk) * BM + feat;
+        const float b = p.col_bias ? p.col_bias[col] : 0.f;
+#pragma unroll
+        for (int j = 0; j < BT; ++j) {
+          if (j >= nvalid) break;
+          const long long r = r0 + j;
+          const long long orow = p.out_row_map ? p.out_row_map[r] : r;
+          out[orow * p.out_ld + col] = v[j] + b;
+        }
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tcgen05_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// The dynamic shared-memory opt-in is set once per kernel and device (not
+// per launch), so launches can be captured into CUDA graphs.
+template <typename K>
+cudaError_t launch_with_smem(K kernel, size_t smem, int grid, const CUtensorMap& a, const CUtensorMap& w,
+                             const GroupedGemmParams& p, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};  // bit d: done on device d
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit);
+  }
+  kernel<<<grid, kThreads, smem, s>>>(a, w, p);
+  return cudaGetLastError();
+}
+
+constexpr size_t rows_smem(int bn, int stages) { return static_cast<size_t>(stages) * (BM * BK * 2 + bn * BK * 2) + 1024; }
+constexpr size_t weights_smem(int bt, int stages) {
+  return static_cast<size_t>(stages) * (BM * BK * 2 + bt * BK * 2) + 1024;
+}
+
+}  // namespace
+
+int grouped_gemm_box_rows_act(int variant) {
+  switch (variant) {
+    case kRowsBN256:
+    case kRowsBN128: return BM;
+    case kWeightsT16: return 16;
+    case kWeightsT32: return 32;
+    case kWeightsT64: return 64;
+  }
+  return 0;
+}
+
+int grouped_gemm_box_rows_w(int variant) {
+  switch (variant) {
+    case kRowsBN256: return 256;
+    case kRowsBN128: return 128;
+    default: return BM;
+  }
+}
+
+cudaError_t grouped_gemm_launch(int variant, const CUtensorMap& tmap_act, const CUtensorMap& tmap_w,
+                                const GroupedGemmParams& p, int grid, cudaStream_t s) {
+  switch (variant) {
+    case kRowsBN256:
+      return launch_with_smem(grouped_gemm_rows_kernel<256, 4>, rows_smem(256, 4), grid, tmap_act, tmap_w, p, s);
+    case kRowsBN128:
+      return launch_with_smem(grouped_gemm_rows_kernel<128, 6>, rows_smem(128, 6), grid, tmap_act, tmap_w, p, s);
+    case kWeightsT16:
+      return launch_with_smem(grouped_gemm_weights_kernel<16, 8>, weights_smem(16, 8), grid, tmap_act, tmap_w, p, s);
+    case kWeightsT32:
+      return launch_with_smem(grouped_gemm_weights_kernel<32, 8>, weights_smem(32, 8), grid, tmap_act, tmap_w, p, s);
+    case kWeightsT64:
+      return launch_with_smem(grouped_gemm_weights_kernel<64, 6>, weights_smem(64, 6), grid, tmap_act, tmap_w, p, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace nkimoe

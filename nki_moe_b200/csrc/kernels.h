@@ -1,0 +1,123 @@
+// Internal launch interface between the C-ABI layer (capi.cu) and the kernel
+// translation units.  Everything here is stream-ordered and allocation-free.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace nkimoe {
+
+// dtype codes shared with include/nkimoe.h
+constexpr int kF32 = 0;
+constexpr int kBF16 = 1;
+constexpr int kI32 = 2;
+constexpr int kI64 = 3;
+
+constexpr int kMaxExperts = 512;
+
+// Stages of a block call, in launch order (for nkimoe_set_stage_events).
+enum Stage : int {
+  kStageRouter = 0,
+  kStageTopk = 1,
+  kStagePermute = 2,
+  kStageGather = 3,
+  kStageGemm1 = 4,
+  kStageGemm2 = 5,
+  kStageCombine = 6,
+  kStageEnd = 7,
+  kNumStageEvents = 8,
+};
+constexpr int kPermuteChunk = 256;  // assignments per block in the permutation kernels
+
+// ----------------------------------------------------------------- norms
+cudaError_t rmsnorm_launch(const void* x, int x_dtype, const void* w, int w_dtype, void* out, int out_dtype,
+                           long long rows, int hidden, float eps, cudaStream_t s);
+cudaError_t add_rmsnorm_launch(const void* x, const void* residual, void* residual_out, const void* w, int w_dtype,
+                               void* out, long long rows, int hidden, float eps, cudaStream_t s);
+cudaError_t qk_norm_rope_launch(const void* qkv_in, void* qkv_out, const void* qw, const void* kw, int w_dtype,
+                                const long long* positions, long long tokens, int n_heads, int n_kv, int head_dim,
+                                float theta, float eps, cudaStream_t s);
+
+// ----------------------------------------------------------------- router
+// fp32 logits = x(bf16) . Wr(fp32)^T (+ bias), CUDA-core fp32 FMA, fixed order.
+cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits,
+                                      int tokens, int hidden, int experts, cudaStream_t s);
+// Split fp32 router weights into three bf16 planes [E, 3H] = hi | mid | lo.
+cudaError_t router_split_launch(const float* wr, __nv_bfloat16* wsplit, int experts, int hidden, cudaStream_t s);
+// softmax -> top-k (by logit, ties to the lower id) -> renormalise.
+cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
+                                cudaStream_t s);
+
+// ----------------------------------------------------------------- permutation
+size_t permute_scratch_bytes(long long tokens, int top_k, int experts);
+cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k, int experts, int32_t* row_token,
+                           int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* scratch,
+                           int* status, cudaStream_t s);
+cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token, const int32_t* expert_offsets,
+                               int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s);
+cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
+                           __nv_bfloat16* out, int tokens, int top_k, int hidden, cudaStream_t s);
+cudaError_t aggregate_launch(const __nv_bfloat16* expert_outputs, __nv_bfloat16* out, int top_k, long long tokens,
+                             int hidden, cudaStream_t s);
+cudaError_t swiglu_launch(const __nv_bfloat16* gate_up, __nv_bfloat16* out, long long rows, int n, cudaStream_t s);
+
+// ----------------------------------------------------------------- weight packing
+// gate_up [E, H, 2I] (gate columns first) -> [E, 2I, H] K-major with the
+// 64-row interleave [gate 64 | up 64] per 128-row block.
+cudaError_t pack_gate_up_nxd_launch(const __nv_bfloat16* in, __nv_bfloat16* out, int experts, int hidden,
+                                    int inter, cudaStream_t s);
+// gate_up [E, 2I, H] (HF layout) -> same packed layout (row permutation).
+cudaError_t pack_gate_up_hf_launch(const __nv_bfloat16* in, __nv_bfloat16* out, int experts, int hidden, int inter,
+                                   cudaStream_t s);
+// [B, R, C] -> [B, C, R] (bf16); used for down_proj [E, I, H] -> [E, H, I].
+cudaError_t transpose_launch(const __nv_bfloat16* in, __nv_bfloat16* out, int batch, int rows, int cols,
+                             cudaStream_t s);
+
+// ----------------------------------------------------------------- grouped GEMM (tcgen05)
+enum Epilogue : int {
+  kEpiSwiGLU = 0,     // bf16 [R, N/2] = silu(gate) * up on the packed gate/up layout
+  kEpiScaleBf16 = 1,  // bf16 [R, N] = slot_weight[row_slot[r]] * acc
+  kEpiStoreBf16 = 2,  // bf16 [R, N]
+  kEpiStoreF32 = 3,   // f32  [R, N] (+ col_bias[N])
+};
+
+struct GroupedGemmParams {
+  const int32_t* expert_offsets;  // [E+1] segment starts of each expert's rows
+  int num_experts;
+  int n;           // output features per expert (rows of one expert's packed weight)
+  int k_blocks;    // 64-wide K blocks iterated
+  int k_blocks_a;  // 64-wide K blocks in an activation row (k coordinate of A wraps modulo this)
+  int epilogue;
+  void* out;
+  long long out_ld;           // elements
+  const float* slot_weight;   // kEpiScaleBf16
+  const int32_t* row_slot;    // kEpiScaleBf16
+  const int32_t* out_row_map; // optional: output row of permuted row r
+  const float* col_bias;      // kEpiStoreF32 optional
+  int* status;
+};
+
+// Tile shape choices exposed to the host.
+enum GemmVariant : int {
+  kRowsBN256 = 0,  // 128 rows x 256 features per tile (prefill)
+  kRowsBN128 = 1,  // 128 rows x 128 features per tile
+  kWeightsT16 = 2, // 128 features x 16 rows per tile (decode, swap-AB)
+  kWeightsT32 = 3, // 128 features x 32 rows per tile
+  kWeightsT64 = 4, // 128 features x 64 rows per tile
+};
+
+// Builds a 2-D bf16 TMA descriptor with 128-byte swizzling over a row-major
+// [rows, cols] tensor; box = 64 columns x box_rows rows.
+bool make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, int box_rows);
+
+cudaError_t grouped_gemm_launch(int variant, const CUtensorMap& tmap_act, const CUtensorMap& tmap_w,
+                                const GroupedGemmParams& p, int grid, cudaStream_t s);
+int grouped_gemm_box_rows_act(int variant);
+int grouped_gemm_box_rows_w(int variant);
+
+int device_sm_count();
+
+}  // namespace nkimoe

@@ -1,0 +1,236 @@
+// K1: RMSNorm over rows of a [rows, hidden] tensor (nki_custom_rmsnorm.py:8-70)
+//     y = x * rsqrt(mean(x^2) + eps) * w, fp32 arithmetic, one warp per row,
+//     128-bit loads/stores.  Optional fused residual add in front of it
+//     (the decoder's `h = h + attn; post_attention_layernorm(h)`,
+//     qwen_with_nki.py:447-452).
+// K6: per-head q/k RMSNorm + rotate-half RoPE on a fused [Q | K | V] row
+//     (qwen_with_nki.py:330-350 with the HF Qwen3-MoE order: norm, then RoPE).
+#include "kernels.h"
+
+namespace nkimoe {
+
+namespace {
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  float4 a = *reinterpret_cast<const float4*>(p);
+  float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void round_bf16(float (&v)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Rows of up to kMaxChunks*8*32 elements are held in registers (one pass over
+// HBM); longer rows are re-read from L2 for the second pass.
+constexpr int kMaxChunks = 8;  // 2048 elements per row in registers
+
+template <typename TX, typename TW, typename TO, bool kResidual>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const TX* x, const TX* residual, TX* residual_out,
+                                                      const TW* __restrict__ w, TO* out, long long rows, int hidden, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nchunk = hidden >> 3;  // 8-element chunks
+  const TX* xr = x + row * hidden;
+  float v[kMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) {
+      load8(xr + c * 8, v[i]);
+      if constexpr (kResidual) {
+        float r[8];
+        load8(residual + row * hidden + c * 8, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+        // the sum is rounded to the residual stream's dtype before the norm
+        round_bf16(v[i]);
+        store8(residual_out + row * hidden + c * 8, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+    }
+  }
+  for (int c = lane + kMaxChunks * 32; c < nchunk; c += 32) {
+    float t[8];
+    if constexpr (kResidual) {
+      float r[8];
+      load8(xr + c * 8, t);
+      load8(residual + row * hidden + c * 8, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] += r[j];
+      round_bf16(t);
+      store8(residual_out + row * hidden + c * 8, t);
+    } else {
+      load8(xr + c * 8, t);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(t[j], t[j], ss);
+  }
+  ss = warp_sum(ss);
+  const float rinv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+  TO* orow = out + row * hidden;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) {
+      float wv[8], o[8];
+      load8(w + c * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rinv * wv[j];
+      store8(orow + c * 8, o);
+    }
+  }
+  const TX* src = kResidual ? residual_out + row * hidden : xr;
+  for (int c = lane + kMaxChunks * 32; c < nchunk; c += 32) {
+    float t[8], wv[8];
+    load8(src + c * 8, t);
+    load8(w + c * 8, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = t[j] * rinv * wv[j];
+    store8(orow + c * 8, t);
+  }
+}
+
+template <typename TX, typename TW, typename TO, bool kRes>
+cudaError_t launch_rms(const void* x, const void* res, void* res_out, const void* w, void* out, long long rows,
+                       int hidden, float eps, cudaStream_t s) {
+  const int warps = 8;
+  const long long blocks = (rows + warps - 1) / warps;
+  rmsnorm_kernel<TX, TW, TO, kRes><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(
+      static_cast<const TX*>(x), static_cast<const TX*>(res), static_cast<TX*>(res_out),
+      static_cast<const TW*>(w), static_cast<TO*>(out), rows, hidden, eps);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t rmsnorm_launch(const void* x, int x_dtype, const void* w, int w_dtype, void* out, int out_dtype,
+                           long long rows, int hidden, float eps, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  using bf = __nv_bfloat16;
+#define NKI_RMS(TX, TW, TO) return launch_rms<TX, TW, TO, false>(x, nullptr, nullptr, w, out, rows, hidden, eps, s)
+  if (x_dtype == kBF16 && w_dtype == kF32 && out_dtype == kBF16) NKI_RMS(bf, float, bf);
+  if (x_dtype == kBF16 && w_dtype == kBF16 && out_dtype == kBF16) NKI_RMS(bf, bf, bf);
+  if (x_dtype == kBF16 && w_dtype == kF32 && out_dtype == kF32) NKI_RMS(bf, float, float);
+  if (x_dtype == kF32 && w_dtype == kF32 && out_dtype == kF32) NKI_RMS(float, float, float);
+  if (x_dtype == kF32 && w_dtype == kF32 && out_dtype == kBF16) NKI_RMS(float, float, bf);
+  if (x_dtype == kF32 && w_dtype == kBF16 && out_dtype == kF32) NKI_RMS(float, bf, float);
+#undef NKI_RMS
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t add_rmsnorm_launch(const void* x, const void* residual, void* residual_out, const void* w, int w_dtype,
+                               void* out, long long rows, int hidden, float eps, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  using bf = __nv_bfloat16;
+  if (w_dtype == kF32) return launch_rms<bf, float, bf, true>(x, residual, residual_out, w, out, rows, hidden, eps, s);
+  if (w_dtype == kBF16) return launch_rms<bf, bf, bf, true>(x, residual, residual_out, w, out, rows, hidden, eps, s);
+  return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------ K6
+// One warp per (token, head) for the q and k heads; v heads are copied when
+// the output is a different buffer.  head_dim 128: lane l owns elements
+// [4l, 4l+4); its rotate-half partner lives in lane l ^ 16.
+namespace {
+
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+__device__ __forceinline__ float wload(const void* w, int w_dtype, int i) {
+  return w_dtype == kF32 ? static_cast<const float*>(w)[i]
+                         : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
+}
+
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, const void* qw,
+                                                           const void* kw, int w_dtype,
+                                                           const long long* __restrict__ positions, long long tokens,
+                                                           int n_heads, int n_kv, float theta, float eps) {
+  constexpr int D = 128;
+  const int lane = threadIdx.x & 31;
+  const int heads_total = n_heads + 2 * n_kv;
+  const long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= tokens * heads_total) return;
+  const long long t = gw / heads_total;
+  const int h = static_cast<int>(gw % heads_total);
+  const long long base = t * heads_total * D + static_cast<long long>(h) * D + lane * 4;
+  float v[4];
+  load4(in + base, v);
+  if (h >= n_heads + n_kv) {  // V head: pass through
+    if (in != out) *reinterpret_cast<uint2*>(out + base) = *reinterpret_cast<const uint2*>(in + base);
+    return;
+  }
+  const void* w = h < n_heads ? qw : kw;
+  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+  ss = warp_sum(ss);
+  const float rinv = rsqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = v[j] * rinv * wload(w, w_dtype, lane * 4 + j);
+  // rotate-half partner: element i pairs with i + 64 (first half) / i - 64
+  float pv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) pv[j] = __shfl_xor_sync(0xffffffffu, v[j], 16);
+  const float pos = static_cast<float>(positions[t]);
+  const bool first = lane < 16;
+  float o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int i = lane * 4 + j;
+    const int fi = i & (D / 2 - 1);  // frequency index (emb = cat(freqs, freqs))
+    const float inv_freq = 1.0f / powf(theta, static_cast<float>(2 * fi) / static_cast<float>(D));
+    const float ang = pos * inv_freq;
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    const float rot = first ? -pv[j] : pv[j];
+    o[j] = v[j] * cs + rot * sn;
+  }
+  uint2 u;
+  u.x = pack_bf16x2(o[0], o[1]);
+  u.y = pack_bf16x2(o[2], o[3]);
+  *reinterpret_cast<uint2*>(out + base) = u;
+}
+
+}  // namespace
+
+cudaError_t qk_norm_rope_launch(const void* qkv_in, void* qkv_out, const void* qw, const void* kw, int w_dtype,
+                                const long long* positions, long long tokens, int n_heads, int n_kv, int head_dim,
+                                float theta, float eps, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (head_dim != 128) return cudaErrorInvalidValue;
+  const long long warps_total = tokens * (n_heads + 2 * n_kv);
+  const int wpb = 8;
+  const long long blocks = (warps_total + wpb - 1) / wpb;
+  qk_norm_rope_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(qkv_in), static_cast<__nv_bfloat16*>(qkv_out), qw, kw, w_dtype, positions,
+      tokens, n_heads, n_kv, theta, eps);
+  return cudaGetLastError();
+}
+
+}  // namespace nkimoe

@@ -1,0 +1,304 @@
+// K3: permutation of the T*K (token, slot) assignments by expert, and the
+// row movers around the expert GEMMs.
+//
+// Order contract (nki_moe_integrated.py:450-467): slot k outer, expert inner,
+// tokens ascending, i.e. inside expert e the rows are sorted by (k, t).  The
+// assignments are walked in k-major order j = k*T + t; the permutation is a
+// stable counting sort of j by expert:
+//   1. count:   per 256-assignment chunk, per-expert counts        [C][E]
+//   2. scan:    per expert, exclusive prefix over chunks + totals   [C][E], [E]
+//   3. scatter: per chunk, expert offset + chunk base + rank of the
+//               assignment among earlier same-expert assignments of its chunk
+//               (warp match_any + popc, then per-warp counts).
+// No host synchronisation: the GEMMs read expert_offsets on the device.
+#include "kernels.h"
+
+namespace nkimoe {
+
+namespace {
+
+template <typename IdxT>
+__device__ __forceinline__ int load_expert(const IdxT* idx, long long j, int T, int K, int E, int* status) {
+  const long long k = j / T, t = j % T;
+  const long long e = static_cast<long long>(idx[t * K + k]);
+  if (e < 0 || e >= E) {
+    atomicOr(status, kDevErrBadIndex);
+    return -1;
+  }
+  return static_cast<int>(e);
+}
+
+template <typename IdxT>
+__global__ void __launch_bounds__(kPermuteChunk) permute_count_kernel(const IdxT* __restrict__ idx, int T, int K,
+                                                                      int E, int* __restrict__ chunk_counts,
+                                                                      int* status) {
+  __shared__ int cnt[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const long long j = static_cast<long long>(blockIdx.x) * kPermuteChunk + threadIdx.x;
+  if (j < static_cast<long long>(T) * K) {
+    const int e = load_expert(idx, j, T, K, E, status);
+    if (e >= 0) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) chunk_counts[static_cast<long long>(blockIdx.x) * E + e] = cnt[e];
+}
+
+// One block per expert: exclusive scan of that expert's chunk counts.
+__global__ void __launch_bounds__(256) permute_scan_kernel(const int* __restrict__ chunk_counts, int C, int E,
+                                                           int* __restrict__ chunk_base, int* __restrict__ totals) {
+  __shared__ int warp_tot[8];
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int running = 0;
+  for (int c0 = 0; c0 < C; c0 += 256) {
+    const int c = c0 + threadIdx.x;
+    const int v = c < C ? chunk_counts[static_cast<long long>(c) * E + e] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      before += w < warp ? warp_tot[w] : 0;
+      all += warp_tot[w];
+    }
+    if (c < C) chunk_base[static_cast<long long>(c) * E + e] = running + before + incl - v;
+    running += all;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) totals[e] = running;
+}
+
+template <typename IdxT>
+__global__ void __launch_bounds__(kPermuteChunk) permute_scatter_kernel(
+    const IdxT* __restrict__ idx, int T, int K, int E, const int* __restrict__ chunk_base,
+    const int* __restrict__ totals, int32_t* __restrict__ row_token, int32_t* __restrict__ row_slot,
+    int32_t* __restrict__ slot_row, int32_t* __restrict__ expert_offsets, int* status) {
+  constexpr int kWarps = kPermuteChunk / 32;
+  __shared__ int offs[kMaxExperts + 1];
+  __shared__ int wcnt[kWarps][kMaxExperts];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == 0) {  // expert offsets = exclusive scan of totals
+    int run = 0;
+    for (int b = 0; b < E; b += 32) {
+      const int e = b + lane;
+      const int v = e < E ? totals[e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (e < E) offs[e] = run + incl - v;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) offs[E] = run;
+  }
+  for (int i = threadIdx.x; i < kWarps * E; i += blockDim.x) wcnt[i / E][i % E] = 0;
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) expert_offsets[e] = offs[e];
+
+  const long long j = static_cast<long long>(blockIdx.x) * kPermuteChunk + threadIdx.x;
+  const bool valid = j < static_cast<long long>(T) * K;
+  int e = -1;
+  if (valid) {
+    // range errors were flagged by the count pass
+    const long long k = j / T, t = j % T;
+    const long long ev = static_cast<long long>(idx[t * K + k]);
+    e = (ev >= 0 && ev < E) ? static_cast<int>(ev) : -1;
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
+  __syncthreads();
+  if (!valid) return;
+  const long long k = j / T, t = j % T;
+  const long long slot = t * K + k;
+  if (e < 0) {
+    slot_row[slot] = -1;
+    return;
+  }
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += wcnt[w][e];
+  const int pos = offs[e] + chunk_base[static_cast<long long>(blockIdx.x) * E + e] + before + rank;
+  row_token[pos] = static_cast<int32_t>(t);
+  row_slot[pos] = static_cast<int32_t>(slot);
+  slot_row[slot] = pos;
+  (void)status;
+}
+
+// x_perm[r] = x[row_token[r]] for r < expert_offsets[E]; 16-byte moves.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                          const int32_t* __restrict__ row_token,
+                                                          const int32_t* __restrict__ expert_offsets, int E,
+                                                          __nv_bfloat16* __restrict__ xp, long long max_rows,
+                                                          int H) {
+  const int chunks = H >> 3;
+  const long long rows = min(static_cast<long long>(expert_offsets[E]), max_rows);
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * chunks;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / chunks;
+    const int c = static_cast<int>(i % chunks);
+    const long long t = row_token[r];
+    reinterpret_cast<uint4*>(xp + r * H)[c] = reinterpret_cast<const uint4*>(x + t * H)[c];
+  }
+}
+
+// out[t] = sum_k w[t,k] * y[slot_row[t*K+k]] in fp32 with k ascending (the
+// accumulation order of nki_moe_integrated.py:482-494).  When slot_weight is
+// null the rows already carry their routing weight.
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ y,
+                                                      const int32_t* __restrict__ slot_row,
+                                                      const float* __restrict__ slot_weight,
+                                                      __nv_bfloat16* __restrict__ out, int T, int K, int H) {
+  const int chunks = H >> 3;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < static_cast<long long>(T) * chunks; i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long t = i / chunks;
+    const int c = static_cast<int>(i % chunks);
+    float acc[8] = {};
+    for (int k = 0; k < K; ++k) {
+      const int r = slot_row[t * K + k];
+      if (r < 0) continue;
+      const uint4 u = reinterpret_cast<const uint4*>(y + static_cast<long long>(r) * H)[c];
+      const float wk = slot_weight ? slot_weight[t * K + k] : 1.f;
+      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+      acc[0] = fmaf(wk, a.x, acc[0]);
+      acc[1] = fmaf(wk, a.y, acc[1]);
+      acc[2] = fmaf(wk, b.x, acc[2]);
+      acc[3] = fmaf(wk, b.y, acc[3]);
+      acc[4] = fmaf(wk, cc.x, acc[4]);
+      acc[5] = fmaf(wk, cc.y, acc[5]);
+      acc[6] = fmaf(wk, d.x, acc[6]);
+      acc[7] = fmaf(wk, d.y, acc[7]);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * H)[c] = o;
+  }
+}
+
+// Sum over the leading top-k axis of [K, T, H] (nki_moe_integrated.py:209-251).
+__global__ void __launch_bounds__(256) aggregate_kernel(const __nv_bfloat16* __restrict__ eo,
+                                                        __nv_bfloat16* __restrict__ out, int K, long long T, int H) {
+  const int chunks = H >> 3;
+  const long long n = T * chunks;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float acc[8] = {};
+    for (int k = 0; k < K; ++k) {
+      const uint4 u = reinterpret_cast<const uint4*>(eo + static_cast<long long>(k) * T * H)[i];
+      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+      acc[0] += a.x; acc[1] += a.y; acc[2] += b.x; acc[3] += b.y;
+      acc[4] += cc.x; acc[5] += cc.y; acc[6] += d.x; acc[7] += d.y;
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+// silu(gate) * up over a [M, 2N] gate|up split (nki_moe_integrated.py:87-139).
+__global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                     __nv_bfloat16* __restrict__ out, long long M, int N) {
+  const long long n = M * N;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / N;
+    const int c = static_cast<int>(i % N);
+    const float g = __bfloat162float(gu[r * 2 * N + c]);
+    const float u = __bfloat162float(gu[r * 2 * N + N + c]);
+    out[i] = __float2bfloat16_rn(silu_f(g) * u);
+  }
+}
+
+unsigned grid_for(long long work, int threads) {
+  const long long b = (work + threads - 1) / threads;
+  const long long cap = static_cast<long long>(device_sm_count()) * 16;
+  return static_cast<unsigned>(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+}  // namespace
+
+size_t permute_scratch_bytes(long long tokens, int top_k, int experts) {
+  const long long C = (tokens * top_k + kPermuteChunk - 1) / kPermuteChunk;
+  // chunk_counts [C][E] + chunk_base [C][E] + totals [E]
+  return static_cast<size_t>((2 * C * experts + experts) * sizeof(int));
+}
+
+cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k, int experts, int32_t* row_token,
+                           int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* scratch,
+                           int* status, cudaStream_t s) {
+  if (experts > kMaxExperts || experts < 1) return cudaErrorInvalidValue;
+  const long long TK = static_cast<long long>(tokens) * top_k;
+  const int C = static_cast<int>((TK + kPermuteChunk - 1) / kPermuteChunk);
+  int* chunk_counts = static_cast<int*>(scratch);
+  int* chunk_base = chunk_counts + static_cast<long long>(C) * experts;
+  int* totals = chunk_base + static_cast<long long>(C) * experts;
+  if (C == 0) {
+    cudaMemsetAsync(expert_offsets, 0, sizeof(int32_t) * (experts + 1), s);
+    return cudaGetLastError();
+  }
+  if (idx_dtype == kI64) {
+    permute_count_kernel<long long><<<C, kPermuteChunk, 0, s>>>(static_cast<const long long*>(idx), tokens, top_k,
+                                                                experts, chunk_counts, status);
+  } else {
+    permute_count_kernel<int32_t><<<C, kPermuteChunk, 0, s>>>(static_cast<const int32_t*>(idx), tokens, top_k,
+                                                              experts, chunk_counts, status);
+  }
+  permute_scan_kernel<<<experts, 256, 0, s>>>(chunk_counts, C, experts, chunk_base, totals);
+  if (idx_dtype == kI64) {
+    permute_scatter_kernel<long long><<<C, kPermuteChunk, 0, s>>>(static_cast<const long long*>(idx), tokens, top_k,
+                                                                  experts, chunk_base, totals, row_token, row_slot,
+                                                                  slot_row, expert_offsets, status);
+  } else {
+    permute_scatter_kernel<int32_t><<<C, kPermuteChunk, 0, s>>>(static_cast<const int32_t*>(idx), tokens, top_k,
+                                                                experts, chunk_base, totals, row_token, row_slot,
+                                                                slot_row, expert_offsets, status);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token, const int32_t* expert_offsets,
+                               int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s) {
+  if (max_rows == 0) return cudaSuccess;
+  gather_rows_kernel<<<grid_for(max_rows * (hidden / 8), 256), 256, 0, s>>>(x, row_token, expert_offsets, experts,
+                                                                              x_perm, max_rows, hidden);
+  return cudaGetLastError();
+}
+
+cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
+                           __nv_bfloat16* out, int tokens, int top_k, int hidden, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  combine_kernel<<<grid_for(static_cast<long long>(tokens) * (hidden / 8), 256), 256, 0, s>>>(
+      y, slot_row, slot_weight, out, tokens, top_k, hidden);
+  return cudaGetLastError();
+}
+
+cudaError_t aggregate_launch(const __nv_bfloat16* eo, __nv_bfloat16* out, int top_k, long long tokens, int hidden,
+                             cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  aggregate_kernel<<<grid_for(tokens * (hidden / 8), 256), 256, 0, s>>>(eo, out, top_k, tokens, hidden);
+  return cudaGetLastError();
+}
+
+cudaError_t swiglu_launch(const __nv_bfloat16* gate_up, __nv_bfloat16* out, long long rows, int n, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  swiglu_kernel<<<grid_for(rows * n, 256), 256, 0, s>>>(gate_up, out, rows, n);
+  return cudaGetLastError();
+}
+
+}  // namespace nkimoe

@@ -1,0 +1,182 @@
+// K2: router of the sparse-MoE block (nki_moe_integrated.py:436-443):
+//   logits = x . Wr^T in fp32 (router dtype fp32, qwen_with_nki.py:276),
+//   p = softmax(logits), (w, idx) = topk(p, K) descending, w /= sum(w).
+#include "kernels.h"
+
+namespace nkimoe {
+
+namespace {
+
+// 64 tokens x 64 experts per CTA, 256 threads, 4x4 outputs per thread,
+// K staged through shared memory 32 at a time; each output is one fp32 FMA
+// chain in ascending k (deterministic, no TF32).
+constexpr int RT = 64, RE = 64, RK = 32;
+
+__global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            const float* __restrict__ wr,
+                                                            const float* __restrict__ bias, float* __restrict__ logits,
+                                                            int T, int H, int E) {
+  __shared__ __align__(16) float xs[RK][RT + 4];
+  __shared__ __align__(16) float ws[RK][RE + 4];
+  const int tid = threadIdx.x;
+  const int t0 = blockIdx.x * RT, e0 = blockIdx.y * RE;
+  const int ty = tid >> 4, tx = tid & 15;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < H; k0 += RK) {
+    {  // x tile: 64 tokens x 32 k (bf16), one 8-element chunk per thread
+      const int r = tid >> 2, c = (tid & 3) * 8;
+      float v[8] = {};
+      if (t0 + r < T) {
+        uint4 u = *reinterpret_cast<const uint4*>(x + static_cast<long long>(t0 + r) * H + k0 + c);
+        float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = cc.x; v[5] = cc.y; v[6] = d.x; v[7] = d.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xs[c + j][r] = v[j];
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {  // w tile: 64 experts x 32 k (fp32)
+      const int idx = tid + i * 256;
+      const int r = idx >> 3, c = (idx & 7) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e0 + r < E) v = *reinterpret_cast<const float4*>(wr + static_cast<long long>(e0 + r) * H + k0 + c);
+      ws[c + 0][r] = v.x;
+      ws[c + 1][r] = v.y;
+      ws[c + 2][r] = v.z;
+      ws[c + 3][r] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < RK; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= T) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e0 + tx * 4 + j;
+      if (e < E) logits[static_cast<long long>(t) * E + e] = acc[i][j] + (bias ? bias[e] : 0.f);
+    }
+  }
+}
+
+__global__ void router_split_kernel(const float* __restrict__ wr, __nv_bfloat16* __restrict__ out, int E, int H) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(E) * H) return;
+  const int e = static_cast<int>(i / H), h = static_cast<int>(i % H);
+  const float w = wr[i];
+  const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+  const float r1 = w - __bfloat162float(hi);
+  const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+  const float r2 = r1 - __bfloat162float(mid);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(r2);
+  __nv_bfloat16* row = out + static_cast<long long>(e) * 3 * H;
+  row[h] = hi;
+  row[H + h] = mid;
+  row[2 * H + h] = lo;
+}
+
+// One warp per token; lane l holds experts l, l+32, ... (VPT of them).
+template <int VPT>
+__global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int K,
+                                                           int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+  const int lane = threadIdx.x & 31;
+  const long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const float* row = logits + t * E;
+  float v[VPT];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? row[e] : -INFINITY;
+    m = fmaxf(m, v[j]);
+  }
+  m = warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E) s += expf(v[j] - m);
+  }
+  s = warp_sum(s);
+  unsigned taken = 0;  // bit j: expert lane + 32j already selected
+  int my_idx = 0;
+  float my_p = 0.f;
+  for (int r = 0; r < K; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((taken >> j) & 1u) && (v[j] > bv || (v[j] == bv && e < bi))) {
+        bv = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (lane == r) {
+      my_idx = bi;
+      my_p = expf(bv - m) / s;
+    }
+  }
+  float tot = warp_sum(lane < K ? my_p : 0.f);
+  if (lane < K) {
+    idx_out[t * K + lane] = my_idx;
+    w_out[t * K + lane] = my_p / tot;
+  }
+}
+
+}  // namespace
+
+cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits,
+                                      int tokens, int hidden, int experts, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (hidden % RK) return cudaErrorInvalidValue;
+  dim3 grid((tokens + RT - 1) / RT, (experts + RE - 1) / RE);
+  router_logits_kernel<<<grid, 256, 0, s>>>(x, wr, bias, logits, tokens, hidden, experts);
+  return cudaGetLastError();
+}
+
+cudaError_t router_split_launch(const float* wr, __nv_bfloat16* wsplit, int experts, int hidden, cudaStream_t s) {
+  const long long n = static_cast<long long>(experts) * hidden;
+  router_split_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(wr, wsplit, experts, hidden);
+  return cudaGetLastError();
+}
+
+cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
+                                cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (top_k < 1 || top_k > 32 || top_k > experts || experts > 256) return cudaErrorInvalidValue;
+  const int wpb = 8;
+  const unsigned blocks = static_cast<unsigned>((tokens + wpb - 1) / wpb);
+  const int vpt = (experts + 31) / 32;
+#define NKI_TOPK(V) topk_softmax_kernel<V><<<blocks, wpb * 32, 0, s>>>(logits, tokens, experts, top_k, idx, w)
+  if (vpt <= 1) NKI_TOPK(1);
+  else if (vpt <= 2) NKI_TOPK(2);
+  else if (vpt <= 4) NKI_TOPK(4);
+  else NKI_TOPK(8);
+#undef NKI_TOPK
+  return cudaGetLastError();
+}
+
+}  // namespace nkimoe

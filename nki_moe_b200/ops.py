@@ -1,0 +1,323 @@
+"""Tensor-level entry points over the C ABI.
+
+PyTorch is used here only as plumbing: device memory, the current CUDA
+stream and dtype conversions at the boundary.  Every computation runs in
+``libnkimoe.so``; CPU tensors are rejected (no CPU fallback).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from collections import OrderedDict
+
+import torch
+
+from . import _lib
+from ._lib import BF16, F32, I32, I64, LAYOUT_HF, LAYOUT_NXD, call, size_call
+
+__all__ = [
+    "rmsnorm", "add_rmsnorm", "qk_norm_rope", "router_logits", "topk_softmax", "permute",
+    "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
+    "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled",
+]
+
+_DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
+
+
+def sync_check_enabled() -> bool:
+    """When NKIMOE_SYNC_CHECK=1, every block call synchronises and raises on a
+    device-flagged fault (timeout, expert id out of range)."""
+    return os.environ.get("NKIMOE_SYNC_CHECK", "0") == "1"
+
+
+def _cuda(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this package has no CPU path)")
+    return t
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None and t.numel() > 0 else ctypes.c_void_p(0)
+
+
+def _s(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _contig(t: torch.Tensor, dtype=None) -> torch.Tensor:
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------- workspace
+_ws_lock = threading.Lock()
+_ws: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A per-(device, stream) scratch buffer from the torch caching allocator,
+    grown on demand and reused by later calls on the same stream."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    with _ws_lock:
+        buf = _ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _ws[key] = buf
+        return buf
+
+
+def read_status(ws: torch.Tensor) -> int:
+    st = ctypes.c_int(0)
+    call("nkimoe_read_status", _p(ws), _s(ws), ctypes.byref(st))
+    return st.value
+
+
+# ---------------------------------------------------------------- norms
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, out_dtype=None) -> torch.Tensor:
+    """``x * rsqrt(mean(x^2) + eps) * weight`` over the last axis (K1)."""
+    _cuda(x, "x")
+    _cuda(weight, "weight")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.to(torch.bfloat16)
+    if weight.dtype not in (torch.float32, torch.bfloat16):
+        weight = weight.float()
+    x = _contig(x)
+    weight = _contig(weight)
+    out_dtype = out_dtype or x.dtype
+    out = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    H = x.shape[-1]
+    rows = x.numel() // H if H else 0
+    call("nkimoe_rmsnorm", _p(x), _DT[x.dtype], _p(weight), _DT[weight.dtype], _p(out), _DT[out_dtype],
+         rows, H, float(eps), _s(x))
+    return out
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                residual_out: torch.Tensor | None = None):
+    """``r = x + residual``; returns ``(rmsnorm(r), r)`` (bf16)."""
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    residual = _contig(_cuda(residual, "residual"), torch.bfloat16)
+    weight = _contig(_cuda(weight, "weight"))
+    if weight.dtype not in (torch.float32, torch.bfloat16):
+        weight = weight.float()
+    if residual_out is None:
+        residual_out = torch.empty_like(x)
+    out = torch.empty_like(x)
+    H = x.shape[-1]
+    call("nkimoe_add_rmsnorm", _p(x), _p(residual), _p(residual_out), _p(weight), _DT[weight.dtype], _p(out),
+         x.numel() // H, H, float(eps), _s(x))
+    return out, residual_out
+
+
+def qk_norm_rope(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, positions: torch.Tensor,
+                 n_heads: int, n_kv_heads: int, head_dim: int = 128, theta: float = 1e6, eps: float = 1e-6,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-head q/k RMSNorm + rotate-half RoPE on a fused ``[T, (nh+2nkv)*d]``
+    bf16 QKV row (K6).  ``out`` may be ``qkv`` (in place)."""
+    qkv = _contig(_cuda(qkv, "qkv"), torch.bfloat16)
+    T = qkv.numel() // ((n_heads + 2 * n_kv_heads) * head_dim)
+    wdt = torch.float32 if q_weight.dtype == torch.float32 else torch.bfloat16
+    qw = _contig(_cuda(q_weight, "q_weight"), wdt)
+    kw = _contig(_cuda(k_weight, "k_weight"), wdt)
+    pos = _contig(_cuda(positions, "positions").reshape(-1), torch.int64)
+    if pos.numel() != T:
+        raise ValueError(f"positions has {pos.numel()} entries for {T} tokens")
+    if out is None:
+        out = torch.empty_like(qkv)
+    call("nkimoe_qk_norm_rope", _p(qkv), _p(out), _p(qw), _p(kw), _DT[wdt], _p(pos), T, n_heads, n_kv_heads,
+         head_dim, float(theta), float(eps), _s(qkv))
+    return out
+
+
+# ---------------------------------------------------------------- router
+def router_logits(x: torch.Tensor, router_w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    rw = _contig(_cuda(router_w, "router_w"), torch.float32)
+    b = _contig(bias, torch.float32) if bias is not None else None
+    T, H = x.shape
+    E = rw.shape[0]
+    out = torch.empty(T, E, dtype=torch.float32, device=x.device)
+    call("nkimoe_router_logits", _p(x), _p(rw), _p(b), _p(out), T, H, E, _s(x))
+    return out
+
+
+def topk_softmax(logits: torch.Tensor, top_k: int):
+    lg = _contig(_cuda(logits, "logits"), torch.float32)
+    T, E = lg.shape
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=lg.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=lg.device)
+    call("nkimoe_topk_softmax", _p(lg), T, E, top_k, _p(idx), _p(w), _s(lg))
+    return idx, w
+
+
+# ---------------------------------------------------------------- permutation
+def permute(idx: torch.Tensor, num_experts: int):
+    """Returns ``(row_token, row_slot, slot_row, expert_offsets)`` (int32)."""
+    idx = _contig(_cuda(idx, "idx"))
+    if idx.dtype not in (torch.int32, torch.int64):
+        idx = idx.to(torch.int64)
+    T, K = idx.shape
+    dev = idx.device
+    rt = torch.empty(T * K, dtype=torch.int32, device=dev)
+    rs = torch.empty(T * K, dtype=torch.int32, device=dev)
+    sr = torch.empty(T * K, dtype=torch.int32, device=dev)
+    off = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    nbytes = size_call("nkimoe_permute_workspace_bytes", T, K, num_experts)
+    ws = workspace(dev, nbytes)
+    call("nkimoe_permute", _p(idx), _DT[idx.dtype], T, K, num_experts, _p(rt), _p(rs), _p(sr), _p(off), _p(ws),
+         ws.numel(), _s(idx))
+    if sync_check_enabled():
+        read_status(ws)
+    return rt, rs, sr, off
+
+
+# ---------------------------------------------------------------- weights
+class PackedExperts:
+    """Expert weights in the GEMM layout: ``w13 [E, 2I, H]`` (K-major, 128-row
+    blocks of [gate 64 | up 64]) and ``w2 [E, H, I]`` (K-major), bf16."""
+
+    def __init__(self, w13: torch.Tensor, w2: torch.Tensor, num_experts: int, hidden: int, inter: int):
+        self.w13, self.w2 = w13, w2
+        self.num_experts, self.hidden, self.inter = num_experts, hidden, inter
+
+
+def pack_gate_up(gate_up: torch.Tensor, layout: str = "nxd") -> torch.Tensor:
+    g = _contig(_cuda(gate_up, "gate_up"), torch.bfloat16)
+    if layout == "nxd":
+        E, H, I2 = g.shape
+        code = LAYOUT_NXD
+    elif layout == "hf":
+        E, I2, H = g.shape
+        code = LAYOUT_HF
+    else:
+        raise ValueError(f"unknown layout {layout}")
+    out = torch.empty(E, I2, H, dtype=torch.bfloat16, device=g.device)
+    call("nkimoe_pack_gate_up", _p(g), code, _p(out), E, H, I2 // 2, _s(g))
+    return out
+
+
+def pack_down(down: torch.Tensor, layout: str = "nxd") -> torch.Tensor:
+    d = _contig(_cuda(down, "down"), torch.bfloat16)
+    if layout == "nxd":
+        E, I, H = d.shape
+        code = LAYOUT_NXD
+    elif layout == "hf":
+        E, H, I = d.shape
+        code = LAYOUT_HF
+    else:
+        raise ValueError(f"unknown layout {layout}")
+    out = torch.empty(E, H, I, dtype=torch.bfloat16, device=d.device)
+    call("nkimoe_pack_down", _p(d), code, _p(out), E, H, I, _s(d))
+    return out
+
+
+_pack_lock = threading.Lock()
+_pack_cache: "OrderedDict[tuple, PackedExperts]" = OrderedDict()
+_PACK_CACHE_MAX = int(os.environ.get("NKIMOE_PACK_CACHE", "4"))
+
+
+def _key(t: torch.Tensor):
+    return (t.data_ptr(), t._version, tuple(t.shape), t.dtype, t.device.index)
+
+
+def packed_experts(gate_up: torch.Tensor, down: torch.Tensor, layout: str = "nxd") -> PackedExperts:
+    """Pack (once) and cache by (pointer, version, shape) of the source tensors."""
+    key = (_key(gate_up), _key(down), layout)
+    with _pack_lock:
+        hit = _pack_cache.get(key)
+        if hit is not None:
+            _pack_cache.move_to_end(key)
+            return hit
+    w13 = pack_gate_up(gate_up.detach(), layout)
+    w2 = pack_down(down.detach(), layout)
+    E, I2, H = w13.shape
+    pe = PackedExperts(w13, w2, E, H, I2 // 2)
+    with _pack_lock:
+        _pack_cache[key] = pe
+        while len(_pack_cache) > _PACK_CACHE_MAX:
+            _pack_cache.popitem(last=False)
+    return pe
+
+
+# ---------------------------------------------------------------- MoE block
+def moe_experts(x: torch.Tensor, experts: PackedExperts, idx: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    """``out[t] = sum_k w[t,k] * FFN_{idx[t,k]}(x[t])`` (bf16 in/out)."""
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    idx = _contig(_cuda(idx, "idx"))
+    if idx.dtype not in (torch.int32, torch.int64):
+        idx = idx.to(torch.int64)
+    w = _contig(_cuda(weights, "weights"), torch.float32)
+    T, H = x.shape
+    K = idx.shape[1]
+    E, I = experts.num_experts, experts.inter
+    if H != experts.hidden or idx.shape[0] != T or w.shape != idx.shape:
+        raise ValueError("shape mismatch between hidden states, routing and expert weights")
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    nbytes = size_call("nkimoe_moe_workspace_bytes", T, H, I, E, K)
+    ws = workspace(x.device, nbytes)
+    call("nkimoe_moe_experts", _p(x), _p(experts.w13), _p(experts.w2), _p(idx), _DT[idx.dtype], _p(w), _p(out),
+         T, H, I, E, K, _p(ws), ws.numel(), _s(x))
+    if sync_check_enabled():
+        read_status(ws)
+    return out
+
+
+def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
+              bias: torch.Tensor | None = None, return_routing: bool = False):
+    """Router (fp32) + softmax/top-k/renormalise + experts (K2..K7)."""
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    rw = _contig(_cuda(router_w, "router_w"), torch.float32)
+    b = _contig(bias, torch.float32) if bias is not None else None
+    T, H = x.shape
+    E, I = experts.num_experts, experts.inter
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+    idx = w = None
+    if return_routing:
+        idx = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    nbytes = size_call("nkimoe_moe_workspace_bytes", T, H, I, E, top_k)
+    ws = workspace(x.device, nbytes)
+    call("nkimoe_moe_block", _p(x), _p(rw), _p(b), _p(experts.w13), _p(experts.w2), _p(out), _p(idx), _p(w),
+         T, H, I, E, top_k, _p(ws), ws.numel(), _s(x))
+    if sync_check_enabled():
+        read_status(ws)
+    return (out, idx, w) if return_routing else out
+
+
+# ---------------------------------------------------------------- pieces
+def grouped_gemm(a: torch.Tensor, w_packed: torch.Tensor, offsets: torch.Tensor,
+                 out_row_map: torch.Tensor | None = None, out_rows: int | None = None) -> torch.Tensor:
+    """``out[r] = a[r] @ w_packed[e]^T`` for rows r of expert segment e."""
+    a = _contig(_cuda(a, "a"), torch.bfloat16)
+    w = _contig(_cuda(w_packed, "w_packed"), torch.bfloat16)
+    off = _contig(_cuda(offsets, "offsets"), torch.int32)
+    M, Kd = a.shape
+    E, N, Kw = w.shape
+    if Kw != Kd:
+        raise ValueError("inner dimensions differ")
+    rows = M if out_rows is None else out_rows
+    out = torch.empty(rows, N, dtype=torch.bfloat16, device=a.device)
+    rm = _contig(out_row_map, torch.int32) if out_row_map is not None else None
+    st = workspace(a.device, 256)
+    call("nkimoe_grouped_gemm", _p(a), _p(w), _p(off), _p(rm), _p(out), M, N, Kd, E, _p(st), _s(a))
+    return out
+
+
+def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
+    g = _contig(_cuda(gate_up, "gate_up"), torch.bfloat16)
+    M, N2 = g.shape
+    out = torch.empty(M, N2 // 2, dtype=torch.bfloat16, device=g.device)
+    call("nkimoe_swiglu", _p(g), _p(out), M, N2 // 2, _s(g))
+    return out
+
+
+def aggregate(expert_outputs: torch.Tensor) -> torch.Tensor:
+    eo = _contig(_cuda(expert_outputs, "expert_outputs"), torch.bfloat16)
+    K, T, H = eo.shape
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=eo.device)
+    call("nkimoe_aggregate", _p(eo), _p(out), K, T, H, _s(eo))
+    return out

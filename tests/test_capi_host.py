@@ -1,0 +1,84 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol that
+include/nkimoe.h declares, and rejects bad arguments before touching a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from nki_moe_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(REPO, "include", "nkimoe.h")).read()
+    return sorted(set(re.findall(r"NKIMOE_API\s+[\w\s\*]+?\b(nkimoe_\w+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "nkimoe_moe_block" in names and "nkimoe_rmsnorm" in names
+    assert len(names) >= 19
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in nkimoe.h but not exported"
+    # the Python binding covers exactly the declared ABI
+    assert set(_lib.SIGNATURES) == set(declared_symbols())
+
+
+def test_version_and_options():
+    lib = _lib.load()
+    assert lib.nkimoe_version() >= 1
+    _lib.set_option("gemm_schedule", 2)
+    _lib.set_option("gemm_schedule", 0)
+    with pytest.raises(_lib.NKIMoEError) as ei:
+        _lib.set_option("no_such_option", 1)
+    assert ei.value.code == _lib.ERR_INVALID_ARG
+
+
+def test_workspace_sizes_are_host_functions():
+    small = _lib.size_call("nkimoe_moe_workspace_bytes", 64, 2048, 768, 128, 8)
+    big = _lib.size_call("nkimoe_moe_workspace_bytes", 8192, 2048, 768, 128, 8)
+    # dominated by the gathered rows (T*K*H bf16) and the SwiGLU output (T*K*I bf16)
+    assert big > 8192 * 8 * (2048 + 768) * 2
+    assert small < big
+    assert _lib.size_call("nkimoe_permute_workspace_bytes", 8192, 8, 128) > 0
+
+
+def test_argument_validation_without_gpu():
+    null = ctypes.c_void_p(0)
+    with pytest.raises(_lib.NKIMoEError) as ei:  # 600 experts > 512
+        _lib.call("nkimoe_moe_experts", null, null, null, null, _lib.I32, null, null, 4, 2048, 768, 600, 8,
+                  null, 0, null)
+    assert ei.value.code == _lib.ERR_UNSUPPORTED
+    with pytest.raises(_lib.NKIMoEError) as ei:  # hidden not a multiple of 8
+        _lib.call("nkimoe_rmsnorm", null, _lib.BF16, null, _lib.F32, null, _lib.BF16, 4, 100, 1e-6, null)
+    assert ei.value.code == _lib.ERR_UNSUPPORTED
+    with pytest.raises(_lib.NKIMoEError) as ei:  # workspace too small
+        _lib.call("nkimoe_moe_block", null, null, null, null, null, null, null, null, 64, 2048, 768, 128, 8,
+                  null, 16, null)
+    assert ei.value.code == _lib.ERR_WORKSPACE
+    with pytest.raises(_lib.NKIMoEError) as ei:
+        _lib.call("nkimoe_qk_norm_rope", null, null, null, null, _lib.F32, null, 4, 32, 4, 64, 1e6, 1e-6, null)
+    assert ei.value.code == _lib.ERR_UNSUPPORTED
+    # zero tokens is a valid no-op that touches nothing
+    _lib.call("nkimoe_rmsnorm", null, _lib.BF16, null, _lib.F32, null, _lib.BF16, 0, 2048, 1e-6, null)
+
+
+def test_reference_module_aliases():
+    import sys
+    import nki_moe_b200
+    nki_moe_b200.install_reference_aliases()
+    for name in nki_moe_b200.REFERENCE_MODULES:
+        assert sys.modules[name].__name__ == f"nki_moe_b200.{name}"
+    from nki_moe_integrated import NKIMoESimple, NKIMoEWrapper, enable_nki_moe, replace_with_nki_moe  # noqa
+    from nki_custom_rmsnorm import NKIRMSNorm, get_nki_rmsnorm_cls, nki_rmsnorm_kernel  # noqa
+    assert get_nki_rmsnorm_cls() is NKIRMSNorm
+    n = NKIRMSNorm(16)
+    with pytest.raises(ValueError):
+        n(__import__("torch").ones(16))  # 1-D input: ValueError, as nki_custom_rmsnorm.py:115
