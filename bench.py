@@ -146,6 +146,9 @@ def algorithmic(wl, idx_np=None):
 
 def stage_events(torch):
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    for e in evs:  # torch creates the CUDA event lazily, on its first record
+        e.record()
+    torch.cuda.synchronize()
     return evs
 
 

@@ -24,7 +24,9 @@
 // expert-major, then feature block, then row block, so concurrently running
 // CTAs share weight panels through L2.
 #include <algorithm>
-#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "kernels.h"
 
@@ -568,19 +570,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // The dynamic shared-memory opt-in is set once per kernel and device (not
 // per launch), so launches can be captured into CUDA graphs.
-template <typename K>
-cudaError_t launch_with_smem(K kernel, size_t smem, int grid, const CUtensorMap& a, const CUtensorMap& w,
-                             const GroupedGemmParams& p, cudaStream_t s) {
-  static std::atomic<uint64_t> configured{0};  // bit d: done on device d
+using GemmKernel = void (*)(CUtensorMap, CUtensorMap, GroupedGemmParams);
+
+cudaError_t ensure_smem_optin(GemmKernel kernel, size_t smem) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;  // (kernel, device)
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  const uint64_t bit = 1ull << (dev & 63);
-  if (!(configured.load() & bit)) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    configured.fetch_or(bit);
-  }
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
+
+cudaError_t launch_with_smem(GemmKernel kernel, size_t smem, int grid, const CUtensorMap& a, const CUtensorMap& w,
+                             const GroupedGemmParams& p, cudaStream_t s) {
+  cudaError_t e = ensure_smem_optin(kernel, smem);
+  if (e != cudaSuccess) return e;
   kernel<<<grid, kThreads, smem, s>>>(a, w, p);
   return cudaGetLastError();
 }

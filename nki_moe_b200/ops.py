@@ -10,6 +10,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
+import weakref
 from collections import OrderedDict
 
 import torch
@@ -216,28 +217,36 @@ def pack_down(down: torch.Tensor, layout: str = "nxd") -> torch.Tensor:
 
 
 _pack_lock = threading.Lock()
-_pack_cache: "OrderedDict[tuple, PackedExperts]" = OrderedDict()
+_pack_cache: "OrderedDict[tuple, tuple]" = OrderedDict()
 _PACK_CACHE_MAX = int(os.environ.get("NKIMOE_PACK_CACHE", "4"))
 
 
-def _key(t: torch.Tensor):
+def _stamp(t: torch.Tensor):
     return (t.data_ptr(), t._version, tuple(t.shape), t.dtype, t.device.index)
 
 
 def packed_experts(gate_up: torch.Tensor, down: torch.Tensor, layout: str = "nxd") -> PackedExperts:
-    """Pack (once) and cache by (pointer, version, shape) of the source tensors."""
-    key = (_key(gate_up), _key(down), layout)
+    """Pack (once) and cache.  An entry is reused only while the very same
+    source tensors are alive and unmodified (weak references + pointer,
+    version and shape stamps), so freed-and-reused memory never hits a stale
+    entry."""
+    key = (id(gate_up), id(down), layout)
     with _pack_lock:
         hit = _pack_cache.get(key)
         if hit is not None:
-            _pack_cache.move_to_end(key)
-            return hit
+            wg, wd, sg, sd, pe = hit
+            if wg() is gate_up and wd() is down and sg == _stamp(gate_up) and sd == _stamp(down):
+                _pack_cache.move_to_end(key)
+                return pe
+            del _pack_cache[key]
     w13 = pack_gate_up(gate_up.detach(), layout)
     w2 = pack_down(down.detach(), layout)
     E, I2, H = w13.shape
     pe = PackedExperts(w13, w2, E, H, I2 // 2)
     with _pack_lock:
-        _pack_cache[key] = pe
+        for k in [k for k, v in _pack_cache.items() if v[0]() is None or v[1]() is None]:
+            del _pack_cache[k]
+        _pack_cache[key] = (weakref.ref(gate_up), weakref.ref(down), _stamp(gate_up), _stamp(down), pe)
         while len(_pack_cache) > _PACK_CACHE_MAX:
             _pack_cache.popitem(last=False)
     return pe
