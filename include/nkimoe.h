@@ -98,6 +98,14 @@ NKIMOE_API int nkimoe_qk_norm_rope(const void* qkv_in, void* qkv_out, const void
 NKIMOE_API int nkimoe_router_logits(const void* x, const float* router_w, const float* router_bias, float* logits, int64_t T,
                          int64_t H, int64_t E, void* stream);
 
+/* Splits fp32 router weights [E,H] into three bf16 planes [E, 3H] =
+ * [hi | mid | lo] with hi + mid + lo == w exactly, for the tensor-core router
+ * of nkimoe_moe_block: with bf16 activations every product is exact and the
+ * accumulation is fp32, so the logits are fp32 logits.  No reference
+ * counterpart (the reference computes the fp32 router with nn.Linear,
+ * nki_moe_integrated.py:437). */
+NKIMOE_API int nkimoe_router_split(const float* router_w, void* router_w_split, int64_t E, int64_t H, void* stream);
+
 /* softmax -> top-k (descending; ties to the lower expert id) -> renormalise
  * (nki_moe_integrated.py:438-443).  idx int32 [T,K], w fp32 [T,K]. */
 NKIMOE_API int nkimoe_topk_softmax(const float* logits, int64_t T, int64_t E, int64_t K, int32_t* topk_idx, float* topk_w,
@@ -144,9 +152,12 @@ NKIMOE_API int nkimoe_moe_experts(const void* x, const void* w13, const void* w2
 
 /* Whole block, router included: NKIMoESimple.forward
  * (nki_moe_integrated.py:428-475) and NKIMoEWrapper._nki_forward (:292-387).
- * router_w fp32 [E,H]; router_bias fp32 [E] or NULL; topk_idx_out (int32
- * [T,K]) and topk_w_out (fp32 [T,K]) may be NULL. */
-NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const float* router_bias, const void* w13, const void* w2,
+ * router_w fp32 [E,H]; router_bias fp32 [E] or NULL; router_w_split (from
+ * nkimoe_router_split) or NULL: when given, large token counts run the router
+ * on the tensor cores; topk_idx_out (int32 [T,K]) and topk_w_out (fp32 [T,K])
+ * may be NULL. */
+NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const float* router_bias,
+                     const void* router_w_split, const void* w13, const void* w2,
                      void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
                      int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 

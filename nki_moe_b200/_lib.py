@@ -45,7 +45,9 @@ SIGNATURES = {
     "nkimoe_pack_down": (_i, [_vp, _i, _vp, _i64, _i64, _i64, _vp]),
     "nkimoe_moe_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "nkimoe_moe_experts": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
-    "nkimoe_moe_block": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "nkimoe_moe_block": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz,
+                              _vp]),
+    "nkimoe_router_split": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_read_status": (_i, [_vp, _vp, _c.POINTER(_i)]),
     "nkimoe_grouped_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "nkimoe_swiglu": (_i, [_vp, _vp, _i64, _i64, _vp]),

@@ -52,6 +52,7 @@ inline void mark(int stage, cudaStream_t s) {
   if (stage < g_num_stage_events && g_stage_events[stage]) cudaEventRecord(g_stage_events[stage], s);
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
+std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
@@ -70,7 +71,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 struct WsLayout {
-  size_t status, logits, idx, w, offsets, row_token, row_slot, slot_row, scratch, xy, h, total;
+  size_t status, logits, partial, idx, w, offsets, row_token, row_slot, slot_row, scratch, xy, h, total;
 };
 
 WsLayout ws_layout(long long T, long long H, long long I, long long E, long long K) {
@@ -79,6 +80,8 @@ WsLayout ws_layout(long long T, long long H, long long I, long long E, long long
   const long long TK = T * K;
   L.status = o; o += 256;
   L.logits = o; o += round256(sizeof(float) * T * E);
+  const long long splits = T > 0 ? router_splits_for(static_cast<int>(T), static_cast<int>(H), static_cast<int>(E)) : 1;
+  L.partial = o; o += round256(sizeof(float) * std::max<long long>(splits, 1) * T * E);
   L.idx = o; o += round256(sizeof(int32_t) * TK);
   L.w = o; o += round256(sizeof(float) * TK);
   L.offsets = o; o += round256(sizeof(int32_t) * (E + 1));
@@ -105,23 +108,28 @@ int choose_variant(long long rows_total, long long E, long long N) {
 }
 
 // One grouped GEMM: act [act_rows, kd] x w [E*N, kd]^T per expert segment.
+// kd_act: K of an activation row; the weight row holds kd >= kd_act and the
+// activation K coordinate wraps modulo kd_act (split-fp32 router: kd = 3 kd_act).
+// offsets == nullptr: one dense segment of act_rows rows.
 int run_gemm(const void* act, long long act_rows, const void* w, long long E, long long N, long long kd,
              const int32_t* offsets, int epilogue, void* out, long long out_ld, const float* slot_w,
              const int32_t* row_slot, const int32_t* out_row_map, const float* col_bias, int* status,
-             cudaStream_t s) {
+             cudaStream_t s, long long kd_act = 0) {
   if (act_rows == 0) return NKIMOE_OK;
+  if (kd_act == 0) kd_act = kd;
   const int variant = choose_variant(act_rows, E, N);
   CUtensorMap ta, tw;
-  NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
+  NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the activation operand");
   NKI_REQUIRE(make_tmap_bf16(&tw, w, E * N, kd, grouped_gemm_box_rows_w(variant)), NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the weight operand");
   GroupedGemmParams p{};
   p.expert_offsets = offsets;
+  p.dense_rows = static_cast<int>(act_rows);
   p.num_experts = static_cast<int>(E);
   p.n = static_cast<int>(N);
   p.k_blocks = static_cast<int>(kd / 64);
-  p.k_blocks_a = static_cast<int>(kd / 64);
+  p.k_blocks_a = static_cast<int>(kd_act / 64);
   p.epilogue = epilogue;
   p.out = out;
   p.out_ld = out_ld;
@@ -146,6 +154,34 @@ int check_moe_shapes(long long T, long long H, long long I, long long E, long lo
   NKI_REQUIRE(H % 128 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden %lld must be a multiple of 128", H);
   NKI_REQUIRE(I % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "intermediate %lld must be a multiple of 64", I);
   NKI_REQUIRE(T * K < (1LL << 31), NKIMOE_ERR_UNSUPPORTED, "T*K too large");
+  return NKIMOE_OK;
+}
+
+// logits -> (idx, w): CUDA-core split-K or tensor-core split-fp32 GEMM, then
+// softmax/top-k/renormalise.
+int router_impl(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                int32_t* idx, float* w, long long T, long long H, long long E, long long K, char* base,
+                const WsLayout& L, int* status, cudaStream_t s) {
+  float* logits = reinterpret_cast<float*>(base + L.logits);
+  const int mode = g_router.load();
+  const bool tensor = router_w_split && E % 128 == 0 && (mode == 2 || (mode == 0 && T >= 256));
+  mark(kStageRouter, s);
+  if (tensor) {
+    int rc = run_gemm(x, T, router_w_split, 1, E, 3 * H, nullptr, kEpiStoreF32, logits, E, nullptr, nullptr,
+                      nullptr, router_bias, status, s, H);
+    if (rc != NKIMOE_OK) return rc;
+    mark(kStageTopk, s);
+    NKI_CUDA(topk_softmax_partials_launch(logits, 1, nullptr, nullptr, static_cast<int>(T), static_cast<int>(E),
+                                          static_cast<int>(K), idx, w, s));
+  } else {
+    float* partial = reinterpret_cast<float*>(base + L.partial);
+    const int splits = router_splits_for(static_cast<int>(T), static_cast<int>(H), static_cast<int>(E));
+    NKI_CUDA(router_splitk_launch(static_cast<const __nv_bfloat16*>(x), router_w, partial, static_cast<int>(T),
+                                  static_cast<int>(H), static_cast<int>(E), splits, s));
+    mark(kStageTopk, s);
+    NKI_CUDA(topk_softmax_partials_launch(partial, splits, router_bias, logits, static_cast<int>(T),
+                                          static_cast<int>(E), static_cast<int>(K), idx, w, s));
+  }
   return NKIMOE_OK;
 }
 
@@ -239,7 +275,10 @@ int nkimoe_set_option(const char* name, long long value) {
     g_weights_rows = static_cast<int>(value);
     return NKIMOE_OK;
   }
-  if (n == "router" && value >= 0 && value <= 2) return NKIMOE_OK;
+  if (n == "router" && value >= 0 && value <= 2) {
+    g_router = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
   return fail(NKIMOE_ERR_INVALID_ARG, "unknown option %s=%lld", name, value);
 }
 
@@ -297,6 +336,14 @@ int nkimoe_router_logits(const void* x, const float* router_w, const float* rout
   NKI_REQUIRE(aligned16(x) && aligned16(router_w), NKIMOE_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
   NKI_CUDA(router_logits_simt_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
                                      static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+int nkimoe_router_split(const float* router_w, void* router_w_split, int64_t E, int64_t H, void* stream) {
+  NKI_REQUIRE(router_w && router_w_split && E > 0 && H > 0, NKIMOE_ERR_INVALID_ARG, "bad argument");
+  NKI_REQUIRE(H % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden must be a multiple of 64");
+  NKI_CUDA(router_split_launch(router_w, static_cast<__nv_bfloat16*>(router_w_split), static_cast<int>(E),
+                               static_cast<int>(H), as_stream(stream)));
   return NKIMOE_OK;
 }
 
@@ -387,9 +434,10 @@ int nkimoe_moe_experts(const void* x, const void* w13, const void* w2, const voi
   return experts_impl(x, w13, w2, topk_idx, idx_dtype, topk_w, out, T, H, I, E, K, workspace, workspace_bytes, s);
 }
 
-int nkimoe_moe_block(const void* x, const float* router_w, const float* router_bias, const void* w13, const void* w2,
-                     void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
-                     int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+int nkimoe_moe_block(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                     const void* w13, const void* w2, void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T,
+                     int64_t H, int64_t I, int64_t E, int64_t K, void* workspace, size_t workspace_bytes,
+                     void* stream) {
   int rc = check_moe_shapes(T, H, I, E, K);
   if (rc != NKIMOE_OK) return rc;
   NKI_REQUIRE(E <= 256, NKIMOE_ERR_UNSUPPORTED, "router top-k supports up to 256 experts");
@@ -402,16 +450,14 @@ int nkimoe_moe_block(const void* x, const float* router_w, const float* router_b
   NKI_REQUIRE(x && router_w && w13 && w2 && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
   NKI_REQUIRE(aligned16(x) && aligned16(router_w) && aligned16(w13) && aligned16(w2) && aligned16(out),
               NKIMOE_ERR_INVALID_ARG, "x, weights and out must be 16-byte aligned");
+  NKI_REQUIRE(!router_w_split || aligned16(router_w_split), NKIMOE_ERR_INVALID_ARG, "router_w_split misaligned");
   const WsLayout L = ws_layout(T, H, I, E, K);
   char* base = static_cast<char*>(workspace);
-  float* logits = reinterpret_cast<float*>(base + L.logits);
   int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(base + L.idx);
   float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(base + L.w);
-  mark(kStageRouter, s);
-  NKI_CUDA(router_logits_simt_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
-                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(E), s));
-  mark(kStageTopk, s);
-  NKI_CUDA(topk_softmax_launch(logits, static_cast<int>(T), static_cast<int>(E), static_cast<int>(K), idx, w, s));
+  rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, base, L,
+                   reinterpret_cast<int*>(base + L.status), s);
+  if (rc != NKIMOE_OK) return rc;
   return experts_impl(x, w13, w2, idx, NKIMOE_I32, w, out, T, H, I, E, K, workspace, workspace_bytes, s);
 }
 

@@ -72,15 +72,16 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Per-expert tile table in smem.  tiles(e) = ceil(rows_e / rows_per_tile) * feat_tiles.
-__device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int E, int rows_per_tile, int feat_tiles) {
+__device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int dense_rows, int E, int rows_per_tile,
+                                 int feat_tiles) {
   const int lane = threadIdx.x & 31;
   int run = 0;
   for (int b = 0; b < E; b += 32) {
     const int e = b + lane;
     int cnt = 0, s0 = 0;
     if (e < E) {
-      s0 = offs[e];
-      cnt = offs[e + 1] - s0;
+      s0 = offs ? offs[e] : 0;
+      cnt = (offs ? offs[e + 1] : dense_rows) - s0;
     }
     const int tiles = ((cnt + rows_per_tile - 1) / rows_per_tile) * feat_tiles;
     int incl = tiles;
@@ -97,7 +98,7 @@ __device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int E, int
   }
   if (lane == 0) {
     ctl.tile_start[E] = run;
-    ctl.seg[E] = offs[E];
+    ctl.seg[E] = offs ? offs[E] : dense_rows;
   }
 }
 
@@ -200,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_w);
   }
   if (warp == 1) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
-  if (warp == 2) build_tile_table(ctl, p.expert_offsets, E, BM, feat_tiles);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BM, feat_tiles);
   tcgen05_fence_before();
   __syncthreads();
   tcgen05_fence_after();
@@ -411,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_w);
   }
   if (warp == 1) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
-  if (warp == 2) build_tile_table(ctl, p.expert_offsets, E, BT, feat_tiles);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BT, feat_tiles);
   tcgen05_fence_before();
   __syncthreads();
   tcgen05_fence_after();

@@ -47,9 +47,17 @@ cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, c
                                       int tokens, int hidden, int experts, cudaStream_t s);
 // Split fp32 router weights into three bf16 planes [E, 3H] = hi | mid | lo.
 cudaError_t router_split_launch(const float* wr, __nv_bfloat16* wsplit, int experts, int hidden, cudaStream_t s);
+// Split-K fp32 router for few tokens: partial[split][T][E].
+cudaError_t router_splitk_launch(const __nv_bfloat16* x, const float* wr, float* partial, int tokens, int hidden,
+                                 int experts, int splits, cudaStream_t s);
+int router_splits_for(int tokens, int hidden, int experts);
 // softmax -> top-k (by logit, ties to the lower id) -> renormalise.
 cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
                                 cudaStream_t s);
+// Same on logits given as `splits` fp32 partial sums [split][T][E] (+ bias[E]);
+// logits_out (nullable) receives the summed logits.
+cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,
+                                         int tokens, int experts, int top_k, int32_t* idx, float* w, cudaStream_t s);
 
 // ----------------------------------------------------------------- permutation
 size_t permute_scratch_bytes(long long tokens, int top_k, int experts);
@@ -85,7 +93,8 @@ enum Epilogue : int {
 };
 
 struct GroupedGemmParams {
-  const int32_t* expert_offsets;  // [E+1] segment starts of each expert's rows
+  const int32_t* expert_offsets;  // [E+1] segment starts of each expert's rows; null: one segment
+  int dense_rows;                 // rows of the single segment when expert_offsets is null
   int num_experts;
   int n;           // output features per expert (rows of one expert's packed weight)
   int k_blocks;    // 64-wide K blocks iterated

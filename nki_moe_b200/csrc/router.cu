@@ -1,6 +1,8 @@
 // K2: router of the sparse-MoE block (nki_moe_integrated.py:436-443):
 //   logits = x . Wr^T in fp32 (router dtype fp32, qwen_with_nki.py:276),
 //   p = softmax(logits), (w, idx) = topk(p, K) descending, w /= sum(w).
+#include <algorithm>
+
 #include "kernels.h"
 
 namespace nkimoe {
@@ -70,6 +72,72 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const __nv_bfloat16*
   }
 }
 
+// Split-K variant for few tokens: a CTA computes 16 tokens x 128 experts over
+// one K span and writes fp32 partial sums [split][T][E]; the top-k kernel adds
+// the splits in ascending order (deterministic).  Each output of a split is
+// one FMA chain in ascending k.
+constexpr int ST = 16, SE = 128, SK = 32;
+
+__global__ void __launch_bounds__(256) router_splitk_kernel(const __nv_bfloat16* __restrict__ x,
+                                                            const float* __restrict__ wr,
+                                                            float* __restrict__ partial, int T, int H, int E,
+                                                            int kspan) {
+  __shared__ __align__(16) float xs[SK][ST];
+  __shared__ __align__(16) float ws[SK][SE + 4];
+  const int tid = threadIdx.x;
+  const int t0 = blockIdx.x * ST, e0 = blockIdx.y * SE;
+  const int kb = blockIdx.z * kspan, ke = min(H, kb + kspan);
+  const int tt = tid >> 4, eg = (tid & 15) * 8;
+  float acc[8] = {};
+  for (int k0 = kb; k0 < ke; k0 += SK) {
+    if (tid < 64) {  // x: 16 tokens x 32 k, 8 bf16 per thread
+      const int r = tid >> 2, c = (tid & 3) * 8;
+      float v[8] = {};
+      if (t0 + r < T) {
+        uint4 u = *reinterpret_cast<const uint4*>(x + static_cast<long long>(t0 + r) * H + k0 + c);
+        float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+        v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = cc.x; v[5] = cc.y; v[6] = d.x; v[7] = d.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xs[c + j][r] = v[j];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // w: 128 experts x 32 k fp32
+      const int idx = tid + i * 256;
+      const int r = idx >> 3, c = (idx & 7) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e0 + r < E) v = *reinterpret_cast<const float4*>(wr + static_cast<long long>(e0 + r) * H + k0 + c);
+      ws[c + 0][r] = v.x;
+      ws[c + 1][r] = v.y;
+      ws[c + 2][r] = v.z;
+      ws[c + 3][r] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < SK; ++k) {
+      const float a = xs[k][tt];
+      const float4 b0 = *reinterpret_cast<const float4*>(&ws[k][eg]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&ws[k][eg + 4]);
+      acc[0] = fmaf(a, b0.x, acc[0]);
+      acc[1] = fmaf(a, b0.y, acc[1]);
+      acc[2] = fmaf(a, b0.z, acc[2]);
+      acc[3] = fmaf(a, b0.w, acc[3]);
+      acc[4] = fmaf(a, b1.x, acc[4]);
+      acc[5] = fmaf(a, b1.y, acc[5]);
+      acc[6] = fmaf(a, b1.z, acc[6]);
+      acc[7] = fmaf(a, b1.w, acc[7]);
+    }
+    __syncthreads();
+  }
+  const int t = t0 + tt;
+  if (t < T) {
+    float* dst = partial + (static_cast<long long>(blockIdx.z) * T + t) * E;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (e0 + eg + j < E) dst[e0 + eg + j] = acc[j];
+  }
+}
+
 __global__ void router_split_kernel(const float* __restrict__ wr, __nv_bfloat16* __restrict__ out, int E, int H) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<long long>(E) * H) return;
@@ -87,19 +155,30 @@ __global__ void router_split_kernel(const float* __restrict__ wr, __nv_bfloat16*
 }
 
 // One warp per token; lane l holds experts l, l+32, ... (VPT of them).
+// The logits of token t are sum_{s < splits} partial[s][t][:] (+ bias), added
+// in ascending s; with splits = 1 and no bias they are read as they are.
 template <int VPT>
-__global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restrict__ logits, int T, int E, int K,
+__global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restrict__ partial, int splits,
+                                                           const float* __restrict__ bias,
+                                                           float* __restrict__ logits_out, int T, int E, int K,
                                                            int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
   const int lane = threadIdx.x & 31;
   const long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
-  const float* row = logits + t * E;
   float v[VPT];
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = lane + 32 * j;
-    v[j] = e < E ? row[e] : -INFINITY;
+    if (e < E) {
+      float acc = partial[t * E + e];
+      for (int sp = 1; sp < splits; ++sp) acc += partial[(static_cast<long long>(sp) * T + t) * E + e];
+      if (bias) acc += bias[e];
+      if (logits_out) logits_out[t * E + e] = acc;
+      v[j] = acc;
+    } else {
+      v[j] = -INFINITY;
+    }
     m = fmaxf(m, v[j]);
   }
   m = warp_max(m);
@@ -163,14 +242,39 @@ cudaError_t router_split_launch(const float* wr, __nv_bfloat16* wsplit, int expe
   return cudaGetLastError();
 }
 
+cudaError_t router_splitk_launch(const __nv_bfloat16* x, const float* wr, float* partial, int tokens, int hidden,
+                                 int experts, int splits, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (hidden % SK || splits < 1) return cudaErrorInvalidValue;
+  const int kspan = ((hidden / splits + SK - 1) / SK) * SK;
+  dim3 grid((tokens + ST - 1) / ST, (experts + SE - 1) / SE, (hidden + kspan - 1) / kspan);
+  router_splitk_kernel<<<grid, 256, 0, s>>>(x, wr, partial, tokens, hidden, experts, kspan);
+  return cudaGetLastError();
+}
+
+int router_splits_for(int tokens, int hidden, int experts) {
+  const long long tiles = static_cast<long long>((tokens + ST - 1) / ST) * ((experts + SE - 1) / SE);
+  long long sp = (2LL * device_sm_count() + tiles - 1) / tiles;
+  sp = std::max<long long>(1, std::min<long long>(sp, hidden / SK));
+  const int kspan = static_cast<int>(((hidden / sp + SK - 1) / SK) * SK);
+  return (hidden + kspan - 1) / kspan;  // the number of splits actually launched
+}
+
 cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
                                 cudaStream_t s) {
+  return topk_softmax_partials_launch(logits, 1, nullptr, nullptr, tokens, experts, top_k, idx, w, s);
+}
+
+cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,
+                                         int tokens, int experts, int top_k, int32_t* idx, float* w, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   if (top_k < 1 || top_k > 32 || top_k > experts || experts > 256) return cudaErrorInvalidValue;
   const int wpb = 8;
   const unsigned blocks = static_cast<unsigned>((tokens + wpb - 1) / wpb);
   const int vpt = (experts + 31) / 32;
-#define NKI_TOPK(V) topk_softmax_kernel<V><<<blocks, wpb * 32, 0, s>>>(logits, tokens, experts, top_k, idx, w)
+#define NKI_TOPK(V)                                                                                          \
+  topk_softmax_kernel<V><<<blocks, wpb * 32, 0, s>>>(partial, splits, bias, logits_out, tokens, experts, top_k, \
+                                                     idx, w)
   if (vpt <= 1) NKI_TOPK(1);
   else if (vpt <= 2) NKI_TOPK(2);
   else if (vpt <= 4) NKI_TOPK(4);

@@ -21,7 +21,7 @@ from ._lib import BF16, F32, I32, I64, LAYOUT_HF, LAYOUT_NXD, call, size_call
 __all__ = [
     "rmsnorm", "add_rmsnorm", "qk_norm_rope", "router_logits", "topk_softmax", "permute",
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
-    "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled",
+    "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -275,10 +275,40 @@ def moe_experts(x: torch.Tensor, experts: PackedExperts, idx: torch.Tensor, weig
     return out
 
 
+_router_lock = threading.Lock()
+_router_cache: "OrderedDict[int, tuple]" = OrderedDict()
+
+
+def router_split(router_w: torch.Tensor) -> torch.Tensor:
+    """fp32 router weights [E, H] -> bf16 planes [E, 3H] (hi | mid | lo, exact
+    sum) for the tensor-core router; cached while the source tensor lives
+    unmodified."""
+    key = id(router_w)
+    with _router_lock:
+        hit = _router_cache.get(key)
+        if hit is not None and hit[0]() is router_w and hit[1] == _stamp(router_w):
+            return hit[2]
+    rw = _contig(_cuda(router_w, "router_w").detach(), torch.float32)
+    E, H = rw.shape
+    out = torch.empty(E, 3 * H, dtype=torch.bfloat16, device=rw.device)
+    call("nkimoe_router_split", _p(rw), _p(out), E, H, _s(rw))
+    with _router_lock:
+        for k in [k for k, v in _router_cache.items() if v[0]() is None]:
+            del _router_cache[k]
+        _router_cache[key] = (weakref.ref(router_w), _stamp(router_w), out)
+        while len(_router_cache) > _PACK_CACHE_MAX:
+            _router_cache.popitem(last=False)
+    return out
+
+
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
-              bias: torch.Tensor | None = None, return_routing: bool = False):
-    """Router (fp32) + softmax/top-k/renormalise + experts (K2..K7)."""
+              bias: torch.Tensor | None = None, return_routing: bool = False, tensor_router: bool = True):
+    """Router (fp32) + softmax/top-k/renormalise + experts (K2..K7).
+
+    With ``tensor_router`` the fp32 router GEMM of large batches runs on the
+    tensor cores over the exact three-plane bf16 split of ``router_w``."""
     x = _contig(_cuda(x, "x"), torch.bfloat16)
+    rsplit = router_split(router_w) if tensor_router and router_w.shape[0] % 128 == 0 else None
     rw = _contig(_cuda(router_w, "router_w"), torch.float32)
     b = _contig(bias, torch.float32) if bias is not None else None
     T, H = x.shape
@@ -290,8 +320,8 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, t
         w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
     nbytes = size_call("nkimoe_moe_workspace_bytes", T, H, I, E, top_k)
     ws = workspace(x.device, nbytes)
-    call("nkimoe_moe_block", _p(x), _p(rw), _p(b), _p(experts.w13), _p(experts.w2), _p(out), _p(idx), _p(w),
-         T, H, I, E, top_k, _p(ws), ws.numel(), _s(x))
+    call("nkimoe_moe_block", _p(x), _p(rw), _p(b), _p(rsplit), _p(experts.w13), _p(experts.w2), _p(out), _p(idx),
+         _p(w), T, H, I, E, top_k, _p(ws), ws.numel(), _s(x))
     if sync_check_enabled():
         read_status(ws)
     return (out, idx, w) if return_routing else out

@@ -60,7 +60,7 @@ def test_argument_validation_without_gpu():
         _lib.call("nkimoe_rmsnorm", null, _lib.BF16, null, _lib.F32, null, _lib.BF16, 4, 100, 1e-6, null)
     assert ei.value.code == _lib.ERR_UNSUPPORTED
     with pytest.raises(_lib.NKIMoEError) as ei:  # workspace too small
-        _lib.call("nkimoe_moe_block", null, null, null, null, null, null, null, null, 64, 2048, 768, 128, 8,
+        _lib.call("nkimoe_moe_block", null, null, null, null, null, null, null, null, null, 64, 2048, 768, 128, 8,
                   null, 16, null)
     assert ei.value.code == _lib.ERR_WORKSPACE
     with pytest.raises(_lib.NKIMoEError) as ei:

@@ -161,6 +161,29 @@ def test_router_logits_and_routing(c1_inputs, golden_dir):
     assert np.all(same | ties), f"{(~same & ~ties).sum()} non-tie tokens routed differently"
 
 
+@pytest.mark.parametrize("router", [1, 2])
+@pytest.mark.parametrize("T", [128, 1000])
+def test_block_router_paths(c1_inputs, router, T):
+    """Both router paths (CUDA-core split-K, tensor-core split-fp32) give fp32
+    logits: identical routing to the oracle outside near ties."""
+    _lib.set_option("router", router)
+    try:
+        x = torch.randn(T, 2048, generator=torch.Generator().manual_seed(T))
+        xb, xn = bf(x)
+        rw = c1_inputs["router"]
+        pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+        _, idx, w = ops.moe_block(xb, rw.cuda(), pe, 8, return_routing=True)
+        lg = oracle.router_logits(xn, rw.numpy())
+        ri, rwt = oracle.topk_softmax(lg, 8)
+        ties = oracle.near_tie_tokens(lg, 8)
+        same = np.all(idx.cpu().numpy() == ri, axis=1)
+        assert np.all(same | ties), f"{(~same & ~ties).sum()} non-tie tokens routed differently"
+        ok = same & ~ties
+        np.testing.assert_allclose(w.cpu().numpy()[ok], rwt[ok], rtol=2e-5, atol=1e-6)
+    finally:
+        _lib.set_option("router", 0)
+
+
 # ---------------------------------------------------------------- K3
 def _check_permute(idx_np, E, dtype=torch.int32):
     rt, rs, sr, off = ops.permute(torch.from_numpy(idx_np).to(dtype).cuda(), E)
