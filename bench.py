@@ -266,17 +266,24 @@ def time_steps(torch, fn, steps, warmup, stream, world, evs=None):
     return ms, stage_ms
 
 
-def measure_stages(torch, fn, steps, evs):
-    """Per-kernel durations from CUDA events recorded by the library between
-    its launches on the launching stream (averaged over `steps` steps)."""
+def measure_stages(torch, fn, steps, evs, graph_of=None):
+    """Per-kernel durations from CUDA events that the library records between
+    its launches on the launching stream, averaged over `steps` steps.  With
+    `graph_of`, the step is captured into a CUDA graph together with its event
+    records and replayed, so the durations exclude CPU launch gaps."""
     set_stage_events(evs)
-    acc = [0.0] * len(STAGES)
-    for _ in range(steps):
-        fn()
-        evs[-1].synchronize()
-        for i in range(len(STAGES)):
-            acc[i] += evs[i].elapsed_time(evs[i + 1])
-    set_stage_events(None)
+    try:
+        run = fn
+        if graph_of is not None:
+            run = graph_of(fn).replay
+        acc = [0.0] * len(STAGES)
+        for _ in range(steps):
+            run()
+            torch.cuda.synchronize()
+            for i in range(len(STAGES)):
+                acc[i] += evs[i].elapsed_time(evs[i + 1])
+    finally:
+        set_stage_events(None)
     return [a / steps for a in acc]
 
 
@@ -357,7 +364,8 @@ def run_b200(args):
         ms, _ = time_steps(torch, run, args.steps, max(args.warmup, 3), stream, world)
         if which == "prefill":
             sampler.mark(False)
-        st = measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch)) if world == 1 else None
+        st = (measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch), graph_of)
+              if world == 1 else None)
         tokens_total = wl.tokens * world
         r = {"ms_per_step": ms, "tokens_per_s": tokens_total / (ms * 1e-3),
              "block_tflops": alg["block_flops"] * world / (ms * 1e-3) / 1e12,

@@ -54,9 +54,13 @@ extern "C" {
 
 NKIMOE_API int nkimoe_version(void);
 NKIMOE_API const char* nkimoe_last_error(void);
-/* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows, 2 weights),
+/* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows on one SM,
+ * 2 weights, 3 rows on an SM pair),
  * "weights_rows" (16, 32 or 64 rows per decode tile), "router" (0 auto,
- * 1 CUDA-core fp32, 2 tensor-core split-fp32).  Returns NKIMOE_OK or
+ * 1 CUDA-core fp32, 2 tensor-core split-fp32), "prefetch" (L2 prefetch
+ * distance of the prefill GEMMs in 64-wide K blocks, 0 = off = default).
+ * No reference counterpart (NKI tile sizes are compile-time constants,
+ * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */
 NKIMOE_API int nkimoe_set_option(const char* name, long long value);
 
@@ -98,8 +102,8 @@ NKIMOE_API int nkimoe_qk_norm_rope(const void* qkv_in, void* qkv_out, const void
 NKIMOE_API int nkimoe_router_logits(const void* x, const float* router_w, const float* router_bias, float* logits, int64_t T,
                          int64_t H, int64_t E, void* stream);
 
-/* Splits fp32 router weights [E,H] into three bf16 planes [E, 3H] =
- * [hi | mid | lo] with hi + mid + lo == w exactly, for the tensor-core router
+/* Splits fp32 router weights [E,H] into three bf16 planes [3, E, H] =
+ * (hi, mid, lo) with hi + mid + lo == w exactly, for the tensor-core router
  * of nkimoe_moe_block: with bf16 activations every product is exact and the
  * accumulation is fp32, so the logits are fp32 logits.  No reference
  * counterpart (the reference computes the fp32 router with nn.Linear,

@@ -48,11 +48,20 @@ std::atomic<int> g_schedule{0};      // 0 auto, 1 rows, 2 weights
 thread_local cudaEvent_t g_stage_events[kNumStageEvents] = {};
 thread_local int g_num_stage_events = 0;
 
+// During stream capture the record must be an external event node to be
+// replayed with the graph (a plain record would only become a dependency).
 inline void mark(int stage, cudaStream_t s) {
-  if (stage < g_num_stage_events && g_stage_events[stage]) cudaEventRecord(g_stage_events[stage], s);
+  if (stage >= g_num_stage_events || !g_stage_events[stage]) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(s, &cs);
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(g_stage_events[stage], s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(g_stage_events[stage], s);
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
+std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
@@ -71,7 +80,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 struct WsLayout {
-  size_t status, logits, partial, idx, w, offsets, row_token, row_slot, slot_row, scratch, xy, h, total;
+  size_t status, logits, partial, idx, w, offsets, row_token, row_slot, slot_row, row_weight, scratch, xy, h, total;
 };
 
 WsLayout ws_layout(long long T, long long H, long long I, long long E, long long K) {
@@ -81,13 +90,14 @@ WsLayout ws_layout(long long T, long long H, long long I, long long E, long long
   L.status = o; o += 256;
   L.logits = o; o += round256(sizeof(float) * T * E);
   const long long splits = T > 0 ? router_splits_for(static_cast<int>(T), static_cast<int>(H), static_cast<int>(E)) : 1;
-  L.partial = o; o += round256(sizeof(float) * std::max<long long>(splits, 1) * T * E);
+  L.partial = o; o += round256(sizeof(float) * std::max<long long>(splits, 3) * T * E);
   L.idx = o; o += round256(sizeof(int32_t) * TK);
   L.w = o; o += round256(sizeof(float) * TK);
   L.offsets = o; o += round256(sizeof(int32_t) * (E + 1));
   L.row_token = o; o += round256(sizeof(int32_t) * TK);
   L.row_slot = o; o += round256(sizeof(int32_t) * TK);
   L.slot_row = o; o += round256(sizeof(int32_t) * TK);
+  L.row_weight = o; o += round256(sizeof(float) * TK);
   L.scratch = o; o += round256(permute_scratch_bytes(T, static_cast<int>(K), static_cast<int>(E)));
   L.xy = o; o += round256(sizeof(uint16_t) * TK * H);
   L.h = o; o += round256(sizeof(uint16_t) * TK * I);
@@ -104,6 +114,10 @@ int choose_variant(long long rows_total, long long E, long long N) {
     if (r == 0) r = avg <= 8.0 ? 16 : (avg <= 24.0 ? 32 : 64);
     return r == 16 ? kWeightsT16 : (r == 32 ? kWeightsT32 : kWeightsT64);
   }
+  // the SM-pair schedule is selected only on request: measured slower than the
+  // 1-SM schedule on B200 for these shapes (TMA completions in the pair run at
+  // about a third of the 1-SM rate)
+  if (N % 256 == 0 && sched == 3) return kRows2BN256;
   return (N % 256 == 0) ? kRowsBN256 : kRowsBN128;
 }
 
@@ -114,10 +128,12 @@ int choose_variant(long long rows_total, long long E, long long N) {
 int run_gemm(const void* act, long long act_rows, const void* w, long long E, long long N, long long kd,
              const int32_t* offsets, int epilogue, void* out, long long out_ld, const float* slot_w,
              const int32_t* row_slot, const int32_t* out_row_map, const float* col_bias, int* status,
-             cudaStream_t s, long long kd_act = 0) {
+             cudaStream_t s, long long kd_act = 0, bool shared_a = false, const float* row_weight = nullptr) {
   if (act_rows == 0) return NKIMOE_OK;
   if (kd_act == 0) kd_act = kd;
-  const int variant = choose_variant(act_rows, E, N);
+  // with shared activation rows every expert has act_rows rows
+  const long long rows_total = shared_a ? act_rows * E : act_rows;
+  const int variant = choose_variant(rows_total, E, N);
   CUtensorMap ta, tw;
   NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the activation operand");
@@ -130,6 +146,9 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.n = static_cast<int>(N);
   p.k_blocks = static_cast<int>(kd / 64);
   p.k_blocks_a = static_cast<int>(kd_act / 64);
+  p.shared_a = shared_a ? 1 : 0;
+  p.row_weight = row_weight;
+  p.prefetch = g_prefetch.load();
   p.epilogue = epilogue;
   p.out = out;
   p.out_ld = out_ld;
@@ -138,11 +157,13 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.out_row_map = out_row_map;
   p.col_bias = col_bias;
   p.status = status;
-  const bool rows = variant == kRowsBN256 || variant == kRowsBN128;
-  const long long rpt = grouped_gemm_box_rows_act(variant);
-  const long long fpt = rows ? grouped_gemm_box_rows_w(variant) : 128;
-  const long long max_tiles = (act_rows / rpt + E) * (N / fpt);
-  const long long grid = std::min<long long>(max_tiles, device_sm_count());
+  const bool pair = variant == kRows2BN256;
+  const bool rows = variant == kRowsBN256 || variant == kRowsBN128 || pair;
+  const long long rpt = pair ? 256 : grouped_gemm_box_rows_act(variant);
+  const long long fpt = pair ? 256 : (rows ? grouped_gemm_box_rows_w(variant) : 128);
+  const long long max_tiles = (rows_total / rpt + E) * (N / fpt);
+  long long grid = std::min<long long>(max_tiles, device_sm_count());
+  if (pair) grid = 2 * std::max<long long>(1, std::min<long long>(max_tiles, device_sm_count() / 2));
   NKI_CUDA(grouped_gemm_launch(variant, ta, tw, p, static_cast<int>(std::max<long long>(grid, 1)), s));
   return NKIMOE_OK;
 }
@@ -167,11 +188,14 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
   const bool tensor = router_w_split && E % 128 == 0 && (mode == 2 || (mode == 0 && T >= 256));
   mark(kStageRouter, s);
   if (tensor) {
-    int rc = run_gemm(x, T, router_w_split, 1, E, 3 * H, nullptr, kEpiStoreF32, logits, E, nullptr, nullptr,
-                      nullptr, router_bias, status, s, H);
+    // the three bf16 planes are three "experts" over the same activation rows;
+    // their fp32 partial logits [3][T][E] are added (hi + mid + lo) by top-k
+    float* partial = reinterpret_cast<float*>(base + L.partial);
+    int rc = run_gemm(x, T, router_w_split, 3, E, H, nullptr, kEpiStoreF32, partial, E, nullptr, nullptr, nullptr,
+                      nullptr, status, s, H, true);
     if (rc != NKIMOE_OK) return rc;
     mark(kStageTopk, s);
-    NKI_CUDA(topk_softmax_partials_launch(logits, 1, nullptr, nullptr, static_cast<int>(T), static_cast<int>(E),
+    NKI_CUDA(topk_softmax_partials_launch(partial, 3, router_bias, logits, static_cast<int>(T), static_cast<int>(E),
                                           static_cast<int>(K), idx, w, s));
   } else {
     float* partial = reinterpret_cast<float*>(base + L.partial);
@@ -195,13 +219,14 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
   int32_t* row_token = reinterpret_cast<int32_t*>(base + L.row_token);
   int32_t* row_slot = reinterpret_cast<int32_t*>(base + L.row_slot);
   int32_t* slot_row = reinterpret_cast<int32_t*>(base + L.slot_row);
+  float* row_weight = reinterpret_cast<float*>(base + L.row_weight);
   __nv_bfloat16* xy = reinterpret_cast<__nv_bfloat16*>(base + L.xy);
   __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(base + L.h);
   const long long TK = T * K;
   if (T == 0) return NKIMOE_OK;
   mark(kStagePermute, s);
   NKI_CUDA(permute_launch(idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
-                          row_slot, slot_row, offsets, base + L.scratch, status, s));
+                          row_slot, slot_row, offsets, base + L.scratch, status, s, topk_w, row_weight));
   mark(kStageGather, s);
   NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(E), xy, TK,
                               static_cast<int>(H), s));
@@ -209,7 +234,8 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
   int rc = run_gemm(xy, TK, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s);
   if (rc != NKIMOE_OK) return rc;
   mark(kStageGemm2, s);
-  rc = run_gemm(h, TK, w2, E, H, I, offsets, kEpiScaleBf16, xy, H, topk_w, row_slot, nullptr, nullptr, status, s);
+  rc = run_gemm(h, TK, w2, E, H, I, offsets, kEpiScaleBf16, xy, H, topk_w, row_slot, nullptr, nullptr, status, s, 0,
+                false, row_weight);
   if (rc != NKIMOE_OK) return rc;
   mark(kStageCombine, s);
   NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
@@ -267,12 +293,16 @@ const char* nkimoe_last_error(void) { return g_err.c_str(); }
 int nkimoe_set_option(const char* name, long long value) {
   if (!name) return fail(NKIMOE_ERR_INVALID_ARG, "null option name");
   const std::string n(name);
-  if (n == "gemm_schedule" && value >= 0 && value <= 2) {
+  if (n == "gemm_schedule" && value >= 0 && value <= 3) {
     g_schedule = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "weights_rows" && (value == 0 || value == 16 || value == 32 || value == 64)) {
     g_weights_rows = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "prefetch" && value >= 0 && value <= 16) {
+    g_prefetch = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "router" && value >= 0 && value <= 2) {

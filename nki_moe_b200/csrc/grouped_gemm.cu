@@ -24,6 +24,7 @@
 // expert-major, then feature block, then row block, so concurrently running
 // CTAs share weight panels through L2.
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -80,8 +81,8 @@ __device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int dense_
     const int e = b + lane;
     int cnt = 0, s0 = 0;
     if (e < E) {
-      s0 = offs ? offs[e] : 0;
-      cnt = (offs ? offs[e + 1] : dense_rows) - s0;
+      s0 = offs ? offs[e] : e * dense_rows;
+      cnt = offs ? offs[e + 1] - s0 : dense_rows;
     }
     const int tiles = ((cnt + rows_per_tile - 1) / rows_per_tile) * feat_tiles;
     int incl = tiles;
@@ -98,7 +99,7 @@ __device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int dense_
   }
   if (lane == 0) {
     ctl.tile_start[E] = run;
-    ctl.seg[E] = offs ? offs[E] : dense_rows;
+    ctl.seg[E] = offs ? offs[E] : E * dense_rows;
   }
 }
 
@@ -160,6 +161,67 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
   }
 }
 
+// Epilogue of a rows-schedule tile for one thread = one output row: reads the
+// row's BN accumulator columns from tensor memory (all lanes of the warp must
+// call it: tcgen05.ld is warp-collective) and stores them per p.epilogue.
+template <int BN>
+__device__ __forceinline__ void rows_epilogue(const GroupedGemmParams& p, uint32_t tbase, int fblk, long long orow,
+                                              bool valid, float scale) {
+  if (p.epilogue == kEpiSwiGLU) {
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+    for (int blk = 0; blk < BN / 128; ++blk) {
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        float g[32], u[32];
+        tmem_ld_cols<32>(tbase + blk * 128 + half * 32, g);
+        tmem_ld_cols<32>(tbase + blk * 128 + 64 + half * 32, u);
+        if (valid) {
+          float h[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) h[j] = silu_f(g[j]) * u[j];
+          const long long col = static_cast<long long>(fblk) * (BN / 2) + blk * 64 + half * 32;
+          store_bf16x32(out + orow * p.out_ld + col, h);
+        }
+      }
+    }
+  } else if (p.epilogue == kEpiScaleBf16 || p.epilogue == kEpiStoreBf16) {
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld_cols<32>(tbase + c, v);
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= scale;
+        store_bf16x32(out + orow * p.out_ld + static_cast<long long>(fblk) * BN + c, v);
+      }
+    }
+  } else {  // kEpiStoreF32
+    float* out = static_cast<float*>(p.out);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld_cols<32>(tbase + c, v);
+      if (valid) {
+        const long long col0 = static_cast<long long>(fblk) * BN + c;
+        float4* dst = reinterpret_cast<float4*>(out + orow * p.out_ld + col0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 f = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          if (p.col_bias) {
+            f.x += p.col_bias[col0 + 4 * q];
+            f.y += p.col_bias[col0 + 4 * q + 1];
+            f.z += p.col_bias[col0 + 4 * q + 2];
+            f.w += p.col_bias[col0 + 4 * q + 3];
+          }
+          dst[q] = f;
+        }
+      }
+    }
+  }
+}
+
 // ============================================================ rows schedule
 // Tile: 128 activation rows x BN packed features.  A = activations (box 64 x
 // 128), B = weights (box 64 x BN), D[row][feature] in TMEM lanes x columns.
@@ -217,7 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
       const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
       const int row0 = ctl.seg[tc.e] + tc.rblk * BM;
+      const int arow0 = p.shared_a ? tc.rblk * BM : row0;
       const int wrow0 = tc.e * p.n + tc.fblk * BN;
+      int ka = 0;  // activation K coordinate (wraps at k_blocks_a blocks)
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
           ok = false;
@@ -225,9 +289,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
-          tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, row0);
+          tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], ka, arow0);
           tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0);
+          // L2 prefetch p.prefetch k-blocks ahead (into the next tile at the end
+          // of this one), so the TMA loads above find their data in L2
+          if (p.prefetch) {
+            int pk = kb + p.prefetch, pa = arow0, pw = wrow0;
+            if (pk >= p.k_blocks && tile + static_cast<int>(gridDim.x) < total_tiles) {
+              const TileCoord nc = decode_tile(ctl, E, tile + gridDim.x, BM, feat_tiles);
+              pk -= p.k_blocks;
+              pw = nc.e * p.n + nc.fblk * BN;
+              pa = p.shared_a ? nc.rblk * BM : ctl.seg[nc.e] + nc.rblk * BM;
+            }
+            if (pk < p.k_blocks) {
+              tma_prefetch_2d(&tmap_act, (pk % p.k_blocks_a) * BK, pa);
+              tma_prefetch_2d(&tmap_w, pk * BK, pw);
+            }
+          }
         }
+        ka += BK;
+        if (ka == p.k_blocks_a * BK) ka = 0;
         issued_mask |= 1u << stage;
         last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
         if (++stage == STAGES) {
@@ -263,13 +344,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tcgen05_fence_after();
         if (lane == 0) {
-          const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
-          const uint32_t b0 = smem_u32(sb + stage * B_BYTES);
+          // K step of 16 bf16 = 32 bytes = 2 in the descriptor's address field
+          const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / UK; ++k) {
-            umma_bf16(d_tmem, umma_desc_sw128(a0 + k * UK * 2), umma_desc_sw128(b0 + k * UK * 2), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / UK; ++k)
+            umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit(&ctl.empty[stage]);
           issued = true;
         }
@@ -296,68 +376,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
       const int acc = t_local & 1;
       const uint32_t acc_phase = (t_local >> 1) & 1;
-      if (!warp_wait(&ctl.acc_full[acc], acc_phase, ctl, p.status)) break;
-      tcgen05_fence_after();
       const int seg_end = ctl.seg[tc.e + 1];
       const int r = ctl.seg[tc.e] + tc.rblk * BM + row_in_tile;
       const bool valid = r < seg_end;
+      // per-row loads issued before the accumulator wait so their latency overlaps it
       const long long orow = valid ? (p.out_row_map ? p.out_row_map[r] : r) : 0;
+      float scale = 1.f;
+      if (p.epilogue == kEpiScaleBf16 && valid) scale = p.row_weight ? p.row_weight[r] : p.slot_weight[p.row_slot[r]];
+      if (!warp_wait(&ctl.acc_full[acc], acc_phase, ctl, p.status)) break;
+      tcgen05_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 
-      if (p.epilogue == kEpiSwiGLU) {
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
-#pragma unroll 1
-        for (int blk = 0; blk < BN / 128; ++blk) {
-#pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            float g[32], u[32];
-            tmem_ld_cols<32>(tbase + blk * 128 + half * 32, g);
-            tmem_ld_cols<32>(tbase + blk * 128 + 64 + half * 32, u);
-            if (valid) {
-              float h[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) h[j] = silu_f(g[j]) * u[j];
-              const long long col = static_cast<long long>(tc.fblk) * (BN / 2) + blk * 64 + half * 32;
-              store_bf16x32(out + orow * p.out_ld + col, h);
-            }
-          }
-        }
-      } else if (p.epilogue == kEpiScaleBf16 || p.epilogue == kEpiStoreBf16) {
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
-        const float scale = (p.epilogue == kEpiScaleBf16 && valid) ? p.slot_weight[p.row_slot[r]] : 1.f;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          tmem_ld_cols<32>(tbase + c, v);
-          if (valid) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= scale;
-            store_bf16x32(out + orow * p.out_ld + static_cast<long long>(tc.fblk) * BN + c, v);
-          }
-        }
-      } else {  // kEpiStoreF32
-        float* out = static_cast<float*>(p.out);
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          tmem_ld_cols<32>(tbase + c, v);
-          if (valid) {
-            const long long col0 = static_cast<long long>(tc.fblk) * BN + c;
-            float4* dst = reinterpret_cast<float4*>(out + orow * p.out_ld + col0);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 f = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-              if (p.col_bias) {
-                f.x += p.col_bias[col0 + 4 * q];
-                f.y += p.col_bias[col0 + 4 * q + 1];
-                f.z += p.col_bias[col0 + 4 * q + 2];
-                f.w += p.col_bias[col0 + 4 * q + 3];
-              }
-              dst[q] = f;
-            }
-          }
-        }
-      }
+      rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale);
       tcgen05_fence_before();
       mbar_arrive(&ctl.acc_empty[acc]);
     }
@@ -368,6 +398,213 @@ __global__ void __launch_bounds__(kThreads, 1)
     tcgen05_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
+}
+
+// ============================================================ rows schedule, SM pair
+// Tile: 256 activation rows x BN features computed by a 2-CTA cluster with
+// tcgen05.mma.cta_group::2 (M = 256).  CTA r of the pair loads activation rows
+// [128 r, 128 r + 128) and weight rows [r BN/2, (r + 1) BN/2) of the tile into
+// its own shared memory (plain TMA loads), so each SM fetches half of the B
+// operand of a 256 x BN tile: 64 B per cycle per SM from L2 at full MMA rate
+// instead of 96 B for a 1-SM 128 x 256 tile.  The even CTA issues the MMAs;
+// the odd CTA relays "stage full" to it, the even CTA's commits release the
+// stages and publish the accumulators in both CTAs (multicast arrive), and the
+// odd CTA's epilogue warps arrive remotely on the even CTA's "accumulator
+// free" barrier.
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_rows2_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
+                              const GroupedGemmParams p) {
+  constexpr int BM2 = 2 * BM;                       // rows per pair tile
+  constexpr uint32_t A_BYTES = BM * BK * 2;         // this CTA's 128 rows
+  constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;   // this CTA's BN/2 weight rows
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  static_assert(STAGES <= 16, "stages");
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SharedCtl ctl;
+  __shared__ uint64_t peer_full[STAGES];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * A_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int E = p.num_experts;
+  const int feat_tiles = p.n / BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.empty[s], 1);
+      mbar_init(&peer_full[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl.acc_full[a], 1);
+      mbar_init(&ctl.acc_empty[a], 2 * 4);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(&ctl.drain, 1);
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_act);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) tmem_alloc_2sm(&ctl.tmem_base, TMEM_COLS);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BM2, feat_tiles);
+  tcgen05_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tcgen05_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total_tiles = ctl.tile_start[E];
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (both CTAs)
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, last_phase_mask = 0;
+    bool ok = true;
+    for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BM2, feat_tiles);
+      const int row0 = ctl.seg[tc.e] + tc.rblk * BM2;
+      const int arow = (p.shared_a ? tc.rblk * BM2 : row0) + static_cast<int>(rank) * BM;
+      const int wrow = tc.e * p.n + tc.fblk * BN + static_cast<int>(rank) * (BN / 2);
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        bool w = true;
+        if (lane == 0) w = mbar_wait_cluster(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status);
+        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
+          tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, arow);
+          tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow);
+        }
+        issued_mask |= 1u << stage;
+        last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      for (int s = 0; s < STAGES; ++s)
+        if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+    }
+  } else if (warp == 1 && rank == 0) {
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    constexpr uint32_t idesc = umma_idesc_bf16_f32(BM2, BN);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true, issued = false;
+    int t_local = 0;
+    for (int tile = pair; ok && tile < total_tiles; tile += npairs, ++t_local) {
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      bool w = true;
+      if (lane == 0) w = mbar_wait_cluster(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status);
+      if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+        ok = false;
+        break;
+      }
+      tcgen05_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        w = true;
+        if (lane == 0) {
+          w = mbar_wait_cluster(&ctl.full[stage], phase, &ctl.abort_flag, p.status) &&
+              mbar_wait_cluster(&peer_full[stage], phase, &ctl.abort_flag, p.status);
+        }
+        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        if (lane == 0) {
+          const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k)
+            umma_bf16_2sm(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_2sm(&ctl.empty[stage], 0x3);
+          issued = true;
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit_2sm(&ctl.acc_full[acc], 0x3);
+      __syncwarp();
+    }
+    if (!ok && lane == 0 && issued) {
+      umma_commit_2sm(&ctl.drain, 0x1);
+      drain_wait(&ctl.drain, 0);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- stage relay (odd CTA)
+    const uint32_t peer_full0 = mapa_shared(smem_u32(&peer_full[0]), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        bool w = true;
+        if (lane == 0) w = mbar_wait_cluster(&ctl.full[stage], phase, &ctl.abort_flag, p.status);
+        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_arrive_remote(peer_full0 + stage * static_cast<uint32_t>(sizeof(uint64_t)));
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int row_in_tile = static_cast<int>(rank) * BM + quarter * 32 + lane;
+    const uint32_t acc_empty0 = mapa_shared(smem_u32(&ctl.acc_empty[0]), 0);
+    int t_local = 0;
+    for (int tile = pair; tile < total_tiles; tile += npairs, ++t_local) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BM2, feat_tiles);
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      const int seg_end = ctl.seg[tc.e + 1];
+      const int r = ctl.seg[tc.e] + tc.rblk * BM2 + row_in_tile;
+      const bool valid = r < seg_end;
+      const long long orow = valid ? (p.out_row_map ? p.out_row_map[r] : r) : 0;
+      float scale = 1.f;
+      if (p.epilogue == kEpiScaleBf16 && valid) scale = p.row_weight ? p.row_weight[r] : p.slot_weight[p.row_slot[r]];
+      bool w = true;
+      if (lane == 0) w = mbar_wait_cluster(&ctl.acc_full[acc], acc_phase, &ctl.abort_flag, p.status);
+      if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) break;
+      tcgen05_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale);
+      tcgen05_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&ctl.acc_empty[acc]);
+        else mbar_arrive_remote(acc_empty0 + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+      }
+    }
+  }
+
+  tcgen05_fence_before();
+  cluster_sync();  // both CTAs done with tensor memory and with each other's barriers
+  tcgen05_fence_after();
+  if (warp == 1) tmem_dealloc_2sm(tmem_base, TMEM_COLS);
 }
 
 // ============================================================ weights schedule
@@ -428,6 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
       const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
       const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
+      const int arow0 = p.shared_a ? tc.rblk * BT : row0;
       const int wrow0 = tc.e * p.n + tc.fblk * BM;
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
@@ -437,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
           tma_load_2d_hint(sa + stage * A_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0, pol_w);
-          tma_load_2d(sb + stage * B_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, row0);
+          tma_load_2d(sb + stage * B_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, arow0);  // small K
         }
         issued_mask |= 1u << stage;
         last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
@@ -473,13 +711,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tcgen05_fence_after();
         if (lane == 0) {
-          const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
-          const uint32_t b0 = smem_u32(sb + stage * B_BYTES);
+          // K step of 16 bf16 = 32 bytes = 2 in the descriptor's address field
+          const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / UK; ++k) {
-            umma_bf16(d_tmem, umma_desc_sw128(a0 + k * UK * 2), umma_desc_sw128(b0 + k * UK * 2), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / UK; ++k)
+            umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit(&ctl.empty[stage]);
           issued = true;
         }
@@ -543,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < BT; ++j) {
           if (j >= nvalid) break;
           const long long r = r0 + j;
-          const float sc = p.epilogue == kEpiScaleBf16 ? p.slot_weight[p.row_slot[r]] : 1.f;
+          const float sc = p.epilogue != kEpiScaleBf16 ? 1.f : (p.row_weight ? p.row_weight[r] : p.slot_weight[p.row_slot[r]]);
           const long long orow = p.out_row_map ? p.out_row_map[r] : r;
           out[orow * p.out_ld + col] = __float2bfloat16_rn(sc * v[j]);
         }
@@ -595,6 +832,55 @@ cudaError_t launch_with_smem(GemmKernel kernel, size_t smem, int grid, const CUt
   return cudaGetLastError();
 }
 
+// Co-resident 2-CTA clusters of `kernel` on the current device (a TPC with a
+// disabled SM cannot host one), cached per (kernel, device).  A persistent
+// grid larger than this would run its last clusters after the others finish.
+int max_active_pairs(GemmKernel kernel, const cudaLaunchConfig_t& cfg_in) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = cfg_in;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = device_sm_count() / 2;
+  }
+  cache[key] = n;
+  return n;
+}
+
+cudaError_t launch_cluster2(GemmKernel kernel, size_t smem, int grid, const CUtensorMap& a, const CUtensorMap& w,
+                            const GroupedGemmParams& p, cudaStream_t s) {
+  cudaError_t e = ensure_smem_optin(kernel, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2, 1, 1);
+  const int pairs = std::max(1, std::min(grid / 2, max_active_pairs(kernel, cfg)));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kernel, a, w, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+constexpr size_t rows2_smem(int bn, int stages) {
+  return static_cast<size_t>(stages) * (BM * BK * 2 + (bn / 2) * BK * 2) + 1024;
+}
+
 constexpr size_t rows_smem(int bn, int stages) { return static_cast<size_t>(stages) * (BM * BK * 2 + bn * BK * 2) + 1024; }
 constexpr size_t weights_smem(int bt, int stages) {
   return static_cast<size_t>(stages) * (BM * BK * 2 + bt * BK * 2) + 1024;
@@ -605,7 +891,8 @@ constexpr size_t weights_smem(int bt, int stages) {
 int grouped_gemm_box_rows_act(int variant) {
   switch (variant) {
     case kRowsBN256:
-    case kRowsBN128: return BM;
+    case kRowsBN128:
+    case kRows2BN256: return BM;
     case kWeightsT16: return 16;
     case kWeightsT32: return 32;
     case kWeightsT64: return 64;
@@ -617,6 +904,7 @@ int grouped_gemm_box_rows_w(int variant) {
   switch (variant) {
     case kRowsBN256: return 256;
     case kRowsBN128: return 128;
+    case kRows2BN256: return 128;  // each CTA of the pair loads half of the 256 features
     default: return BM;
   }
 }
@@ -628,6 +916,9 @@ cudaError_t grouped_gemm_launch(int variant, const CUtensorMap& tmap_act, const 
       return launch_with_smem(grouped_gemm_rows_kernel<256, 4>, rows_smem(256, 4), grid, tmap_act, tmap_w, p, s);
     case kRowsBN128:
       return launch_with_smem(grouped_gemm_rows_kernel<128, 6>, rows_smem(128, 6), grid, tmap_act, tmap_w, p, s);
+    case kRows2BN256:
+      if (grid % 2) return cudaErrorInvalidValue;
+      return launch_cluster2(grouped_gemm_rows2_kernel<256, 6>, rows2_smem(256, 6), grid, tmap_act, tmap_w, p, s);
     case kWeightsT16:
       return launch_with_smem(grouped_gemm_weights_kernel<16, 8>, weights_smem(16, 8), grid, tmap_act, tmap_w, p, s);
     case kWeightsT32:

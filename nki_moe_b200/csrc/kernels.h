@@ -45,7 +45,7 @@ cudaError_t qk_norm_rope_launch(const void* qkv_in, void* qkv_out, const void* q
 // fp32 logits = x(bf16) . Wr(fp32)^T (+ bias), CUDA-core fp32 FMA, fixed order.
 cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits,
                                       int tokens, int hidden, int experts, cudaStream_t s);
-// Split fp32 router weights into three bf16 planes [E, 3H] = hi | mid | lo.
+// Split fp32 router weights into three bf16 planes [3, E, H] = hi, mid, lo.
 cudaError_t router_split_launch(const float* wr, __nv_bfloat16* wsplit, int experts, int hidden, cudaStream_t s);
 // Split-K fp32 router for few tokens: partial[split][T][E].
 cudaError_t router_splitk_launch(const __nv_bfloat16* x, const float* wr, float* partial, int tokens, int hidden,
@@ -63,7 +63,8 @@ cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const
 size_t permute_scratch_bytes(long long tokens, int top_k, int experts);
 cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k, int experts, int32_t* row_token,
                            int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* scratch,
-                           int* status, cudaStream_t s);
+                           int* status, cudaStream_t s, const float* slot_weight = nullptr,
+                           float* row_weight = nullptr);
 cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token, const int32_t* expert_offsets,
                                int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s);
 cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
@@ -94,7 +95,10 @@ enum Epilogue : int {
 
 struct GroupedGemmParams {
   const int32_t* expert_offsets;  // [E+1] segment starts of each expert's rows; null: one segment
-  int dense_rows;                 // rows of the single segment when expert_offsets is null
+  int dense_rows;                 // expert_offsets null: every expert has dense_rows rows, expert e
+                                  // starting at row e * dense_rows
+  int shared_a;                   // 1: every expert reads activation rows [0, dense_rows) (its
+                                  // output rows stay [e * dense_rows, (e + 1) * dense_rows))
   int num_experts;
   int n;           // output features per expert (rows of one expert's packed weight)
   int k_blocks;    // 64-wide K blocks iterated
@@ -102,8 +106,10 @@ struct GroupedGemmParams {
   int epilogue;
   void* out;
   long long out_ld;           // elements
-  const float* slot_weight;   // kEpiScaleBf16
-  const int32_t* row_slot;    // kEpiScaleBf16
+  const float* slot_weight;   // kEpiScaleBf16: weight of row r = slot_weight[row_slot[r]] ...
+  const int32_t* row_slot;
+  const float* row_weight;    // ... or row_weight[r] when given (permuted order, one coalesced load)
+  int prefetch;               // k-blocks of operands prefetched into L2 ahead of the TMA loads (0: off)
   const int32_t* out_row_map; // optional: output row of permuted row r
   const float* col_bias;      // kEpiStoreF32 optional
   int* status;
@@ -116,6 +122,7 @@ enum GemmVariant : int {
   kWeightsT16 = 2, // 128 features x 16 rows per tile (decode, swap-AB)
   kWeightsT32 = 3, // 128 features x 32 rows per tile
   kWeightsT64 = 4, // 128 features x 64 rows per tile
+  kRows2BN256 = 5, // 256 rows x 256 features per tile on an SM pair (cta_group::2)
 };
 
 // Builds a 2-D bf16 TMA descriptor with 128-byte swizzling over a row-major

@@ -79,7 +79,8 @@ template <typename IdxT>
 __global__ void __launch_bounds__(kPermuteChunk) permute_scatter_kernel(
     const IdxT* __restrict__ idx, int T, int K, int E, const int* __restrict__ chunk_base,
     const int* __restrict__ totals, int32_t* __restrict__ row_token, int32_t* __restrict__ row_slot,
-    int32_t* __restrict__ slot_row, int32_t* __restrict__ expert_offsets, int* status) {
+    int32_t* __restrict__ slot_row, int32_t* __restrict__ expert_offsets, const float* __restrict__ slot_weight,
+    float* __restrict__ row_weight, int* status) {
   constexpr int kWarps = kPermuteChunk / 32;
   __shared__ int offs[kMaxExperts + 1];
   __shared__ int wcnt[kWarps][kMaxExperts];
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(kPermuteChunk) permute_scatter_kernel(
   row_token[pos] = static_cast<int32_t>(t);
   row_slot[pos] = static_cast<int32_t>(slot);
   slot_row[slot] = pos;
+  if (row_weight) row_weight[pos] = slot_weight[slot];
   (void)status;
 }
 
@@ -241,7 +243,7 @@ size_t permute_scratch_bytes(long long tokens, int top_k, int experts) {
 
 cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k, int experts, int32_t* row_token,
                            int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* scratch,
-                           int* status, cudaStream_t s) {
+                           int* status, cudaStream_t s, const float* slot_weight, float* row_weight) {
   if (experts > kMaxExperts || experts < 1) return cudaErrorInvalidValue;
   const long long TK = static_cast<long long>(tokens) * top_k;
   const int C = static_cast<int>((TK + kPermuteChunk - 1) / kPermuteChunk);
@@ -263,11 +265,13 @@ cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k
   if (idx_dtype == kI64) {
     permute_scatter_kernel<long long><<<C, kPermuteChunk, 0, s>>>(static_cast<const long long*>(idx), tokens, top_k,
                                                                   experts, chunk_base, totals, row_token, row_slot,
-                                                                  slot_row, expert_offsets, status);
+                                                                  slot_row, expert_offsets, slot_weight, row_weight,
+                                                                  status);
   } else {
     permute_scatter_kernel<int32_t><<<C, kPermuteChunk, 0, s>>>(static_cast<const int32_t*>(idx), tokens, top_k,
                                                                 experts, chunk_base, totals, row_token, row_slot,
-                                                                slot_row, expert_offsets, status);
+                                                                slot_row, expert_offsets, slot_weight, row_weight,
+                                                                status);
   }
   return cudaGetLastError();
 }

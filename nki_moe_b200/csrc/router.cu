@@ -148,10 +148,10 @@ __global__ void router_split_kernel(const float* __restrict__ wr, __nv_bfloat16*
   const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
   const float r2 = r1 - __bfloat162float(mid);
   const __nv_bfloat16 lo = __float2bfloat16_rn(r2);
-  __nv_bfloat16* row = out + static_cast<long long>(e) * 3 * H;
-  row[h] = hi;
-  row[H + h] = mid;
-  row[2 * H + h] = lo;
+  const long long plane = static_cast<long long>(E) * H;
+  out[static_cast<long long>(e) * H + h] = hi;
+  out[plane + static_cast<long long>(e) * H + h] = mid;
+  out[2 * plane + static_cast<long long>(e) * H + h] = lo;
 }
 
 // One warp per token; lane l holds experts l, l+32, ... (VPT of them).
@@ -253,9 +253,11 @@ cudaError_t router_splitk_launch(const __nv_bfloat16* x, const float* wr, float*
 }
 
 int router_splits_for(int tokens, int hidden, int experts) {
+  // about a quarter of the SMs busy and at most 8 partial sums per logit: the
+  // router reads only E*H*4 bytes, latency matters more than bandwidth
   const long long tiles = static_cast<long long>((tokens + ST - 1) / ST) * ((experts + SE - 1) / SE);
-  long long sp = (2LL * device_sm_count() + tiles - 1) / tiles;
-  sp = std::max<long long>(1, std::min<long long>(sp, hidden / SK));
+  long long sp = (device_sm_count() / 4 + tiles - 1) / tiles;
+  sp = std::max<long long>(1, std::min<long long>({sp, 8LL, static_cast<long long>(hidden / SK)}));
   const int kspan = static_cast<int>(((hidden / sp + SK - 1) / SK) * SK);
   return (hidden + kspan - 1) / kspan;  // the number of splits actually launched
 }

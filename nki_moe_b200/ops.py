@@ -280,7 +280,7 @@ _router_cache: "OrderedDict[int, tuple]" = OrderedDict()
 
 
 def router_split(router_w: torch.Tensor) -> torch.Tensor:
-    """fp32 router weights [E, H] -> bf16 planes [E, 3H] (hi | mid | lo, exact
+    """fp32 router weights [E, H] -> bf16 planes [3, E, H] (hi, mid, lo; exact
     sum) for the tensor-core router; cached while the source tensor lives
     unmodified."""
     key = id(router_w)
@@ -290,7 +290,7 @@ def router_split(router_w: torch.Tensor) -> torch.Tensor:
             return hit[2]
     rw = _contig(_cuda(router_w, "router_w").detach(), torch.float32)
     E, H = rw.shape
-    out = torch.empty(E, 3 * H, dtype=torch.bfloat16, device=rw.device)
+    out = torch.empty(3, E, H, dtype=torch.bfloat16, device=rw.device)
     call("nkimoe_router_split", _p(rw), _p(out), E, H, _s(rw))
     with _router_lock:
         for k in [k for k, v in _router_cache.items() if v[0]() is None]:

@@ -225,7 +225,7 @@ def test_bad_expert_id_is_reported():
 
 
 # ---------------------------------------------------------------- K4/K5
-@pytest.mark.parametrize("schedule,rows", [(1, 0), (2, 16), (2, 32), (2, 64)])
+@pytest.mark.parametrize("schedule,rows", [(1, 0), (2, 16), (2, 32), (2, 64), (3, 0)])
 def test_grouped_gemm(schedule, rows):
     _lib.set_option("gemm_schedule", schedule)
     _lib.set_option("weights_rows", rows)
@@ -251,7 +251,7 @@ def test_grouped_gemm(schedule, rows):
         _lib.set_option("weights_rows", 0)
 
 
-@pytest.mark.parametrize("schedule,rows", [(0, 0), (1, 0), (2, 16), (2, 32), (2, 64)])
+@pytest.mark.parametrize("schedule,rows", [(0, 0), (1, 0), (2, 16), (2, 32), (2, 64), (3, 0)])
 def test_moe_experts_tiny(golden_dir, schedule, rows):
     """The reference test's module case (H=256, I=512, E=4, top-2) given routing."""
     _lib.set_option("gemm_schedule", schedule)
@@ -298,7 +298,7 @@ def _oracle_block(xn, gun, dn, rwn, bias, idx_gpu, w_gpu):
     return oracle.experts_forward(xn, gun, dn, idx_gpu, w_gpu)
 
 
-@pytest.mark.parametrize("schedule", [0, 1, 2])
+@pytest.mark.parametrize("schedule", [0, 1, 2, 3])
 def test_moe_block_c1(c1_inputs, golden_dir, schedule):
     _lib.set_option("gemm_schedule", schedule)
     try:
@@ -324,11 +324,16 @@ def test_moe_block_c2_decode():
     assert len(np.unique(idx)) > 100  # natural routing touches ~all experts
 
 
-def test_moe_block_c3_prefill_sampled_tokens():
+@pytest.mark.parametrize("schedule", [0, 1])
+def test_moe_block_c3_prefill_sampled_tokens(schedule):
     """Full prefill size (8192 tokens); each token's output depends only on
     that token, so 256 sampled tokens are checked against the oracle."""
-    inp = make_moe_inputs(WORKLOADS["c3"])
-    out, idx, w, (xn, gun, dn, rwn, _) = _block_case(inp)
+    _lib.set_option("gemm_schedule", schedule)
+    try:
+        inp = make_moe_inputs(WORKLOADS["c3"])
+        out, idx, w, (xn, gun, dn, rwn, _) = _block_case(inp)
+    finally:
+        _lib.set_option("gemm_schedule", 0)
     rng = np.random.default_rng(0)
     sel = np.sort(rng.choice(xn.shape[0], 256, replace=False))
     ref = oracle.experts_forward(xn[sel], gun, dn, idx[sel], w[sel])
