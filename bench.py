@@ -308,7 +308,7 @@ def run_b200(args):
     sampler = ClockSampler(local)
     sampler.start()
 
-    def setup(wl, seed_offset=0):
+    def setup(wl):
         inp = make_moe_inputs(wl, device="cuda")
         moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
         with torch.no_grad():
@@ -316,6 +316,9 @@ def run_b200(args):
             moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
             moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
         x = inp["x"].to(torch.bfloat16)
+        if world > 1:  # every rank has its own tokens (data-parallel shard)
+            g = torch.Generator(device="cuda").manual_seed(wl.seed * 1000 + rank)
+            x = torch.randn(wl.tokens, wl.hidden, generator=g, device="cuda").to(torch.bfloat16)
         return inp, moe, x
 
     def graph_of(fn):

@@ -170,6 +170,51 @@ NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const floa
  * NKIMOE_ERR_CUDA. */
 NKIMOE_API int nkimoe_read_status(void* workspace, void* stream, int* status_out);
 
+/* ---------------------------------------------------------------- expert parallel */
+/* The expert-parallel block splits nkimoe_moe_block into the pieces around
+ * its two all-to-all exchanges (NCCL, issued by the host layer).  The
+ * reference has no kernels for them: its EP lives inside NxDI
+ * (moe_ep_degree, qwen.py:272, :515). */
+
+NKIMOE_API size_t nkimoe_route_workspace_bytes(int64_t T, int64_t H, int64_t E, int64_t K);
+
+/* Router + softmax/top-k/renormalise only (nki_moe_integrated.py:436-443):
+ * int32 topk_idx [T,K], fp32 topk_w [T,K]. */
+NKIMOE_API int nkimoe_route(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                            int32_t* topk_idx, float* topk_w, int64_t T, int64_t H, int64_t E, int64_t K,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+NKIMOE_API size_t nkimoe_dispatch_workspace_bytes(int64_t T, int64_t K, int64_t E);
+
+/* Permutation by global expert and row gather: x_perm [T*K, H] bf16 in
+ * (expert, k, t) order, so the rows for the ranks owning experts
+ * [r*E/P, (r+1)*E/P) are contiguous; row_weight [T*K] the routing weight of
+ * each permuted row; slot_row [T*K] the inverse permutation (for
+ * nkimoe_combine); expert_counts [E] rows per expert.  Follows the dispatch
+ * order of nki_moe_integrated.py:450-467. */
+NKIMOE_API int nkimoe_dispatch(const void* x, const void* topk_idx, int idx_dtype, const float* topk_w, int64_t T,
+                               int64_t H, int64_t E, int64_t K, void* x_perm, float* row_weight, int32_t* slot_row,
+                               int32_t* expert_counts, void* workspace, size_t workspace_bytes, void* stream);
+
+NKIMOE_API size_t nkimoe_segment_experts_workspace_bytes(int64_t rows, int64_t I, int64_t segments);
+
+/* Expert FFNs over `segments` consecutive row segments of a (bf16 [rows, H]);
+ * segment s has segment_counts[s] rows (device int32) and uses local expert
+ * s % experts_per_group of w13 [experts_per_group, 2I, H] / w2 [.., H, I];
+ * y [rows, H] bf16 = row_weight[r] * FFN(a[r]).  With segments ordered
+ * (source rank, local expert) this runs on the rows an all-to-all delivered
+ * without re-sorting them (nki_moe_integrated.py:142-206 per expert). */
+NKIMOE_API int nkimoe_segment_experts(const void* a, const float* row_weight, const int32_t* segment_counts,
+                                      int64_t segments, int64_t experts_per_group, const void* w13, const void* w2,
+                                      void* y, int64_t rows, int64_t H, int64_t I, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
+/* out[t] = sum_k (slot_weight ? slot_weight[t*K+k] : 1) * y[slot_row[t*K+k]]
+ * in fp32, k ascending, bf16 out (nki_moe_integrated.py:482-494,
+ * nki_moe_aggregate :209-251); slot_row < 0 is skipped. */
+NKIMOE_API int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T,
+                              int64_t K, int64_t H, void* stream);
+
 /* ---------------------------------------------------------------- pieces */
 
 /* Grouped GEMM over expert segments: for each expert e, rows

@@ -50,6 +50,13 @@ SIGNATURES = {
     "nkimoe_router_split": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_read_status": (_i, [_vp, _vp, _c.POINTER(_i)]),
     "nkimoe_grouped_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "nkimoe_route_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "nkimoe_route": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "nkimoe_dispatch_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "nkimoe_dispatch": (_i, [_vp, _vp, _i, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "nkimoe_segment_experts_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "nkimoe_segment_experts": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "nkimoe_combine": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "nkimoe_swiglu": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_aggregate": (_i, [_vp, _vp, _i64, _i64, _i64, _vp]),
 }

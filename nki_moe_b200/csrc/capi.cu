@@ -128,7 +128,8 @@ int choose_variant(long long rows_total, long long E, long long N) {
 int run_gemm(const void* act, long long act_rows, const void* w, long long E, long long N, long long kd,
              const int32_t* offsets, int epilogue, void* out, long long out_ld, const float* slot_w,
              const int32_t* row_slot, const int32_t* out_row_map, const float* col_bias, int* status,
-             cudaStream_t s, long long kd_act = 0, bool shared_a = false, const float* row_weight = nullptr) {
+             cudaStream_t s, long long kd_act = 0, bool shared_a = false, const float* row_weight = nullptr,
+             long long weight_experts = 0, int weight_mod = 0) {
   if (act_rows == 0) return NKIMOE_OK;
   if (kd_act == 0) kd_act = kd;
   // with shared activation rows every expert has act_rows rows
@@ -137,7 +138,8 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   CUtensorMap ta, tw;
   NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the activation operand");
-  NKI_REQUIRE(make_tmap_bf16(&tw, w, E * N, kd, grouped_gemm_box_rows_w(variant)), NKIMOE_ERR_CUDA,
+  if (weight_experts == 0) weight_experts = E;
+  NKI_REQUIRE(make_tmap_bf16(&tw, w, weight_experts * N, kd, grouped_gemm_box_rows_w(variant)), NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the weight operand");
   GroupedGemmParams p{};
   p.expert_offsets = offsets;
@@ -147,6 +149,7 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.k_blocks = static_cast<int>(kd / 64);
   p.k_blocks_a = static_cast<int>(kd_act / 64);
   p.shared_a = shared_a ? 1 : 0;
+  p.weight_mod = weight_mod;
   p.row_weight = row_weight;
   p.prefetch = g_prefetch.load();
   p.epilogue = epilogue;
@@ -532,6 +535,116 @@ int nkimoe_aggregate(const void* expert_outputs, void* out, int64_t K, int64_t T
               "null or unaligned pointer");
   NKI_CUDA(aggregate_launch(static_cast<const __nv_bfloat16*>(expert_outputs), static_cast<__nv_bfloat16*>(out),
                             static_cast<int>(K), T, static_cast<int>(H), as_stream(stream)));
+  return NKIMOE_OK;
+}
+
+// ------------------------------------------------------------ expert parallel pieces
+
+size_t nkimoe_route_workspace_bytes(int64_t T, int64_t H, int64_t E, int64_t K) {
+  const WsLayout L = ws_layout(T, H, 64, E, K);
+  return L.partial + round256(sizeof(float) * std::max<long long>(
+                                  T > 0 ? router_splits_for(static_cast<int>(T), static_cast<int>(H),
+                                                            static_cast<int>(E))
+                                        : 1,
+                                  3) *
+                              T * E);
+}
+
+int nkimoe_route(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                 int32_t* topk_idx, float* topk_w, int64_t T, int64_t H, int64_t E, int64_t K, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  NKI_REQUIRE(T >= 0 && H > 0 && E > 0 && K > 0 && K <= 32 && K <= E && E <= 256, NKIMOE_ERR_UNSUPPORTED,
+              "route: bad shape");
+  NKI_REQUIRE(H % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden must be a multiple of 64");
+  const size_t need = nkimoe_route_workspace_bytes(T, H, E, K);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  const cudaStream_t s = as_stream(stream);
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && router_w && topk_idx && topk_w && aligned16(x) && aligned16(router_w), NKIMOE_ERR_INVALID_ARG,
+              "null or misaligned pointer");
+  const WsLayout L = ws_layout(T, H, 64, E, K);
+  char* base = static_cast<char*>(workspace);
+  return router_impl(x, router_w, router_bias, router_w_split, topk_idx, topk_w, T, H, E, K, base, L,
+                     reinterpret_cast<int*>(base + L.status), s);
+}
+
+size_t nkimoe_dispatch_workspace_bytes(int64_t T, int64_t K, int64_t E) {
+  const long long TK = T * K;
+  return 256 + round256(sizeof(int32_t) * (E + 1)) + 2 * round256(sizeof(int32_t) * TK) +
+         round256(permute_scratch_bytes(T, static_cast<int>(K), static_cast<int>(E)));
+}
+
+int nkimoe_dispatch(const void* x, const void* topk_idx, int idx_dtype, const float* topk_w, int64_t T, int64_t H,
+                    int64_t E, int64_t K, void* x_perm, float* row_weight, int32_t* slot_row, int32_t* expert_counts,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  NKI_REQUIRE(T >= 0 && H > 0 && E > 0 && K > 0 && E <= kMaxExperts && H % 8 == 0, NKIMOE_ERR_UNSUPPORTED,
+              "dispatch: bad shape");
+  NKI_REQUIRE(idx_dtype == NKIMOE_I32 || idx_dtype == NKIMOE_I64, NKIMOE_ERR_INVALID_ARG, "idx dtype must be I32/I64");
+  const size_t need = nkimoe_dispatch_workspace_bytes(T, K, E);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  const cudaStream_t s = as_stream(stream);
+  char* base = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(base);
+  NKI_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+  int32_t* offsets = reinterpret_cast<int32_t*>(base + 256);
+  if (T == 0) {
+    NKI_CUDA(cudaMemsetAsync(expert_counts, 0, sizeof(int32_t) * E, s));
+    return NKIMOE_OK;
+  }
+  NKI_REQUIRE(x && topk_idx && topk_w && x_perm && row_weight && slot_row && expert_counts && aligned16(x) &&
+                  aligned16(x_perm),
+              NKIMOE_ERR_INVALID_ARG, "null or misaligned pointer");
+  const long long TK = T * K;
+  int32_t* row_token = offsets + round256(sizeof(int32_t) * (E + 1)) / sizeof(int32_t);
+  int32_t* row_slot = row_token + round256(sizeof(int32_t) * TK) / sizeof(int32_t);
+  void* scratch = row_slot + round256(sizeof(int32_t) * TK) / sizeof(int32_t);
+  NKI_CUDA(permute_launch(topk_idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
+                          row_slot, slot_row, offsets, scratch, status, s, topk_w, row_weight));
+  NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(E),
+                              static_cast<__nv_bfloat16*>(x_perm), TK, static_cast<int>(H), s));
+  NKI_CUDA(offsets_to_counts_launch(offsets, expert_counts, static_cast<int>(E), s));
+  return NKIMOE_OK;
+}
+
+size_t nkimoe_segment_experts_workspace_bytes(int64_t rows, int64_t I, int64_t segments) {
+  return 256 + round256(sizeof(int32_t) * (segments + 1)) + round256(sizeof(uint16_t) * rows * I);
+}
+
+int nkimoe_segment_experts(const void* a, const float* row_weight, const int32_t* segment_counts, int64_t segments,
+                           int64_t experts_per_group, const void* w13, const void* w2, void* y, int64_t rows,
+                           int64_t H, int64_t I, void* workspace, size_t workspace_bytes, void* stream) {
+  NKI_REQUIRE(rows >= 0 && H > 0 && I > 0 && segments > 0 && segments <= kMaxExperts && experts_per_group > 0,
+              NKIMOE_ERR_UNSUPPORTED, "segment experts: bad shape");
+  NKI_REQUIRE(H % 128 == 0 && I % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "H %% 128 == 0 and I %% 64 == 0 required");
+  const size_t need = nkimoe_segment_experts_workspace_bytes(rows, I, segments);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  const cudaStream_t s = as_stream(stream);
+  char* base = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(base);
+  NKI_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+  if (rows == 0) return NKIMOE_OK;
+  NKI_REQUIRE(a && row_weight && segment_counts && w13 && w2 && y && aligned16(a) && aligned16(w13) && aligned16(w2) &&
+                  aligned16(y),
+              NKIMOE_ERR_INVALID_ARG, "null or misaligned pointer");
+  int32_t* offsets = reinterpret_cast<int32_t*>(base + 256);
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(base + 256 + round256(sizeof(int32_t) * (segments + 1)));
+  NKI_CUDA(counts_to_offsets_launch(segment_counts, offsets, static_cast<int>(segments), s));
+  int rc = run_gemm(a, rows, w13, segments, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr,
+                    status, s, 0, false, nullptr, experts_per_group, static_cast<int>(experts_per_group));
+  if (rc != NKIMOE_OK) return rc;
+  return run_gemm(h, rows, w2, segments, H, I, offsets, kEpiScaleBf16, y, H, nullptr, nullptr, nullptr, nullptr,
+                  status, s, 0, false, row_weight, experts_per_group, static_cast<int>(experts_per_group));
+}
+
+int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T, int64_t K,
+                   int64_t H, void* stream) {
+  NKI_REQUIRE(T >= 0 && K > 0 && H > 0 && H % 8 == 0, NKIMOE_ERR_INVALID_ARG, "combine: bad shape");
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(y && slot_row && out && aligned16(y) && aligned16(out), NKIMOE_ERR_INVALID_ARG,
+              "null or misaligned pointer");
+  NKI_CUDA(combine_launch(static_cast<const __nv_bfloat16*>(y), slot_row, slot_weight, static_cast<__nv_bfloat16*>(out),
+                          static_cast<int>(T), static_cast<int>(K), static_cast<int>(H), as_stream(stream)));
   return NKIMOE_OK;
 }
 

@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
       const int row0 = ctl.seg[tc.e] + tc.rblk * BM;
       const int arow0 = p.shared_a ? tc.rblk * BM : row0;
-      const int wrow0 = tc.e * p.n + tc.fblk * BN;
+      const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN;
       int ka = 0;  // activation K coordinate (wraps at k_blocks_a blocks)
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (pk >= p.k_blocks && tile + static_cast<int>(gridDim.x) < total_tiles) {
               const TileCoord nc = decode_tile(ctl, E, tile + gridDim.x, BM, feat_tiles);
               pk -= p.k_blocks;
-              pw = nc.e * p.n + nc.fblk * BN;
+              pw = (p.weight_mod ? nc.e % p.weight_mod : nc.e) * p.n + nc.fblk * BN;
               pa = p.shared_a ? nc.rblk * BM : ctl.seg[nc.e] + nc.rblk * BM;
             }
             if (pk < p.k_blocks) {
@@ -471,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord tc = decode_tile(ctl, E, tile, BM2, feat_tiles);
       const int row0 = ctl.seg[tc.e] + tc.rblk * BM2;
       const int arow = (p.shared_a ? tc.rblk * BM2 : row0) + static_cast<int>(rank) * BM;
-      const int wrow = tc.e * p.n + tc.fblk * BN + static_cast<int>(rank) * (BN / 2);
+      const int wrow = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN + static_cast<int>(rank) * (BN / 2);
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         bool w = true;
         if (lane == 0) w = mbar_wait_cluster(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status);
@@ -666,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
       const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
       const int arow0 = p.shared_a ? tc.rblk * BT : row0;
-      const int wrow0 = tc.e * p.n + tc.fblk * BM;
+      const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BM;
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
           ok = false;

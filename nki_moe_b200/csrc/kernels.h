@@ -69,6 +69,10 @@ cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token,
                                int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s);
 cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
                            __nv_bfloat16* out, int tokens, int top_k, int hidden, cudaStream_t s);
+// counts[e] = offsets[e+1] - offsets[e]
+cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s);
+// offsets[0] = 0, offsets[i+1] = offsets[i] + counts[i] (n <= kMaxExperts)
+cudaError_t counts_to_offsets_launch(const int32_t* counts, int32_t* offsets, int n, cudaStream_t s);
 cudaError_t aggregate_launch(const __nv_bfloat16* expert_outputs, __nv_bfloat16* out, int top_k, long long tokens,
                              int hidden, cudaStream_t s);
 cudaError_t swiglu_launch(const __nv_bfloat16* gate_up, __nv_bfloat16* out, long long rows, int n, cudaStream_t s);
@@ -97,6 +101,8 @@ struct GroupedGemmParams {
   const int32_t* expert_offsets;  // [E+1] segment starts of each expert's rows; null: one segment
   int dense_rows;                 // expert_offsets null: every expert has dense_rows rows, expert e
                                   // starting at row e * dense_rows
+  int weight_mod;                 // > 0: segment e uses weight block e % weight_mod (expert-parallel
+                                  // segments ordered (source rank, local expert)); 0: block e
   int shared_a;                   // 1: every expert reads activation rows [0, dense_rows) (its
                                   // output rows stay [e * dense_rows, (e + 1) * dense_rows))
   int num_experts;

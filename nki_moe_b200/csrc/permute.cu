@@ -227,6 +227,31 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
   }
 }
 
+__global__ void offsets_to_counts_kernel(const int32_t* __restrict__ offsets, int32_t* __restrict__ counts, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) counts[i] = offsets[i + 1] - offsets[i];
+}
+
+// One block of 512 threads: exclusive scan of n <= 512 counts.
+__global__ void __launch_bounds__(512) counts_to_offsets_kernel(const int32_t* __restrict__ counts,
+                                                                int32_t* __restrict__ offsets, int n) {
+  __shared__ int warp_tot[16];
+  const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
+  const int v = i < n ? counts[i] : 0;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int before = 0;
+  for (int w = 0; w < warp; ++w) before += warp_tot[w];
+  if (i < n) offsets[i + 1] = before + incl;
+  if (i == 0) offsets[0] = 0;
+}
+
 unsigned grid_for(long long work, int threads) {
   const long long b = (work + threads - 1) / threads;
   const long long cap = static_cast<long long>(device_sm_count()) * 16;
@@ -289,6 +314,18 @@ cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, cons
   if (tokens == 0) return cudaSuccess;
   combine_kernel<<<grid_for(static_cast<long long>(tokens) * (hidden / 8), 256), 256, 0, s>>>(
       y, slot_row, slot_weight, out, tokens, top_k, hidden);
+  return cudaGetLastError();
+}
+
+cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  offsets_to_counts_kernel<<<(n + 255) / 256, 256, 0, s>>>(offsets, counts, n);
+  return cudaGetLastError();
+}
+
+cudaError_t counts_to_offsets_launch(const int32_t* counts, int32_t* offsets, int n, cudaStream_t s) {
+  if (n <= 0 || n > 512) return cudaErrorInvalidValue;
+  counts_to_offsets_kernel<<<1, 512, 0, s>>>(counts, offsets, n);
   return cudaGetLastError();
 }
 

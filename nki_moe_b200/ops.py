@@ -22,6 +22,7 @@ __all__ = [
     "rmsnorm", "add_rmsnorm", "qk_norm_rope", "router_logits", "topk_softmax", "permute",
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
+    "route", "dispatch", "segment_experts", "combine",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -359,4 +360,73 @@ def aggregate(expert_outputs: torch.Tensor) -> torch.Tensor:
     K, T, H = eo.shape
     out = torch.empty(T, H, dtype=torch.bfloat16, device=eo.device)
     call("nkimoe_aggregate", _p(eo), _p(out), K, T, H, _s(eo))
+    return out
+
+
+# ---------------------------------------------------------------- expert-parallel pieces
+def route(x: torch.Tensor, router_w: torch.Tensor, top_k: int, bias: torch.Tensor | None = None,
+          tensor_router: bool = True):
+    """Router + softmax/top-k/renormalise: ``(idx int32 [T,K], w fp32 [T,K])``."""
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    rsplit = router_split(router_w) if tensor_router and router_w.shape[0] % 128 == 0 else None
+    rw = _contig(_cuda(router_w, "router_w"), torch.float32)
+    b = _contig(bias, torch.float32) if bias is not None else None
+    T, H = x.shape
+    E = rw.shape[0]
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    ws = workspace(x.device, size_call("nkimoe_route_workspace_bytes", T, H, E, top_k))
+    call("nkimoe_route", _p(x), _p(rw), _p(b), _p(rsplit), _p(idx), _p(w), T, H, E, top_k, _p(ws), ws.numel(), _s(x))
+    return idx, w
+
+
+def dispatch(x: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, num_experts: int):
+    """Group the (token, slot) rows by global expert: returns ``(x_perm [T*K, H],
+    row_weight [T*K], slot_row [T*K], expert_counts [E])``."""
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    idx = _contig(_cuda(idx, "idx"))
+    if idx.dtype not in (torch.int32, torch.int64):
+        idx = idx.to(torch.int64)
+    w = _contig(_cuda(weights, "weights"), torch.float32)
+    T, H = x.shape
+    K = idx.shape[1]
+    dev = x.device
+    x_perm = torch.empty(T * K, H, dtype=torch.bfloat16, device=dev)
+    row_weight = torch.empty(T * K, dtype=torch.float32, device=dev)
+    slot_row = torch.empty(T * K, dtype=torch.int32, device=dev)
+    counts = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    ws = workspace(dev, size_call("nkimoe_dispatch_workspace_bytes", T, K, num_experts))
+    call("nkimoe_dispatch", _p(x), _p(idx), _DT[idx.dtype], _p(w), T, H, num_experts, K, _p(x_perm), _p(row_weight),
+         _p(slot_row), _p(counts), _p(ws), ws.numel(), _s(x))
+    if sync_check_enabled():
+        read_status(ws)
+    return x_perm, row_weight, slot_row, counts
+
+
+def segment_experts(a: torch.Tensor, row_weight: torch.Tensor, segment_counts: torch.Tensor,
+                    experts: PackedExperts) -> torch.Tensor:
+    """``y[r] = row_weight[r] * FFN_{s % E_local}(a[r])`` for rows r of segment s."""
+    a = _contig(_cuda(a, "a"), torch.bfloat16)
+    rw = _contig(_cuda(row_weight, "row_weight"), torch.float32)
+    sc = _contig(_cuda(segment_counts, "segment_counts").reshape(-1), torch.int32)
+    R, H = a.shape
+    S = sc.numel()
+    y = torch.empty(R, H, dtype=torch.bfloat16, device=a.device)
+    ws = workspace(a.device, size_call("nkimoe_segment_experts_workspace_bytes", R, experts.inter, S))
+    call("nkimoe_segment_experts", _p(a), _p(rw), _p(sc), S, experts.num_experts, _p(experts.w13), _p(experts.w2),
+         _p(y), R, H, experts.inter, _p(ws), ws.numel(), _s(a))
+    if sync_check_enabled():
+        read_status(ws)
+    return y
+
+
+def combine(y: torch.Tensor, slot_row: torch.Tensor, tokens: int, top_k: int,
+            slot_weight: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[t] = sum_k (w[t,k]) * y[slot_row[t*K+k]]`` (fp32 sum, k ascending)."""
+    y = _contig(_cuda(y, "y"), torch.bfloat16)
+    sr = _contig(_cuda(slot_row, "slot_row"), torch.int32)
+    sw = _contig(slot_weight, torch.float32) if slot_weight is not None else None
+    H = y.shape[1]
+    out = torch.empty(tokens, H, dtype=torch.bfloat16, device=y.device)
+    call("nkimoe_combine", _p(y), _p(sr), _p(sw), _p(out), tokens, top_k, H, _s(y))
     return out
