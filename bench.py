@@ -31,9 +31,10 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-# Per-launch DRAM traffic (read + write bytes) of the dominant kernel, from
-# the ncu captures summarised in profiles/ (None until captured).
-NCU_TRAFFIC_BYTES = {"prefill": None, "decode": None}
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernel (GEMM-1), from the ncu captures summarised in
+# profiles/grouped_gemm_prefill_c3_t8192.md and profiles/grouped_gemm_decode_c2_t64.md.
+NCU_TRAFFIC_BYTES = {"prefill": 1.0739e9 + 92.66e6, "decode": 794.89e6 + 3.64e6}
 
 
 def parse():
