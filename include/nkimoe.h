@@ -165,6 +165,25 @@ NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const floa
                      void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
                      int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
+/* nkimoe_moe_block for callers that cannot allocate GPU memory (a server that
+ * reserved all device memory up front, a runtime whose allocator may not be
+ * entered where the layer is issued, an embedding that forbids allocation
+ * while it records CUDA graphs).  It has no counterpart in the reference.
+ * Same arguments and results as nkimoe_moe_block without the workspace: the
+ * scratch is a fixed 8 MiB array inside the library, held by every GPU that
+ * loads the library until the process exits (enough for up to 170 tokens at
+ * H=2048, I=768, E=128, K=8; larger batches return NKIMOE_ERR_WORKSPACE
+ * without touching the GPU).  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  All calls on a device share the array, which keeps the
+ * last call's contents (each call clears what must start at zero): two calls
+ * that overlap on the GPU, e.g. issued on two streams or from two host
+ * threads without ordering, race on it. */
+NKIMOE_API int nkimoe_moe_block_noalloc(const void* x, const float* router_w, const float* router_bias,
+                                        const void* router_w_split, const void* w13, const void* w2, void* out,
+                                        int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,
+                                        int64_t E, int64_t K, void* stream);
+
 /* Reads and clears the device status word of a workspace (synchronises the
  * stream).  Returns NKIMOE_OK, NKIMOE_ERR_DEVICE (status in *status_out), or
  * NKIMOE_ERR_CUDA. */

@@ -49,6 +49,8 @@ SIGNATURES = {
                               _vp]),
     "nkimoe_router_split": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_read_status": (_i, [_vp, _vp, _c.POINTER(_i)]),
+    "nkimoe_moe_block_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                      _vp]),
     "nkimoe_grouped_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "nkimoe_route_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "nkimoe_route": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),

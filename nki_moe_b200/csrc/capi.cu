@@ -262,6 +262,8 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long lon
   return r == CUDA_SUCCESS;
 }
 
+void set_last_error(const char* msg) { g_err = msg ? msg : ""; }
+
 int device_sm_count() {
   static int counts[64] = {0};
   int dev = 0;

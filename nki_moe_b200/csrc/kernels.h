@@ -142,4 +142,7 @@ int grouped_gemm_box_rows_w(int variant);
 
 int device_sm_count();
 
+// Sets the calling thread's message returned by nkimoe_last_error().
+void set_last_error(const char* msg);
+
 }  // namespace nkimoe
