@@ -121,8 +121,9 @@ NKIMOE_API size_t nkimoe_permute_workspace_bytes(int64_t T, int64_t K, int64_t E
 
 /* Stable grouping of the T*K assignments by expert, (k, t) order inside an
  * expert (nki_moe_integrated.py:450-467).  topk_idx is [T,K] of idx_dtype
- * (I32 or I64).  Outputs: row_token[T*K], row_slot[T*K] (= t*K + k),
- * slot_row[T*K] (inverse; -1 for an out-of-range id), expert_offsets[E+1]. */
+ * (I32 or I64); a negative id is an empty slot, an id >= E an error.  Outputs:
+ * row_token[T*K], row_slot[T*K] (= t*K + k), slot_row[T*K] (inverse; -1 for
+ * an empty or out-of-range slot), expert_offsets[E+1]. */
 NKIMOE_API int nkimoe_permute(const void* topk_idx, int idx_dtype, int64_t T, int64_t K, int64_t E, int32_t* row_token,
                    int32_t* row_slot, int32_t* slot_row, int32_t* expert_offsets, void* workspace,
                    size_t workspace_bytes, void* stream);
@@ -144,7 +145,7 @@ NKIMOE_API int nkimoe_pack_down(const void* down, int layout, void* w2, int64_t 
 NKIMOE_API size_t nkimoe_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
 
 /* Expert stage given routing: out[T,H] (bf16) = sum_k w[t,k] *
- * FFN_{idx[t,k]}(x[t]).  The whole-block kernels nki_moe_full_forward /
+ * FFN_{idx[t,k]}(x[t]); a negative idx[t,k] marks an empty slot.  The whole-block kernels nki_moe_full_forward /
  * nki_moe_optimized (nki_moe_kernel.py:185-423), nki_moe_expert_kernel /
  * nki_moe_expert_fused_kernel_v2 (nki_moe_expert.py:21-355), all
  * (hidden_states[T,H], gate_up_proj, down_proj, expert_indices[T,K],
@@ -227,6 +228,22 @@ NKIMOE_API int nkimoe_segment_experts(const void* a, const float* row_weight, co
                                       int64_t segments, int64_t experts_per_group, const void* w13, const void* w2,
                                       void* y, int64_t rows, int64_t H, int64_t I, void* workspace,
                                       size_t workspace_bytes, void* stream);
+
+NKIMOE_API size_t nkimoe_ep_dispatch_workspace_bytes(int64_t T, int64_t P);
+
+/* De-duplicated expert-parallel dispatch over P ranks with experts_per_rank
+ * experts each (rank d owns [d*El, (d+1)*El)): one send row per (token, rank)
+ * pair that has at least one of the token's experts, rows grouped by rank and
+ * ordered by token.  Outputs x_send [<= T*P, H] bf16, slots_send [.., K] int32
+ * (the token's K slots as the destination sees them: local expert id or -1),
+ * weights_send [.., K] fp32 (routing weight, 0 for -1 slots), rank_counts [P]
+ * rows per rank, slot_row [T, P] (row of (t, d) or -1) for the final
+ * nkimoe_combine with K = P.  The receiver runs nkimoe_moe_experts on the
+ * rows with slots/weights as routing (negative ids are empty slots). */
+NKIMOE_API int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w, int64_t T, int64_t H,
+                                  int64_t K, int64_t num_ranks, int64_t experts_per_rank, void* x_send,
+                                  int32_t* slots_send, float* weights_send, int32_t* rank_counts, int32_t* slot_row,
+                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* out[t] = sum_k (slot_weight ? slot_weight[t*K+k] : 1) * y[slot_row[t*K+k]]
  * in fp32, k ascending, bf16 out (nki_moe_integrated.py:482-494,

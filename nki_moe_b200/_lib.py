@@ -59,6 +59,9 @@ SIGNATURES = {
     "nkimoe_segment_experts_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "nkimoe_segment_experts": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "nkimoe_combine": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "nkimoe_ep_dispatch_workspace_bytes": (_sz, [_i64, _i64]),
+    "nkimoe_ep_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
+                                _vp]),
     "nkimoe_swiglu": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_aggregate": (_i, [_vp, _vp, _i64, _i64, _i64, _vp]),
 }

@@ -639,6 +639,52 @@ int nkimoe_segment_experts(const void* a, const float* row_weight, const int32_t
                   status, s, 0, false, row_weight, experts_per_group, static_cast<int>(experts_per_group));
 }
 
+size_t nkimoe_ep_dispatch_workspace_bytes(int64_t T, int64_t P) {
+  const long long TP = T * P;
+  return 256 + round256(sizeof(int32_t) * (P + 1)) + 3 * round256(sizeof(int32_t) * TP) +
+         round256(permute_scratch_bytes(T, static_cast<int>(P), static_cast<int>(P)));
+}
+
+int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w, int64_t T, int64_t H, int64_t K,
+                       int64_t num_ranks, int64_t experts_per_rank, void* x_send, int32_t* slots_send,
+                       float* weights_send, int32_t* rank_counts, int32_t* slot_row, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  const long long P = num_ranks, El = experts_per_rank;
+  NKI_REQUIRE(T >= 0 && H > 0 && K > 0 && P > 0 && El > 0 && P <= kMaxExperts && H % 8 == 0,
+              NKIMOE_ERR_UNSUPPORTED, "ep dispatch: bad shape");
+  const size_t need = nkimoe_ep_dispatch_workspace_bytes(T, P);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  const cudaStream_t s = as_stream(stream);
+  char* base = static_cast<char*>(workspace);
+  int* status = reinterpret_cast<int*>(base);
+  NKI_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+  if (T == 0) {
+    NKI_CUDA(cudaMemsetAsync(rank_counts, 0, sizeof(int32_t) * P, s));
+    return NKIMOE_OK;
+  }
+  NKI_REQUIRE(x && topk_idx && topk_w && x_send && slots_send && weights_send && rank_counts && slot_row &&
+                  aligned16(x) && aligned16(x_send),
+              NKIMOE_ERR_INVALID_ARG, "null or misaligned pointer");
+  const long long TP = T * P;
+  int32_t* offsets = reinterpret_cast<int32_t*>(base + 256);
+  int32_t* dest = offsets + round256(sizeof(int32_t) * (P + 1)) / sizeof(int32_t);
+  int32_t* row_token = dest + round256(sizeof(int32_t) * TP) / sizeof(int32_t);
+  int32_t* row_slot = row_token + round256(sizeof(int32_t) * TP) / sizeof(int32_t);
+  void* scratch = row_slot + round256(sizeof(int32_t) * TP) / sizeof(int32_t);
+  // (token, rank) pairs grouped by rank, tokens ascending: the permutation of
+  // the [T, P] destination matrix with ranks as the sort keys
+  NKI_CUDA(ep_dest_launch(topk_idx, static_cast<int>(T), static_cast<int>(K), static_cast<int>(P),
+                          static_cast<int>(El), dest, s));
+  NKI_CUDA(permute_launch(dest, NKIMOE_I32, static_cast<int>(T), static_cast<int>(P), static_cast<int>(P), row_token,
+                          row_slot, slot_row, offsets, scratch, status, s));
+  NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(P),
+                              static_cast<__nv_bfloat16*>(x_send), TP, static_cast<int>(H), s));
+  NKI_CUDA(ep_slots_launch(topk_idx, topk_w, row_token, row_slot, offsets, TP, static_cast<int>(P),
+                           static_cast<int>(K), static_cast<int>(El), slots_send, weights_send, s));
+  NKI_CUDA(offsets_to_counts_launch(offsets, rank_counts, static_cast<int>(P), s));
+  return NKIMOE_OK;
+}
+
 int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T, int64_t K,
                    int64_t H, void* stream) {
   NKI_REQUIRE(T >= 0 && K > 0 && H > 0 && H % 8 == 0, NKIMOE_ERR_INVALID_ARG, "combine: bad shape");

@@ -69,6 +69,11 @@ cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token,
                                int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s);
 cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
                            __nv_bfloat16* out, int tokens, int top_k, int hidden, cudaStream_t s);
+// Expert-parallel de-duplicated dispatch helpers (see permute.cu).
+cudaError_t ep_dest_launch(const int32_t* idx, int T, int K, int P, int El, int32_t* dest, cudaStream_t s);
+cudaError_t ep_slots_launch(const int32_t* idx, const float* w, const int32_t* row_token, const int32_t* row_slot,
+                            const int32_t* rank_offsets, long long max_rows, int P, int K, int El, int32_t* slots,
+                            float* wts, cudaStream_t s);
 // counts[e] = offsets[e+1] - offsets[e]
 cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s);
 // offsets[0] = 0, offsets[i+1] = offsets[i] + counts[i] (n <= kMaxExperts)

@@ -17,11 +17,13 @@ namespace nkimoe {
 
 namespace {
 
+// A negative id marks an empty slot (skipped); an id >= E is an error.
 template <typename IdxT>
 __device__ __forceinline__ int load_expert(const IdxT* idx, long long j, int T, int K, int E, int* status) {
   const long long k = j / T, t = j % T;
   const long long e = static_cast<long long>(idx[t * K + k]);
-  if (e < 0 || e >= E) {
+  if (e < 0) return -1;
+  if (e >= E) {
     atomicOr(status, kDevErrBadIndex);
     return -1;
   }
@@ -252,6 +254,44 @@ __global__ void __launch_bounds__(512) counts_to_offsets_kernel(const int32_t* _
   if (i == 0) offsets[0] = 0;
 }
 
+// Expert-parallel dispatch, step 1: dest[t][d] = d if one of token t's
+// experts lives on rank d (experts [d*El, (d+1)*El)), else -1.  The
+// permutation kernels then group the (token, rank) pairs by rank, tokens
+// ascending.
+__global__ void ep_dest_kernel(const int32_t* __restrict__ idx, int T, int K, int P, int El,
+                               int32_t* __restrict__ dest) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(T) * P) return;
+  const long long t = i / P;
+  const int d = static_cast<int>(i % P);
+  int hit = 0;
+  for (int k = 0; k < K; ++k) {
+    const int e = idx[t * K + k];
+    hit |= (e >= d * El && e < (d + 1) * El);
+  }
+  dest[i] = hit ? d : -1;
+}
+
+// Step 2: for send row r = (token t, rank d) the K slots as rank d sees them:
+// local expert id (or -1 when slot k's expert lives elsewhere) and weight.
+__global__ void ep_slots_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w,
+                                const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
+                                const int32_t* __restrict__ rank_offsets, int P, int K, int El,
+                                int32_t* __restrict__ slots, float* __restrict__ wts) {
+  const long long rows = rank_offsets[P];
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * K;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / K;
+    const int k = static_cast<int>(i % K);
+    const long long t = row_token[r];
+    const int d = row_slot[r] % P;
+    const int e = idx[t * K + k];
+    const bool local = e >= d * El && e < (d + 1) * El;
+    slots[i] = local ? e - d * El : -1;
+    wts[i] = local ? w[t * K + k] : 0.f;
+  }
+}
+
 unsigned grid_for(long long work, int threads) {
   const long long b = (work + threads - 1) / threads;
   const long long cap = static_cast<long long>(device_sm_count()) * 16;
@@ -326,6 +366,22 @@ cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, in
 cudaError_t counts_to_offsets_launch(const int32_t* counts, int32_t* offsets, int n, cudaStream_t s) {
   if (n <= 0 || n > 512) return cudaErrorInvalidValue;
   counts_to_offsets_kernel<<<1, 512, 0, s>>>(counts, offsets, n);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_dest_launch(const int32_t* idx, int T, int K, int P, int El, int32_t* dest, cudaStream_t s) {
+  const long long n = static_cast<long long>(T) * P;
+  if (n == 0) return cudaSuccess;
+  ep_dest_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(idx, T, K, P, El, dest);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_slots_launch(const int32_t* idx, const float* w, const int32_t* row_token, const int32_t* row_slot,
+                            const int32_t* rank_offsets, long long max_rows, int P, int K, int El, int32_t* slots,
+                            float* wts, cudaStream_t s) {
+  if (max_rows == 0) return cudaSuccess;
+  ep_slots_kernel<<<grid_for(max_rows * K, 256), 256, 0, s>>>(idx, w, row_token, row_slot, rank_offsets, P, K, El,
+                                                              slots, wts);
   return cudaGetLastError();
 }
 

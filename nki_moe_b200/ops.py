@@ -22,7 +22,7 @@ __all__ = [
     "rmsnorm", "add_rmsnorm", "qk_norm_rope", "router_logits", "topk_softmax", "permute",
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
-    "route", "dispatch", "segment_experts", "combine",
+    "route", "dispatch", "segment_experts", "combine", "ep_dispatch",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -430,3 +430,31 @@ def combine(y: torch.Tensor, slot_row: torch.Tensor, tokens: int, top_k: int,
     out = torch.empty(tokens, H, dtype=torch.bfloat16, device=y.device)
     call("nkimoe_combine", _p(y), _p(sr), _p(sw), _p(out), tokens, top_k, H, _s(y))
     return out
+
+
+def ep_dispatch(x: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor, num_ranks: int, experts_per_rank: int):
+    """De-duplicated expert-parallel dispatch: one send row per (token, rank).
+
+    Returns ``(x_send [R, H], slots [R, K] int32, wts [R, K] fp32, rank_counts [P]
+    int32, slot_row [T, P] int32)``; the buffers hold ``T*min(P, K)`` rows, of
+    which ``rank_counts.sum()`` are valid.
+    """
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    idx = _contig(_cuda(idx, "idx"), torch.int32)
+    w = _contig(_cuda(weights, "weights"), torch.float32)
+    T, H = x.shape
+    K = idx.shape[1]
+    P = num_ranks
+    dev = x.device
+    cap = T * min(P, K)
+    x_send = torch.empty(cap, H, dtype=torch.bfloat16, device=dev)
+    slots = torch.empty(cap, K, dtype=torch.int32, device=dev)
+    wts = torch.empty(cap, K, dtype=torch.float32, device=dev)
+    counts = torch.empty(P, dtype=torch.int32, device=dev)
+    slot_row = torch.empty(T, P, dtype=torch.int32, device=dev)
+    ws = workspace(dev, size_call("nkimoe_ep_dispatch_workspace_bytes", T, P))
+    call("nkimoe_ep_dispatch", _p(x), _p(idx), _p(w), T, H, K, P, experts_per_rank, _p(x_send), _p(slots), _p(wts),
+         _p(counts), _p(slot_row), _p(ws), ws.numel(), _s(x))
+    if sync_check_enabled():
+        read_status(ws)
+    return x_send, slots, wts, counts, slot_row

@@ -111,25 +111,29 @@ def permute(idx, num_experts: int):
     rows are in (k, t) lexicographic order (the same order HF's
     ``torch.where(expert_mask[e])`` gives).
 
+    A negative id marks an empty slot (no row; used for the per-rank slot
+    lists of the expert-parallel dispatch); an id >= E is an error.
+
     Returns ``(row_token, row_slot, offsets, slot_row)``:
       row_token[r] = t of permuted row r; row_slot[r] = t*K + k;
       offsets[E+1] = exclusive prefix of per-expert counts;
-      slot_row[t*K + k] = r (inverse permutation).
+      slot_row[t*K + k] = r (inverse permutation; -1 for an empty slot).
     """
     idx = np.asarray(idx)
     T, K = idx.shape
     flat = idx.T.reshape(-1).astype(np.int64)  # j = k*T + t
-    if flat.size and (flat.min() < 0 or flat.max() >= num_experts):
+    if flat.size and flat.max() >= num_experts:
         raise ValueError("expert index out of range")
-    order = np.argsort(flat, kind="stable")
+    valid = np.nonzero(flat >= 0)[0]
+    order = valid[np.argsort(flat[valid], kind="stable")]
     row_k = order // max(T, 1)
     row_t = order % max(T, 1)
-    counts = np.bincount(flat, minlength=num_experts)
+    counts = np.bincount(flat[valid], minlength=num_experts)
     offsets = np.zeros(num_experts + 1, dtype=np.int32)
     offsets[1:] = np.cumsum(counts)
     row_slot = (row_t * K + row_k).astype(np.int32)
-    slot_row = np.empty(T * K, dtype=np.int32)
-    slot_row[row_slot] = np.arange(T * K, dtype=np.int32)
+    slot_row = np.full(T * K, -1, dtype=np.int32)
+    slot_row[row_slot] = np.arange(row_slot.size, dtype=np.int32)
     return row_t.astype(np.int32), row_slot, offsets, slot_row
 
 
@@ -171,7 +175,7 @@ def experts_forward(x, gate_up, down, idx, wt) -> np.ndarray:
     K = idx.shape[1]
     E = gate_up.shape[0]
     row_t, row_slot, offsets, slot_row = permute(idx, E)
-    y = np.zeros((T * K, H), dtype=np.float32)
+    y = np.zeros((max(row_t.size, 1), H), dtype=np.float32)
     for e in range(E):
         s, f = int(offsets[e]), int(offsets[e + 1])
         if f > s:
@@ -179,7 +183,8 @@ def experts_forward(x, gate_up, down, idx, wt) -> np.ndarray:
     out = np.zeros((T, H), dtype=np.float32)
     rows = slot_row.reshape(T, K)
     for k in range(K):
-        out += wt[:, k:k + 1] * y[rows[:, k]]
+        ok = rows[:, k] >= 0  # empty slots contribute nothing
+        out[ok] += wt[ok, k:k + 1] * y[rows[ok, k]]
     return out
 
 

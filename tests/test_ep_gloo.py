@@ -47,11 +47,38 @@ class OracleKernels:
             o += c
         return out
 
+    def ep_dispatch(self, x, idx, w, num_ranks, el):
+        T, K = idx.shape
+        dest = np.full((T, num_ranks), -1, np.int32)
+        for t in range(T):
+            for e in idx[t].tolist():
+                dest[t, e // el] = e // el
+        row_t, row_slot, offsets, slot_row = oracle.permute(dest, num_ranks)
+        d_of = row_slot % num_ranks
+        ids = idx.numpy()[row_t]
+        local = (ids // el) == d_of[:, None]
+        slots = np.where(local, ids - d_of[:, None] * el, -1).astype(np.int32)
+        wts = np.where(local, w.numpy()[row_t], 0.0).astype(np.float32)
+        return (x[torch.from_numpy(row_t).long()], torch.from_numpy(slots), torch.from_numpy(wts),
+                torch.from_numpy(np.diff(offsets).astype(np.int32)), torch.from_numpy(slot_row.reshape(T, num_ranks)))
+
+    def routed_experts(self, recv_x, recv_slots, recv_w, module):
+        out = torch.zeros_like(recv_x)
+        for r in range(recv_x.shape[0]):
+            for k in range(recv_slots.shape[1]):
+                e = int(recv_slots[r, k])
+                if e >= 0:
+                    y = oracle.expert_ffn(recv_x[r:r + 1].numpy(), module.gate_up_local[e].numpy(),
+                                          module.down_local[e].numpy())[0]
+                    out[r] += float(recv_w[r, k]) * torch.from_numpy(y)
+        return out
+
     def combine(self, y, slot_row, tokens, top_k):
         rows = slot_row.reshape(tokens, top_k).long()
         out = torch.zeros(tokens, y.shape[1])
         for k in range(top_k):
-            out += y[rows[:, k]]
+            ok = rows[:, k] >= 0
+            out[ok] += y[rows[ok, k]]
         return out
 
 
@@ -66,7 +93,7 @@ def weights(skew):
     return router, gate_up, down, bias
 
 
-def worker(rank, world, port, skew, result_dir, fail_rank):
+def worker(rank, world, port, skew, result_dir, fail_rank, dedup=True):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
@@ -74,7 +101,7 @@ def worker(rank, world, port, skew, result_dir, fail_rank):
     x = torch.randn(T, H, generator=torch.Generator().manual_seed(100 + rank))
     el = E // world
     ep = ExpertParallelMoE(router, gate_up[rank * el:(rank + 1) * el], down[rank * el:(rank + 1) * el], E, K,
-                           router_bias=bias, kernels=OracleKernels())
+                           router_bias=bias, kernels=OracleKernels(), dedup=dedup)
     if rank == fail_rank:
         os._exit(3)  # this rank dies before the exchange
     try:
@@ -98,10 +125,11 @@ def free_port():
     return p
 
 
+@pytest.mark.parametrize("dedup", [True, False])
 @pytest.mark.parametrize("skew", [False, True])
-def test_ep_matches_single_process_oracle(tmp_path, skew):
+def test_ep_matches_single_process_oracle(tmp_path, skew, dedup):
     world = 2
-    mp.start_processes(worker, args=(world, free_port(), skew, str(tmp_path), -1), nprocs=world, join=True,
+    mp.start_processes(worker, args=(world, free_port(), skew, str(tmp_path), -1, dedup), nprocs=world, join=True,
                        start_method="spawn")
     router, gate_up, down, bias = weights(skew)
     for r in range(world):

@@ -151,3 +151,6 @@ def test_permute_edge_cases():
     assert off[4] - off[3] == 5
     with pytest.raises(ValueError):
         oracle.permute(np.full((2, 2), 16, np.int32), 16)
+    # negative ids are empty slots: no rows, slot_row -1
+    rt, rs, off, sr = oracle.permute(np.array([[2, -1], [-1, 0]], np.int32), 4)
+    assert off[-1] == 2 and list(sr) == [1, -1, -1, 0]
