@@ -57,8 +57,11 @@ NKIMOE_API const char* nkimoe_last_error(void);
 /* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows on one SM,
  * 2 weights, 3 rows on an SM pair),
  * "weights_rows" (16, 32 or 64 rows per decode tile), "router" (0 auto,
- * 1 CUDA-core fp32, 2 tensor-core split-fp32), "prefetch" (L2 prefetch
- * distance of the prefill GEMMs in 64-wide K blocks, 0 = off = default).
+ * 1 CUDA-core fp32, 2 tensor-core split-fp32), "prefetch" (64-wide K blocks
+ * of a prefill GEMM CTA's next tile pulled into L2 when it starts a tile;
+ * 0 = off),
+ * "gather_fused" (1: GEMM-1 gathers its token rows with cp.async in its
+ * producer warp instead of a separate gather kernel; 0 = default).
  * No reference counterpart (NKI tile sizes are compile-time constants,
  * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */

@@ -61,6 +61,7 @@ inline void mark(int stage, cudaStream_t s) {
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
+std::atomic<int> g_gather_fused{0};  // 1: GEMM-1 gathers its rows itself (cp.async in the producer warp)
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -129,12 +130,15 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
              const int32_t* offsets, int epilogue, void* out, long long out_ld, const float* slot_w,
              const int32_t* row_slot, const int32_t* out_row_map, const float* col_bias, int* status,
              cudaStream_t s, long long kd_act = 0, bool shared_a = false, const float* row_weight = nullptr,
-             long long weight_experts = 0, int weight_mod = 0) {
+             long long weight_experts = 0, int weight_mod = 0, const int32_t* a_row_map = nullptr,
+             long long problem_rows = 0) {
   if (act_rows == 0) return NKIMOE_OK;
   if (kd_act == 0) kd_act = kd;
-  // with shared activation rows every expert has act_rows rows
-  const long long rows_total = shared_a ? act_rows * E : act_rows;
-  const int variant = choose_variant(rows_total, E, N);
+  // with shared activation rows every expert has act_rows rows; with gathered
+  // rows the problem has problem_rows rows taken from the act_rows of `act`
+  const long long rows_total = a_row_map ? problem_rows : (shared_a ? act_rows * E : act_rows);
+  int variant = choose_variant(rows_total, E, N);
+  if (a_row_map && variant == kRows2BN256) variant = kRowsBN256;  // the pair kernel loads A by TMA only
   CUtensorMap ta, tw;
   NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the activation operand");
@@ -150,6 +154,9 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.k_blocks_a = static_cast<int>(kd_act / 64);
   p.shared_a = shared_a ? 1 : 0;
   p.weight_mod = weight_mod;
+  p.a_row_map = a_row_map;
+  p.a_ptr = static_cast<const __nv_bfloat16*>(act);
+  p.a_ld = kd_act;
   p.row_weight = row_weight;
   p.prefetch = g_prefetch.load();
   p.epilogue = epilogue;
@@ -230,11 +237,20 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
   mark(kStagePermute, s);
   NKI_CUDA(permute_launch(idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
                           row_slot, slot_row, offsets, base + L.scratch, status, s, topk_w, row_weight));
-  mark(kStageGather, s);
-  NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(E), xy, TK,
-                              static_cast<int>(H), s));
-  mark(kStageGemm1, s);
-  int rc = run_gemm(xy, TK, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s);
+  int rc;
+  if (g_gather_fused.load()) {
+    // GEMM-1 gathers its activation rows (x[row_token[r]]) in its producer warp
+    mark(kStageGather, s);
+    mark(kStageGemm1, s);
+    rc = run_gemm(x, T, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s, 0,
+                  false, nullptr, 0, 0, row_token, TK);
+  } else {
+    mark(kStageGather, s);
+    NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(E), xy, TK,
+                                static_cast<int>(H), s));
+    mark(kStageGemm1, s);
+    rc = run_gemm(xy, TK, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s);
+  }
   if (rc != NKIMOE_OK) return rc;
   mark(kStageGemm2, s);
   rc = run_gemm(h, TK, w2, E, H, I, offsets, kEpiScaleBf16, xy, H, topk_w, row_slot, nullptr, nullptr, status, s, 0,
@@ -304,6 +320,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "weights_rows" && (value == 0 || value == 16 || value == 32 || value == 64)) {
     g_weights_rows = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "gather_fused" && (value == 0 || value == 1)) {
+    g_gather_fused = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "prefetch" && value >= 0 && value <= 16) {

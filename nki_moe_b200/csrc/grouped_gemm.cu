@@ -222,6 +222,27 @@ __device__ __forceinline__ void rows_epilogue(const GroupedGemmParams& p, uint32
   }
 }
 
+// Producer-warp gather of one 64-element K block of NR activation rows into a
+// stage laid out exactly as a 128-byte-swizzled TMA box (16-byte chunk c of
+// row i at chunk c ^ (i % 8) of the row's 128 bytes).  src_row[j] is the
+// source row of tile row lane + 32 j (-1: zero fill).
+template <int NR>
+__device__ __forceinline__ void gather_k_block(uint32_t sdst, const __nv_bfloat16* a, long long ld, int kcol,
+                                               const int (&src_row)[(NR + 31) / 32], int lane) {
+#pragma unroll
+  for (int j = 0; j < (NR + 31) / 32; ++j) {
+    const int i = lane + 32 * j;
+    if (NR % 32 == 0 || i < NR) {
+      const int sr = src_row[j];
+      const __nv_bfloat16* src = a + (sr >= 0 ? static_cast<long long>(sr) * ld : 0) + kcol;
+      const uint32_t nbytes = sr >= 0 ? 16u : 0u;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        cp_async_16(sdst + i * 128 + ((c ^ (i & 7)) << 4), src + c * 8, nbytes);
+    }
+  }
+}
+
 // ============================================================ rows schedule
 // Tile: 128 activation rows x BN packed features.  A = activations (box 64 x
 // 128), B = weights (box 64 x BN), D[row][feature] in TMEM lanes x columns.
@@ -245,9 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int E = p.num_experts;
   const int feat_tiles = p.n / BN;
 
+  const bool gather_a = p.a_row_map != nullptr;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.full[s], gather_a ? 1 + 32 : 1);  // + one cp.async arrival per producer lane
       mbar_init(&ctl.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -272,101 +294,126 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, last_phase_mask = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-      const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
-      const int row0 = ctl.seg[tc.e] + tc.rblk * BM;
-      const int arow0 = p.shared_a ? tc.rblk * BM : row0;
-      const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN;
-      int ka = 0;  // activation K coordinate (wraps at k_blocks_a blocks)
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
-          tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], ka, arow0);
-          tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0);
-          // L2 prefetch p.prefetch k-blocks ahead (into the next tile at the end
-          // of this one), so the TMA loads above find their data in L2
-          if (p.prefetch) {
-            int pk = kb + p.prefetch, pa = arow0, pw = wrow0;
-            if (pk >= p.k_blocks && tile + static_cast<int>(gridDim.x) < total_tiles) {
-              const TileCoord nc = decode_tile(ctl, E, tile + gridDim.x, BM, feat_tiles);
-              pk -= p.k_blocks;
-              pw = (p.weight_mod ? nc.e % p.weight_mod : nc.e) * p.n + nc.fblk * BN;
-              pa = p.shared_a ? nc.rblk * BM : ctl.seg[nc.e] + nc.rblk * BM;
-            }
-            if (pk < p.k_blocks) {
-              tma_prefetch_2d(&tmap_act, (pk % p.k_blocks_a) * BK, pa);
-              tma_prefetch_2d(&tmap_w, pk * BK, pw);
-            }
+    // TMA mode: lane 0 alone runs the loop (no per-stage warp collectives);
+    // gather mode: the whole warp issues the cp.async row gathers.
+    if (gather_a || lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase_mask = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+        const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
+        const int row0 = ctl.seg[tc.e] + tc.rblk * BM;
+        const int arow0 = p.shared_a ? tc.rblk * BM : row0;
+        const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN;
+        int src_row[BM / 32];
+        if (gather_a) {
+          const int seg_end = ctl.seg[tc.e + 1];
+#pragma unroll
+          for (int j = 0; j < BM / 32; ++j) {
+            const int r = row0 + lane + 32 * j;
+            src_row[j] = r < seg_end ? p.a_row_map[r] : -1;
           }
         }
-        ka += BK;
-        if (ka == p.k_blocks_a * BK) ka = 0;
-        issued_mask |= 1u << stage;
-        last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+        int ka = 0;  // activation K coordinate (wraps at k_blocks_a blocks)
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (gather_a) {
+            if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&ctl.full[stage], B_BYTES);
+              tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0);
+            }
+            gather_k_block<BM>(smem_u32(sa + stage * A_BYTES), p.a_ptr, p.a_ld, ka, src_row, lane);
+            cp_async_mbar_arrive(&ctl.full[stage]);
+          } else {
+            if (!mbar_wait(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
+            tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], ka, arow0);
+            tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0);
+            // At the start of a tile, pull the first p.prefetch K blocks of this
+            // CTA's next tile into L2: its weight panel then comes from L2, not
+            // DRAM, when the ring reaches it (hides the tile-boundary latency).
+            if (kb == 0 && p.prefetch && tile + static_cast<int>(gridDim.x) < total_tiles) {
+              const TileCoord nc = decode_tile(ctl, E, tile + gridDim.x, BM, feat_tiles);
+              const int pw = (p.weight_mod ? nc.e % p.weight_mod : nc.e) * p.n + nc.fblk * BN;
+              const int pa = p.shared_a ? nc.rblk * BM : ctl.seg[nc.e] + nc.rblk * BM;
+              const int npf = min(p.prefetch, p.k_blocks);
+              for (int pk = 0; pk < npf; ++pk) {
+                tma_prefetch_2d(&tmap_act, (pk % p.k_blocks_a) * BK, pa);
+                tma_prefetch_2d(&tmap_w, pk * BK, pw);
+              }
+            }
+          }
+          ka += BK;
+          if (ka == p.k_blocks_a * BK) ka = 0;
+          issued_mask |= 1u << stage;
+          last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
+      if (!ok && lane == 0) {  // let copies in flight land before the CTA exits
+        for (int s = 0; s < STAGES; ++s)
+          if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+      }
     }
-    if (!ok && lane == 0) {  // let copies in flight land before the CTA exits
-      for (int s = 0; s < STAGES; ++s)
-        if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
-    }
+    __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true, issued = false;
-    int t_local = 0;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
-      const int acc = t_local & 1;
-      const uint32_t acc_phase = (t_local >> 1) & 1;
-      if (!warp_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, ctl, p.status)) {
-        ok = false;
-        break;
-      }
-      tcgen05_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!warp_wait(&ctl.full[stage], phase, ctl, p.status)) {
+    // One thread issues every MMA and commit; its loop has no warp
+    // collectives.  The mbarrier wait orders the TMA-written stage before the
+    // MMAs that read it; tcgen05 fences are needed only at the TMEM hand-offs.
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued = false;
+      int t_local = 0;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t acc_phase = (t_local >> 1) & 1;
+        if (!mbar_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status)) {
           ok = false;
           break;
         }
         tcgen05_fence_after();
-        if (lane == 0) {
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&ctl.full[stage], phase, &ctl.abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          if (gather_a) fence_proxy_async_shared();  // cp.async-written A -> tensor-core reads
           // K step of 16 bf16 = 32 bytes = 2 in the descriptor's address field
           const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
           const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / UK; ++k)
-            umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / UK; ++kk)
+            umma_bf16(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
           umma_commit(&ctl.empty[stage]);
           issued = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        umma_commit(&ctl.acc_full[acc]);
       }
-      if (!ok) break;
-      if (lane == 0) umma_commit(&ctl.acc_full[acc]);
-      __syncwarp();
+      if (!ok && issued) {  // wait for issued MMAs before TMEM is released
+        umma_commit(&ctl.drain);
+        drain_wait(&ctl.drain, 0);
+      }
     }
-    if (!ok && lane == 0 && issued) {  // wait for issued MMAs before TMEM is released
-      umma_commit(&ctl.drain);
-      drain_wait(&ctl.drain, 0);
-    }
+    __syncwarp();
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
@@ -631,9 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int E = p.num_experts;
   const int feat_tiles = p.n / BM;
 
+  const bool gather_a = p.a_row_map != nullptr;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.full[s], gather_a ? 1 + 32 : 1);  // + one cp.async arrival per producer lane
       mbar_init(&ctl.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -657,83 +705,108 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total_tiles = ctl.tile_start[E];
 
   if (warp == 0) {
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, last_phase_mask = 0;
-    bool ok = true;
-    const uint64_t pol_w = policy_evict_first();
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
-      const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
-      const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
-      const int arow0 = p.shared_a ? tc.rblk * BT : row0;
-      const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BM;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
-          ok = false;
-          break;
+    // TMA mode: lane 0 alone runs the loop; gather mode: the whole warp
+    if (gather_a || lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase_mask = 0;
+      bool ok = true;
+      const uint64_t pol_w = policy_evict_first();
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+        const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
+        const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
+        const int arow0 = p.shared_a ? tc.rblk * BT : row0;
+        const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BM;
+        int src_row[(BT + 31) / 32];
+        if (gather_a) {
+          const int seg_end = ctl.seg[tc.e + 1];
+#pragma unroll
+          for (int j = 0; j < (BT + 31) / 32; ++j) {
+            const int r = row0 + lane + 32 * j;
+            src_row[j] = (lane + 32 * j < BT && r < seg_end) ? p.a_row_map[r] : -1;
+          }
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
-          tma_load_2d_hint(sa + stage * A_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0, pol_w);
-          tma_load_2d(sb + stage * B_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, arow0);  // small K
-        }
-        issued_mask |= 1u << stage;
-        last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+        int ka = 0;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (gather_a) {
+            if (!warp_wait(&ctl.empty[stage], phase ^ 1u, ctl, p.status)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&ctl.full[stage], A_BYTES);
+              tma_load_2d_hint(sa + stage * A_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0, pol_w);
+            }
+            gather_k_block<BT>(smem_u32(sb + stage * B_BYTES), p.a_ptr, p.a_ld, ka, src_row, lane);
+            cp_async_mbar_arrive(&ctl.full[stage]);
+          } else {
+            if (!mbar_wait(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
+            tma_load_2d_hint(sa + stage * A_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0, pol_w);
+            tma_load_2d(sb + stage * B_BYTES, &tmap_act, &ctl.full[stage], ka, arow0);
+          }
+          ka += BK;
+          if (ka == p.k_blocks_a * BK) ka = 0;
+          issued_mask |= 1u << stage;
+          last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
+      if (!ok && lane == 0) {
+        for (int s = 0; s < STAGES; ++s)
+          if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+      }
     }
-    if (!ok && lane == 0) {
-      for (int s = 0; s < STAGES; ++s)
-        if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
-    }
+    __syncwarp();
   } else if (warp == 1) {
-    constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BT);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true, issued = false;
-    int t_local = 0;
-    for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
-      const int acc = t_local & 1;
-      const uint32_t acc_phase = (t_local >> 1) & 1;
-      if (!warp_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, ctl, p.status)) {
-        ok = false;
-        break;
-      }
-      tcgen05_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * BT;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!warp_wait(&ctl.full[stage], phase, ctl, p.status)) {
+    if (lane == 0) {  // one thread issues every MMA and commit
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(BM, BT);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued = false;
+      int t_local = 0;
+      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t acc_phase = (t_local >> 1) & 1;
+        if (!mbar_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status)) {
           ok = false;
           break;
         }
         tcgen05_fence_after();
-        if (lane == 0) {
-          // K step of 16 bf16 = 32 bytes = 2 in the descriptor's address field
+        const uint32_t d_tmem = tmem_base + acc * BT;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&ctl.full[stage], phase, &ctl.abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          if (gather_a) fence_proxy_async_shared();  // cp.async-written B -> tensor-core reads
           const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
           const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
 #pragma unroll
-          for (int k = 0; k < BK / UK; ++k)
-            umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int kq = 0; kq < BK / UK; ++kq)
+            umma_bf16(d_tmem, da + 2 * kq, db + 2 * kq, idesc, (kb | kq) != 0 ? 1u : 0u);
           umma_commit(&ctl.empty[stage]);
           issued = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        umma_commit(&ctl.acc_full[acc]);
       }
-      if (!ok) break;
-      if (lane == 0) umma_commit(&ctl.acc_full[acc]);
-      __syncwarp();
+      if (!ok && issued) {
+        umma_commit(&ctl.drain);
+        drain_wait(&ctl.drain, 0);
+      }
     }
-    if (!ok && lane == 0 && issued) {
-      umma_commit(&ctl.drain);
-      drain_wait(&ctl.drain, 0);
-    }
+    __syncwarp();
   } else {
     const int quarter = warp & 3;
     const int feat = quarter * 32 + lane;  // TMEM lane = feature row of the tile

@@ -120,7 +120,13 @@ struct GroupedGemmParams {
   const float* slot_weight;   // kEpiScaleBf16: weight of row r = slot_weight[row_slot[r]] ...
   const int32_t* row_slot;
   const float* row_weight;    // ... or row_weight[r] when given (permuted order, one coalesced load)
-  int prefetch;               // k-blocks of operands prefetched into L2 ahead of the TMA loads (0: off)
+  int prefetch;               // K blocks of the next tile prefetched into L2 at each tile start (0: off)
+  // Gathered activations: when a_row_map is set, activation row r of the
+  // grouped problem is row a_row_map[r] of a_ptr (row stride a_ld elements),
+  // loaded with cp.async by the producer warp instead of a TMA tile load.
+  const int32_t* a_row_map;
+  const __nv_bfloat16* a_ptr;
+  long long a_ld;
   const int32_t* out_row_map; // optional: output row of permuted row r
   const float* col_bias;      // kEpiStoreF32 optional
   int* status;

@@ -362,6 +362,21 @@ def test_moe_block_odd_token_counts():
     assert_block_close(out, ref)
 
 
+@pytest.mark.parametrize("schedule", [1, 2])
+def test_moe_block_gather_fused(c1_inputs, schedule):
+    """GEMM-1 loading its gathered token rows itself (cp.async) instead of the
+    separate gather kernel gives the same result."""
+    _lib.set_option("gemm_schedule", schedule)
+    try:
+        ref = _block_case(c1_inputs)[0]
+        _lib.set_option("gather_fused", 1)
+        out = _block_case(c1_inputs)[0]
+        assert np.array_equal(out, ref)
+    finally:
+        _lib.set_option("gather_fused", 0)
+        _lib.set_option("gemm_schedule", 0)
+
+
 def test_moe_block_deterministic(c1_inputs):
     a = _block_case(c1_inputs)[0]
     b = _block_case(c1_inputs)[0]
