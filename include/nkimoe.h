@@ -55,13 +55,14 @@ extern "C" {
 NKIMOE_API int nkimoe_version(void);
 NKIMOE_API const char* nkimoe_last_error(void);
 /* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows on one SM,
- * 2 weights, 3 rows on an SM pair),
+ * 2 weights, 3 rows on an SM pair, 4 features x rows on an SM pair),
  * "weights_rows" (16, 32 or 64 rows per decode tile), "router" (0 auto,
  * 1 CUDA-core fp32, 2 tensor-core split-fp32), "prefetch" (64-wide K blocks
  * of a prefill GEMM CTA's next tile pulled into L2 when it starts a tile;
  * 0 = off),
- * "gather_fused" (1: GEMM-1 gathers its token rows with cp.async in its
- * producer warp instead of a separate gather kernel; 0 = default).
+ * "gather_fused" (GEMM-1 loads its token rows itself instead of a separate
+ * gather kernel writing them out: 1 with cp.async in its producer warp,
+ * 2 with TMA tile::gather4; 0 = separate gather kernel).
  * No reference counterpart (NKI tile sizes are compile-time constants,
  * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */
@@ -250,7 +251,8 @@ NKIMOE_API int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const 
 
 /* out[t] = sum_k (slot_weight ? slot_weight[t*K+k] : 1) * y[slot_row[t*K+k]]
  * in fp32, k ascending, bf16 out (nki_moe_integrated.py:482-494,
- * nki_moe_aggregate :209-251); slot_row < 0 is skipped. */
+ * nki_moe_aggregate :209-251); slot_row < 0 is skipped.  T * H / 8 and
+ * T * K below 2^31 (NKIMOE_ERR_UNSUPPORTED otherwise). */
 NKIMOE_API int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T,
                               int64_t K, int64_t H, void* stream);
 

@@ -61,7 +61,7 @@ inline void mark(int stage, cudaStream_t s) {
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
-std::atomic<int> g_gather_fused{0};  // 1: GEMM-1 gathers its rows itself (cp.async in the producer warp)
+std::atomic<int> g_gather_fused{0};  // GEMM-1 gathers its rows itself: 1 cp.async, 2 TMA gather4
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -119,6 +119,7 @@ int choose_variant(long long rows_total, long long E, long long N) {
   // 1-SM schedule on B200 for these shapes (TMA completions in the pair run at
   // about a third of the 1-SM rate)
   if (N % 256 == 0 && sched == 3) return kRows2BN256;
+  if (N % 256 == 0 && sched == 4) return kTokens2;
   return (N % 256 == 0) ? kRowsBN256 : kRowsBN128;
 }
 
@@ -138,9 +139,16 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   // rows the problem has problem_rows rows taken from the act_rows of `act`
   const long long rows_total = a_row_map ? problem_rows : (shared_a ? act_rows * E : act_rows);
   int variant = choose_variant(rows_total, E, N);
-  if (a_row_map && variant == kRows2BN256) variant = kRowsBN256;  // the pair kernel loads A by TMA only
+  // the SM-pair kernels load A by TMA tiles only; the tokens kernel has no fp32 epilogue
+  if ((variant == kRows2BN256 || variant == kTokens2) && (a_row_map || epilogue == kEpiStoreF32))
+    variant = kRowsBN256;
+  // the tokens kernel stores 16-byte vectors of an output row
+  if (variant == kTokens2 && (reinterpret_cast<uintptr_t>(out) % 16 != 0 || out_ld % 8 != 0)) variant = kRowsBN256;
+  // gathered rows by TMA gather4 read the activation map one row per box row
+  const bool gather4 = a_row_map && g_gather_fused.load() == 2;
   CUtensorMap ta, tw;
-  NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, grouped_gemm_box_rows_act(variant)), NKIMOE_ERR_CUDA,
+  NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, gather4 ? 1 : grouped_gemm_box_rows_act(variant)),
+              NKIMOE_ERR_CUDA,
               "cuTensorMapEncodeTiled failed for the activation operand");
   if (weight_experts == 0) weight_experts = E;
   NKI_REQUIRE(make_tmap_bf16(&tw, w, weight_experts * N, kd, grouped_gemm_box_rows_w(variant)), NKIMOE_ERR_CUDA,
@@ -157,6 +165,7 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.a_row_map = a_row_map;
   p.a_ptr = static_cast<const __nv_bfloat16*>(act);
   p.a_ld = kd_act;
+  p.tma_gather4 = gather4 ? 1 : 0;
   p.row_weight = row_weight;
   p.prefetch = g_prefetch.load();
   p.epilogue = epilogue;
@@ -167,7 +176,7 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.out_row_map = out_row_map;
   p.col_bias = col_bias;
   p.status = status;
-  const bool pair = variant == kRows2BN256;
+  const bool pair = variant == kRows2BN256 || variant == kTokens2;
   const bool rows = variant == kRowsBN256 || variant == kRowsBN128 || pair;
   const long long rpt = pair ? 256 : grouped_gemm_box_rows_act(variant);
   const long long fpt = pair ? 256 : (rows ? grouped_gemm_box_rows_w(variant) : 128);
@@ -314,7 +323,7 @@ const char* nkimoe_last_error(void) { return g_err.c_str(); }
 int nkimoe_set_option(const char* name, long long value) {
   if (!name) return fail(NKIMOE_ERR_INVALID_ARG, "null option name");
   const std::string n(name);
-  if (n == "gemm_schedule" && value >= 0 && value <= 3) {
+  if (n == "gemm_schedule" && value >= 0 && value <= 4) {
     g_schedule = static_cast<int>(value);
     return NKIMOE_OK;
   }
@@ -322,7 +331,7 @@ int nkimoe_set_option(const char* name, long long value) {
     g_weights_rows = static_cast<int>(value);
     return NKIMOE_OK;
   }
-  if (n == "gather_fused" && (value == 0 || value == 1)) {
+  if (n == "gather_fused" && value >= 0 && value <= 2) {
     g_gather_fused = static_cast<int>(value);
     return NKIMOE_OK;
   }
@@ -708,6 +717,7 @@ int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk
 int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T, int64_t K,
                    int64_t H, void* stream) {
   NKI_REQUIRE(T >= 0 && K > 0 && H > 0 && H % 8 == 0, NKIMOE_ERR_INVALID_ARG, "combine: bad shape");
+  NKI_REQUIRE(T * (H / 8) < (1LL << 31) && T * K < (1LL << 31), NKIMOE_ERR_UNSUPPORTED, "combine: T too large");
   if (T == 0) return NKIMOE_OK;
   NKI_REQUIRE(y && slot_row && out && aligned16(y) && aligned16(out), NKIMOE_ERR_INVALID_ARG,
               "null or misaligned pointer");

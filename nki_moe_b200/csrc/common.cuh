@@ -201,6 +201,35 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const void* tma
       : "memory");
 }
 
+// 2-D tiled load issued by either CTA of an SM pair (tcgen05 cta_group::2):
+// writes the issuing CTA's own shared memory and completes its bytes on
+// `bar_cluster`, a shared::cluster barrier address (mapa) that may belong to
+// the peer CTA, so one barrier in the pair's leader tracks both halves of a
+// stage.  Each CTA fetches only its own box.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Indexed-row load (sm_100 tile::gather4): four rows r0..r3 of a 2-D tensor
+// map whose box is one row high, columns [c0, c0 + box width), written to four
+// consecutive box rows at smem_dst with the map's swizzle (the swizzle follows
+// the shared-memory address, so a 512-byte-aligned destination inside a
+// 1024-byte swizzle atom lands each row where a tiled load would put it).
+// Completes 4 x box bytes on `bar`.
+__device__ __forceinline__ void tma_gather4_2d(void* smem_dst, const void* tmap, uint64_t* bar, int c0, int r0,
+                                               int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
+
 // L2 prefetch of one box of a tensor map (no shared-memory destination).
 __device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int c0, int c1) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(

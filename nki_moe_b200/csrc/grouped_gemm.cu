@@ -267,9 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int feat_tiles = p.n / BN;
 
   const bool gather_a = p.a_row_map != nullptr;
+  const bool gather_cp = gather_a && !p.tma_gather4;  // rows written by cp.async (generic proxy)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl.full[s], gather_a ? 1 + 32 : 1);  // + one cp.async arrival per producer lane
+      mbar_init(&ctl.full[s], gather_cp ? 1 + 32 : 1);  // + one cp.async arrival per producer lane
       mbar_init(&ctl.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -306,13 +307,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row0 = ctl.seg[tc.e] + tc.rblk * BM;
         const int arow0 = p.shared_a ? tc.rblk * BM : row0;
         const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN;
+        // cp.async gather: tile row lane + 32 j; TMA gather4: tile rows 4 lane + j
+        // (rows past the segment end re-read the tile's first row; their
+        // accumulator rows are never stored)
         int src_row[BM / 32];
         if (gather_a) {
           const int seg_end = ctl.seg[tc.e + 1];
+          const int first = p.a_row_map[row0];
 #pragma unroll
           for (int j = 0; j < BM / 32; ++j) {
-            const int r = row0 + lane + 32 * j;
-            src_row[j] = r < seg_end ? p.a_row_map[r] : -1;
+            const int r = gather_cp ? row0 + lane + 32 * j : row0 + 4 * lane + j;
+            src_row[j] = r < seg_end ? p.a_row_map[r] : (gather_cp ? -1 : first);
           }
         }
         int ka = 0;  // activation K coordinate (wraps at k_blocks_a blocks)
@@ -323,11 +328,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             if (lane == 0) {
-              mbar_arrive_expect_tx(&ctl.full[stage], B_BYTES);
+              mbar_arrive_expect_tx(&ctl.full[stage], gather_cp ? B_BYTES : STAGE_BYTES);
               tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0);
             }
-            gather_k_block<BM>(smem_u32(sa + stage * A_BYTES), p.a_ptr, p.a_ld, ka, src_row, lane);
-            cp_async_mbar_arrive(&ctl.full[stage]);
+            if (gather_cp) {
+              gather_k_block<BM>(smem_u32(sa + stage * A_BYTES), p.a_ptr, p.a_ld, ka, src_row, lane);
+              cp_async_mbar_arrive(&ctl.full[stage]);
+            } else {  // 32 lanes x 4 rows x 128 bytes = the 128-row A stage
+              __syncwarp();
+              tma_gather4_2d(sa + stage * A_BYTES + lane * 512, &tmap_act, &ctl.full[stage], ka, src_row[0],
+                             src_row[1], src_row[2], src_row[3]);
+            }
           } else {
             if (!mbar_wait(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status)) {
               ok = false;
@@ -391,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (gather_a) fence_proxy_async_shared();  // cp.async-written A -> tensor-core reads
+          if (gather_cp) fence_proxy_async_shared();  // cp.async-written A -> tensor-core reads
           // K step of 16 bf16 = 32 bytes = 2 in the descriptor's address field
           const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
           const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
@@ -451,13 +462,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Tile: 256 activation rows x BN features computed by a 2-CTA cluster with
 // tcgen05.mma.cta_group::2 (M = 256).  CTA r of the pair loads activation rows
 // [128 r, 128 r + 128) and weight rows [r BN/2, (r + 1) BN/2) of the tile into
-// its own shared memory (plain TMA loads), so each SM fetches half of the B
-// operand of a 256 x BN tile: 64 B per cycle per SM from L2 at full MMA rate
-// instead of 96 B for a 1-SM 128 x 256 tile.  The even CTA issues the MMAs;
-// the odd CTA relays "stage full" to it, the even CTA's commits release the
-// stages and publish the accumulators in both CTAs (multicast arrive), and the
-// odd CTA's epilogue warps arrive remotely on the even CTA's "accumulator
-// free" barrier.
+// its own shared memory, so each SM fetches half of the B operand of a
+// 256 x BN tile: 64 B per cycle per SM from L2 at full MMA rate instead of
+// 96 B for a 1-SM 128 x 256 tile.  Both CTAs' loads complete on the even
+// (leader) CTA's stage barrier (cta_group::2 form of the tiled load; each CTA
+// fetches only its own box), which the leader arms with both halves' bytes;
+// the leader issues the MMAs, its tcgen05.commit arrives on the stage and
+// accumulator barriers of both CTAs, and the odd CTA's epilogue warps arrive
+// remotely on the leader's "accumulator free" barrier.
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_rows2_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
@@ -471,7 +483,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedCtl ctl;
-  __shared__ uint64_t peer_full[STAGES];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * A_BYTES;
@@ -484,9 +495,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.full[s], 1);   // used in the leader only
       mbar_init(&ctl.empty[s], 1);
-      mbar_init(&peer_full[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&ctl.acc_full[a], 1);
@@ -509,70 +519,76 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total_tiles = ctl.tile_start[E];
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- producer (both CTAs)
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, last_phase_mask = 0;
-    bool ok = true;
-    for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
-      const TileCoord tc = decode_tile(ctl, E, tile, BM2, feat_tiles);
-      const int row0 = ctl.seg[tc.e] + tc.rblk * BM2;
-      const int arow = (p.shared_a ? tc.rblk * BM2 : row0) + static_cast<int>(rank) * BM;
-      const int wrow = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN + static_cast<int>(rank) * (BN / 2);
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        bool w = true;
-        if (lane == 0) w = mbar_wait_cluster(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status);
-        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
-          ok = false;
-          break;
+    // ---------------------------------------------------------------- producer (both CTAs, one thread)
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(smem_u32(&ctl.full[0]), 0);  // the leader's stage barriers
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase_mask = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
+        const TileCoord tc = decode_tile(ctl, E, tile, BM2, feat_tiles);
+        const int row0 = ctl.seg[tc.e] + tc.rblk * BM2;
+        const int arow = (p.shared_a ? tc.rblk * BM2 : row0) + static_cast<int>(rank) * BM;
+        const int wrow =
+            (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BN + static_cast<int>(rank) * (BN / 2);
+        int ka = 0;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          // the stage is free in this CTA once the leader's MMAs that read it completed
+          if (!mbar_wait_cluster(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&ctl.full[stage], 2 * STAGE_BYTES);
+          const uint32_t bar = full0 + stage * static_cast<uint32_t>(sizeof(uint64_t));
+          tma_load_2d_pair(sa + stage * A_BYTES, &tmap_act, bar, ka, arow);
+          tma_load_2d_pair(sb + stage * B_BYTES, &tmap_w, bar, kb * BK, wrow);
+          ka += BK;
+          if (ka == p.k_blocks_a * BK) ka = 0;
+          issued_mask |= 1u << stage;
+          last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&ctl.full[stage], STAGE_BYTES);
-          tma_load_2d(sa + stage * A_BYTES, &tmap_act, &ctl.full[stage], (kb % p.k_blocks_a) * BK, arow);
-          tma_load_2d(sb + stage * B_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow);
-        }
-        issued_mask |= 1u << stage;
-        last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+      }
+      if (!ok) {
+        // let copies in flight land before the CTA exits: the leader watches
+        // its stage barriers; the odd CTA cannot, and waits a fixed bounded time
+        if (rank == 0) {
+          for (int s = 0; s < STAGES; ++s)
+            if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+        } else if (issued_mask) {
+          const long long t0 = clock64();
+          while (clock64() - t0 < kWaitBudgetCycles / 64) {
+          }
         }
       }
     }
-    if (!ok && lane == 0) {
-      for (int s = 0; s < STAGES; ++s)
-        if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
-    }
-  } else if (warp == 1 && rank == 0) {
-    // ---------------------------------------------------------------- MMA issuer (even CTA)
-    constexpr uint32_t idesc = umma_idesc_bf16_f32(BM2, BN);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true, issued = false;
-    int t_local = 0;
-    for (int tile = pair; ok && tile < total_tiles; tile += npairs, ++t_local) {
-      const int acc = t_local & 1;
-      const uint32_t acc_phase = (t_local >> 1) & 1;
-      bool w = true;
-      if (lane == 0) w = mbar_wait_cluster(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status);
-      if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
-        ok = false;
-        break;
-      }
-      tcgen05_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        w = true;
-        if (lane == 0) {
-          w = mbar_wait_cluster(&ctl.full[stage], phase, &ctl.abort_flag, p.status) &&
-              mbar_wait_cluster(&peer_full[stage], phase, &ctl.abort_flag, p.status);
-        }
-        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader CTA, one thread)
+    if (rank == 0 && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(BM2, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued = false;
+      int t_local = 0;
+      for (int tile = pair; ok && tile < total_tiles; tile += npairs, ++t_local) {
+        const int acc = t_local & 1;
+        const uint32_t acc_phase = (t_local >> 1) & 1;
+        if (!mbar_wait_cluster(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status)) {
           ok = false;
           break;
         }
         tcgen05_fence_after();
-        if (lane == 0) {
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_cluster(&ctl.full[stage], phase, &ctl.abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
           const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
           const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
 #pragma unroll
@@ -580,43 +596,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_bf16_2sm(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit_2sm(&ctl.empty[stage], 0x3);
           issued = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        umma_commit_2sm(&ctl.acc_full[acc], 0x3);
       }
-      if (!ok) break;
-      if (lane == 0) umma_commit_2sm(&ctl.acc_full[acc], 0x3);
-      __syncwarp();
-    }
-    if (!ok && lane == 0 && issued) {
-      umma_commit_2sm(&ctl.drain, 0x1);
-      drain_wait(&ctl.drain, 0);
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- stage relay (odd CTA)
-    const uint32_t peer_full0 = mapa_shared(smem_u32(&peer_full[0]), 0);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        bool w = true;
-        if (lane == 0) w = mbar_wait_cluster(&ctl.full[stage], phase, &ctl.abort_flag, p.status);
-        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) mbar_arrive_remote(peer_full0 + stage * static_cast<uint32_t>(sizeof(uint64_t)));
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+      if (!ok && issued) {
+        umma_commit_2sm(&ctl.drain, 0x1);
+        drain_wait(&ctl.drain, 0);
       }
     }
+    __syncwarp();
   } else {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quarter = warp & 3;
@@ -639,6 +632,261 @@ __global__ void __launch_bounds__(kThreads, 1)
       tcgen05_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
       rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale);
+      tcgen05_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&ctl.acc_empty[acc]);
+        else mbar_arrive_remote(acc_empty0 + acc * static_cast<uint32_t>(sizeof(uint64_t)));
+      }
+    }
+  }
+
+  tcgen05_fence_before();
+  cluster_sync();  // both CTAs done with tensor memory and with each other's barriers
+  tcgen05_fence_after();
+  if (warp == 1) tmem_dealloc_2sm(tmem_base, TMEM_COLS);
+}
+
+// ============================================================ tokens schedule, SM pair
+// Swap-AB tile on a 2-CTA cluster (tcgen05.mma.cta_group::2): 256 packed
+// features are the MMA's M (weight rows, 128 per CTA) and up to 256 rows of
+// one expert's segment are its N (half of the tile's rows loaded by each CTA).
+// N is chosen per tile as the rows present rounded up to 16, so an expert's
+// last, partial row block costs only the MMA work of the rows it holds (a
+// 256-row M tile would pad it to 256).  Both CTAs' loads complete on the
+// leader's stage barrier; the leader issues the MMAs; each CTA's TMEM holds
+// D[its 128 features][N rows].  Epilogue: thread = feature, one 32-row chunk
+// of the accumulator at a time; for SwiGLU the gate warp (features f) and the
+// up warp (features f + 64) of the same 32 h columns swap half of each chunk
+// through shared memory, so both compute 16 rows; a warp's 32 lanes store 32
+// consecutive features (64 contiguous bytes) of one output row.
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_tokens2_kernel(const __grid_constant__ CUtensorMap tmap_act,
+                                const __grid_constant__ CUtensorMap tmap_w, const GroupedGemmParams p) {
+  constexpr int BF = 2 * BM;                         // packed features per pair tile (MMA M)
+  constexpr int BT = 256;                            // rows per tile at most (MMA N)
+  constexpr uint32_t A_BYTES = BM * BK * 2;          // this CTA's 128 weight rows
+  constexpr uint32_t B_BYTES = (BT / 2) * BK * 2;    // box of 128 activation rows (N/2 used)
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BT;
+  static_assert(STAGES <= 16, "stages");
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SharedCtl ctl;
+  __shared__ float xch[2][2][2][32][17];  // [buffer][warp pair][0 gate, 1 up][lane][16 rows + pad]
+  __shared__ __align__(16) __nv_bfloat16 stg[4][32][40];  // per epilogue warp: [row][32 features + pad]
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * A_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int E = p.num_experts;
+  const int feat_tiles = p.n / BF;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&ctl.full[s], 1);  // used in the leader only
+      mbar_init(&ctl.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&ctl.acc_full[a], 1);
+      mbar_init(&ctl.acc_empty[a], 2 * 4);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(&ctl.drain, 1);
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_act);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) tmem_alloc_2sm(&ctl.tmem_base, TMEM_COLS);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BT, feat_tiles);
+  tcgen05_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  tcgen05_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total_tiles = ctl.tile_start[E];
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (both CTAs, one thread)
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(smem_u32(&ctl.full[0]), 0);  // the leader's stage barriers
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase_mask = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
+        const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
+        const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
+        const int nt = min(BT, ctl.seg[tc.e + 1] - row0);
+        const int half = ((nt + 15) & ~15) >> 1;  // rows of the MMA's N supplied by each CTA
+        const int brow = (p.shared_a ? tc.rblk * BT : row0) + static_cast<int>(rank) * half;
+        const int wrow = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BF + static_cast<int>(rank) * BM;
+        int ka = 0;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_cluster(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&ctl.full[stage], 2 * STAGE_BYTES);
+          const uint32_t bar = full0 + stage * static_cast<uint32_t>(sizeof(uint64_t));
+          tma_load_2d_pair(sa + stage * A_BYTES, &tmap_w, bar, kb * BK, wrow);
+          tma_load_2d_pair(sb + stage * B_BYTES, &tmap_act, bar, ka, brow);
+          ka += BK;
+          if (ka == p.k_blocks_a * BK) ka = 0;
+          issued_mask |= 1u << stage;
+          last_phase_mask = (last_phase_mask & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        if (rank == 0) {
+          for (int s = 0; s < STAGES; ++s)
+            if ((issued_mask >> s) & 1u) drain_wait(&ctl.full[s], (last_phase_mask >> s) & 1u);
+        } else if (issued_mask) {
+          const long long t0 = clock64();
+          while (clock64() - t0 < kWaitBudgetCycles / 64) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader CTA, one thread)
+    if (rank == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued = false;
+      int t_local = 0;
+      for (int tile = pair; ok && tile < total_tiles; tile += npairs, ++t_local) {
+        const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
+        const int nt = min(BT, ctl.seg[tc.e + 1] - ctl.seg[tc.e] - tc.rblk * BT);
+        const uint32_t idesc = umma_idesc_bf16_f32(BF, (nt + 15) & ~15);
+        const int acc = t_local & 1;
+        const uint32_t acc_phase = (t_local >> 1) & 1;
+        if (!mbar_wait_cluster(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BT;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_cluster(&ctl.full[stage], phase, &ctl.abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
+          const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / UK; ++k)
+            umma_bf16_2sm(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_2sm(&ctl.empty[stage], 0x3);
+          issued = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_2sm(&ctl.acc_full[acc], 0x3);
+      }
+      if (!ok && issued) {
+        umma_commit_2sm(&ctl.drain, 0x1);
+        drain_wait(&ctl.drain, 0);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int quarter = warp & 3;       // TMEM lanes [32 quarter, 32 quarter + 32) = features
+    const int wpair = quarter & 1;      // SwiGLU: gate quarter q pairs with up quarter q + 2
+    const bool is_up = quarter >= 2;
+    const uint32_t acc_empty0 = mapa_shared(smem_u32(&ctl.acc_empty[0]), 0);
+    int t_local = 0;
+    for (int tile = pair; tile < total_tiles; tile += npairs, ++t_local) {
+      const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
+      const int acc = t_local & 1;
+      const uint32_t acc_phase = (t_local >> 1) & 1;
+      const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
+      const int nt = min(BT, ctl.seg[tc.e + 1] - row0);
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait_cluster(&ctl.acc_full[acc], acc_phase, &ctl.abort_flag, p.status);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      // the SwiGLU hand-off uses named barriers between warps: all four take
+      // the same path, so stopping is a vote over the 128 epilogue threads
+      if (named_bar_any(1, 128, !ok)) break;
+      tcgen05_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BT;
+      // Output rows leave through the warp's staging tile: thread = feature
+      // writes its column, then lane l stores 16 bytes (8 features) of row
+      // l / 4 + 8 i, so a store instruction covers 8 rows x 64 bytes.
+      __nv_bfloat16(*st)[40] = stg[quarter];
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+      if (p.epilogue == kEpiSwiGLU) {
+        const long long hcol0 = static_cast<long long>(tc.fblk) * (BF / 2) + rank * (BM / 2) + wpair * 32;
+        int buf = 0;
+        for (int c = 0; c < nt; c += 32, buf ^= 1) {
+          float v[32];
+          tmem_ld_cols<32>(taddr + c, v);
+          // the gate warp computes rows c..c+15, the up warp rows c+16..c+31
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xch[buf][wpair][is_up ? 1 : 0][lane][j] = is_up ? v[j] : v[16 + j];
+          named_bar_sync(2 + wpair, 64);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float g = is_up ? xch[buf][wpair][0][lane][j] : v[j];
+            const float u = is_up ? v[16 + j] : xch[buf][wpair][1][lane][j];
+            st[j][lane] = __float2bfloat16_rn(silu_f(g) * u);
+          }
+          __syncwarp();
+          const int c0 = c + (is_up ? 16 : 0);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int rr = (lane >> 2) + 8 * i;
+            if (c0 + rr < nt) {
+              const long long r = row0 + c0 + rr;
+              const long long orow = p.out_row_map ? p.out_row_map[r] : r;
+              *reinterpret_cast<uint4*>(out + orow * p.out_ld + hcol0 + (lane & 3) * 8) =
+                  *reinterpret_cast<const uint4*>(&st[rr][(lane & 3) * 8]);
+            }
+          }
+          __syncwarp();
+        }
+      } else {  // kEpiScaleBf16 / kEpiStoreBf16
+        const long long col0 = static_cast<long long>(tc.fblk) * BF + rank * BM + quarter * 32;
+        for (int c = 0; c < nt; c += 32) {
+          float v[32];
+          tmem_ld_cols<32>(taddr + c, v);
+          if (p.epilogue == kEpiScaleBf16) {
+            const int rl = row0 + c + lane;
+            const float wl =
+                (c + lane < nt) ? (p.row_weight ? p.row_weight[rl] : p.slot_weight[p.row_slot[rl]]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, wl, j);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) st[j][lane] = __float2bfloat16_rn(v[j]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = (lane >> 2) + 8 * i;
+            if (c + rr < nt) {
+              const long long r = row0 + c + rr;
+              const long long orow = p.out_row_map ? p.out_row_map[r] : r;
+              *reinterpret_cast<uint4*>(out + orow * p.out_ld + col0 + (lane & 3) * 8) =
+                  *reinterpret_cast<const uint4*>(&st[rr][(lane & 3) * 8]);
+            }
+          }
+          __syncwarp();
+        }
+      }
       tcgen05_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -679,9 +927,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int feat_tiles = p.n / BM;
 
   const bool gather_a = p.a_row_map != nullptr;
+  const bool gather_cp = gather_a && !p.tma_gather4;  // rows written by cp.async (generic proxy)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&ctl.full[s], gather_a ? 1 + 32 : 1);  // + one cp.async arrival per producer lane
+      mbar_init(&ctl.full[s], gather_cp ? 1 + 32 : 1);  // + one cp.async arrival per producer lane
       mbar_init(&ctl.empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -717,13 +966,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
         const int arow0 = p.shared_a ? tc.rblk * BT : row0;
         const int wrow0 = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BM;
+        // cp.async gather: tile row lane + 32 j; TMA gather4: lanes < BT / 4
+        // load tile rows 4 lane + j (rows past the segment end re-read the
+        // tile's first row; their accumulator columns are never stored)
         int src_row[(BT + 31) / 32];
-        if (gather_a) {
+        int g4[4];
+        if (gather_cp) {
           const int seg_end = ctl.seg[tc.e + 1];
 #pragma unroll
           for (int j = 0; j < (BT + 31) / 32; ++j) {
             const int r = row0 + lane + 32 * j;
             src_row[j] = (lane + 32 * j < BT && r < seg_end) ? p.a_row_map[r] : -1;
+          }
+        } else if (gather_a) {
+          const int seg_end = ctl.seg[tc.e + 1];
+          const int first = p.a_row_map[row0];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int r = row0 + 4 * lane + j;
+            g4[j] = (4 * lane + j < BT && r < seg_end) ? p.a_row_map[r] : first;
           }
         }
         int ka = 0;
@@ -734,11 +995,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             if (lane == 0) {
-              mbar_arrive_expect_tx(&ctl.full[stage], A_BYTES);
+              mbar_arrive_expect_tx(&ctl.full[stage], gather_cp ? A_BYTES : STAGE_BYTES);
               tma_load_2d_hint(sa + stage * A_BYTES, &tmap_w, &ctl.full[stage], kb * BK, wrow0, pol_w);
             }
-            gather_k_block<BT>(smem_u32(sb + stage * B_BYTES), p.a_ptr, p.a_ld, ka, src_row, lane);
-            cp_async_mbar_arrive(&ctl.full[stage]);
+            if (gather_cp) {
+              gather_k_block<BT>(smem_u32(sb + stage * B_BYTES), p.a_ptr, p.a_ld, ka, src_row, lane);
+              cp_async_mbar_arrive(&ctl.full[stage]);
+            } else {  // BT / 4 lanes x 4 rows x 128 bytes = the BT-row B stage
+              __syncwarp();
+              if (lane < BT / 4)
+                tma_gather4_2d(sb + stage * B_BYTES + lane * 512, &tmap_act, &ctl.full[stage], ka, g4[0], g4[1],
+                               g4[2], g4[3]);
+            }
           } else {
             if (!mbar_wait(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, p.status)) {
               ok = false;
@@ -785,7 +1053,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (gather_a) fence_proxy_async_shared();  // cp.async-written B -> tensor-core reads
+          if (gather_cp) fence_proxy_async_shared();  // cp.async-written B -> tensor-core reads
           const uint64_t da = umma_desc_sw128(smem_u32(sa + stage * A_BYTES));
           const uint64_t db = umma_desc_sw128(smem_u32(sb + stage * B_BYTES));
 #pragma unroll
@@ -954,6 +1222,8 @@ constexpr size_t rows2_smem(int bn, int stages) {
   return static_cast<size_t>(stages) * (BM * BK * 2 + (bn / 2) * BK * 2) + 1024;
 }
 
+constexpr size_t tokens2_smem(int stages) { return static_cast<size_t>(stages) * (BM * BK * 2 + 128 * BK * 2) + 1024; }
+
 constexpr size_t rows_smem(int bn, int stages) { return static_cast<size_t>(stages) * (BM * BK * 2 + bn * BK * 2) + 1024; }
 constexpr size_t weights_smem(int bt, int stages) {
   return static_cast<size_t>(stages) * (BM * BK * 2 + bt * BK * 2) + 1024;
@@ -966,6 +1236,7 @@ int grouped_gemm_box_rows_act(int variant) {
     case kRowsBN256:
     case kRowsBN128:
     case kRows2BN256: return BM;
+    case kTokens2: return 128;  // up to 128 of the tile's rows per CTA
     case kWeightsT16: return 16;
     case kWeightsT32: return 32;
     case kWeightsT64: return 64;
@@ -992,6 +1263,11 @@ cudaError_t grouped_gemm_launch(int variant, const CUtensorMap& tmap_act, const 
     case kRows2BN256:
       if (grid % 2) return cudaErrorInvalidValue;
       return launch_cluster2(grouped_gemm_rows2_kernel<256, 6>, rows2_smem(256, 6), grid, tmap_act, tmap_w, p, s);
+    case kTokens2:
+      if (grid % 2 || (p.epilogue != kEpiSwiGLU && p.epilogue != kEpiScaleBf16 && p.epilogue != kEpiStoreBf16) ||
+          p.n % 256 != 0 || p.a_row_map)
+        return cudaErrorInvalidValue;
+      return launch_cluster2(grouped_gemm_tokens2_kernel<6>, tokens2_smem(6), grid, tmap_act, tmap_w, p, s);
     case kWeightsT16:
       return launch_with_smem(grouped_gemm_weights_kernel<16, 8>, weights_smem(16, 8), grid, tmap_act, tmap_w, p, s);
     case kWeightsT32:

@@ -123,10 +123,13 @@ struct GroupedGemmParams {
   int prefetch;               // K blocks of the next tile prefetched into L2 at each tile start (0: off)
   // Gathered activations: when a_row_map is set, activation row r of the
   // grouped problem is row a_row_map[r] of a_ptr (row stride a_ld elements),
-  // loaded with cp.async by the producer warp instead of a TMA tile load.
+  // loaded by the producer warp instead of a TMA tile load: with
+  // tma_gather4 != 0 by TMA tile::gather4 through the activation tensor map
+  // (box one row high; each lane loads four rows), else with cp.async.
   const int32_t* a_row_map;
   const __nv_bfloat16* a_ptr;
   long long a_ld;
+  int tma_gather4;
   const int32_t* out_row_map; // optional: output row of permuted row r
   const float* col_bias;      // kEpiStoreF32 optional
   int* status;
@@ -140,6 +143,7 @@ enum GemmVariant : int {
   kWeightsT32 = 3, // 128 features x 32 rows per tile
   kWeightsT64 = 4, // 128 features x 64 rows per tile
   kRows2BN256 = 5, // 256 rows x 256 features per tile on an SM pair (cta_group::2)
+  kTokens2 = 6,    // 256 features x up to 256 rows per tile on an SM pair (swap-AB, N per tile)
 };
 
 // Builds a 2-D bf16 TMA descriptor with 128-byte swizzling over a row-major

@@ -138,57 +138,81 @@ __global__ void __launch_bounds__(kPermuteChunk) permute_scatter_kernel(
   (void)status;
 }
 
-// x_perm[r] = x[row_token[r]] for r < expert_offsets[E]; 16-byte moves.
+// x_perm[r] = x[row_token[r]] for r < expert_offsets[E].  One warp per row;
+// each lane keeps up to 8 independent 16-byte loads in flight (a 4 KB row of
+// H = 2048 is one pass).
 __global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                                           const int32_t* __restrict__ row_token,
                                                           const int32_t* __restrict__ expert_offsets, int E,
                                                           __nv_bfloat16* __restrict__ xp, long long max_rows,
                                                           int H) {
-  const int chunks = H >> 3;
+  const int chunks = H >> 3;  // 16-byte chunks per row
+  const int lane = threadIdx.x & 31;
   const long long rows = min(static_cast<long long>(expert_offsets[E]), max_rows);
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * chunks;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long r = i / chunks;
-    const int c = static_cast<int>(i % chunks);
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += nwarps) {
     const long long t = row_token[r];
-    reinterpret_cast<uint4*>(xp + r * H)[c] = reinterpret_cast<const uint4*>(x + t * H)[c];
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * H);
+    uint4* dst = reinterpret_cast<uint4*>(xp + r * H);
+    for (int c0 = lane; c0 < chunks; c0 += 256) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + 32 * j < chunks) v[j] = src[c0 + 32 * j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + 32 * j < chunks) __stcs(dst + c0 + 32 * j, v[j]);  // streaming: keeps x resident in L2
+    }
   }
 }
 
 // out[t] = sum_k w[t,k] * y[slot_row[t*K+k]] in fp32 with k ascending (the
 // accumulation order of nki_moe_integrated.py:482-494).  When slot_weight is
-// null the rows already carry their routing weight.
+// null the rows already carry their routing weight.  One thread per 16-byte
+// column chunk of a token (32-bit index math; T * H / 8 < 2^31), its K row
+// loads in flight together; y rows are read once, so they are loaded with
+// the evict-first hint.
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ y,
                                                       const int32_t* __restrict__ slot_row,
                                                       const float* __restrict__ slot_weight,
                                                       __nv_bfloat16* __restrict__ out, int T, int K, int H) {
-  const int chunks = H >> 3;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-       i < static_cast<long long>(T) * chunks; i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long t = i / chunks;
-    const int c = static_cast<int>(i % chunks);
+  const uint32_t chunks = static_cast<uint32_t>(H) >> 3;
+  const uint32_t n = static_cast<uint32_t>(T) * chunks;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint32_t t = i / chunks;
+    const uint32_t c = i - t * chunks;
     float acc[8] = {};
-    for (int k = 0; k < K; ++k) {
-      const int r = slot_row[t * K + k];
-      if (r < 0) continue;
-      const uint4 u = reinterpret_cast<const uint4*>(y + static_cast<long long>(r) * H)[c];
-      const float wk = slot_weight ? slot_weight[t * K + k] : 1.f;
-      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
-      acc[0] = fmaf(wk, a.x, acc[0]);
-      acc[1] = fmaf(wk, a.y, acc[1]);
-      acc[2] = fmaf(wk, b.x, acc[2]);
-      acc[3] = fmaf(wk, b.y, acc[3]);
-      acc[4] = fmaf(wk, cc.x, acc[4]);
-      acc[5] = fmaf(wk, cc.y, acc[5]);
-      acc[6] = fmaf(wk, d.x, acc[6]);
-      acc[7] = fmaf(wk, d.y, acc[7]);
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      uint4 u[8];
+      int rr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        rr[j] = k0 + j < K ? slot_row[t * K + k0 + j] : -1;
+        if (rr[j] >= 0) u[j] = __ldcs(reinterpret_cast<const uint4*>(y + static_cast<long long>(rr[j]) * H) + c);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (rr[j] < 0) continue;
+        const float wk = slot_weight ? slot_weight[t * K + k0 + j] : 1.f;
+        const float2 a = unpack_bf16x2(u[j].x), b = unpack_bf16x2(u[j].y), cc = unpack_bf16x2(u[j].z),
+                     d = unpack_bf16x2(u[j].w);
+        acc[0] = fmaf(wk, a.x, acc[0]);
+        acc[1] = fmaf(wk, a.y, acc[1]);
+        acc[2] = fmaf(wk, b.x, acc[2]);
+        acc[3] = fmaf(wk, b.y, acc[3]);
+        acc[4] = fmaf(wk, cc.x, acc[4]);
+        acc[5] = fmaf(wk, cc.y, acc[5]);
+        acc[6] = fmaf(wk, d.x, acc[6]);
+        acc[7] = fmaf(wk, d.y, acc[7]);
+      }
     }
     uint4 o;
     o.x = pack_bf16x2(acc[0], acc[1]);
     o.y = pack_bf16x2(acc[2], acc[3]);
     o.z = pack_bf16x2(acc[4], acc[5]);
     o.w = pack_bf16x2(acc[6], acc[7]);
-    reinterpret_cast<uint4*>(out + t * H)[c] = o;
+    reinterpret_cast<uint4*>(out + static_cast<long long>(t) * H)[c] = o;
   }
 }
 
@@ -344,14 +368,15 @@ cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k
 cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token, const int32_t* expert_offsets,
                                int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s) {
   if (max_rows == 0) return cudaSuccess;
-  gather_rows_kernel<<<grid_for(max_rows * (hidden / 8), 256), 256, 0, s>>>(x, row_token, expert_offsets, experts,
-                                                                              x_perm, max_rows, hidden);
+  gather_rows_kernel<<<grid_for(max_rows * 32, 256), 256, 0, s>>>(x, row_token, expert_offsets, experts, x_perm,
+                                                                    max_rows, hidden);
   return cudaGetLastError();
 }
 
 cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
                            __nv_bfloat16* out, int tokens, int top_k, int hidden, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
+  if (static_cast<long long>(tokens) * (hidden / 8) >= (1LL << 31)) return cudaErrorInvalidValue;
   combine_kernel<<<grid_for(static_cast<long long>(tokens) * (hidden / 8), 256), 256, 0, s>>>(
       y, slot_row, slot_weight, out, tokens, top_k, hidden);
   return cudaGetLastError();

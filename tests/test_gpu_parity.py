@@ -225,13 +225,16 @@ def test_bad_expert_id_is_reported():
 
 
 # ---------------------------------------------------------------- K4/K5
-@pytest.mark.parametrize("schedule,rows", [(1, 0), (2, 16), (2, 32), (2, 64), (3, 0)])
-def test_grouped_gemm(schedule, rows):
+@pytest.mark.parametrize("counts", [(5, 0, 130, 64, 1), (300, 17, 0, 256, 513, 16)])
+@pytest.mark.parametrize("schedule,rows", [(1, 0), (2, 16), (2, 32), (2, 64), (3, 0), (4, 0)])
+def test_grouped_gemm(schedule, rows, counts):
+    """Ragged segments: empty, one-row, exact multiples of the tile and
+    partial last tiles (300 = 256 + 44 rows) for every schedule."""
     _lib.set_option("gemm_schedule", schedule)
     _lib.set_option("weights_rows", rows)
     try:
         g = torch.Generator().manual_seed(17)
-        counts = [5, 0, 130, 64, 1]
+        counts = list(counts)
         E, N, Kd = len(counts), 256, 192
         M = sum(counts)
         a = torch.randn(M, Kd, generator=g)
@@ -251,7 +254,7 @@ def test_grouped_gemm(schedule, rows):
         _lib.set_option("weights_rows", 0)
 
 
-@pytest.mark.parametrize("schedule,rows", [(0, 0), (1, 0), (2, 16), (2, 32), (2, 64), (3, 0)])
+@pytest.mark.parametrize("schedule,rows", [(0, 0), (1, 0), (2, 16), (2, 32), (2, 64), (3, 0), (4, 0)])
 def test_moe_experts_tiny(golden_dir, schedule, rows):
     """The reference test's module case (H=256, I=512, E=4, top-2) given routing."""
     _lib.set_option("gemm_schedule", schedule)
@@ -298,7 +301,7 @@ def _oracle_block(xn, gun, dn, rwn, bias, idx_gpu, w_gpu):
     return oracle.experts_forward(xn, gun, dn, idx_gpu, w_gpu)
 
 
-@pytest.mark.parametrize("schedule", [0, 1, 2, 3])
+@pytest.mark.parametrize("schedule", [0, 1, 2, 3, 4])
 def test_moe_block_c1(c1_inputs, golden_dir, schedule):
     _lib.set_option("gemm_schedule", schedule)
     try:
@@ -324,7 +327,7 @@ def test_moe_block_c2_decode():
     assert len(np.unique(idx)) > 100  # natural routing touches ~all experts
 
 
-@pytest.mark.parametrize("schedule", [0, 1])
+@pytest.mark.parametrize("schedule", [0, 1, 4])
 def test_moe_block_c3_prefill_sampled_tokens(schedule):
     """Full prefill size (8192 tokens); each token's output depends only on
     that token, so 256 sampled tokens are checked against the oracle."""
@@ -345,10 +348,15 @@ def test_moe_block_c3_prefill_sampled_tokens(schedule):
     assert np.isfinite(out).all()
 
 
-def test_moe_block_skewed_routing():
+@pytest.mark.parametrize("schedule", [0, 4])
+def test_moe_block_skewed_routing(schedule):
     wl = WORKLOADS["c4"]
     inp = make_moe_inputs(wl, tokens=2048)
-    out, idx, w, (xn, gun, dn, rwn, bias) = _block_case(inp, bias=True)
+    _lib.set_option("gemm_schedule", schedule)
+    try:
+        out, idx, w, (xn, gun, dn, rwn, bias) = _block_case(inp, bias=True)
+    finally:
+        _lib.set_option("gemm_schedule", 0)
     counts = np.bincount(idx.ravel(), minlength=128)
     assert counts.max() > 8 * counts.mean()  # heavily imbalanced
     ref = _oracle_block(xn, gun, dn, rwn, bias, idx, w)
@@ -362,18 +370,41 @@ def test_moe_block_odd_token_counts():
     assert_block_close(out, ref)
 
 
+@pytest.mark.parametrize("mode", [1, 2])
 @pytest.mark.parametrize("schedule", [1, 2])
-def test_moe_block_gather_fused(c1_inputs, schedule):
-    """GEMM-1 loading its gathered token rows itself (cp.async) instead of the
-    separate gather kernel gives the same result."""
+def test_moe_block_gather_fused(c1_inputs, schedule, mode):
+    """GEMM-1 loading its gathered token rows itself (1: cp.async, 2: TMA
+    gather4) instead of the separate gather kernel gives the same result."""
     _lib.set_option("gemm_schedule", schedule)
     try:
+        _lib.set_option("gather_fused", 0)
         ref = _block_case(c1_inputs)[0]
-        _lib.set_option("gather_fused", 1)
+        _lib.set_option("gather_fused", mode)
         out = _block_case(c1_inputs)[0]
         assert np.array_equal(out, ref)
     finally:
         _lib.set_option("gather_fused", 0)
+        _lib.set_option("gemm_schedule", 0)
+
+
+@pytest.mark.parametrize("schedule,rows", [(2, 16), (2, 32), (2, 64), (1, 0)])
+def test_moe_block_gather4_skewed(schedule, rows):
+    """TMA gather4 row loads on ragged, heavily skewed expert segments (rows
+    past a segment's end inside a tile, one-row segments) equal the separate
+    gather kernel bit for bit, for every decode tile width."""
+    inp = make_moe_inputs(WORKLOADS["c4"], tokens=600)
+    _lib.set_option("gemm_schedule", schedule)
+    _lib.set_option("weights_rows", rows)
+    try:
+        _lib.set_option("gather_fused", 0)
+        ref, idx, w, _ = _block_case(inp, bias=True)
+        _lib.set_option("gather_fused", 2)
+        out, idx2, _, _ = _block_case(inp, bias=True)
+        assert np.array_equal(idx, idx2)
+        assert np.array_equal(out, ref)
+    finally:
+        _lib.set_option("gather_fused", 0)
+        _lib.set_option("weights_rows", 0)
         _lib.set_option("gemm_schedule", 0)
 
 
