@@ -54,6 +54,13 @@ int router_splits_for(int tokens, int hidden, int experts);
 // softmax -> top-k (by logit, ties to the lower id) -> renormalise.
 cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
                                 cudaStream_t s);
+// Router logits + softmax + top-k in one launch for few tokens: 8-CTA
+// clusters, each CTA one eighth of the experts, top-k over distributed shared
+// memory.  Supported when E <= 256, H % 128 == 0, 1 <= K <= min(32, E).
+bool router_topk_fused_supported(int hidden, int experts, int top_k);
+cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
+                                     int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
+                                     cudaStream_t s);
 // Same on logits given as `splits` fp32 partial sums [split][T][E] (+ bias[E]);
 // logits_out (nullable) receives the summed logits.
 cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,
