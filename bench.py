@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement")
     ap.add_argument("--profile-once", action="store_true", help="one warm step only (for ncu launch lists)")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder-stack TTFT / decode run")
     return ap.parse_args()
 
 
@@ -61,19 +62,36 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the background."""
+    """SM clock and clock-event (throttle) reasons during the timed region,
+    polled through NVML every ~2 ms in a background thread (read-only
+    queries), so that a timed region of tens of milliseconds still holds
+    samples; falls back to ``nvidia-smi -lms 100`` when NVML is missing."""
 
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.rows = []  # (time, sm_mhz, max_mhz, set of reasons)
         self.t_start = self.t_end = None
+        self._stop = threading.Event()
+        self._nvml = None
+        self.proc = None
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self._nvml = (pynvml, h)
+            threading.Thread(target=self._poll_nvml, daemon=True).start()
+            return
+        except Exception:  # noqa: BLE001 - no NVML: use nvidia-smi
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.gpu),
@@ -81,11 +99,32 @@ class ClockSampler:
         except (FileNotFoundError, OSError):
             self.proc = None
             return
-        threading.Thread(target=self._read, daemon=True).start()
+        threading.Thread(target=self._read_smi, daemon=True).start()
 
-    def _read(self):
+    def _poll_nvml(self):
+        nv, h = self._nvml
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception:  # noqa: BLE001
+                break
+            self.rows.append((time.time(), float(sm), float(mx),
+                              {n for b, n in self.REASONS.items() if bits & b}))
+            time.sleep(0.002)
+
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.lines.append((time.time(), line.strip()))
+            parts = [p.strip() for p in line.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+                rs = {n for n, v in zip(names, parts[5:9]) if v.lower() in ("active", "1", "yes")}
+                self.rows.append((time.time(), float(parts[1]), float(parts[2]), rs))
+            except ValueError:
+                continue
 
     def mark(self, start: bool):
         if start:
@@ -94,6 +133,7 @@ class ClockSampler:
             self.t_end = time.time()
 
     def stop(self):
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -102,28 +142,18 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        rows = []
-        for t, line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((t, float(parts[1]), float(parts[2]), parts))
-            except ValueError:
-                continue
+        rows = list(self.rows)
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"], "samples": 0}
         inwin = [r for r in rows if self.t_start and self.t_end and self.t_start <= r[0] <= self.t_end]
         use = inwin or rows
         mhz = sorted(r[1] for r in use)
-        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
         for r in use:
-            for name, v in zip(names[1:], r[3][5:9]):
-                if v.lower() in ("active", "1", "yes"):
-                    reasons.add(name)
+            reasons |= r[3]
         return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": max(r[2] for r in use), "reasons": sorted(reasons),
-                "samples": len(use), "samples_in_timed_region": len(inwin)}
+                "samples": len(use), "samples_in_timed_region": len(inwin),
+                "source": "nvml" if self._nvml else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------- helpers
@@ -288,6 +318,29 @@ def measure_stages(torch, fn, steps, evs, graph_of=None):
     return [a / steps for a in acc]
 
 
+def measure_stack(torch):
+    """The full-stack configuration: random-init Qwen3-30B-A3B (48 layers),
+    batch 8 x 512-token prompts, 128 greedy tokens.  TTFT is the prefill
+    through the first token; decode steps replay one CUDA graph each."""
+    from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
+
+    cfg = Qwen3MoEConfig()
+    B, S, new = 8, 512, 128
+    st = Qwen3MoEStack.random_init(cfg, seed=0, max_batch=B, max_seq=S + new)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(0))
+    st.generate(ids, 8)  # warm-up, graph capture
+    _, t = st.generate(ids, new)
+    st.release_graph()
+    del st
+    torch.cuda.empty_cache()
+    return {"config": f"Qwen3-30B-A3B decoder stack, {cfg.num_hidden_layers} layers, random-init bf16 weights "
+                      f"(router fp32); batch {B} x {S}-token prompts (uniform random ids, seed 0); {new} greedy "
+                      f"tokens", "ttft_ms": t["ttft_ms"], "decode_ms_per_step": t["decode_ms"] / t["decode_steps"],
+            "decode_tok_s": t["decode_tok_s"],
+            "output_tok_s": B * new / ((t["ttft_ms"] + t["decode_ms"]) * 1e-3),
+            "timing": "CUDA events; one CUDA graph replay per decode step", "data": "synthetic"}
+
+
 def run_b200(args):
     import numpy as np
     import torch
@@ -409,14 +462,15 @@ def run_b200(args):
                         "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                         "d2h_bytes_per_step": outh.numel() * outh.element_size()}
         if not args.no_cpu_baseline and rank == 0 and world == 1:
-            sample = 512 if which == "prefill" else wl.tokens
-            sub = {k: (v[:sample] if k == "x" else v) for k, v in inp.items()}
-            cin = cpu_inputs(sub, torch)
-            cpu_oracle_tokens_per_s(cin, wl, min(sample, 32))
-            tps, dt = cpu_oracle_tokens_per_s(cin, wl, sample)
+            # the whole batch of the workload, repeated to about 10 s of CPU work
+            sample = wl.tokens
+            cin = cpu_inputs(inp, torch)
+            _, one = cpu_oracle_tokens_per_s(cin, wl, sample)
+            rep = max(1, min(int(10.0 / max(one, 1e-3)) + 1, int(30.0 / max(one, 1e-3))))
+            tps, dt = cpu_oracle_tokens_per_s(cin, wl, sample, repeat=rep)
             r["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-                                 "sample": f"{sample} tokens of the {wl.name} workload (numpy oracle, fp32), "
-                                           f"{dt:.2f} s"}
+                                 "sample": f"the {sample}-token {wl.name} batch x {rep} (numpy oracle, fp32), "
+                                           f"{dt * rep:.1f} s"}
         result[which] = r
         del moe, inp, x
         torch.cuda.empty_cache()
@@ -453,6 +507,8 @@ def run_b200(args):
                           "roofline_block": d.get("roofline_block"), "stages_ms": d["stages_ms"],
                           "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline"),
                           "unique_experts": d["alg"]["unique_experts"]}
+    if world == 1 and not args.no_stack:
+        line["stack"] = measure_stack(torch)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

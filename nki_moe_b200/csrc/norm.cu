@@ -56,20 +56,37 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const TX* x, const TX* res
   const TX* xr = x + row * hidden;
   float v[kMaxChunks][8];
   float ss = 0.f;
+  // Every load of the register-held part of the row is issued before any
+  // store: x, residual and residual_out may alias (in-place residual update),
+  // so a store between them would serialise the loads one round trip each.
 #pragma unroll
   for (int i = 0; i < kMaxChunks; ++i) {
     const int c = lane + i * 32;
-    if (c < nchunk) {
-      load8(xr + c * 8, v[i]);
-      if constexpr (kResidual) {
-        float r[8];
-        load8(residual + row * hidden + c * 8, r);
+    if (c < nchunk) load8(xr + c * 8, v[i]);
+  }
+  if constexpr (kResidual) {
+    float r[kMaxChunks][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = lane + i * 32;
+      if (c < nchunk) load8(residual + row * hidden + c * 8, r[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = lane + i * 32;
+      if (c < nchunk) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[i][j];
         // the sum is rounded to the residual stream's dtype before the norm
         round_bf16(v[i]);
         store8(residual_out + row * hidden + c * 8, v[i]);
       }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
     }

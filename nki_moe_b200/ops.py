@@ -30,8 +30,9 @@ _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: 
 
 def sync_check_enabled() -> bool:
     """When NKIMOE_SYNC_CHECK=1, every block call synchronises and raises on a
-    device-flagged fault (timeout, expert id out of range)."""
-    return os.environ.get("NKIMOE_SYNC_CHECK", "0") == "1"
+    device-flagged fault (timeout, expert id out of range) -- except while a
+    CUDA graph is being captured, where a synchronisation is not allowed."""
+    return os.environ.get("NKIMOE_SYNC_CHECK", "0") == "1" and not torch.cuda.is_current_stream_capturing()
 
 
 def _cuda(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -303,13 +304,18 @@ def router_split(router_w: torch.Tensor) -> torch.Tensor:
 
 
 def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
-              bias: torch.Tensor | None = None, return_routing: bool = False, tensor_router: bool = True):
+              bias: torch.Tensor | None = None, return_routing: bool = False, tensor_router: bool = True,
+              router_w_split: torch.Tensor | None = None):
     """Router (fp32) + softmax/top-k/renormalise + experts (K2..K7).
 
     With ``tensor_router`` the fp32 router GEMM of large batches runs on the
-    tensor cores over the exact three-plane bf16 split of ``router_w``."""
+    tensor cores over the exact three-plane bf16 split of ``router_w``
+    (``router_w_split``, [3, E, H] from :func:`router_split`, when the caller
+    keeps it; otherwise taken from a small cache)."""
     x = _contig(_cuda(x, "x"), torch.bfloat16)
-    rsplit = router_split(router_w) if tensor_router and router_w.shape[0] % 128 == 0 else None
+    rsplit = None
+    if tensor_router and router_w.shape[0] % 128 == 0:
+        rsplit = router_w_split if router_w_split is not None else router_split(router_w)
     rw = _contig(_cuda(router_w, "router_w"), torch.float32)
     b = _contig(bias, torch.float32) if bias is not None else None
     T, H = x.shape
