@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement")
     ap.add_argument("--profile-once", action="store_true", help="one warm step only (for ncu launch lists)")
     ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder-stack TTFT / decode run")
+    ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: exchange over peer memory (library kernels) or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -395,9 +397,14 @@ def run_b200(args):
     for which in workloads:
         wl = WORKLOADS["c3" if which == "prefill" else "c2"]
         inp, moe, x = setup(wl)
+        block = None
         if world > 1:
-            from nki_moe_b200.ep import ExpertParallelMoE
-            block = ExpertParallelMoE.from_dense(moe, torch.distributed.group.WORLD)
+            if args.ep == "peer":
+                from nki_moe_b200.ep_peer import PeerExpertParallelMoE
+                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=wl.tokens)
+            else:
+                from nki_moe_b200.ep import ExpertParallelMoE
+                block = ExpertParallelMoE.from_dense(moe, torch.distributed.group.WORLD)
             fwd = lambda: block(x)  # noqa: E731
         else:
             pe = moe.packed()
@@ -472,7 +479,9 @@ def run_b200(args):
                                  "sample": f"the {sample}-token {wl.name} batch x {rep} (numpy oracle, fp32), "
                                            f"{dt * rep:.1f} s"}
         result[which] = r
-        del moe, inp, x
+        if block is not None and hasattr(block, "close"):
+            block.close()
+        del moe, inp, x, block
         torch.cuda.empty_cache()
 
     sampler.stop()
@@ -480,14 +489,18 @@ def run_b200(args):
     main_key = workloads[0]
     m = result[main_key]
     wl = WORKLOADS["c3" if main_key == "prefill" else "c2"]
-    launches_per_step = 9
+    # this library's kernels per step: single GPU 9 (router, top-k, 3 permutation,
+    # gather, 2 GEMMs, combine); EP over peer memory 18 (+ rank sort, send,
+    # 2 waits, mask, receiver permutation, final sum); EP over NCCL 17 of ours
+    # (NCCL's own kernels not counted)
+    launches_per_step = 9 if world == 1 else (18 if args.ep == "peer" else 17)
     line = {
         "metric": "moe_block_tokens_per_s", "value": m["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": m["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": wl.name, "tokens_per_gpu": wl.tokens, "hidden": wl.hidden, "experts": wl.experts,
                    "top_k": wl.top_k, "intermediate": wl.intermediate,
-                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "parallelism": f"ep{world}-{args.ep}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.21 GB of expert weights read per step)",
                    "timing": "CUDA graph replay, CUDA events" if world == 1 else "eager, CUDA events, max over ranks"},
         "roofline": m.get("roofline"),

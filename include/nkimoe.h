@@ -52,6 +52,8 @@ extern "C" {
 #define NKIMOE_LAYOUT_NXD 0        /* gate_up [E,H,2I], down [E,I,H] (qwen.py:164-226)          */
 #define NKIMOE_LAYOUT_HF 1         /* gate_up [E,2I,H], down [E,H,I] (HF Qwen3MoeExperts)       */
 
+#define NKIMOE_IPC_HANDLE_BYTES 64 /* cudaIpcMemHandle_t, for nkimoe_peer_alloc / nkimoe_peer_open */
+
 NKIMOE_API int nkimoe_version(void);
 NKIMOE_API const char* nkimoe_last_error(void);
 /* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows on one SM,
@@ -255,6 +257,47 @@ NKIMOE_API int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const 
  * T * K below 2^31 (NKIMOE_ERR_UNSUPPORTED otherwise). */
 NKIMOE_API int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T,
                               int64_t K, int64_t H, void* stream);
+
+/* ---------------------------------------------------------------- expert parallel over peer memory
+ *
+ * No reference counterpart: the reference's expert parallelism is NxDI's
+ * (qwen.py:35, :240), which is not in the reference tree.  This is the
+ * one-process-per-GPU exchange of this library: every rank allocates one
+ * exchange buffer (nkimoe_peer_alloc), the ranks swap the IPC handles (through
+ * their process group), and each opens the others' buffers (nkimoe_peer_open).
+ * No multicast object is created; peers are reached by plain NVLink stores. */
+
+/* Bytes of one rank's exchange buffer for num_ranks ranks of at most
+ * max_tokens tokens each. */
+NKIMOE_API size_t nkimoe_ep_peer_buffer_bytes(int64_t num_ranks, int64_t max_tokens, int64_t H, int64_t K);
+
+/* cudaMalloc (zero-filled) + its IPC handle (NKIMOE_IPC_HANDLE_BYTES bytes). */
+NKIMOE_API int nkimoe_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another process's buffer (cudaIpcOpenMemHandle, peer access enabled). */
+NKIMOE_API int nkimoe_peer_open(const void* ipc_handle, void** ptr);
+NKIMOE_API int nkimoe_peer_close(void* ptr);
+NKIMOE_API int nkimoe_peer_free(void* ptr);
+
+NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                                 int64_t num_ranks, int64_t max_tokens);
+
+/* The expert-parallel MoE block for this rank's T <= max_tokens tokens, one
+ * stream-ordered call with no host synchronisation: route (as
+ * nkimoe_moe_block) -> each token's row sent once to every rank owning one of
+ * its experts (stores into that rank's buffer) -> wait for the num_ranks
+ * senders -> this rank's experts (w13_local/w2_local: packed weights of
+ * experts [rank*E/P, (rank+1)*E/P)) over the received rows -> each row's
+ * weighted sum stored back into its source's buffer -> wait -> sum of the
+ * num_ranks partial sums into out [T, H].  peer_buffers: the num_ranks
+ * buffers as mapped in this process (this rank's own at index rank).  Every
+ * rank calls this once per step with the same epoch, nonzero and increasing
+ * between steps.  A peer that never arrives sets NKIMOE_DEV_TIMEOUT in the
+ * status word (nkimoe_read_status) after a bounded wait (~10 s). */
+NKIMOE_API int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias,
+                                      const void* router_w_split, const void* w13_local, const void* w2_local,
+                                      void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                      int64_t num_ranks, int64_t rank, int64_t max_tokens, void* const* peer_buffers,
+                                      uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- pieces */
 

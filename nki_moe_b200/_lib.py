@@ -59,6 +59,14 @@ SIGNATURES = {
     "nkimoe_segment_experts_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "nkimoe_segment_experts": (_i, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "nkimoe_combine": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "nkimoe_ep_peer_buffer_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "nkimoe_peer_alloc": (_i, [_sz, _c.POINTER(_vp), _vp]),
+    "nkimoe_peer_open": (_i, [_vp, _c.POINTER(_vp)]),
+    "nkimoe_peer_close": (_i, [_vp]),
+    "nkimoe_peer_free": (_i, [_vp]),
+    "nkimoe_ep_peer_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "nkimoe_ep_peer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                    _i64, _c.POINTER(_vp), _c.c_uint32, _vp, _sz, _vp]),
     "nkimoe_ep_dispatch_workspace_bytes": (_sz, [_i64, _i64]),
     "nkimoe_ep_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                 _vp]),

@@ -22,7 +22,8 @@ REPO = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(REPO, "_build")
 LIB = os.path.join(PKG, "libnkimoe.so")
-SOURCES = ["norm.cu", "router.cu", "permute.cu", "pack.cu", "grouped_gemm.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["norm.cu", "router.cu", "permute.cu", "pack.cu", "grouped_gemm.cu", "ep_peer.cu", "capi.cu",
+           "noalloc.cu"]
 HEADERS = ["common.cuh", "kernels.h"]
 
 

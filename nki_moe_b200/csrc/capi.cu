@@ -9,6 +9,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -234,12 +235,22 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
   return NKIMOE_OK;
 }
 
+// Expert-parallel receiver: instead of writing `out`, the block's final sum of
+// each row goes straight to the row's source rank (ep_peer.cu).
+struct PeerCombine {
+  EpPeerPtrs peers;
+  EpPeerLayout L;
+  int P, me, Tm;
+  unsigned* counter;
+  uint32_t epoch;
+};
+
 int experts_impl(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype, const float* topk_w,
                  void* out, long long T, long long H, long long I, long long E, long long K, void* ws, size_t ws_bytes,
-                 cudaStream_t s) {
+                 cudaStream_t s, const PeerCombine* pc = nullptr, int* status_word = nullptr) {
   const WsLayout L = ws_layout(T, H, I, E, K);
   char* base = static_cast<char*>(ws);
-  int* status = reinterpret_cast<int*>(base + L.status);
+  int* status = status_word ? status_word : reinterpret_cast<int*>(base + L.status);
   int32_t* offsets = reinterpret_cast<int32_t*>(base + L.offsets);
   int32_t* row_token = reinterpret_cast<int32_t*>(base + L.row_token);
   int32_t* row_slot = reinterpret_cast<int32_t*>(base + L.row_slot);
@@ -272,10 +283,37 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
                 false, row_weight);
   if (rc != NKIMOE_OK) return rc;
   mark(kStageCombine, s);
-  NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
-                          static_cast<int>(K), static_cast<int>(H), s));
+  if (pc) {
+    NKI_CUDA(ep_peer_combine_launch(xy, slot_row, static_cast<int>(T), static_cast<int>(K), static_cast<int>(H),
+                                    pc->Tm, pc->me, pc->peers, pc->L, pc->P, pc->counter, pc->epoch, s));
+  } else {
+    NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
+                            static_cast<int>(K), static_cast<int>(H), s));
+  }
   mark(kStageEnd, s);
   return NKIMOE_OK;
+}
+
+// Workspace of nkimoe_ep_peer_forward: routing of the local tokens, the
+// (token, rank) sort, the row map of the final sum, two completion counters,
+// and the receiver's expert block over all P * max_tokens region rows.
+struct PeerWs {
+  size_t route, disp, slot_in, slot_out, counters, recv, total;
+};
+
+size_t ep_dispatch_ws_bytes(long long T, long long P);
+
+PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, long long P, long long Tm) {
+  PeerWs W{};
+  size_t o = 0;
+  W.route = o; o += round256(ws_layout(T, H, I, E, K).offsets);  // status, logits, partials, idx, w
+  W.disp = o; o += round256(ep_dispatch_ws_bytes(T, P));
+  W.slot_in = o; o += round256(sizeof(int32_t) * T * P);
+  W.slot_out = o; o += round256(sizeof(int32_t) * T * P);
+  W.counters = o; o += 256;
+  W.recv = o; o += ws_layout(P * Tm, H, I, E / P, K).total;
+  W.total = o;
+  return W;
 }
 
 }  // namespace
@@ -294,6 +332,14 @@ bool make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long lon
 }
 
 void set_last_error(const char* msg) { g_err = msg ? msg : ""; }
+
+namespace {
+size_t ep_dispatch_ws_bytes(long long T, long long P) {
+  const long long TP = T * P;
+  return 256 + round256(sizeof(int32_t) * (P + 1)) + 3 * round256(sizeof(int32_t) * TP) +
+         round256(permute_scratch_bytes(T, static_cast<int>(P), static_cast<int>(P)));
+}
+}  // namespace
 
 int device_sm_count() {
   static int counts[64] = {0};
@@ -674,11 +720,7 @@ int nkimoe_segment_experts(const void* a, const float* row_weight, const int32_t
                   status, s, 0, false, row_weight, experts_per_group, static_cast<int>(experts_per_group));
 }
 
-size_t nkimoe_ep_dispatch_workspace_bytes(int64_t T, int64_t P) {
-  const long long TP = T * P;
-  return 256 + round256(sizeof(int32_t) * (P + 1)) + 3 * round256(sizeof(int32_t) * TP) +
-         round256(permute_scratch_bytes(T, static_cast<int>(P), static_cast<int>(P)));
-}
+size_t nkimoe_ep_dispatch_workspace_bytes(int64_t T, int64_t P) { return ep_dispatch_ws_bytes(T, P); }
 
 int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk_w, int64_t T, int64_t H, int64_t K,
                        int64_t num_ranks, int64_t experts_per_rank, void* x_send, int32_t* slots_send,
@@ -717,6 +759,138 @@ int nkimoe_ep_dispatch(const void* x, const int32_t* topk_idx, const float* topk
   NKI_CUDA(ep_slots_launch(topk_idx, topk_w, row_token, row_slot, offsets, TP, static_cast<int>(P),
                            static_cast<int>(K), static_cast<int>(El), slots_send, weights_send, s));
   NKI_CUDA(offsets_to_counts_launch(offsets, rank_counts, static_cast<int>(P), s));
+  return NKIMOE_OK;
+}
+
+size_t nkimoe_ep_peer_buffer_bytes(int64_t num_ranks, int64_t max_tokens, int64_t H, int64_t K) {
+  if (num_ranks <= 0 || max_tokens < 0 || H <= 0 || K <= 0) return 0;
+  return ep_peer_layout(num_ranks, max_tokens, H, K).total;
+}
+
+int nkimoe_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  NKI_REQUIRE(bytes > 0 && ptr && ipc_handle, NKIMOE_ERR_INVALID_ARG, "peer alloc: bad arguments");
+  static_assert(sizeof(cudaIpcMemHandle_t) == NKIMOE_IPC_HANDLE_BYTES, "IPC handle size");
+  void* p = nullptr;
+  NKI_CUDA(cudaMalloc(&p, bytes));
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaMemset(p, 0, bytes);  // epoch flags start at 0
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(NKIMOE_ERR_CUDA, "peer alloc: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return NKIMOE_OK;
+}
+
+int nkimoe_peer_open(const void* ipc_handle, void** ptr) {
+  NKI_REQUIRE(ipc_handle && ptr, NKIMOE_ERR_INVALID_ARG, "peer open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  NKI_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return NKIMOE_OK;
+}
+
+int nkimoe_peer_close(void* ptr) {
+  NKI_REQUIRE(ptr, NKIMOE_ERR_INVALID_ARG, "peer close: null pointer");
+  NKI_CUDA(cudaIpcCloseMemHandle(ptr));
+  return NKIMOE_OK;
+}
+
+int nkimoe_peer_free(void* ptr) {
+  NKI_REQUIRE(ptr, NKIMOE_ERR_INVALID_ARG, "peer free: null pointer");
+  NKI_CUDA(cudaFree(ptr));
+  return NKIMOE_OK;
+}
+
+size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K, int64_t num_ranks,
+                                      int64_t max_tokens) {
+  if (num_ranks <= 0 || E % num_ranks != 0) return 0;
+  return peer_ws(T, H, I, E, K, num_ranks, max_tokens).total;
+}
+
+int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                           const void* w13_local, const void* w2_local, void* out, int64_t T, int64_t H, int64_t I,
+                           int64_t E, int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
+                           void* const* peer_buffers, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  const long long P = num_ranks, Tm = max_tokens;
+  int rc = check_moe_shapes(std::max<long long>(T, 1), H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
+  NKI_REQUIRE(P >= 1 && P <= kMaxPeers && E % P == 0 && rank >= 0 && rank < P, NKIMOE_ERR_UNSUPPORTED,
+              "ep peer: need 1 <= ranks <= %d dividing the experts, 0 <= rank < ranks", kMaxPeers);
+  NKI_REQUIRE(T >= 0 && T <= Tm && P * Tm * K < (1LL << 31) && P * Tm * (H / 8) < (1LL << 31) && E <= 256,
+              NKIMOE_ERR_UNSUPPORTED, "ep peer: tokens %lld exceed max_tokens %lld or the buffers are too large",
+              static_cast<long long>(T), Tm);
+  NKI_REQUIRE(epoch != 0, NKIMOE_ERR_INVALID_ARG, "ep peer: epoch must be nonzero (flags start at 0)");
+  const PeerWs W = peer_ws(T, H, I, E, K, P, Tm);
+  NKI_REQUIRE(workspace && workspace_bytes >= W.total && aligned16(workspace), NKIMOE_ERR_WORKSPACE,
+              "workspace %zu < %zu", workspace_bytes, W.total);
+  NKI_REQUIRE(peer_buffers && router_w && w13_local && w2_local && (T == 0 || (x && out)), NKIMOE_ERR_INVALID_ARG,
+              "null pointer");
+  EpPeerPtrs peers{};
+  for (long long r = 0; r < P; ++r) {
+    NKI_REQUIRE(peer_buffers[r] && (reinterpret_cast<uintptr_t>(peer_buffers[r]) & 255u) == 0,
+                NKIMOE_ERR_INVALID_ARG, "peer buffer %lld null or not 256-byte aligned", r);
+    peers.base[r] = static_cast<char*>(peer_buffers[r]);
+  }
+  NKI_REQUIRE(T == 0 || (aligned16(x) && aligned16(out)), NKIMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
+  const cudaStream_t s = as_stream(stream);
+  const EpPeerLayout PL = ep_peer_layout(P, Tm, H, K);
+  const long long El = E / P;
+  char* b = static_cast<char*>(workspace);
+  // routing of the local tokens (its status word is the call's status word)
+  const WsLayout R = ws_layout(T, H, I, E, K);
+  char* rb = b + W.route;
+  int* status = reinterpret_cast<int*>(rb + R.status);
+  int32_t* idx = reinterpret_cast<int32_t*>(rb + R.idx);
+  float* w = reinterpret_cast<float*>(rb + R.w);
+  unsigned* counters = reinterpret_cast<unsigned*>(b + W.counters);
+  NKI_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+  NKI_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned), s));
+  if (T > 0) {
+    rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, rb, R, status, s);
+    if (rc != NKIMOE_OK) return rc;
+  }
+  // (token, rank) pairs grouped by rank, tokens ascending
+  char* db = b + W.disp;
+  int32_t* offsets = reinterpret_cast<int32_t*>(db + 256);
+  int32_t* dest = offsets + round256(sizeof(int32_t) * (P + 1)) / sizeof(int32_t);
+  int32_t* row_token = dest + round256(sizeof(int32_t) * T * P) / sizeof(int32_t);
+  int32_t* row_slot = row_token + round256(sizeof(int32_t) * T * P) / sizeof(int32_t);
+  void* scratch = row_slot + round256(sizeof(int32_t) * T * P) / sizeof(int32_t);
+  int32_t* slot_in = reinterpret_cast<int32_t*>(b + W.slot_in);
+  int32_t* slot_out = reinterpret_cast<int32_t*>(b + W.slot_out);
+  if (T > 0)
+    NKI_CUDA(ep_dest_launch(idx, static_cast<int>(T), static_cast<int>(K), static_cast<int>(P), static_cast<int>(El),
+                            dest, s));
+  NKI_CUDA(permute_launch(dest, NKIMOE_I32, static_cast<int>(T), static_cast<int>(P), static_cast<int>(P), row_token,
+                          row_slot, slot_in, offsets, scratch, status, s));
+  // rows to their owners' buffers, then this rank's incoming rows
+  NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets, slot_in,
+                               slot_out, static_cast<int>(T), static_cast<int>(H), static_cast<int>(K),
+                               static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), static_cast<int>(rank),
+                               peers, PL, counters, epoch, s));
+  char* own = peers.base[rank];
+  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.disp_flag), static_cast<int>(P), epoch,
+                               status, s));
+  int32_t* recv_slots = reinterpret_cast<int32_t*>(own + PL.recv_slots);
+  NKI_CUDA(ep_peer_mask_launch(recv_slots, reinterpret_cast<const int32_t*>(own + PL.counts), static_cast<int>(P),
+                               static_cast<int>(Tm), static_cast<int>(K), s));
+  // this rank's experts over every region; sums go back to the sources
+  const PeerCombine pc{peers, PL, static_cast<int>(P), static_cast<int>(rank), static_cast<int>(Tm), counters + 1,
+                       epoch};
+  rc = experts_impl(own + PL.recv_x, w13_local, w2_local, recv_slots, NKIMOE_I32,
+                    reinterpret_cast<const float*>(own + PL.recv_w), nullptr, P * Tm, H, I, El, K, b + W.recv,
+                    workspace_bytes - W.recv, s, &pc, status);
+  if (rc != NKIMOE_OK) return rc;
+  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.res_flag), static_cast<int>(P), epoch,
+                               status, s));
+  if (T > 0)
+    NKI_CUDA(combine_launch(reinterpret_cast<const __nv_bfloat16*>(own + PL.ret_y), slot_out, nullptr,
+                            static_cast<__nv_bfloat16*>(out), static_cast<int>(T), static_cast<int>(P),
+                            static_cast<int>(H), s));
   return NKIMOE_OK;
 }
 

@@ -1,0 +1,276 @@
+// Expert-parallel exchange over peer memory (NVLink), without a collective
+// library on the data path.
+//
+// Every rank owns one buffer that all ranks map (CUDA IPC; no multicast
+// object), laid out by ep_peer_layout():
+//   disp_flag[P], res_flag[P]  u32 epoch flags (written by the peers)
+//   counts[P]                  i32 rows sent by each source this step
+//   recv_slots [P][Tm][K]      i32 local expert ids (-1: empty slot)
+//   recv_w     [P][Tm][K]      f32 routing weights
+//   recv_x     [P][Tm][H]      bf16 token rows, region s written by source s
+//   ret_y      [P][Tm][H]      bf16 partial sums, region d written by rank d
+// Source s sends token t to rank d once when any of t's experts lives on d
+// (the de-duplicated dispatch) as row j of region s of d's buffer; rank d runs
+// its local experts over all regions (empty slots skipped) and writes row j's
+// weighted sum into region d of s's ret_y; s adds its P partial sums.
+//
+// Publication: each CTA of a sending kernel fences its peer stores at system
+// scope, the last CTA to finish (a counter in local memory) publishes the
+// counts and then the epoch flag with st.release.sys; a waiting rank polls its
+// own flags with ld.acquire.sys under a bounded budget.  Flags hold the step's
+// epoch (increasing), so they never need resetting.  Region reuse is ordered
+// by the protocol itself: a rank writes into a peer's regions for step n+1
+// only after it has that peer's step-n results.
+#include "kernels.h"
+
+namespace nkimoe {
+
+namespace {
+
+// ~10 s at 2 GHz: a peer that has not reached this step by then is reported
+constexpr long long kPeerWaitBudgetCycles = 20000000000LL;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct EpPeerView {
+  uint32_t* disp_flag;
+  uint32_t* res_flag;
+  int32_t* counts;
+  int32_t* recv_slots;
+  float* recv_w;
+  __nv_bfloat16* recv_x;
+  __nv_bfloat16* ret_y;
+};
+
+__device__ __forceinline__ EpPeerView view_of(char* base, const EpPeerLayout& L) {
+  EpPeerView v;
+  v.disp_flag = reinterpret_cast<uint32_t*>(base + L.disp_flag);
+  v.res_flag = reinterpret_cast<uint32_t*>(base + L.res_flag);
+  v.counts = reinterpret_cast<int32_t*>(base + L.counts);
+  v.recv_slots = reinterpret_cast<int32_t*>(base + L.recv_slots);
+  v.recv_w = reinterpret_cast<float*>(base + L.recv_w);
+  v.recv_x = reinterpret_cast<__nv_bfloat16*>(base + L.recv_x);
+  v.ret_y = reinterpret_cast<__nv_bfloat16*>(base + L.ret_y);
+  return v;
+}
+
+// The last CTA of the grid to get here (after every CTA fenced its stores at
+// system scope) returns true.  The counter is left at zero for the next use.
+__device__ __forceinline__ bool last_block_done(unsigned* counter) {
+  __shared__ bool last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(counter, 1u);
+    last = prev == gridDim.x - 1;
+    if (last) *counter = 0;
+  }
+  __syncthreads();
+  return last;
+}
+
+// Source side: send row r (token row_token[r], destination d = row_slot[r] % P,
+// j = r - rank_offsets[d]) to region src of d's buffer: the token row, its K
+// slots as d sees them and their weights.  Also rewrites slot_row for the final
+// sum: (t, d) -> d * Tm + j in this rank's ret_y.  One warp per row.
+__global__ void __launch_bounds__(256) ep_peer_send_kernel(
+    const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx, const float* __restrict__ w,
+    const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
+    const int32_t* __restrict__ rank_offsets, const int32_t* __restrict__ slot_row_in,
+    int32_t* __restrict__ slot_row_out, int T, int H, int K, int P, int El, int Tm, int src, EpPeerPtrs peers,
+    EpPeerLayout L, unsigned* counter, uint32_t epoch) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long rows = rank_offsets[P];
+  const int chunks = H >> 3;
+  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += nw) {
+    const int t = row_token[r];
+    const int d = row_slot[r] % P;
+    const long long j = r - rank_offsets[d];
+    const EpPeerView pv = view_of(peers.base[d], L);
+    const long long dst_row = static_cast<long long>(src) * Tm + j;
+    const uint4* s4 = reinterpret_cast<const uint4*>(x + static_cast<long long>(t) * H);
+    uint4* d4 = reinterpret_cast<uint4*>(pv.recv_x + dst_row * H);
+    for (int c0 = lane; c0 < chunks; c0 += 256) {
+      uint4 v[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (c0 + 32 * q < chunks) v[q] = s4[c0 + 32 * q];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (c0 + 32 * q < chunks) d4[c0 + 32 * q] = v[q];
+    }
+    if (lane < K) {
+      const int e = idx[static_cast<long long>(t) * K + lane];
+      const bool mine = e >= d * El && e < (d + 1) * El;
+      pv.recv_slots[dst_row * K + lane] = mine ? e - d * El : -1;
+      pv.recv_w[dst_row * K + lane] = mine ? w[static_cast<long long>(t) * K + lane] : 0.f;
+    }
+  }
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < static_cast<long long>(T) * P;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int d = static_cast<int>(i % P);
+    const int sr = slot_row_in[i];
+    slot_row_out[i] = sr >= 0 ? d * Tm + (sr - rank_offsets[d]) : -1;
+  }
+  if (last_block_done(counter) && threadIdx.x < P) {
+    const int d = threadIdx.x;
+    const EpPeerView pv = view_of(peers.base[d], L);
+    pv.counts[src] = rank_offsets[d + 1] - rank_offsets[d];
+    __threadfence_system();
+    st_release_sys(pv.disp_flag + src, epoch);
+  }
+}
+
+// Poll this rank's P flags until each holds `epoch` (bounded).  One warp.
+__global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, uint32_t epoch, int* status) {
+  const int lane = threadIdx.x;
+  bool ok = true;
+  if (lane < P) {
+    const long long t0 = clock64();
+    while (static_cast<int>(ld_acquire_sys(flags + lane) - epoch) < 0) {
+      if (clock64() - t0 > kPeerWaitBudgetCycles) {
+        ok = false;
+        break;
+      }
+      __nanosleep(200);
+    }
+  }
+  if (!ok) atomicOr(status, kDevErrTimeout);
+}
+
+// Receiver: rows past each source's count get empty slots (the region holds
+// whatever an earlier step left there).
+__global__ void ep_peer_mask_kernel(int32_t* __restrict__ slots, const int32_t* __restrict__ counts, int P, int Tm,
+                                    int K) {
+  const long long n = static_cast<long long>(P) * Tm * K;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / K;
+    const int s = static_cast<int>(row / Tm);
+    const long long j = row - static_cast<long long>(s) * Tm;
+    if (j >= counts[s]) slots[i] = -1;
+  }
+}
+
+// Receiver: the routing-weighted sum of row r's K expert outputs (fp32, k
+// ascending, as combine_kernel), stored straight into region `me` of the
+// source's ret_y (source s = r / Tm, row j = r % Tm).  Rows without a local
+// expert are skipped.  The last CTA raises every source's result flag.
+__global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat16* __restrict__ y,
+                                                              const int32_t* __restrict__ slot_row, int rows, int K,
+                                                              int H, int Tm, int me, EpPeerPtrs peers,
+                                                              EpPeerLayout L, int P, unsigned* counter,
+                                                              uint32_t epoch) {
+  const uint32_t chunks = static_cast<uint32_t>(H) >> 3;
+  const uint32_t n = static_cast<uint32_t>(rows) * chunks;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint32_t r = i / chunks;
+    const uint32_t c = i - r * chunks;
+    float acc[8] = {};
+    bool any = false;
+    for (int k = 0; k < K; ++k) {
+      const int yr = slot_row[static_cast<long long>(r) * K + k];
+      if (yr < 0) continue;
+      any = true;
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(y + static_cast<long long>(yr) * H) + c);
+      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+      acc[0] += a.x;
+      acc[1] += a.y;
+      acc[2] += b.x;
+      acc[3] += b.y;
+      acc[4] += cc.x;
+      acc[5] += cc.y;
+      acc[6] += d.x;
+      acc[7] += d.y;
+    }
+    if (!any) continue;
+    const int s = static_cast<int>(r / static_cast<uint32_t>(Tm));
+    const long long j = r - static_cast<uint32_t>(s) * static_cast<uint32_t>(Tm);
+    const EpPeerView pv = view_of(peers.base[s], L);
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(pv.ret_y + (static_cast<long long>(me) * Tm + j) * H)[c] = o;
+  }
+  if (last_block_done(counter) && threadIdx.x < P) {
+    const EpPeerView pv = view_of(peers.base[threadIdx.x], L);
+    st_release_sys(pv.res_flag + me, epoch);
+  }
+}
+
+unsigned grid_cap(long long work, int threads) {
+  const long long b = (work + threads - 1) / threads;
+  const long long cap = static_cast<long long>(device_sm_count()) * 8;
+  return static_cast<unsigned>(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+size_t r256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+}  // namespace
+
+EpPeerLayout ep_peer_layout(long long P, long long Tm, long long H, long long K) {
+  EpPeerLayout L{};
+  size_t o = 0;
+  L.disp_flag = o;
+  o += r256(sizeof(uint32_t) * P);
+  L.res_flag = o;
+  o += r256(sizeof(uint32_t) * P);
+  L.counts = o;
+  o += r256(sizeof(int32_t) * P);
+  L.recv_slots = o;
+  o += r256(sizeof(int32_t) * P * Tm * K);
+  L.recv_w = o;
+  o += r256(sizeof(float) * P * Tm * K);
+  L.recv_x = o;
+  o += r256(sizeof(uint16_t) * P * Tm * H);
+  L.ret_y = o;
+  o += r256(sizeof(uint16_t) * P * Tm * H);
+  L.total = o;
+  return L;
+}
+
+cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
+                                const int32_t* row_slot, const int32_t* rank_offsets, const int32_t* slot_row_in,
+                                int32_t* slot_row_out, int T, int H, int K, int P, int El, int Tm, int src,
+                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter, uint32_t epoch,
+                                cudaStream_t s) {
+  // one warp per send row (at most T * P rows); at least one CTA so that the
+  // flags are raised even when nothing is sent
+  const unsigned grid = grid_cap(static_cast<long long>(T) * P * 32, 256);
+  ep_peer_send_kernel<<<grid, 256, 0, s>>>(x, idx, w, row_token, row_slot, rank_offsets, slot_row_in, slot_row_out, T,
+                                           H, K, P, El, Tm, src, peers, L, counter, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, uint32_t epoch, int* status, cudaStream_t s) {
+  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, P, epoch, status);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, int Tm, int K, cudaStream_t s) {
+  ep_peer_mask_kernel<<<grid_cap(static_cast<long long>(P) * Tm * K, 256), 256, 0, s>>>(slots, counts, P, Tm, K);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
+                                   int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
+                                   uint32_t epoch, cudaStream_t s) {
+  if (static_cast<long long>(rows) * (H / 8) >= (1LL << 31)) return cudaErrorInvalidValue;
+  const unsigned grid = grid_cap(static_cast<long long>(rows) * (H / 8), 256);
+  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, rows, K, H, Tm, me, peers, L, P, counter, epoch);
+  return cudaGetLastError();
+}
+
+}  // namespace nkimoe

@@ -1,0 +1,136 @@
+"""Expert-parallel sparse-MoE block exchanging over peer memory (NVLink).
+
+The same partitioning as :class:`nki_moe_b200.ep.ExpertParallelMoE` (rank r
+owns experts ``[r*E/P, (r+1)*E/P)``, each rank keeps its own tokens, one row
+per (token, owning rank)), but the exchange is done by the library's own
+kernels with stores into the other GPUs' memory instead of NCCL all-to-alls,
+and the whole block is one stream-ordered library call per step with no host
+synchronisation (``nkimoe_ep_peer_forward``):
+
+    route -> sort (token, rank) pairs -> store rows into the owners' buffers
+    -> wait for the P senders -> local experts over the received rows -> store
+    each row's weighted sum back into its sender's buffer -> wait -> sum
+
+Every rank allocates one exchange buffer with ``cudaMalloc`` and shares it by
+CUDA IPC (handles swapped through the process group); no NVLink multicast
+object is created.  Waits for peers are bounded on the device (~10 s) and
+reported in the status word (``NKIMOE_SYNC_CHECK=1`` raises on it).
+
+The reference leaves expert parallelism to NxDI (``moe_ep_degree``,
+qwen.py:272, :515).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from . import ops
+from ._lib import call, size_call
+
+IPC_HANDLE_BYTES = 64
+
+
+class PeerExpertParallelMoE(nn.Module):
+    """``forward(x [T, H]) -> [T, H]`` for this rank's ``T <= max_tokens``
+    tokens.  Without an initialised process group (or with a group of one)
+    it runs as a single rank that sends to itself."""
+
+    def __init__(self, router_w: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor,
+                 num_experts: int, top_k: int, max_tokens: int, group=None, router_bias: torch.Tensor | None = None):
+        super().__init__()
+        distributed = dist.is_available() and dist.is_initialized()
+        self.group = (group if group is not None else dist.group.WORLD) if distributed else None
+        self.world = dist.get_world_size(self.group) if distributed else 1
+        self.rank = dist.get_rank(self.group) if distributed else 0
+        if num_experts % self.world or gate_up_local.shape[0] != num_experts // self.world:
+            raise ValueError("local expert weights do not match num_experts / world size")
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        self.num_experts, self.top_k, self.max_tokens = num_experts, top_k, max_tokens
+        self.device = gate_up_local.device
+        self.hidden = gate_up_local.shape[1]
+        self.inter = gate_up_local.shape[2] // 2
+        self.router_w = router_w.detach().float().contiguous()
+        self.router_bias = router_bias.detach().float().contiguous() if router_bias is not None else None
+        self.router_split = ops.router_split(self.router_w) if num_experts % 128 == 0 else None
+        self.gate_up_local, self.down_local = gate_up_local, down_local
+        self.epoch = 0
+        self._own = None
+        self._opened = []
+        self.bases = self._setup_buffers()
+
+    @classmethod
+    def from_dense(cls, moe, max_tokens: int, group=None):
+        """Slice this rank's experts out of an ``NKIMoESimple`` holding all of them."""
+        distributed = dist.is_available() and dist.is_initialized()
+        g = (group if group is not None else dist.group.WORLD) if distributed else None
+        world = dist.get_world_size(g) if distributed else 1
+        rank = dist.get_rank(g) if distributed else 0
+        el = moe.num_experts // world
+        lo, hi = rank * el, (rank + 1) * el
+        return cls(moe.router.weight, moe.gate_up_proj.detach()[lo:hi].contiguous(),
+                   moe.down_proj.detach()[lo:hi].contiguous(), moe.num_experts, moe.top_k, max_tokens, group=g,
+                   router_bias=moe.router_bias)
+
+    def packed(self):
+        return ops.packed_experts(self.gate_up_local, self.down_local, "nxd")
+
+    def _setup_buffers(self):
+        nbytes = size_call("nkimoe_ep_peer_buffer_bytes", self.world, self.max_tokens, self.hidden, self.top_k)
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            call("nkimoe_peer_alloc", nbytes, ctypes.byref(ptr), handle)
+            self._own = ptr.value
+            if self.world == 1:
+                return [self._own]
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+            bases = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                hb = (ctypes.c_uint8 * IPC_HANDLE_BYTES).from_buffer_copy(h)
+                call("nkimoe_peer_open", hb, ctypes.byref(p))
+                self._opened.append(p.value)
+                bases.append(p.value)
+        return bases
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x = ops._contig(ops._cuda(x, "x"), torch.bfloat16)
+        T, H = x.shape
+        if T > self.max_tokens or H != self.hidden:
+            raise ValueError(f"x [{T}, {H}] does not fit max_tokens {self.max_tokens} / hidden {self.hidden}")
+        E, K, I, P = self.num_experts, self.top_k, self.inter, self.world
+        pe = self.packed()
+        nbytes = size_call("nkimoe_ep_peer_workspace_bytes", T, H, I, E, K, P, self.max_tokens)
+        ws = ops.workspace(x.device, nbytes)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+        self.epoch = self.epoch % 0xFFFFFFFF + 1  # nonzero, increasing between steps
+        bases = (ctypes.c_void_p * P)(*self.bases)
+        call("nkimoe_ep_peer_forward", ops._p(x), ops._p(self.router_w), ops._p(self.router_bias),
+             ops._p(self.router_split), ops._p(pe.w13), ops._p(pe.w2), ops._p(out), T, H, I, E, K, P, self.rank,
+             self.max_tokens, bases, self.epoch, ops._p(ws), ws.numel(), ops._s(x))
+        if ops.sync_check_enabled():
+            ops.read_status(ws)
+        return out
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after every rank is
+        done with the exchange)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                call("nkimoe_peer_close", ctypes.c_void_p(p))
+            call("nkimoe_peer_free", ctypes.c_void_p(self._own))
+        self._opened, self._own = [], None

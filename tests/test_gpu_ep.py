@@ -10,6 +10,7 @@ import torch
 
 import oracle
 from nki_moe_b200 import _lib, ops
+from nki_moe_b200.workloads import WORKLOADS, make_moe_inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -107,6 +108,33 @@ def test_given_routing_block_skips_empty_slots():
     assert oracle.normwise_rel_err(out, ref) < 2e-2 and oracle.cosine(out, ref) > 0.999
 
 
+def test_peer_ep_single_rank_equals_block():
+    """The peer-memory EP block as a single rank (rows sent to itself, epoch
+    flags, masking of rows left from an earlier, larger step) equals the
+    single-GPU block bit for bit, step after step."""
+    from nki_moe_b200.ep_peer import PeerExpertParallelMoE
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+
+    wl = WORKLOADS["c3"]
+    inp = make_moe_inputs(wl, device="cuda", tokens=1024)
+    moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        moe.router.weight.copy_(inp["router"])
+        moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
+        moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+    peer = PeerExpertParallelMoE.from_dense(moe, max_tokens=1024)
+    try:
+        for step, T in enumerate((1024, 600, 1024)):
+            x = torch.randn(T, wl.hidden, generator=torch.Generator(device="cuda").manual_seed(70 + step),
+                            device="cuda").to(torch.bfloat16)
+            y = peer(x)
+            assert ops.read_status(ops.workspace(x.device, 1)) == 0  # no bounded wait ran out
+            ref = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k)
+            assert torch.equal(y, ref), f"step {step}: max diff {(y.float() - ref.float()).abs().max().item()}"
+    finally:
+        peer.close()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -139,7 +167,19 @@ def _ep_worker(rank, world, port, out_dir):
     y_dedup = ExpertParallelMoE.from_dense(moe, dedup=True)(x)
     y_ep = ExpertParallelMoE.from_dense(moe, dedup=False)(x)
     y_one = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k)
+    # peer-memory exchange: two steps (the second with fewer tokens on rank 1)
+    from nki_moe_b200.ep_peer import PeerExpertParallelMoE
+    peer = PeerExpertParallelMoE.from_dense(moe, max_tokens=1024)
+    x2 = x[: 1024 if rank == 0 else 700].flip(0).contiguous()
+    y_peer1 = peer(x)
+    y_peer2 = peer(x2)
+    assert ops.read_status(ops.workspace(x.device, 1)) == 0  # no bounded wait ran out
+    y_dedup2 = ExpertParallelMoE.from_dense(moe, dedup=True)(x2)
     torch.cuda.synchronize()
+    peer.close()
+    np.save(os.path.join(out_dir, f"peer{rank}.npy"), y_peer1.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"peer2_{rank}.npy"), y_peer2.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"dedup2_{rank}.npy"), y_dedup2.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"dedup{rank}.npy"), y_dedup.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"ep{rank}.npy"), y_ep.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"one{rank}.npy"), y_one.float().cpu().numpy())
@@ -163,3 +203,7 @@ def test_expert_parallel_two_gpus_matches_single_gpu(tmp_path):
         # final sum, so the block-output tolerance applies
         d = np.load(tmp_path / f"dedup{r}.npy")
         assert oracle.normwise_rel_err(d, b) < 2e-2 and oracle.cosine(d, b) > 0.999
+        # the peer-memory exchange computes exactly what the NCCL de-duplicated
+        # exchange computes (same rows, same order, same sums)
+        assert np.array_equal(np.load(tmp_path / f"peer{r}.npy"), d), f"rank {r}: peer != dedup"
+        assert np.array_equal(np.load(tmp_path / f"peer2_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
