@@ -64,7 +64,10 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * 0 = off),
  * "gather_fused" (GEMM-1 loads its token rows itself instead of a separate
  * gather kernel writing them out: 1 with cp.async in its producer warp,
- * 2 with TMA tile::gather4; 0 = separate gather kernel).
+ * 2 with TMA tile::gather4; 0 = separate gather kernel),
+ * "epilogue_staging" (prefill GEMM bf16 outputs written through a per-warp
+ * shared-memory tile as whole-sector row stores: bit 0 the SwiGLU output,
+ * bit 1 the routing-weight-scaled output; default 3).
  * No reference counterpart (NKI tile sizes are compile-time constants,
  * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */

@@ -62,6 +62,7 @@ inline void mark(int stage, cudaStream_t s) {
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
+std::atomic<int> g_stage_stores{3};  // rows-schedule epilogue staging: bit 0 SwiGLU, bit 1 scaled bf16
 std::atomic<int> g_gather_fused{0};  // GEMM-1 gathers its rows itself: 1 cp.async, 2 TMA gather4
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
 
@@ -169,6 +170,7 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.tma_gather4 = gather4 ? 1 : 0;
   p.row_weight = row_weight;
   p.prefetch = g_prefetch.load();
+  p.stage_stores = g_stage_stores.load();
   p.epilogue = epilogue;
   p.out = out;
   p.out_ld = out_ld;
@@ -381,6 +383,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "weights_rows" && (value == 0 || value == 16 || value == 32 || value == 64)) {
     g_weights_rows = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "epilogue_staging" && value >= 0 && value <= 3) {
+    g_stage_stores = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "gather_fused" && value >= 0 && value <= 2) {

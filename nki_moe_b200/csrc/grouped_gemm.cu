@@ -161,12 +161,43 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
   }
 }
 
+// Store 32 bf16 values of this lane's output row (columns [col, col + 32))
+// through the warp's 32 x 32 staging tile: each lane writes its row, then lane
+// l stores 16 bytes of row l / 4 + 8 i, so one store instruction covers 8 rows
+// x 64 contiguous bytes (whole sectors) instead of 32 rows x 16 bytes.
+__device__ __forceinline__ void store_row32_staged(__nv_bfloat16 (*st)[40], __nv_bfloat16* out, long long ld,
+                                                   long long orow, bool valid, long long col, const float (&v)[32],
+                                                   int lane) {
+  uint4* srow = reinterpret_cast<uint4*>(&st[lane][0]);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+    u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+    u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+    u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+    srow[q] = u;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = (lane >> 2) + 8 * i;
+    const long long o = __shfl_sync(0xffffffffu, orow, rr);
+    const bool vr = __shfl_sync(0xffffffffu, valid ? 1 : 0, rr) != 0;
+    if (vr)
+      *reinterpret_cast<uint4*>(out + o * ld + col + (lane & 3) * 8) =
+          *reinterpret_cast<const uint4*>(&st[rr][(lane & 3) * 8]);
+  }
+  __syncwarp();
+}
+
 // Epilogue of a rows-schedule tile for one thread = one output row: reads the
 // row's BN accumulator columns from tensor memory (all lanes of the warp must
-// call it: tcgen05.ld is warp-collective) and stores them per p.epilogue.
+// call it: tcgen05.ld is warp-collective) and stores them per p.epilogue
+// (bf16 outputs through the warp's staging tile `st`).
 template <int BN>
 __device__ __forceinline__ void rows_epilogue(const GroupedGemmParams& p, uint32_t tbase, int fblk, long long orow,
-                                              bool valid, float scale) {
+                                              bool valid, float scale, __nv_bfloat16 (*st)[40], int lane) {
   if (p.epilogue == kEpiSwiGLU) {
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
 #pragma unroll 1
@@ -176,13 +207,12 @@ __device__ __forceinline__ void rows_epilogue(const GroupedGemmParams& p, uint32
         float g[32], u[32];
         tmem_ld_cols<32>(tbase + blk * 128 + half * 32, g);
         tmem_ld_cols<32>(tbase + blk * 128 + 64 + half * 32, u);
-        if (valid) {
-          float h[32];
+        float h[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) h[j] = silu_f(g[j]) * u[j];
-          const long long col = static_cast<long long>(fblk) * (BN / 2) + blk * 64 + half * 32;
-          store_bf16x32(out + orow * p.out_ld + col, h);
-        }
+        for (int j = 0; j < 32; ++j) h[j] = silu_f(g[j]) * u[j];
+        const long long col = static_cast<long long>(fblk) * (BN / 2) + blk * 64 + half * 32;
+        if (p.stage_stores & 1) store_row32_staged(st, out, p.out_ld, orow, valid, col, h, lane);
+        else if (valid) store_bf16x32(out + orow * p.out_ld + col, h);
       }
     }
   } else if (p.epilogue == kEpiScaleBf16 || p.epilogue == kEpiStoreBf16) {
@@ -191,11 +221,11 @@ __device__ __forceinline__ void rows_epilogue(const GroupedGemmParams& p, uint32
     for (int c = 0; c < BN; c += 32) {
       float v[32];
       tmem_ld_cols<32>(tbase + c, v);
-      if (valid) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= scale;
-        store_bf16x32(out + orow * p.out_ld + static_cast<long long>(fblk) * BN + c, v);
-      }
+      for (int j = 0; j < 32; ++j) v[j] *= scale;
+      const long long col = static_cast<long long>(fblk) * BN + c;
+      if (p.stage_stores & 2) store_row32_staged(st, out, p.out_ld, orow, valid, col, v, lane);
+      else if (valid) store_bf16x32(out + orow * p.out_ld + col, v);
     }
   } else {  // kEpiStoreF32
     float* out = static_cast<float*>(p.out);
@@ -258,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedCtl ctl;
+  __shared__ __align__(16) __nv_bfloat16 stg[4][32][40];  // per epilogue warp: output staging
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * A_BYTES;
@@ -445,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tcgen05_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 
-      rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale);
+      rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale, stg[quarter], lane);
       tcgen05_fence_before();
       mbar_arrive(&ctl.acc_empty[acc]);
     }
@@ -483,6 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ SharedCtl ctl;
+  __shared__ __align__(16) __nv_bfloat16 stg[4][32][40];  // per epilogue warp: output staging
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * A_BYTES;
@@ -631,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) break;
       tcgen05_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
-      rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale);
+      rows_epilogue<BN>(p, tbase, tc.fblk, orow, valid, scale, stg[quarter], lane);
       tcgen05_fence_before();
       __syncwarp();
       if (lane == 0) {

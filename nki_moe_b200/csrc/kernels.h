@@ -148,6 +148,8 @@ struct GroupedGemmParams {
   const int32_t* row_slot;
   const float* row_weight;    // ... or row_weight[r] when given (permuted order, one coalesced load)
   int prefetch;               // K blocks of the next tile prefetched into L2 at each tile start (0: off)
+  int stage_stores;           // rows schedule, bf16 outputs through a per-warp staging tile: bit 0 SwiGLU,
+                              // bit 1 scaled/plain bf16 (whole-sector row stores instead of 16-byte pieces)
   // Gathered activations: when a_row_map is set, activation row r of the
   // grouped problem is row a_row_map[r] of a_ptr (row stride a_ld elements),
   // loaded by the producer warp instead of a TMA tile load: with

@@ -408,6 +408,21 @@ def test_moe_block_gather4_skewed(schedule, rows):
         _lib.set_option("gemm_schedule", 0)
 
 
+@pytest.mark.parametrize("staging", [0, 1, 2])
+def test_epilogue_staging_is_bit_identical(staging):
+    """Writing the GEMM outputs through the shared-memory staging tile changes
+    only how the same bf16 values reach memory."""
+    inp = make_moe_inputs(WORKLOADS["c3"], tokens=1500)
+    try:
+        _lib.set_option("epilogue_staging", 3)
+        ref = _block_case(inp)[0]
+        _lib.set_option("epilogue_staging", staging)
+        out = _block_case(inp)[0]
+        assert np.array_equal(out, ref)
+    finally:
+        _lib.set_option("epilogue_staging", 3)
+
+
 def test_moe_block_deterministic(c1_inputs):
     a = _block_case(c1_inputs)[0]
     b = _block_case(c1_inputs)[0]
