@@ -227,26 +227,36 @@ __device__ __forceinline__ void rows_epilogue(const GroupedGemmParams& p, uint32
       if (p.stage_stores & 2) store_row32_staged(st, out, p.out_ld, orow, valid, col, v, lane);
       else if (valid) store_bf16x32(out + orow * p.out_ld + col, v);
     }
-  } else {  // kEpiStoreF32
+  } else {  // kEpiStoreF32: two 16-column passes through the staging tile (64 B per row)
     float* out = static_cast<float*>(p.out);
+    float(*sf)[20] = reinterpret_cast<float(*)[20]>(st);
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       float v[32];
       tmem_ld_cols<32>(tbase + c, v);
-      if (valid) {
-        const long long col0 = static_cast<long long>(fblk) * BN + c;
-        float4* dst = reinterpret_cast<float4*>(out + orow * p.out_ld + col0);
+      const long long col0 = static_cast<long long>(fblk) * BN + c;
+      if (p.col_bias) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 f = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          if (p.col_bias) {
-            f.x += p.col_bias[col0 + 4 * q];
-            f.y += p.col_bias[col0 + 4 * q + 1];
-            f.z += p.col_bias[col0 + 4 * q + 2];
-            f.w += p.col_bias[col0 + 4 * q + 3];
-          }
-          dst[q] = f;
+        for (int j = 0; j < 32; ++j) v[j] += p.col_bias[col0 + j];
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float4* srow = reinterpret_cast<float4*>(&sf[lane][0]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          srow[q] = make_float4(v[hf * 16 + 4 * q], v[hf * 16 + 4 * q + 1], v[hf * 16 + 4 * q + 2],
+                                v[hf * 16 + 4 * q + 3]);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = (lane >> 2) + 8 * i;
+          const long long o = __shfl_sync(0xffffffffu, orow, rr);
+          const bool vr = __shfl_sync(0xffffffffu, valid ? 1 : 0, rr) != 0;
+          if (vr)
+            *reinterpret_cast<float4*>(out + o * p.out_ld + col0 + hf * 16 + (lane & 3) * 4) =
+                *reinterpret_cast<const float4*>(&sf[rr][(lane & 3) * 4]);
         }
+        __syncwarp();
       }
     }
   }

@@ -154,9 +154,20 @@ __global__ void router_split_kernel(const float* __restrict__ wr, __nv_bfloat16*
   out[2 * plane + static_cast<long long>(e) * H + h] = lo;
 }
 
+// Order-preserving map of a float to u32 (a > b  <=>  key(a) > key(b)).
+__device__ __forceinline__ uint32_t order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;  // -0 == +0 (a tie, broken by id)
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 // Softmax -> top-k -> renormalise for one token held by a warp: lane l holds
 // the logits of experts l, l+32, ... (v[j] = expert l + 32 j, -inf past E).
 // Selection is by logit, ties to the lower id; p = exp(v - max) / sum.
+// Each lane sorts its VPT values (descending, ties by id); a round takes the
+// warp maximum of the lane heads (redux.sync on an order-preserving key) and
+// the lowest id holding it (a second redux), and the winning lane pops its
+// head.
 template <int VPT>
 __device__ __forceinline__ void topk_select_warp(const float (&v)[VPT], int E, int K, int lane,
                                                  int32_t* __restrict__ idx_row, float* __restrict__ w_row) {
@@ -171,33 +182,47 @@ __device__ __forceinline__ void topk_select_warp(const float (&v)[VPT], int E, i
     if (e < E) s += expf(v[j] - m);
   }
   s = warp_sum(s);
-  unsigned taken = 0;  // bit j: expert lane + 32j already selected
+  // this lane's candidates, sorted descending (stable: equal values keep the
+  // lower id first); past-E slots carry key 0 (below every real logit)
+  uint32_t key[VPT];
+  int id[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    id[j] = lane + 32 * j;
+    key[j] = id[j] < E ? order_key(v[j]) : 0u;
+  }
+#pragma unroll
+  for (int i = 1; i < VPT; ++i) {
+#pragma unroll
+    for (int j = i; j > 0; --j) {
+      const bool sw = key[j] > key[j - 1];
+      const uint32_t tk = sw ? key[j - 1] : key[j];
+      const int ti = sw ? id[j - 1] : id[j];
+      key[j - 1] = sw ? key[j] : key[j - 1];
+      id[j - 1] = sw ? id[j] : id[j - 1];
+      key[j] = tk;
+      id[j] = ti;
+    }
+  }
   int my_idx = 0;
   float my_p = 0.f;
   for (int r = 0; r < K; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && !((taken >> j) & 1u) && (v[j] > bv || (v[j] == bv && e < bi))) {
-        bv = v[j];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
+    const int win = static_cast<int>(
+        __reduce_min_sync(0xffffffffu, key[0] == best ? static_cast<uint32_t>(id[0]) : 0xffffffffu));
     if (lane == r) {
-      my_idx = bi;
-      my_p = expf(bv - m) / s;
+      my_idx = win;
+      const uint32_t bits = (best & 0x80000000u) ? (best & 0x7fffffffu) : ~best;
+      my_p = expf(__uint_as_float(bits) - m) / s;
+    }
+    if (id[0] == win) {  // the winner pops its head
+#pragma unroll
+      for (int j = 0; j + 1 < VPT; ++j) {
+        key[j] = key[j + 1];
+        id[j] = id[j + 1];
+      }
+      key[VPT - 1] = 0u;
+      id[VPT - 1] = 0x7fffffff;
     }
   }
   float tot = warp_sum(lane < K ? my_p : 0.f);
@@ -218,13 +243,26 @@ __global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restri
   const int lane = threadIdx.x & 31;
   const long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
+  // every split's partial is loaded before any is added (one round trip, not
+  // one per split); the sum keeps ascending split order
+  constexpr int kMaxSplits = 8;
+  float pv[VPT][kMaxSplits];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int e = lane + 32 * j;
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp)
+      pv[j][sp] = (e < E && sp < splits) ? partial[(static_cast<long long>(sp) * T + t) * E + e] : 0.f;
+  }
   float v[VPT];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int e = lane + 32 * j;
     if (e < E) {
-      float acc = partial[t * E + e];
-      for (int sp = 1; sp < splits; ++sp) acc += partial[(static_cast<long long>(sp) * T + t) * E + e];
+      float acc = pv[j][0];
+#pragma unroll
+      for (int sp = 1; sp < kMaxSplits; ++sp)
+        if (sp < splits) acc += pv[j][sp];
       if (bias) acc += bias[e];
       if (logits_out) logits_out[t * E + e] = acc;
       v[j] = acc;
@@ -403,7 +441,8 @@ cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, in
 cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,
                                          int tokens, int experts, int top_k, int32_t* idx, float* w, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  if (top_k < 1 || top_k > 32 || top_k > experts || experts > 256) return cudaErrorInvalidValue;
+  if (top_k < 1 || top_k > 32 || top_k > experts || experts > 256 || splits < 1 || splits > 8)
+    return cudaErrorInvalidValue;
   const int wpb = 8;
   const unsigned blocks = static_cast<unsigned>((tokens + wpb - 1) / wpb);
   const int vpt = (experts + 31) / 32;
