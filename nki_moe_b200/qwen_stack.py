@@ -142,6 +142,36 @@ class Qwen3MoEStack:
         return cls(cfg, bf(model.model.embed_tokens.weight), layers, bf(model.model.norm.weight),
                    bf(model.lm_head.weight), max_batch, max_seq)
 
+    @classmethod
+    def from_safetensors(cls, path: str, device="cuda", max_batch: int = 8,
+                         max_seq: int = 640) -> "Qwen3MoEStack":
+        """Load an HF Qwen3-MoE checkpoint directory (hub format, bf16 or FP8
+        with block scales) tensor by tensor: each layer's experts are read in
+        the HF fused layout and packed on the device (``hf_loader``)."""
+        from .hf_loader import Qwen3MoECheckpoint
+
+        ck = Qwen3MoECheckpoint(path, device=device)
+        cfg = Qwen3MoEConfig.from_hf(ck.hf_config)
+        pre = ck.reader.prefix
+        layers = []
+        for l in range(cfg.num_hidden_layers):  # noqa: E741
+            t = lambda rest, dtype=None: ck.layer_tensor(l, rest, dtype)  # noqa: E731
+            qkv = torch.cat([t("self_attn.q_proj.weight"), t("self_attn.k_proj.weight"),
+                             t("self_attn.v_proj.weight")], 0).contiguous()
+            gate_up, down = ck.experts(l)
+            I = gate_up.shape[1] // 2
+            experts = ops.PackedExperts(ops.pack_gate_up(gate_up, "hf"), ops.pack_down(down, "hf"),
+                                        cfg.num_experts, cfg.hidden_size, I)
+            del gate_up, down
+            layers.append(_Layer(t("input_layernorm.weight"), qkv, t("self_attn.q_norm.weight"),
+                                 t("self_attn.k_norm.weight"), t("self_attn.o_proj.weight"),
+                                 t("post_attention_layernorm.weight"),
+                                 t("mlp.gate.weight", torch.float32).contiguous(), experts))
+        lm = "lm_head.weight"
+        lm_head = ck.tensor(lm) if ck.reader.has(lm) else ck.tensor(f"{pre}embed_tokens.weight")
+        return cls(cfg, ck.tensor(f"{pre}embed_tokens.weight"), layers, ck.tensor(f"{pre}norm.weight"), lm_head,
+                   max_batch, max_seq)
+
     # ------------------------------------------------------------ layers
     def _moe(self, lyr: _Layer, x: torch.Tensor) -> torch.Tensor:
         return ops.moe_block(x, lyr.router_w, lyr.experts, self.cfg.num_experts_per_tok,

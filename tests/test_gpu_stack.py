@@ -123,3 +123,56 @@ def test_generate_timing_keys(pair):
     st.release_graph()
     assert toks.shape == (2, 6)
     assert t["ttft_ms"] > 0 and t["decode_tok_s"] > 0 and t["decode_steps"] == 5
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_from_safetensors_equals_from_hf(tmp_path, fp8):
+    """A hub-format checkpoint (per-expert weights; FP8 blocks with inverse
+    scales) loaded tensor by tensor gives the same stack as the in-memory HF
+    model holding the same (dequantised) weights: identical logits."""
+    import copy
+    import json
+
+    from safetensors.torch import load_file, save_file
+
+    from nki_moe_b200.qwen_stack import Qwen3MoEStack
+    from oracle import hf_convert
+
+    hf = tiny_hf(seed=7)
+    hf.save_pretrained(tmp_path, safe_serialization=True)
+    if fp8:
+        sd = load_file(str(tmp_path / "model.safetensors"))
+        ref_model = copy.deepcopy(hf)
+        params = dict(ref_model.named_parameters())
+        for k in [k for k in sd if ".mlp.experts." in k]:
+            w = sd[k].float()
+            scale = torch.zeros(w.shape[0] // 128, w.shape[1] // 128)
+            q = torch.empty_like(w, dtype=torch.float8_e4m3fn)
+            for i in range(scale.shape[0]):
+                for j in range(scale.shape[1]):
+                    t = w[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128]
+                    scale[i, j] = t.abs().max().clamp(min=1e-8) / 448.0
+                    q[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128] = (t / scale[i, j]).to(torch.float8_e4m3fn)
+            sd[k], sd[k + "_scale_inv"] = q, scale
+        save_file(sd, str(tmp_path / "model.safetensors"))
+        cfg = json.load(open(tmp_path / "config.json"))
+        cfg["quantization_config"] = {"quant_method": "fp8", "weight_block_size": [128, 128]}
+        json.dump(cfg, open(tmp_path / "config.json", "w"))
+        # the reference model holds the dequantised expert weights (qwen.py:101-116)
+        with torch.no_grad():
+            for li, lyr in enumerate(ref_model.model.layers):
+                ex = lyr.mlp.experts
+                for e in range(ex.gate_up_proj.shape[0]):
+                    deq = {n: hf_convert.dequantize_fp8_blocks(sd[f"model.layers.{li}.mlp.experts.{e}.{n}.weight"],
+                                                               sd[f"model.layers.{li}.mlp.experts.{e}.{n}.weight_scale_inv"],
+                                                               (128, 128), torch.float32)
+                           for n in ("gate_proj", "up_proj", "down_proj")}
+                    I = deq["gate_proj"].shape[0]
+                    ex.gate_up_proj[e, :I] = deq["gate_proj"]
+                    ex.gate_up_proj[e, I:] = deq["up_proj"]
+                    ex.down_proj[e] = deq["down_proj"]
+        hf = ref_model
+    a = Qwen3MoEStack.from_hf(hf, max_batch=2, max_seq=64)
+    b = Qwen3MoEStack.from_safetensors(str(tmp_path), max_batch=2, max_seq=64)
+    ids = torch.randint(0, 1024, (2, 24), generator=torch.Generator().manual_seed(9))
+    assert torch.equal(a.prefill(ids, all_logits=True), b.prefill(ids, all_logits=True))
