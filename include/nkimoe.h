@@ -40,7 +40,7 @@ extern "C" {
 
 /* device status bits (nkimoe_read_status) */
 #define NKIMOE_DEV_TIMEOUT 1       /* a bounded device-side wait ran out       */
-#define NKIMOE_DEV_BAD_INDEX 2     /* an expert id outside [0, num_experts)    */
+#define NKIMOE_DEV_BAD_INDEX 2     /* an expert id outside [0, num_experts) or a cache position outside [0, max_seq) */
 
 /* dtype codes */
 #define NKIMOE_F32 0
@@ -103,6 +103,34 @@ NKIMOE_API int nkimoe_add_rmsnorm(const void* x, const void* residual, void* res
 NKIMOE_API int nkimoe_qk_norm_rope(const void* qkv_in, void* qkv_out, const void* q_weight, const void* k_weight, int w_dtype,
                         const int64_t* positions, int64_t tokens, int n_heads, int n_kv_heads, int head_dim,
                         float rope_theta, float eps, void* stream);
+
+/* ---------------------------------------------------------------- decode attention */
+
+/* Workspace of nkimoe_decode_attention: a status word, one counter per
+ * (sequence, kv head) and the split partials.  It must be zero-filled once
+ * before its first use; every call leaves the counters at zero again. */
+NKIMOE_API size_t nkimoe_decode_attention_workspace_bytes(int64_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                                          int64_t max_seq);
+
+/* One decode step of grouped-query attention over a KV cache, fused with its
+ * inputs' preparation: for every sequence b at position p = positions[b *
+ * pos_stride] (pos_stride 0: one position for all), the step's fused QKV row
+ * qkv [B, (n_heads + 2*n_kv_heads) * 128] (bf16, before the q/k norms) gets
+ * per-head q/k RMSNorm + rotate-half RoPE (as nkimoe_qk_norm_rope), the new
+ * key and value are stored at position p of k_cache/v_cache
+ * [B, n_kv_heads, max_seq, 128] (bf16, one layer), and query head h attends,
+ * with weight softmax(scale * q.k), to positions 0..p of kv head
+ * h / (n_heads / n_kv_heads).  out: bf16 [B, n_heads * 128], the layout the
+ * O projection takes.  Positions outside [0, max_seq) are reported through
+ * the status word (NKIMOE_DEV_BAD_INDEX) and their rows are left unwritten.
+ * Reference: nki_flash_attention_decode (nki_attention.py:252-373, online
+ * softmax :333-359) with the q/k norms and RoPE of qwen_with_nki.py:330-350;
+ * the reference's kernel takes pre-rotated q/k and keeps no cache. */
+NKIMOE_API int nkimoe_decode_attention(const void* qkv, const void* q_weight, const void* k_weight, int w_dtype,
+                                       const int64_t* positions, int64_t pos_stride, void* k_cache, void* v_cache,
+                                       void* out, int64_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                       int64_t max_seq, float rope_theta, float eps, float scale, void* workspace,
+                                       size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- router */
 
@@ -181,7 +209,7 @@ NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const floa
  * while it records CUDA graphs).  It has no counterpart in the reference.
  * Same arguments and results as nkimoe_moe_block without the workspace: the
  * scratch is a fixed 8 MiB array inside the library, held by every GPU that
- * loads the library until the process exits (enough for up to 170 tokens at
+ * loads the library until the process exits (enough for up to 168 tokens at
  * H=2048, I=768, E=128, K=8; larger batches return NKIMOE_ERR_WORKSPACE
  * without touching the GPU).  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) and should come before any

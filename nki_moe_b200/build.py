@@ -23,8 +23,8 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(REPO, "_build")
 LIB = os.path.join(PKG, "libnkimoe.so")
 SOURCES = ["norm.cu", "router.cu", "permute.cu", "pack.cu", "grouped_gemm.cu", "ep_peer.cu", "capi.cu",
-           "noalloc.cu"]
-HEADERS = ["common.cuh", "kernels.h"]
+           "noalloc.cu", "attention.cu"]
+HEADERS = ["common.cuh", "kernels.h", "rope.cuh"]
 
 
 def nvcc() -> str:

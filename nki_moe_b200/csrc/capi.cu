@@ -92,8 +92,13 @@ WsLayout ws_layout(long long T, long long H, long long I, long long E, long long
   const long long TK = T * K;
   L.status = o; o += 256;
   L.logits = o; o += round256(sizeof(float) * T * E);
-  const long long splits = T > 0 ? router_splits_for(static_cast<int>(T), static_cast<int>(H), static_cast<int>(E)) : 1;
-  L.partial = o; o += round256(sizeof(float) * std::max<long long>(splits, 3) * T * E);
+  long long splits = 3;  // partial logits: tensor-core planes, split-K router or decode router slices
+  if (T > 0) {
+    splits = std::max<long long>(splits, router_splits_for(static_cast<int>(T), static_cast<int>(H), static_cast<int>(E)));
+    if (H % 128 == 0 && (T + 7) / 8 <= router_topk_max_groups())
+      splits = std::max<long long>(splits, router_topk_slices(static_cast<int>(T), static_cast<int>(H), static_cast<int>(E)));
+  }
+  L.partial = o; o += round256(sizeof(float) * splits * T * E);
   L.idx = o; o += round256(sizeof(int32_t) * TK);
   L.w = o; o += round256(sizeof(float) * TK);
   L.offsets = o; o += round256(sizeof(int32_t) * (E + 1));
@@ -219,11 +224,15 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
     mark(kStageTopk, s);
     NKI_CUDA(topk_softmax_partials_launch(partial, 3, router_bias, logits, static_cast<int>(T), static_cast<int>(E),
                                           static_cast<int>(K), idx, w, s));
-  } else if (router_topk_fused_supported(static_cast<int>(H), static_cast<int>(E), static_cast<int>(K))) {
-    // logits and top-k in one launch; the top-k stage marker follows it
+  } else if (router_topk_fused_supported(static_cast<int>(H), static_cast<int>(E), static_cast<int>(K)) &&
+             (T + 7) / 8 <= router_topk_max_groups()) {
+    // logits and top-k in one launch; the top-k stage marker follows it.  Its
+    // per-group counters sit in the status block after the status word, which
+    // every caller clears (256 bytes) before the block.
     NKI_CUDA(router_topk_fused_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
                                       static_cast<int>(T), static_cast<int>(H), static_cast<int>(E),
-                                      static_cast<int>(K), idx, w, s));
+                                      static_cast<int>(K), idx, w, reinterpret_cast<float*>(base + L.partial),
+                                      reinterpret_cast<int*>(base + L.status + 64), s));
     mark(kStageTopk, s);
   } else {
     float* partial = reinterpret_cast<float*>(base + L.partial);
@@ -449,6 +458,41 @@ int nkimoe_qk_norm_rope(const void* qkv_in, void* qkv_out, const void* q_weight,
   return NKIMOE_OK;
 }
 
+size_t nkimoe_decode_attention_workspace_bytes(int64_t batch, int n_heads, int n_kv_heads, int head_dim,
+                                               int64_t max_seq) {
+  if (batch < 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim != 128 || max_seq <= 0) return 0;
+  return decode_attention_workspace_bytes(batch, n_heads, n_kv_heads, static_cast<int>(max_seq));
+}
+
+int nkimoe_decode_attention(const void* qkv, const void* q_weight, const void* k_weight, int w_dtype,
+                            const int64_t* positions, int64_t pos_stride, void* k_cache, void* v_cache, void* out,
+                            int64_t batch, int n_heads, int n_kv_heads, int head_dim, int64_t max_seq,
+                            float rope_theta, float eps, float scale, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  NKI_REQUIRE(batch >= 0 && n_heads > 0 && n_kv_heads > 0 && max_seq > 0 && pos_stride >= 0,
+              NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(head_dim == 128, NKIMOE_ERR_UNSUPPORTED, "head_dim %d (only 128 is supported)", head_dim);
+  NKI_REQUIRE(n_heads % n_kv_heads == 0, NKIMOE_ERR_INVALID_ARG, "n_heads %d is not a multiple of n_kv_heads %d",
+              n_heads, n_kv_heads);
+  NKI_REQUIRE(n_heads / n_kv_heads <= 16, NKIMOE_ERR_UNSUPPORTED, "more than 16 query heads per kv head");
+  NKI_REQUIRE(max_seq <= (1LL << 30) && batch <= 65535 && n_kv_heads <= 65535, NKIMOE_ERR_UNSUPPORTED,
+              "shape too large");
+  NKI_REQUIRE(w_dtype == NKIMOE_F32 || w_dtype == NKIMOE_BF16, NKIMOE_ERR_INVALID_ARG, "bad weight dtype");
+  if (batch == 0) return NKIMOE_OK;
+  NKI_REQUIRE(qkv && q_weight && k_weight && positions && k_cache && v_cache && out && workspace,
+              NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(qkv) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out) && aligned16(workspace),
+              NKIMOE_ERR_INVALID_ARG, "qkv, caches, out and workspace must be 16-byte aligned");
+  const size_t need = decode_attention_workspace_bytes(batch, n_heads, n_kv_heads, static_cast<int>(max_seq));
+  NKI_REQUIRE(workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu bytes < %zu", workspace_bytes, need);
+  NKI_CUDA(decode_attention_launch(static_cast<const __nv_bfloat16*>(qkv), q_weight, k_weight, w_dtype,
+                                   reinterpret_cast<const long long*>(positions), pos_stride,
+                                   static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
+                                   static_cast<__nv_bfloat16*>(out), static_cast<int>(batch), n_heads, n_kv_heads,
+                                   static_cast<int>(max_seq), rope_theta, eps, scale, workspace, as_stream(stream)));
+  return NKIMOE_OK;
+}
+
 int nkimoe_router_logits(const void* x, const float* router_w, const float* router_bias, float* logits, int64_t T,
                          int64_t H, int64_t E, void* stream) {
   NKI_REQUIRE(T >= 0 && H > 0 && E > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
@@ -567,7 +611,7 @@ int nkimoe_moe_block(const void* x, const float* router_w, const float* router_b
   NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
   NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
   const cudaStream_t s = as_stream(stream);
-  NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
   if (T == 0) return NKIMOE_OK;
   NKI_REQUIRE(x && router_w && w13 && w2 && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
   NKI_REQUIRE(aligned16(x) && aligned16(router_w) && aligned16(w13) && aligned16(w2) && aligned16(out),
@@ -591,7 +635,7 @@ int nkimoe_read_status(void* workspace, void* stream, int* status_out) {
   NKI_CUDA(cudaStreamSynchronize(s));
   NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
   if (status_out) *status_out = v;
-  if (v != 0) return fail(NKIMOE_ERR_DEVICE, "device status 0x%x (1 = wait timeout, 2 = expert id out of range)", v);
+  if (v != 0) return fail(NKIMOE_ERR_DEVICE, "device status 0x%x (1 = wait timeout, 2 = expert id or cache position out of range)", v);
   return NKIMOE_OK;
 }
 
@@ -648,7 +692,7 @@ int nkimoe_route(const void* x, const float* router_w, const float* router_bias,
   const size_t need = nkimoe_route_workspace_bytes(T, H, E, K);
   NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
   const cudaStream_t s = as_stream(stream);
-  NKI_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), s));
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
   if (T == 0) return NKIMOE_OK;
   NKI_REQUIRE(x && router_w && topk_idx && topk_w && aligned16(x) && aligned16(router_w), NKIMOE_ERR_INVALID_ARG,
               "null or misaligned pointer");
@@ -853,7 +897,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   int32_t* idx = reinterpret_cast<int32_t*>(rb + R.idx);
   float* w = reinterpret_cast<float*>(rb + R.w);
   unsigned* counters = reinterpret_cast<unsigned*>(b + W.counters);
-  NKI_CUDA(cudaMemsetAsync(status, 0, sizeof(int), s));
+  NKI_CUDA(cudaMemsetAsync(status, 0, 256, s));  // status word and router counters
   NKI_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned), s));
   if (T > 0) {
     rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, rb, R, status, s);

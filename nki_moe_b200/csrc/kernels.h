@@ -41,6 +41,15 @@ cudaError_t qk_norm_rope_launch(const void* qkv_in, void* qkv_out, const void* q
                                 const long long* positions, long long tokens, int n_heads, int n_kv, int head_dim,
                                 float theta, float eps, cudaStream_t s);
 
+// ----------------------------------------------------------------- decode attention
+int decode_attention_chunk(int max_seq);
+size_t decode_attention_workspace_bytes(long long B, int n_heads, int n_kv, int max_seq);
+cudaError_t decode_attention_launch(const __nv_bfloat16* qkv, const void* qw, const void* kw, int w_dtype,
+                                    const long long* positions, long long pos_stride, __nv_bfloat16* k_cache,
+                                    __nv_bfloat16* v_cache, __nv_bfloat16* out, int B, int n_heads, int n_kv,
+                                    int max_seq, float theta, float eps, float scale, void* workspace,
+                                    cudaStream_t s);
+
 // ----------------------------------------------------------------- router
 // fp32 logits = x(bf16) . Wr(fp32)^T (+ bias), CUDA-core fp32 FMA, fixed order.
 cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits,
@@ -54,13 +63,18 @@ int router_splits_for(int tokens, int hidden, int experts);
 // softmax -> top-k (by logit, ties to the lower id) -> renormalise.
 cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
                                 cudaStream_t s);
-// Router logits + softmax + top-k in one launch for few tokens: 8-CTA
-// clusters, each CTA one eighth of the experts, top-k over distributed shared
-// memory.  Supported when E <= 256, H % 128 == 0, 1 <= K <= min(32, E).
+// Router logits + softmax + top-k in one launch for few tokens (T < 8 * 48):
+// CTAs over (8-expert block, hidden slice, 8-token group) write fp32 partial
+// logits [slice][T][E] to `partial`; the last CTA of a token group adds the
+// slices in order and selects its top-k.  `counters` (one int per token group,
+// zero on entry, left at zero) count the finished CTAs.  Supported when
+// E <= 256, H % 128 == 0, 1 <= K <= min(32, E).
 bool router_topk_fused_supported(int hidden, int experts, int top_k);
+int router_topk_slices(int tokens, int hidden, int experts);
+int router_topk_max_groups();
 cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                      int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
-                                     cudaStream_t s);
+                                     float* partial, int* counters, cudaStream_t s);
 // Same on logits given as `splits` fp32 partial sums [split][T][E] (+ bias[E]);
 // logits_out (nullable) receives the summed logits.
 cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,

@@ -6,6 +6,7 @@
 // K6: per-head q/k RMSNorm + rotate-half RoPE on a fused [Q | K | V] row
 //     (qwen_with_nki.py:330-350 with the HF Qwen3-MoE order: norm, then RoPE).
 #include "kernels.h"
+#include "rope.cuh"
 
 namespace nkimoe {
 
@@ -132,9 +133,86 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const TX* x, const TX* res
   }
 }
 
+// Few rows (a decode step): one CTA per row so that the row's loads are spread
+// over 256 threads and all of them -- x, residual and the norm weight -- are
+// in flight at once; the sum of squares is reduced across the CTA.  Rows of
+// up to kRowChunks * 8 * 256 elements.
+constexpr int kRowThreads = 256;
+constexpr int kRowChunks = 4;
+
+template <typename TX, typename TW, typename TO, bool kResidual>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_row_kernel(const TX* x, const TX* residual, TX* residual_out,
+                                                                  const TW* __restrict__ w, TO* out, int hidden,
+                                                                  float eps) {
+  __shared__ float red[kRowThreads / 32];
+  const long long row = blockIdx.x;
+  const int nchunk = hidden >> 3;
+  float v[kRowChunks][8], wv[kRowChunks][8];
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+      load8(x + row * hidden + c * 8, v[i]);
+      load8(w + c * 8, wv[i]);
+    }
+  }
+  if constexpr (kResidual) {
+    float r[kRowChunks][8];
+#pragma unroll
+    for (int i = 0; i < kRowChunks; ++i) {
+      const int c = threadIdx.x + i * kRowThreads;
+      if (c < nchunk) load8(residual + row * hidden + c * 8, r[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kRowChunks; ++i) {
+      const int c = threadIdx.x + i * kRowThreads;
+      if (c < nchunk) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[i][j];
+        round_bf16(v[i]);
+        store8(residual_out + row * hidden + c * 8, v[i]);
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRowThreads / 32; ++k) ss += red[k];
+  const float rinv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rinv * wv[i][j];
+      store8(out + row * hidden + c * 8, o);
+    }
+  }
+}
+
+constexpr long long kRowKernelMaxRows = 512;
+
 template <typename TX, typename TW, typename TO, bool kRes>
 cudaError_t launch_rms(const void* x, const void* res, void* res_out, const void* w, void* out, long long rows,
                        int hidden, float eps, cudaStream_t s) {
+  if (rows <= kRowKernelMaxRows && hidden <= kRowChunks * 8 * kRowThreads) {
+    rmsnorm_row_kernel<TX, TW, TO, kRes><<<static_cast<unsigned>(rows), kRowThreads, 0, s>>>(
+        static_cast<const TX*>(x), static_cast<const TX*>(res), static_cast<TX*>(res_out),
+        static_cast<const TW*>(w), static_cast<TO*>(out), hidden, eps);
+    return cudaGetLastError();
+  }
   const int warps = 8;
   const long long blocks = (rows + warps - 1) / warps;
   rmsnorm_kernel<TX, TW, TO, kRes><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(
@@ -175,22 +253,11 @@ cudaError_t add_rmsnorm_launch(const void* x, const void* residual, void* residu
 // [4l, 4l+4); its rotate-half partner lives in lane l ^ 16.
 namespace {
 
-__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
-  uint2 u = *reinterpret_cast<const uint2*>(p);
-  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
-  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
-}
-
-__device__ __forceinline__ float wload(const void* w, int w_dtype, int i) {
-  return w_dtype == kF32 ? static_cast<const float*>(w)[i]
-                         : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
-}
-
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, const void* qw,
                                                            const void* kw, int w_dtype,
                                                            const long long* __restrict__ positions, long long tokens,
                                                            int n_heads, int n_kv, float theta, float eps) {
-  constexpr int D = 128;
+  constexpr int D = kHeadDim;
   const int lane = threadIdx.x & 31;
   const int heads_total = n_heads + 2 * n_kv;
   const long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -199,39 +266,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __nv_bfloat16* 
   const int h = static_cast<int>(gw % heads_total);
   const long long base = t * heads_total * D + static_cast<long long>(h) * D + lane * 4;
   float v[4];
-  load4(in + base, v);
+  head_load4(in + base, v);
   if (h >= n_heads + n_kv) {  // V head: pass through
     if (in != out) *reinterpret_cast<uint2*>(out + base) = *reinterpret_cast<const uint2*>(in + base);
     return;
   }
-  const void* w = h < n_heads ? qw : kw;
-  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-  ss = warp_sum(ss);
-  const float rinv = rsqrtf(ss / static_cast<float>(D) + eps);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) v[j] = v[j] * rinv * wload(w, w_dtype, lane * 4 + j);
-  // rotate-half partner: element i pairs with i + 64 (first half) / i - 64
-  float pv[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) pv[j] = __shfl_xor_sync(0xffffffffu, v[j], 16);
-  const float pos = static_cast<float>(positions[t]);
-  const bool first = lane < 16;
   float o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int i = lane * 4 + j;
-    const int fi = i & (D / 2 - 1);  // frequency index (emb = cat(freqs, freqs))
-    const float inv_freq = 1.0f / powf(theta, static_cast<float>(2 * fi) / static_cast<float>(D));
-    const float ang = pos * inv_freq;
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
-    const float rot = first ? -pv[j] : pv[j];
-    o[j] = v[j] * cs + rot * sn;
-  }
-  uint2 u;
-  u.x = pack_bf16x2(o[0], o[1]);
-  u.y = pack_bf16x2(o[2], o[3]);
-  *reinterpret_cast<uint2*>(out + base) = u;
+  norm_rope_head128(v, h < n_heads ? qw : kw, w_dtype, static_cast<float>(positions[t]), theta, eps, lane, o);
+  head_store4(out + base, o);
 }
 
 }  // namespace

@@ -273,98 +273,121 @@ __global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restri
   topk_select_warp<VPT>(v, E, K, lane, idx_out + t * K, w_out + t * K);
 }
 
-// Router + softmax + top-k for few tokens (decode), in one launch: an 8-CTA
-// cluster takes 8 tokens; CTA c computes the fp32 logits of experts
-// [c EG, (c + 1) EG) for those tokens (it reads only its 1/8 of the router
-// weights), keeps them in shared memory, and after a cluster barrier warp 0
-// of CTA c gathers token t0 + c's E logits from the 8 CTAs (distributed
-// shared memory) and selects its top-k.  A logit is one fp32 FMA chain per
-// lane over k = 4 lane + 128 i + j, then a butterfly sum over the lanes.
-constexpr int kRouterCluster = 8;
+// Router + softmax + top-k for few tokens (decode), in one launch spread over
+// many SMs (the work is 2*T*H*E FLOP on E*H*4 bytes of weights, so a handful
+// of SMs would be compute-bound).  CTA (eb, s, g) computes fp32 partial
+// logits of experts [8 eb, 8 eb + 8) -- one per warp -- for the 8 tokens of
+// group g over the hidden slice s: lane (token tl, quarter kc) runs one FMA
+// chain over k = k0 + 32 kc + [0, 32) of every 128-wide block of the slice,
+// and the four quarters are added with a fixed butterfly.  The partials go to
+// partial[s][t][e]; the last CTA of the group to finish (device-scope counter,
+// no spinning) adds the slices in ascending order and selects each token's
+// top-k (one warp per token).  The counters start at zero (the caller clears
+// them with the status word) and are left at zero.
+constexpr int kRouterTokens = 8;
+constexpr int kRouterExpertsPerCta = 8;
+constexpr int kRouterMaxSlices = 8;
+constexpr int kRouterMaxGroups = 48;  // counters in the 256-byte status block, after 64 bytes
 
-template <int EG>
-__global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(256)
-    router_topk_cluster_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wr,
-                               const float* __restrict__ bias, float* __restrict__ logits_out, int T, int H, int E,
-                               int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-  extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [8][H]: the cluster's token rows
-  __shared__ float lg[kRouterCluster][EG];
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    router_topk_split_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wr,
+                             const float* __restrict__ bias, float* __restrict__ logits_out, int T, int H, int E,
+                             int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out, float* partial,
+                             int* counters, int kslice) {
+  __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();
-  const long long t0 = static_cast<long long>(blockIdx.x / kRouterCluster) * kRouterCluster;
-  // stage the 8 token rows: every thread's loads are issued before its stores
-  const int hc = H >> 3;  // 16-byte chunks per row
-  for (int i0 = threadIdx.x; i0 < kRouterCluster * hc; i0 += 8 * blockDim.x) {
-    uint4 u[8];
+  const int eb = blockIdx.x, sl = blockIdx.y, gi = blockIdx.z;
+  const int e = eb * kRouterExpertsPerCta + warp;
+  const int tl = lane >> 2, kc = lane & 3;
+  const long long t = static_cast<long long>(gi) * kRouterTokens + tl;
+  const int kb = sl * kslice, ke = min(H, kb + kslice);
+  float acc = 0.f;
+  if (e < E) {
+    const float* we = wr + static_cast<long long>(e) * H;
+    const __nv_bfloat16* xt = x + (t < T ? t : 0) * H;
+    // two 128-wide blocks per step: all of a lane's loads for them in flight
+    for (int k0 = kb + 32 * kc; k0 < ke; k0 += 256) {
+      const bool two = k0 + 128 < ke;
+      float4 w4[2][8];
+      uint4 xu[2][4];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int i = i0 + q * blockDim.x, r = i / hc, c = i - r * hc;
-      u[q] = make_uint4(0u, 0u, 0u, 0u);
-      if (i < kRouterCluster * hc && t0 + r < T) u[q] = reinterpret_cast<const uint4*>(x + (t0 + r) * H)[c];
-    }
+      for (int hb = 0; hb < 2; ++hb) {
+        const int k = k0 + 128 * hb;
+        const bool live = hb == 0 || two;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int i = i0 + q * blockDim.x, r = i / hc, c = i - r * hc;
-      if (i < kRouterCluster * hc) reinterpret_cast<uint4*>(xs + static_cast<long long>(r) * H)[c] = u[q];
+        for (int q = 0; q < 8; ++q)
+          w4[hb][q] = live ? *reinterpret_cast<const float4*>(we + k + 4 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          xu[hb][q] = live ? *reinterpret_cast<const uint4*>(xt + k + 8 * q) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        if (hb == 1 && !two) break;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 a = unpack_bf16x2(xu[hb][q].x), b = unpack_bf16x2(xu[hb][q].y);
+          const float2 c = unpack_bf16x2(xu[hb][q].z), d = unpack_bf16x2(xu[hb][q].w);
+          const float4 w0 = w4[hb][2 * q], w1 = w4[hb][2 * q + 1];
+          acc = fmaf(a.x, w0.x, acc);
+          acc = fmaf(a.y, w0.y, acc);
+          acc = fmaf(b.x, w0.z, acc);
+          acc = fmaf(b.y, w0.w, acc);
+          acc = fmaf(c.x, w1.x, acc);
+          acc = fmaf(c.y, w1.y, acc);
+          acc = fmaf(d.x, w1.z, acc);
+          acc = fmaf(d.y, w1.w, acc);
+        }
+      }
     }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  if (kc == 0 && e < E && t < T) __stcg(partial + (static_cast<long long>(sl) * T + t) * E + e, acc);
+
+  // the CTA barrier orders the partial stores before thread 0's fence and count
+  __syncthreads();
+  const int total = gridDim.x * gridDim.y;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int done = atomicAdd(counters + gi, 1);
+    s_last = (done == total - 1);
+    if (s_last) __threadfence();
   }
   __syncthreads();
-  for (int el = warp; el < EG; el += 8) {
-    const int e = static_cast<int>(rank) * EG + el;
-    float acc[kRouterCluster] = {};
-    if (e < E) {
-      const float* we = wr + static_cast<long long>(e) * H;
-      for (int k0 = 4 * lane; k0 < H; k0 += 16 * 128) {
-        float4 w4[16];  // 16 weight loads in flight per lane
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const int k = k0 + 128 * q;
-          w4[q] = k < H ? *reinterpret_cast<const float4*>(we + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const int k = k0 + 128 * q;
-          if (k >= H) break;
-#pragma unroll
-          for (int t = 0; t < kRouterCluster; ++t) {
-            const uint2 u = *reinterpret_cast<const uint2*>(xs + static_cast<long long>(t) * H + k);
-            const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
-            acc[t] = fmaf(a.x, w4[q].x, acc[t]);
-            acc[t] = fmaf(a.y, w4[q].y, acc[t]);
-            acc[t] = fmaf(b.x, w4[q].z, acc[t]);
-            acc[t] = fmaf(b.y, w4[q].w, acc[t]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < kRouterCluster; ++t) {
-      const float sum = warp_sum(acc[t]);
-      if (lane == 0) lg[t][el] = sum;
-    }
-  }
-  cluster_sync();  // every CTA's logits written and visible to the cluster
-  const long long t = t0 + rank;
-  if (warp == 0 && t < T) {
-    constexpr int VPT = (kRouterCluster * EG + 31) / 32;
-    float v[VPT];
-    const uint32_t lg_local = smem_u32(&lg[rank][0]);
+  if (!s_last) return;
+  const long long tt = static_cast<long long>(gi) * kRouterTokens + warp;
+  if (tt < T) {
+    // every partial of the token is loaded before the first add (one L2
+    // round trip), then the slices are added in ascending order
+    const int nsl = static_cast<int>(gridDim.y);
+    float pv[VPT][kRouterMaxSlices];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int e = lane + 32 * j;
+      const int ee = lane + 32 * j;
+#pragma unroll
+      for (int s2 = 0; s2 < kRouterMaxSlices; ++s2)
+        pv[j][s2] = (ee < E && s2 < nsl) ? __ldcg(partial + (static_cast<long long>(s2) * T + tt) * E + ee) : 0.f;
+    }
+    float v[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int ee = lane + 32 * j;
       v[j] = -INFINITY;
-      if (e < E) {
-        const uint32_t src = mapa_shared(lg_local + static_cast<uint32_t>(e % EG) * 4u, static_cast<uint32_t>(e / EG));
-        float val;
-        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(val) : "r"(src) : "memory");
-        if (bias) val += bias[e];
-        if (logits_out) logits_out[t * E + e] = val;
-        v[j] = val;
+      if (ee < E) {
+        float sum = pv[j][0];
+#pragma unroll
+        for (int s2 = 1; s2 < kRouterMaxSlices; ++s2)
+          if (s2 < nsl) sum += pv[j][s2];
+        if (bias) sum += bias[ee];
+        if (logits_out) logits_out[tt * E + ee] = sum;
+        v[j] = sum;
       }
     }
-    topk_select_warp<VPT>(v, E, K, lane, idx_out + t * K, w_out + t * K);
+    topk_select_warp<VPT>(v, E, K, lane, idx_out + tt * K, w_out + tt * K);
   }
-  cluster_sync();  // no CTA leaves while another still reads its logits
+  if (threadIdx.x == 0) counters[gi] = 0;
 }
 
 }  // namespace
@@ -408,28 +431,38 @@ bool router_topk_fused_supported(int hidden, int experts, int top_k) {
   return experts >= 1 && experts <= 256 && hidden % 128 == 0 && top_k >= 1 && top_k <= 32 && top_k <= experts;
 }
 
+int router_topk_slices(int tokens, int hidden, int experts) {
+  // as many slices as allowed: a lane's loads for its slice are then all in
+  // flight at once (hidden 2048: two 128-wide blocks per slice)
+  (void)tokens;
+  (void)experts;
+  const int sl = kRouterMaxSlices;
+  const int blocks = hidden / 128;
+  const int per = (blocks + sl - 1) / sl;  // 128-wide blocks per slice
+  return (blocks + per - 1) / per;
+}
+
+int router_topk_max_groups() { return kRouterMaxGroups; }
+
 cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                      int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
-                                     cudaStream_t s) {
+                                     float* partial, int* counters, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   if (!router_topk_fused_supported(hidden, experts, top_k)) return cudaErrorInvalidValue;
-  const size_t smem = static_cast<size_t>(kRouterCluster) * hidden * sizeof(__nv_bfloat16);
-  const unsigned grid = static_cast<unsigned>((tokens + kRouterCluster - 1) / kRouterCluster) * kRouterCluster;
-  const int eg = (experts + kRouterCluster - 1) / kRouterCluster;
-#define NKI_RTC(EGV)                                                                                         \
-  do {                                                                                                      \
-    auto k = router_topk_cluster_kernel<EGV>;                                                               \
-    if (smem > 48 * 1024) {                                                                                 \
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-      if (e != cudaSuccess) return e;                                                                       \
-    }                                                                                                       \
-    k<<<grid, 256, smem, s>>>(x, wr, bias, logits_out, tokens, hidden, experts, top_k, idx, w);              \
-  } while (0)
-  if (eg <= 4) NKI_RTC(4);
-  else if (eg <= 8) NKI_RTC(8);
-  else if (eg <= 16) NKI_RTC(16);
-  else NKI_RTC(32);
-#undef NKI_RTC
+  const int groups = (tokens + kRouterTokens - 1) / kRouterTokens;
+  if (groups > kRouterMaxGroups) return cudaErrorInvalidValue;
+  const int slices = router_topk_slices(tokens, hidden, experts);
+  const int kslice = ((hidden / 128 + slices - 1) / slices) * 128;
+  const dim3 grid((experts + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta, slices, groups);
+  const int vpt = (experts + 31) / 32;
+#define NKI_RTS(V)                                                                                           \
+  router_topk_split_kernel<V><<<grid, 256, 0, s>>>(x, wr, bias, logits_out, tokens, hidden, experts, top_k, idx, w, \
+                                                   partial, counters, kslice)
+  if (vpt <= 1) NKI_RTS(1);
+  else if (vpt <= 2) NKI_RTS(2);
+  else if (vpt <= 4) NKI_RTS(4);
+  else NKI_RTS(8);
+#undef NKI_RTS
   return cudaGetLastError();
 }
 

@@ -22,7 +22,7 @@ __all__ = [
     "rmsnorm", "add_rmsnorm", "qk_norm_rope", "router_logits", "topk_softmax", "permute",
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
-    "route", "dispatch", "segment_experts", "combine", "ep_dispatch",
+    "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -133,6 +133,69 @@ def qk_norm_rope(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tens
         out = torch.empty_like(qkv)
     call("nkimoe_qk_norm_rope", _p(qkv), _p(out), _p(qw), _p(kw), _DT[wdt], _p(pos), T, n_heads, n_kv_heads,
          head_dim, float(theta), float(eps), _s(qkv))
+    return out
+
+
+_attn_ws: dict = {}
+
+
+def _attention_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-filled per-(device, stream) workspace of the decode attention
+    (its split counters must start at zero; every call leaves them at zero)."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index, stream)
+    with _ws_lock:
+        buf = _attn_ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            _attn_ws[key] = buf
+        return buf
+
+
+def decode_attention(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, positions: torch.Tensor,
+                     k_cache: torch.Tensor, v_cache: torch.Tensor, n_heads: int, n_kv_heads: int,
+                     theta: float = 1e6, eps: float = 1e-6, scale: float | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of grouped-query attention over a KV cache, fused with
+    the q/k RMSNorm + RoPE of the step's token and the store of its key and
+    value at its position.
+
+    ``qkv``: ``[B, (n_heads + 2*n_kv_heads) * 128]`` bf16, the QKV projection
+    before the norms; ``positions``: int64 ``[B]`` or ``[1]`` (one position for
+    every sequence); ``k_cache``/``v_cache``: one layer's ``[B', n_kv_heads,
+    max_seq, 128]`` bf16 caches (B' >= B, updated in place).  Returns
+    ``[B, n_heads * 128]`` bf16."""
+    hd = 128
+    qkv = _cuda(qkv, "qkv")
+    if qkv.dtype != torch.bfloat16 or not qkv.is_contiguous():
+        raise ValueError("qkv must be a contiguous bf16 tensor")
+    B = qkv.numel() // ((n_heads + 2 * n_kv_heads) * hd)
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        _cuda(c, name)
+        if c.dtype != torch.bfloat16 or c.dim() != 4 or c.shape[1] != n_kv_heads or c.shape[3] != hd:
+            raise ValueError(f"{name} must be bf16 [B, {n_kv_heads}, max_seq, {hd}]")
+        if c.shape[0] < B or not c[:B].is_contiguous():
+            raise ValueError(f"{name} must hold {B} contiguous sequences")
+    max_seq = k_cache.shape[2]
+    if v_cache.shape != k_cache.shape:
+        raise ValueError("k_cache and v_cache differ in shape")
+    wdt = torch.float32 if q_weight.dtype == torch.float32 else torch.bfloat16
+    qw = _contig(_cuda(q_weight, "q_weight"), wdt)
+    kw = _contig(_cuda(k_weight, "k_weight"), wdt)
+    pos = _cuda(positions, "positions").reshape(-1)
+    if pos.dtype != torch.int64 or not pos.is_contiguous():
+        raise ValueError("positions must be a contiguous int64 tensor")
+    if pos.numel() not in (1, B):
+        raise ValueError(f"positions has {pos.numel()} entries for {B} sequences")
+    if out is None:
+        out = torch.empty(B, n_heads * hd, dtype=torch.bfloat16, device=qkv.device)
+    nbytes = size_call("nkimoe_decode_attention_workspace_bytes", B, n_heads, n_kv_heads, hd, max_seq)
+    ws = _attention_workspace(qkv.device, nbytes)
+    call("nkimoe_decode_attention", _p(qkv), _p(qw), _p(kw), _DT[wdt], _p(pos), 0 if pos.numel() == 1 else 1,
+         _p(k_cache), _p(v_cache), _p(out), B, n_heads, n_kv_heads, hd, max_seq, float(theta), float(eps),
+         float(scale if scale is not None else hd ** -0.5), _p(ws), ws.numel(), _s(qkv))
+    if sync_check_enabled():
+        read_status(ws)
     return out
 
 

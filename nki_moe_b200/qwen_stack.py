@@ -12,14 +12,15 @@ head_dim^-0.5) and a final RMSNorm + LM head (``qwen_with_nki.py:495``).
 
 Library kernels on the path: RMSNorm and the fused residual-add + RMSNorm
 (``nkimoe_rmsnorm`` / ``nkimoe_add_rmsnorm``), q/k RMSNorm + RoPE on the fused
-QKV rows (``nkimoe_qk_norm_rope``) and the whole MoE block
-(``nkimoe_moe_block``).  The dense projections (QKV, O, LM head) are plain
-cuBLAS GEMMs through torch and attention is torch's scaled-dot-product
-attention; neither is part of the MoE hot path.
+QKV rows (``nkimoe_qk_norm_rope``, prefill), the decode step's attention fused
+with its q/k norms, RoPE and KV-cache store (``nkimoe_decode_attention``) and
+the whole MoE block (``nkimoe_moe_block``).  The dense projections (QKV, O,
+LM head) are plain cuBLAS GEMMs through torch and prefill attention is torch's
+scaled-dot-product attention; neither is part of the MoE hot path.
 
 Decode keeps every shape static (a KV cache of ``max_seq`` positions, the
-current position in a device tensor, attention masked to positions <= it), so
-one decode step over all layers is captured into a single CUDA graph.
+current position in a device tensor that the attention kernel reads), so one
+decode step over all layers is captured into a single CUDA graph.
 """
 
 from __future__ import annotations
@@ -191,8 +192,10 @@ class Qwen3MoEStack:
         v = qkv[:, (nq + nkv) * hd:].view(B, S, nkv, hd).transpose(1, 2)
         return q, k, v
 
-    def _layers(self, h: torch.Tensor, B: int, S: int, positions: torch.Tensor, attend, store_kv):
-        """Run every layer on h [B*S, H]; returns the final residual stream."""
+    def _layers(self, h: torch.Tensor, attention):
+        """Run every layer on h [T, H]; ``attention(li, lyr, xn)`` returns the
+        attention output [T, nq*hd] before the O projection.  Returns the
+        final norm of the residual stream."""
         c = self.cfg
         eps = c.rms_norm_eps
         res = None
@@ -203,11 +206,7 @@ class Qwen3MoEStack:
                 xn = ops.rmsnorm(h, lyr.in_norm, eps)
             else:  # the previous layer's MoE output joins the residual here
                 xn, res = ops.add_rmsnorm(h, res, lyr.in_norm, eps)
-            q, k, v = self._split(self._qkv(lyr, xn, positions), B, S)
-            store_kv(li, k, v)
-            o = attend(li, q, k, v)  # [B, nq, S, hd]
-            o = o.transpose(1, 2).reshape(B * S, c.num_attention_heads * c.head_dim)
-            a = F.linear(o, lyr.o_w)
+            a = F.linear(attention(li, lyr, xn), lyr.o_w)
             xn, res = ops.add_rmsnorm(a, res, lyr.post_norm, eps)
             h = self._moe(lyr, xn)
         return ops.add_rmsnorm(h, res, self.final_norm, eps)[0]
@@ -224,15 +223,16 @@ class Qwen3MoEStack:
         ids = input_ids.to(self.device)
         h = F.embedding(ids.reshape(-1), self.embed)
         positions = torch.arange(S, device=self.device, dtype=torch.int64).repeat(B)
+        c = self.cfg
 
-        def store(li, k, v):
+        def attention(li, lyr, xn):
+            q, k, v = self._split(self._qkv(lyr, xn, positions), B, S)
             self.k_cache[li, :B, :, :S].copy_(k)
             self.v_cache[li, :B, :, :S].copy_(v)
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)  # [B, nq, S, hd]
+            return o.transpose(1, 2).reshape(B * S, c.num_attention_heads * c.head_dim)
 
-        def attend(li, q, k, v):
-            return F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
-
-        hn = self._layers(h, B, S, positions, attend, store)
+        hn = self._layers(h, attention)
         self.length = S
         if all_logits:
             return F.linear(hn, self.lm_head).view(B, S, -1)
@@ -241,25 +241,19 @@ class Qwen3MoEStack:
 
     # ------------------------------------------------------------ decode
     def _decode_body(self, B: int) -> torch.Tensor:
+        """One decode step for ``self._tokens[:B]`` at position ``self._pos``:
+        per layer the QKV projection, then one library kernel for the q/k
+        norms + RoPE, the KV-cache store and the attention over the cache
+        (``ops.decode_attention``)."""
         c = self.cfg
-        nq, nkv, hd = c.num_attention_heads, c.num_key_value_heads, c.head_dim
-        grp = nq // nkv
-        pos = self._pos
         h = F.embedding(self._tokens[:B], self.embed)
-        positions = pos.expand(B)
-        visible = (torch.arange(self.max_seq, device=self.device) <= pos).view(1, 1, 1, -1)
 
-        def store(li, k, v):
-            self.k_cache[li, :B].index_copy_(2, pos, k)
-            self.v_cache[li, :B].index_copy_(2, pos, v)
+        def attention(li, lyr, xn):
+            qkv = F.linear(xn, lyr.qkv_w)
+            return ops.decode_attention(qkv, lyr.q_norm, lyr.k_norm, self._pos, self.k_cache[li], self.v_cache[li],
+                                        c.num_attention_heads, c.num_key_value_heads, c.rope_theta, c.rms_norm_eps)
 
-        def attend(li, q, k, v):
-            # q head j*grp + i reads kv head j: fold the group into the query axis
-            qg = q.reshape(B, nkv, grp, hd)
-            o = F.scaled_dot_product_attention(qg, self.k_cache[li, :B], self.v_cache[li, :B], attn_mask=visible)
-            return o.reshape(B, nq, 1, hd)
-
-        hn = self._layers(h, B, 1, positions, attend, store)
+        hn = self._layers(h, attention)
         return F.linear(hn, self.lm_head)
 
     @torch.inference_mode()

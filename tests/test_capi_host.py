@@ -70,6 +70,27 @@ def test_argument_validation_without_gpu():
     _lib.call("nkimoe_rmsnorm", null, _lib.BF16, null, _lib.F32, null, _lib.BF16, 0, 2048, 1e-6, null)
 
 
+def test_decode_attention_validation_without_gpu():
+    null = ctypes.c_void_p(0)
+
+    def attn(B, nq, nkv, hd, S, ws_bytes, ws=null):
+        _lib.call("nkimoe_decode_attention", null, null, null, _lib.BF16, null, 0, null, null, null, B, nq, nkv, hd, S,
+                  1e6, 1e-6, 0.088, ws, ws_bytes, null)
+
+    for args, code in (((8, 32, 4, 64, 640, 1 << 20), _lib.ERR_UNSUPPORTED),    # head_dim 64
+                       ((8, 30, 4, 128, 640, 1 << 20), _lib.ERR_INVALID_ARG),   # 30 heads over 4 kv heads
+                       ((8, 64, 2, 128, 640, 1 << 20), _lib.ERR_UNSUPPORTED),   # 32 q heads per kv head
+                       ((8, 32, 4, 128, 640, 1 << 20), _lib.ERR_INVALID_ARG)):  # null pointers
+        with pytest.raises(_lib.NKIMoEError) as ei:
+            attn(*args)
+        assert ei.value.code == code
+    need = _lib.size_call("nkimoe_decode_attention_workspace_bytes", 8, 32, 4, 128, 640)
+    # status + counters + partials: 8 sequences x 4 kv heads x 10 splits x 8 heads x (128 + 4) floats
+    assert need >= 8 * 4 * 10 * 8 * 132 * 4
+    assert _lib.size_call("nkimoe_decode_attention_workspace_bytes", 8, 32, 4, 64, 640) == 0
+    attn(0, 32, 4, 128, 640, 0)  # an empty batch is a no-op
+
+
 def test_reference_module_aliases():
     import sys
     import nki_moe_b200

@@ -74,13 +74,17 @@ def test_rmsnorm_bf16(rows, hidden):
     assert np.max(np.abs(y - ref) / (np.abs(ref) + 1e-3)) < 8e-3  # one bf16 rounding of the output
 
 
-def test_add_rmsnorm():
-    g = torch.Generator().manual_seed(3)
-    x, res = torch.randn(100, 2048, generator=g), torch.randn(100, 2048, generator=g)
-    w = 1 + 0.1 * torch.randn(2048, generator=g)
+@pytest.mark.parametrize("rows,hidden,in_place", [(100, 2048, False), (8, 2048, True), (1000, 2048, True),
+                                                  (3, 8192, False), (5, 10240, True)])
+def test_add_rmsnorm(rows, hidden, in_place):
+    """Row-per-CTA path (few rows), warp-per-row path (many rows or long
+    rows), and the decoder's in-place residual update."""
+    g = torch.Generator().manual_seed(3 + rows)
+    x, res = torch.randn(rows, hidden, generator=g), torch.randn(rows, hidden, generator=g)
+    w = 1 + 0.1 * torch.randn(hidden, generator=g)
     xb, xn = bf(x)
     rb, rn = bf(res)
-    out, r_out = ops.add_rmsnorm(xb, rb, w.cuda(), 1e-6)
+    out, r_out = ops.add_rmsnorm(xb, rb, w.cuda(), 1e-6, residual_out=rb if in_place else None)
     s = oracle.bf16_round(xn + rn)
     np.testing.assert_array_equal(r_out.float().cpu().numpy(), s)
     ref = oracle.rmsnorm(s, w.numpy(), 1e-6)
