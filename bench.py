@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement")
     ap.add_argument("--profile-once", action="store_true", help="one warm step only (for ncu launch lists)")
     ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder-stack TTFT / decode run")
+    ap.add_argument("--stack-profile-layers", type=int, default=0,
+                    help="with --profile-once: build a decoder stack of this many layers, prefill batch 8 x 512 "
+                         "and run one eager decode step inside the NVTX range 'decode_step' (for ncu launch lists)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: exchange over peer memory (library kernels) or NCCL all-to-all")
     return ap.parse_args()
@@ -360,6 +363,22 @@ def run_b200(args):
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     _lib.load()
+    if args.profile_once and args.stack_profile_layers > 0:
+        from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
+
+        st = Qwen3MoEStack.random_init(Qwen3MoEConfig(num_hidden_layers=args.stack_profile_layers), seed=0,
+                                       max_batch=8, max_seq=640)
+        ids = torch.randint(0, st.cfg.vocab_size, (8, 512), generator=torch.Generator().manual_seed(0))
+        st.prefill(ids)
+        tok = torch.zeros(8, dtype=torch.int64, device="cuda")
+        for _ in range(3):
+            st.decode(tok, graph=False)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_step")
+        st.decode(tok, graph=False)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        return
     hbm_gbs, tf_burst, tf_sus, peak_src = peaks()
     sampler = ClockSampler(local)
     sampler.start()

@@ -132,6 +132,18 @@ NKIMOE_API int nkimoe_decode_attention(const void* qkv, const void* q_weight, co
                                        int64_t max_seq, float rope_theta, float eps, float scale, void* workspace,
                                        size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- decode projections */
+
+/* y[M, N] = x[M, K] . w[N, K]^T for decode batches, M <= 16 (bf16 in and out,
+ * fp32 accumulation, deterministic); w in the nn.Linear layout [out, in].
+ * N % 16 == 0, K % 32 == 0, pointers 16-byte aligned.  Streams w once at
+ * HBM rate.  The decode step's projections: nki_qkv_projection
+ * (nki_attention.py:32-169), the O projection (qwen_with_nki.py:330-350) and
+ * the LM head (qwen_with_nki.py:495); NKI tile matmul nki_matmul_tiled
+ * (nki_moe_integrated.py:27-84). */
+NKIMOE_API int nkimoe_skinny_linear(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K,
+                                    void* stream);
+
 /* ---------------------------------------------------------------- router */
 
 /* logits[T,E] (fp32) = x(bf16)[T,H] . router_w(fp32)[E,H]^T (+ router_bias[E])

@@ -40,6 +40,7 @@ SIGNATURES = {
     "nkimoe_decode_attention_workspace_bytes": (_sz, [_i64, _i, _i, _i, _i64]),
     "nkimoe_decode_attention": (_i, [_vp, _vp, _vp, _i, _vp, _i64, _vp, _vp, _vp, _i64, _i, _i, _i, _i64, _f, _f, _f,
                                      _vp, _sz, _vp]),
+    "nkimoe_skinny_linear": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "nkimoe_router_logits": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "nkimoe_topk_softmax": (_i, [_vp, _i64, _i64, _i64, _vp, _vp, _vp]),
     "nkimoe_permute_workspace_bytes": (_sz, [_i64, _i64, _i64]),

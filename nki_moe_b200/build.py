@@ -23,7 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(REPO, "_build")
 LIB = os.path.join(PKG, "libnkimoe.so")
 SOURCES = ["norm.cu", "router.cu", "permute.cu", "pack.cu", "grouped_gemm.cu", "ep_peer.cu", "capi.cu",
-           "noalloc.cu", "attention.cu"]
+           "noalloc.cu", "attention.cu", "linear.cu"]
 HEADERS = ["common.cuh", "kernels.h", "rope.cuh"]
 
 

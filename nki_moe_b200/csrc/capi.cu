@@ -493,6 +493,21 @@ int nkimoe_decode_attention(const void* qkv, const void* q_weight, const void* k
   return NKIMOE_OK;
 }
 
+int nkimoe_skinny_linear(const void* x, const void* w, void* y, int64_t M, int64_t N, int64_t K, void* stream) {
+  NKI_REQUIRE(M >= 0 && N >= 0 && K > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");
+  NKI_REQUIRE(M <= 16, NKIMOE_ERR_UNSUPPORTED, "skinny_linear takes at most 16 rows (%lld)", (long long)M);
+  NKI_REQUIRE(N % 16 == 0 && K % 32 == 0, NKIMOE_ERR_UNSUPPORTED, "N %% 16 and K %% 32 must be 0 (N=%lld K=%lld)",
+              (long long)N, (long long)K);
+  NKI_REQUIRE(N / 16 <= 0x7fffffffLL && K <= 0x7fffffffLL, NKIMOE_ERR_UNSUPPORTED, "shape too large");
+  if (M == 0 || N == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && w && y, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(w) && aligned16(y), NKIMOE_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  NKI_CUDA(skinny_linear_launch(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w),
+                                static_cast<__nv_bfloat16*>(y), static_cast<int>(M), static_cast<int>(N),
+                                static_cast<int>(K), as_stream(stream)));
+  return NKIMOE_OK;
+}
+
 int nkimoe_router_logits(const void* x, const float* router_w, const float* router_bias, float* logits, int64_t T,
                          int64_t H, int64_t E, void* stream) {
   NKI_REQUIRE(T >= 0 && H > 0 && E > 0, NKIMOE_ERR_INVALID_ARG, "bad shape");

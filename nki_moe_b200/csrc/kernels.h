@@ -50,6 +50,10 @@ cudaError_t decode_attention_launch(const __nv_bfloat16* qkv, const void* qw, co
                                     int max_seq, float theta, float eps, float scale, void* workspace,
                                     cudaStream_t s);
 
+// ----------------------------------------------------------------- decode projections
+cudaError_t skinny_linear_launch(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int M, int N,
+                                 int K, cudaStream_t s);
+
 // ----------------------------------------------------------------- router
 // fp32 logits = x(bf16) . Wr(fp32)^T (+ bias), CUDA-core fp32 FMA, fixed order.
 cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits,

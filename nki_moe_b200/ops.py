@@ -22,7 +22,7 @@ __all__ = [
     "rmsnorm", "add_rmsnorm", "qk_norm_rope", "router_logits", "topk_softmax", "permute",
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
-    "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention",
+    "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention", "skinny_linear",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -196,6 +196,26 @@ def decode_attention(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.
          float(scale if scale is not None else hd ** -0.5), _p(ws), ws.numel(), _s(qkv))
     if sync_check_enabled():
         read_status(ws)
+    return out
+
+
+def skinny_linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ w.T`` for at most 16 rows of ``x`` (bf16, fp32 accumulation):
+    the decode step's projections, streaming ``w`` [N, K] once."""
+    x = _cuda(x, "x")
+    w = _cuda(w, "w")
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("skinny_linear takes bf16 x and w")
+    x = _contig(x)
+    w = _contig(w)
+    K = x.shape[-1]
+    M = x.numel() // K if K else 0
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"w is {tuple(w.shape)}, x has {K} columns")
+    if out is None:
+        out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    call("nkimoe_skinny_linear", _p(x), _p(w), _p(out), M, N, K, _s(x))
     return out
 
 

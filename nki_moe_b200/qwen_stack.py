@@ -91,6 +91,11 @@ class Qwen3MoEStack:
         self._graph = None
         self._graph_batch = None
         self._graph_out = None
+        # the skinny linear kernel takes N % 16 == 0 and K % 32 == 0
+        H, hd = cfg.hidden_size, cfg.head_dim
+        nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+        self._skinny_ok = (H % 32 == 0 and (nq * hd) % 32 == 0 and ((nq + 2 * nkv) * hd) % 16 == 0
+                           and H % 16 == 0 and cfg.vocab_size % 16 == 0)
 
     # ------------------------------------------------------------ construction
     @classmethod
@@ -192,10 +197,10 @@ class Qwen3MoEStack:
         v = qkv[:, (nq + nkv) * hd:].view(B, S, nkv, hd).transpose(1, 2)
         return q, k, v
 
-    def _layers(self, h: torch.Tensor, attention):
+    def _layers(self, h: torch.Tensor, attention, linear=F.linear):
         """Run every layer on h [T, H]; ``attention(li, lyr, xn)`` returns the
-        attention output [T, nq*hd] before the O projection.  Returns the
-        final norm of the residual stream."""
+        attention output [T, nq*hd] before the O projection (``linear``).
+        Returns the final norm of the residual stream."""
         c = self.cfg
         eps = c.rms_norm_eps
         res = None
@@ -206,7 +211,7 @@ class Qwen3MoEStack:
                 xn = ops.rmsnorm(h, lyr.in_norm, eps)
             else:  # the previous layer's MoE output joins the residual here
                 xn, res = ops.add_rmsnorm(h, res, lyr.in_norm, eps)
-            a = F.linear(attention(li, lyr, xn), lyr.o_w)
+            a = linear(attention(li, lyr, xn), lyr.o_w)
             xn, res = ops.add_rmsnorm(a, res, lyr.post_norm, eps)
             h = self._moe(lyr, xn)
         return ops.add_rmsnorm(h, res, self.final_norm, eps)[0]
@@ -247,14 +252,17 @@ class Qwen3MoEStack:
         (``ops.decode_attention``)."""
         c = self.cfg
         h = F.embedding(self._tokens[:B], self.embed)
+        # the projections of a decode batch (<= 16 rows) stream their weights
+        # through the library's skinny linear kernel
+        linear = ops.skinny_linear if B <= 16 and self._skinny_ok else F.linear
 
         def attention(li, lyr, xn):
-            qkv = F.linear(xn, lyr.qkv_w)
+            qkv = linear(xn, lyr.qkv_w)
             return ops.decode_attention(qkv, lyr.q_norm, lyr.k_norm, self._pos, self.k_cache[li], self.v_cache[li],
                                         c.num_attention_heads, c.num_key_value_heads, c.rope_theta, c.rms_norm_eps)
 
-        hn = self._layers(h, attention)
-        return F.linear(hn, self.lm_head)
+        hn = self._layers(h, attention, linear)
+        return linear(hn, self.lm_head)
 
     @torch.inference_mode()
     def decode(self, tokens: torch.Tensor, graph: bool = True) -> torch.Tensor:
