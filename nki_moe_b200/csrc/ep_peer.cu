@@ -80,40 +80,58 @@ __device__ __forceinline__ bool last_block_done(unsigned* counter) {
 // Source side: send row r (token row_token[r], destination d = row_slot[r] % P,
 // j = r - rank_offsets[d]) to region src of d's buffer: the token row, its K
 // slots as d sees them and their weights.  Also rewrites slot_row for the final
-// sum: (t, d) -> d * Tm + j in this rank's ret_y.  One warp per row.
+// sum: (t, d) -> d * Tm + j in this rank's ret_y.  One warp per pair of rows:
+// both rows' metadata, then both rows' 4 KB of loads, are in flight before the
+// stores (the stores to a peer are posted; the loads set the pace).
 __global__ void __launch_bounds__(256) ep_peer_send_kernel(
     const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx, const float* __restrict__ w,
     const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ rank_offsets, const int32_t* __restrict__ slot_row_in,
     int32_t* __restrict__ slot_row_out, int T, int H, int K, int P, int El, int Tm, int src, EpPeerPtrs peers,
     EpPeerLayout L, unsigned* counter, uint32_t epoch) {
+  constexpr int kRowsPerWarp = 2;
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const long long rows = rank_offsets[P];
   const int chunks = H >> 3;
-  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
-       r += nw) {
-    const int t = row_token[r];
-    const int d = row_slot[r] % P;
-    const long long j = r - rank_offsets[d];
-    const EpPeerView pv = view_of(peers.base[d], L);
-    const long long dst_row = static_cast<long long>(src) * Tm + j;
-    const uint4* s4 = reinterpret_cast<const uint4*>(x + static_cast<long long>(t) * H);
-    uint4* d4 = reinterpret_cast<uint4*>(pv.recv_x + dst_row * H);
-    for (int c0 = lane; c0 < chunks; c0 += 256) {
-      uint4 v[8];
+  for (long long r0 = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kRowsPerWarp;
+       r0 < rows; r0 += nw * kRowsPerWarp) {
+    int t[kRowsPerWarp], d[kRowsPerWarp];
+    long long dst_row[kRowsPerWarp];
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (c0 + 32 * q < chunks) v[q] = s4[c0 + 32 * q];
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (c0 + 32 * q < chunks) d4[c0 + 32 * q] = v[q];
+    for (int q = 0; q < kRowsPerWarp; ++q) {
+      const long long r = r0 + q < rows ? r0 + q : r0;
+      t[q] = row_token[r];
+      d[q] = row_slot[r] % P;
     }
-    if (lane < K) {
-      const int e = idx[static_cast<long long>(t) * K + lane];
-      const bool mine = e >= d * El && e < (d + 1) * El;
-      pv.recv_slots[dst_row * K + lane] = mine ? e - d * El : -1;
-      pv.recv_w[dst_row * K + lane] = mine ? w[static_cast<long long>(t) * K + lane] : 0.f;
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q) dst_row[q] = static_cast<long long>(src) * Tm + (r0 + q - rank_offsets[d[q]]);
+    for (int c0 = lane; c0 < chunks; c0 += 256) {
+      uint4 v[kRowsPerWarp][8];
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(x + static_cast<long long>(t[q]) * H);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + 32 * u < chunks) v[q][u] = s4[c0 + 32 * u];
+      }
+#pragma unroll
+      for (int q = 0; q < kRowsPerWarp; ++q) {
+        if (r0 + q >= rows) break;
+        uint4* d4 = reinterpret_cast<uint4*>(view_of(peers.base[d[q]], L).recv_x + dst_row[q] * H);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (c0 + 32 * u < chunks) d4[c0 + 32 * u] = v[q][u];
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kRowsPerWarp; ++q) {
+      if (r0 + q >= rows || lane >= K) continue;
+      const EpPeerView pv = view_of(peers.base[d[q]], L);
+      const int e = idx[static_cast<long long>(t[q]) * K + lane];
+      const bool mine = e >= d[q] * El && e < (d[q] + 1) * El;
+      pv.recv_slots[dst_row[q] * K + lane] = mine ? e - d[q] * El : -1;
+      pv.recv_w[dst_row[q] * K + lane] = mine ? w[static_cast<long long>(t[q]) * K + lane] : 0.f;
     }
   }
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < static_cast<long long>(T) * P;
@@ -165,44 +183,61 @@ __global__ void ep_peer_mask_kernel(int32_t* __restrict__ slots, const int32_t* 
 // Receiver: the routing-weighted sum of row r's K expert outputs (fp32, k
 // ascending, as combine_kernel), stored straight into region `me` of the
 // source's ret_y (source s = r / Tm, row j = r % Tm).  Rows without a local
-// expert are skipped.  The last CTA raises every source's result flag.
+// expert are skipped.  One warp per row: its K output-row indices come in one
+// load, then each present slot's whole 4 KB row is loaded (8 x 16 bytes per
+// lane in flight) and added; the sum leaves as 4 KB of contiguous stores.  The
+// last CTA raises every source's result flag.
 __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat16* __restrict__ y,
                                                               const int32_t* __restrict__ slot_row, int rows, int K,
                                                               int H, int Tm, int me, EpPeerPtrs peers,
                                                               EpPeerLayout L, int P, unsigned* counter,
                                                               uint32_t epoch) {
-  const uint32_t chunks = static_cast<uint32_t>(H) >> 3;
-  const uint32_t n = static_cast<uint32_t>(rows) * chunks;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const uint32_t r = i / chunks;
-    const uint32_t c = i - r * chunks;
-    float acc[8] = {};
-    bool any = false;
-    for (int k = 0; k < K; ++k) {
-      const int yr = slot_row[static_cast<long long>(r) * K + k];
-      if (yr < 0) continue;
-      any = true;
-      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(y + static_cast<long long>(yr) * H) + c);
-      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
-      acc[0] += a.x;
-      acc[1] += a.y;
-      acc[2] += b.x;
-      acc[3] += b.y;
-      acc[4] += cc.x;
-      acc[5] += cc.y;
-      acc[6] += d.x;
-      acc[7] += d.y;
+  const int lane = threadIdx.x & 31;
+  const int chunks = H >> 3;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += nw) {
+    const int my_yr = lane < K ? slot_row[r * K + lane] : -1;
+    const unsigned present = __ballot_sync(0xffffffffu, my_yr >= 0);
+    if (present == 0u) continue;
+    const int s = static_cast<int>(r / Tm);
+    const long long j = r - static_cast<long long>(s) * Tm;
+    uint4* dst = reinterpret_cast<uint4*>(view_of(peers.base[s], L).ret_y + (static_cast<long long>(me) * Tm + j) * H);
+    for (int c0 = lane; c0 < chunks; c0 += 256) {
+      float acc[8][8] = {};
+      for (unsigned m = present; m != 0u; m &= m - 1u) {  // slots in ascending k
+        const int yr = __shfl_sync(0xffffffffu, my_yr, __ffs(m) - 1);
+        const uint4* src = reinterpret_cast<const uint4*>(y + static_cast<long long>(yr) * H);
+        uint4 u[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (c0 + 32 * q < chunks) u[q] = __ldcs(src + c0 + 32 * q);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (c0 + 32 * q >= chunks) break;
+          const float2 a = unpack_bf16x2(u[q].x), b = unpack_bf16x2(u[q].y);
+          const float2 cc = unpack_bf16x2(u[q].z), dd = unpack_bf16x2(u[q].w);
+          acc[q][0] += a.x;
+          acc[q][1] += a.y;
+          acc[q][2] += b.x;
+          acc[q][3] += b.y;
+          acc[q][4] += cc.x;
+          acc[q][5] += cc.y;
+          acc[q][6] += dd.x;
+          acc[q][7] += dd.y;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (c0 + 32 * q >= chunks) break;
+        uint4 o;
+        o.x = pack_bf16x2(acc[q][0], acc[q][1]);
+        o.y = pack_bf16x2(acc[q][2], acc[q][3]);
+        o.z = pack_bf16x2(acc[q][4], acc[q][5]);
+        o.w = pack_bf16x2(acc[q][6], acc[q][7]);
+        dst[c0 + 32 * q] = o;
+      }
     }
-    if (!any) continue;
-    const int s = static_cast<int>(r / static_cast<uint32_t>(Tm));
-    const long long j = r - static_cast<uint32_t>(s) * static_cast<uint32_t>(Tm);
-    const EpPeerView pv = view_of(peers.base[s], L);
-    uint4 o;
-    o.x = pack_bf16x2(acc[0], acc[1]);
-    o.y = pack_bf16x2(acc[2], acc[3]);
-    o.z = pack_bf16x2(acc[4], acc[5]);
-    o.w = pack_bf16x2(acc[6], acc[7]);
-    reinterpret_cast<uint4*>(pv.ret_y + (static_cast<long long>(me) * Tm + j) * H)[c] = o;
   }
   if (last_block_done(counter) && threadIdx.x < P) {
     const EpPeerView pv = view_of(peers.base[threadIdx.x], L);
@@ -267,8 +302,7 @@ cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, in
 cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
                                    int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
                                    uint32_t epoch, cudaStream_t s) {
-  if (static_cast<long long>(rows) * (H / 8) >= (1LL << 31)) return cudaErrorInvalidValue;
-  const unsigned grid = grid_cap(static_cast<long long>(rows) * (H / 8), 256);
+  const unsigned grid = grid_cap(static_cast<long long>(rows) * 32, 256);  // one warp per row
   ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, rows, K, H, Tm, me, peers, L, P, counter, epoch);
   return cudaGetLastError();
 }
