@@ -432,11 +432,12 @@ bool router_topk_fused_supported(int hidden, int experts, int top_k) {
 }
 
 int router_topk_slices(int tokens, int hidden, int experts) {
-  // as many slices as allowed: a lane's loads for its slice are then all in
-  // flight at once (hidden 2048: two 128-wide blocks per slice)
-  (void)tokens;
-  (void)experts;
-  const int sl = kRouterMaxSlices;
+  // as many slices as fit one wave of resident CTAs (4 per SM at 256 threads x
+  // 64 registers): a second wave would add a whole round of load latency
+  const int groups = (tokens + kRouterTokens - 1) / kRouterTokens;
+  const int eblocks = (experts + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta;
+  const int wave = 4 * device_sm_count();
+  const int sl = std::max(1, std::min(kRouterMaxSlices, wave / std::max(1, groups * eblocks)));
   const int blocks = hidden / 128;
   const int per = (blocks + sl - 1) / sl;  // 128-wide blocks per slice
   return (blocks + per - 1) / per;
