@@ -43,7 +43,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode"])
+    ap.add_argument("--workload", default="prefill", choices=["prefill", "decode", "skewed"],
+                    help="prefill: 8192 tokens per GPU; decode: 64 tokens; skewed: 16384 tokens in all, split "
+                         "over the GPUs, Zipf(1.2) router bias (strong scaling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement")
@@ -390,8 +392,12 @@ def run_b200(args):
             moe.router.weight.copy_(inp["router"])
             moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
             moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+        if wl.zipf_s is not None:
+            moe.router_bias = inp["router_bias"]
         x = inp["x"].to(torch.bfloat16)
-        if world > 1:  # every rank has its own tokens (data-parallel shard)
+        if wl.zipf_s is not None and world > 1:  # the batch is split over the ranks
+            x = x.view(world, wl.tokens // world, wl.hidden)[rank].contiguous()
+        elif world > 1:  # every rank has its own tokens (data-parallel shard)
             g = torch.Generator(device="cuda").manual_seed(wl.seed * 1000 + rank)
             x = torch.randn(wl.tokens, wl.hidden, generator=g, device="cuda").to(torch.bfloat16)
         return inp, moe, x
@@ -410,17 +416,18 @@ def run_b200(args):
         return g
 
     result = {}
-    workloads = ["prefill"] if args.workload == "prefill" else ["decode"]
+    workloads = [args.workload]
     if args.workload == "prefill" and world == 1 and not args.no_decode:
         workloads.append("decode")
+    wl_key = {"prefill": "c3", "decode": "c2", "skewed": "c4"}
     for which in workloads:
-        wl = WORKLOADS["c3" if which == "prefill" else "c2"]
+        wl = WORKLOADS[wl_key[which]]
         inp, moe, x = setup(wl)
         block = None
         if world > 1:
             if args.ep == "peer":
                 from nki_moe_b200.ep_peer import PeerExpertParallelMoE
-                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=wl.tokens)
+                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=x.shape[0])
             else:
                 from nki_moe_b200.ep import ExpertParallelMoE
                 block = ExpertParallelMoE.from_dense(moe, torch.distributed.group.WORLD)
@@ -428,11 +435,19 @@ def run_b200(args):
         else:
             pe = moe.packed()
             rw = moe.router.weight
-            fwd = lambda: ops.moe_block(x, rw, pe, wl.top_k)  # noqa: E731
+            rb = moe.router_bias
+            fwd = lambda: ops.moe_block(x, rw, pe, wl.top_k, bias=rb)  # noqa: E731
         stream = torch.cuda.current_stream()
         # routing of this batch (for the algorithmic byte count) and warm-up
-        _, idx, _ = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k, return_routing=True)
+        _, idx, _ = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k, bias=moe.router_bias,
+                                  return_routing=True)
         alg = algorithmic(wl, idx.cpu().numpy())
+        if which == "skewed":
+            # hottest rank's (token, slot) rows against the mean: the imbalance
+            # that caps an expert-parallel step
+            ep = max(world, 1)
+            per_rank = np.bincount((idx.cpu().numpy().ravel() // (wl.experts // ep)), minlength=ep)
+            alg["rank_rows_max_over_mean"] = float(per_rank.max() / per_rank.mean())
         if args.profile_once:
             fwd()
             torch.cuda.synchronize()
@@ -449,13 +464,16 @@ def run_b200(args):
             sampler.mark(False)
         st = (measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch), graph_of)
               if world == 1 else None)
-        tokens_total = wl.tokens * world
+        # skewed: the workload's tokens are split over the ranks (strong scaling)
+        per_rank_share = 1.0 / world if which == "skewed" else 1.0
+        tokens_total = x.shape[0] * world
         r = {"ms_per_step": ms, "tokens_per_s": tokens_total / (ms * 1e-3),
-             "block_tflops": alg["block_flops"] * world / (ms * 1e-3) / 1e12,
-             "block_gbs": alg["block_bytes"] * world / (ms * 1e-3) / 1e9, "alg": alg, "stages_ms": None}
+             "block_tflops": alg["block_flops"] * per_rank_share * world / (ms * 1e-3) / 1e12,
+             "block_gbs": alg["block_bytes"] * per_rank_share * world / (ms * 1e-3) / 1e9, "alg": alg,
+             "stages_ms": None}
         if st is not None:
             r["stages_ms"] = dict(zip(STAGES, [round(v, 4) for v in st]))
-            if which == "prefill":
+            if which in ("prefill", "skewed"):
                 t = st[4] * 1e-3
                 r["roofline"] = {"bound": "tensor", "kernel": "grouped_gemm_rows (gate/up + SwiGLU)",
                                  "achieved": alg["gemm1_flops"] / t / 1e12, "peak": tf_burst, "unit": "TFLOP/s",
@@ -507,7 +525,7 @@ def run_b200(args):
     clocks = sampler.summary()
     main_key = workloads[0]
     m = result[main_key]
-    wl = WORKLOADS["c3" if main_key == "prefill" else "c2"]
+    wl = WORKLOADS[wl_key[main_key]]
     # this library's kernels per step: single GPU 9 (router, top-k, 3 permutation,
     # gather, 2 GEMMs, combine); EP over peer memory 18 (+ rank sort, send,
     # 2 waits, mask, receiver permutation, final sum); EP over NCCL 17 of ours
@@ -516,8 +534,11 @@ def run_b200(args):
     line = {
         "metric": "moe_block_tokens_per_s", "value": m["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": m["ms_per_step"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": wl.name, "tokens_per_gpu": wl.tokens, "hidden": wl.hidden, "experts": wl.experts,
+        "higher_is_better": True, "scaling": "strong" if main_key == "skewed" else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": wl.name,
+                   "tokens_per_gpu": wl.tokens // world if main_key == "skewed" else wl.tokens,
+                   "hidden": wl.hidden, "experts": wl.experts,
                    "top_k": wl.top_k, "intermediate": wl.intermediate,
                    "parallelism": f"ep{world}-{args.ep}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.21 GB of expert weights read per step)",
@@ -532,6 +553,8 @@ def run_b200(args):
     }
     if "roofline_gemm2" in m:
         line["roofline_gemm2"] = m["roofline_gemm2"]
+    if main_key == "skewed":
+        line["rank_rows_max_over_mean"] = m["alg"]["rank_rows_max_over_mean"]
     if "decode" in result and main_key != "decode":
         d = result["decode"]
         line["decode"] = {"workload": WORKLOADS["c2"].name, "tokens_per_s": d["tokens_per_s"],

@@ -333,9 +333,12 @@ NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I
  * weighted sum stored back into its source's buffer -> wait -> sum of the
  * num_ranks partial sums into out [T, H].  peer_buffers: the num_ranks
  * buffers as mapped in this process (this rank's own at index rank).  Every
- * rank calls this once per step with the same epoch, nonzero and increasing
- * between steps.  A peer that never arrives sets NKIMOE_DEV_TIMEOUT in the
- * status word (nkimoe_read_status) after a bounded wait (~10 s). */
+ * rank calls this once per step with the same epoch, increasing between
+ * steps; epoch 0 lets each rank's buffer count the steps on the device (its
+ * own counter + 1 per call), so that a step captured in a CUDA graph can be
+ * replayed -- a caller uses one mode for the buffer's lifetime.  A peer that
+ * never arrives sets NKIMOE_DEV_TIMEOUT in the status word
+ * (nkimoe_read_status) after a bounded wait (~10 s). */
 NKIMOE_API int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias,
                                       const void* router_w_split, const void* w13_local, const void* w2_local,
                                       void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,

@@ -253,7 +253,7 @@ struct PeerCombine {
   EpPeerLayout L;
   int P, me, Tm;
   unsigned* counter;
-  uint32_t epoch;
+  const uint32_t* epoch_p;
 };
 
 int experts_impl(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype, const float* topk_w,
@@ -296,7 +296,7 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
   mark(kStageCombine, s);
   if (pc) {
     NKI_CUDA(ep_peer_combine_launch(xy, slot_row, static_cast<int>(T), static_cast<int>(K), static_cast<int>(H),
-                                    pc->Tm, pc->me, pc->peers, pc->L, pc->P, pc->counter, pc->epoch, s));
+                                    pc->Tm, pc->me, pc->peers, pc->L, pc->P, pc->counter, pc->epoch_p, s));
   } else {
     NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
                             static_cast<int>(K), static_cast<int>(H), s));
@@ -888,7 +888,6 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   NKI_REQUIRE(T >= 0 && T <= Tm && P * Tm * K < (1LL << 31) && P * Tm * (H / 8) < (1LL << 31) && E <= 256,
               NKIMOE_ERR_UNSUPPORTED, "ep peer: tokens %lld exceed max_tokens %lld or the buffers are too large",
               static_cast<long long>(T), Tm);
-  NKI_REQUIRE(epoch != 0, NKIMOE_ERR_INVALID_ARG, "ep peer: epoch must be nonzero (flags start at 0)");
   const PeerWs W = peer_ws(T, H, I, E, K, P, Tm);
   NKI_REQUIRE(workspace && workspace_bytes >= W.total && aligned16(workspace), NKIMOE_ERR_WORKSPACE,
               "workspace %zu < %zu", workspace_bytes, W.total);
@@ -914,6 +913,9 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   unsigned* counters = reinterpret_cast<unsigned*>(b + W.counters);
   NKI_CUDA(cudaMemsetAsync(status, 0, 256, s));  // status word and router counters
   NKI_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned), s));
+  // this step's epoch: the caller's, or this rank's device-side count + 1
+  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(peers.base[rank] + PL.step);
+  NKI_CUDA(ep_peer_step_launch(epoch_p, epoch, s));
   if (T > 0) {
     rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, rb, R, status, s);
     if (rc != NKIMOE_OK) return rc;
@@ -936,21 +938,21 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets, slot_in,
                                slot_out, static_cast<int>(T), static_cast<int>(H), static_cast<int>(K),
                                static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), static_cast<int>(rank),
-                               peers, PL, counters, epoch, s));
+                               peers, PL, counters, epoch_p, s));
   char* own = peers.base[rank];
-  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.disp_flag), static_cast<int>(P), epoch,
+  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.disp_flag), static_cast<int>(P), epoch_p,
                                status, s));
   int32_t* recv_slots = reinterpret_cast<int32_t*>(own + PL.recv_slots);
   NKI_CUDA(ep_peer_mask_launch(recv_slots, reinterpret_cast<const int32_t*>(own + PL.counts), static_cast<int>(P),
                                static_cast<int>(Tm), static_cast<int>(K), s));
   // this rank's experts over every region; sums go back to the sources
   const PeerCombine pc{peers, PL, static_cast<int>(P), static_cast<int>(rank), static_cast<int>(Tm), counters + 1,
-                       epoch};
+                       epoch_p};
   rc = experts_impl(own + PL.recv_x, w13_local, w2_local, recv_slots, NKIMOE_I32,
                     reinterpret_cast<const float*>(own + PL.recv_w), nullptr, P * Tm, H, I, El, K, b + W.recv,
                     workspace_bytes - W.recv, s, &pc, status);
   if (rc != NKIMOE_OK) return rc;
-  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.res_flag), static_cast<int>(P), epoch,
+  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.res_flag), static_cast<int>(P), epoch_p,
                                status, s));
   if (T > 0)
     NKI_CUDA(combine_launch(reinterpret_cast<const __nv_bfloat16*>(own + PL.ret_y), slot_out, nullptr,

@@ -3,6 +3,7 @@
 //
 // Every rank owns one buffer that all ranks map (CUDA IPC; no multicast
 // object), laid out by ep_peer_layout():
+//   step                       u32 this step's epoch (this rank's own counter)
 //   disp_flag[P], res_flag[P]  u32 epoch flags (written by the peers)
 //   counts[P]                  i32 rows sent by each source this step
 //   recv_slots [P][Tm][K]      i32 local expert ids (-1: empty slot)
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(256) ep_peer_send_kernel(
     const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ rank_offsets, const int32_t* __restrict__ slot_row_in,
     int32_t* __restrict__ slot_row_out, int T, int H, int K, int P, int El, int Tm, int src, EpPeerPtrs peers,
-    EpPeerLayout L, unsigned* counter, uint32_t epoch) {
+    EpPeerLayout L, unsigned* counter, const uint32_t* epoch_p) {
   constexpr int kRowsPerWarp = 2;
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
@@ -145,12 +146,13 @@ __global__ void __launch_bounds__(256) ep_peer_send_kernel(
     const EpPeerView pv = view_of(peers.base[d], L);
     pv.counts[src] = rank_offsets[d + 1] - rank_offsets[d];
     __threadfence_system();
-    st_release_sys(pv.disp_flag + src, epoch);
+    st_release_sys(pv.disp_flag + src, *epoch_p);
   }
 }
 
-// Poll this rank's P flags until each holds `epoch` (bounded).  One warp.
-__global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, uint32_t epoch, int* status) {
+// Poll this rank's P flags until each holds the step's epoch (bounded).  One warp.
+__global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status) {
+  const uint32_t epoch = *epoch_p;
   const int lane = threadIdx.x;
   bool ok = true;
   if (lane < P) {
@@ -191,7 +193,7 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
                                                               const int32_t* __restrict__ slot_row, int rows, int K,
                                                               int H, int Tm, int me, EpPeerPtrs peers,
                                                               EpPeerLayout L, int P, unsigned* counter,
-                                                              uint32_t epoch) {
+                                                              const uint32_t* epoch_p) {
   const int lane = threadIdx.x & 31;
   const int chunks = H >> 3;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
@@ -241,8 +243,15 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
   }
   if (last_block_done(counter) && threadIdx.x < P) {
     const EpPeerView pv = view_of(peers.base[threadIdx.x], L);
-    st_release_sys(pv.res_flag + me, epoch);
+    st_release_sys(pv.res_flag + me, *epoch_p);
   }
+}
+
+// The step's epoch in this rank's own buffer: `value` when nonzero (the
+// caller counts steps), otherwise the stored epoch + 1 (the device counts, so
+// that a captured CUDA graph advances it on every replay).
+__global__ void ep_peer_step_kernel(uint32_t* step, uint32_t value) {
+  *step = value != 0u ? value : *step + 1u;
 }
 
 unsigned grid_cap(long long work, int threads) {
@@ -258,6 +267,8 @@ size_t r256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 EpPeerLayout ep_peer_layout(long long P, long long Tm, long long H, long long K) {
   EpPeerLayout L{};
   size_t o = 0;
+  L.step = o;
+  o += 256;
   L.disp_flag = o;
   o += r256(sizeof(uint32_t) * P);
   L.res_flag = o;
@@ -279,18 +290,23 @@ EpPeerLayout ep_peer_layout(long long P, long long Tm, long long H, long long K)
 cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
                                 const int32_t* row_slot, const int32_t* rank_offsets, const int32_t* slot_row_in,
                                 int32_t* slot_row_out, int T, int H, int K, int P, int El, int Tm, int src,
-                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter, uint32_t epoch,
-                                cudaStream_t s) {
+                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter,
+                                const uint32_t* epoch_p, cudaStream_t s) {
   // one warp per send row (at most T * P rows); at least one CTA so that the
   // flags are raised even when nothing is sent
   const unsigned grid = grid_cap(static_cast<long long>(T) * P * 32, 256);
   ep_peer_send_kernel<<<grid, 256, 0, s>>>(x, idx, w, row_token, row_slot, rank_offsets, slot_row_in, slot_row_out, T,
-                                           H, K, P, El, Tm, src, peers, L, counter, epoch);
+                                           H, K, P, El, Tm, src, peers, L, counter, epoch_p);
   return cudaGetLastError();
 }
 
-cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, uint32_t epoch, int* status, cudaStream_t s) {
-  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, P, epoch, status);
+cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s) {
+  ep_peer_step_kernel<<<1, 1, 0, s>>>(step, value);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status, cudaStream_t s) {
+  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, P, epoch_p, status);
   return cudaGetLastError();
 }
 
@@ -301,9 +317,9 @@ cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, in
 
 cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
                                    int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
-                                   uint32_t epoch, cudaStream_t s) {
+                                   const uint32_t* epoch_p, cudaStream_t s) {
   const unsigned grid = grid_cap(static_cast<long long>(rows) * 32, 256);  // one warp per row
-  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, rows, K, H, Tm, me, peers, L, P, counter, epoch);
+  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, rows, K, H, Tm, me, peers, L, P, counter, epoch_p);
   return cudaGetLastError();
 }
 

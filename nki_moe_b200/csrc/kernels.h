@@ -105,19 +105,21 @@ struct EpPeerPtrs {
   char* base[kMaxPeers];  // every rank's exchange buffer, mapped into this process
 };
 struct EpPeerLayout {  // byte offsets inside an exchange buffer (ep_peer.cu)
-  size_t disp_flag, res_flag, counts, recv_slots, recv_w, recv_x, ret_y, total;
+  size_t step, disp_flag, res_flag, counts, recv_slots, recv_w, recv_x, ret_y, total;
 };
 EpPeerLayout ep_peer_layout(long long P, long long max_tokens, long long H, long long K);
 cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
                                 const int32_t* row_slot, const int32_t* rank_offsets, const int32_t* slot_row_in,
                                 int32_t* slot_row_out, int T, int H, int K, int P, int El, int Tm, int src,
-                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter, uint32_t epoch,
-                                cudaStream_t s);
-cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, uint32_t epoch, int* status, cudaStream_t s);
+                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter,
+                                const uint32_t* epoch_p, cudaStream_t s);
+// epoch := value when nonzero, else epoch + 1 (device-side step count)
+cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s);
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status, cudaStream_t s);
 cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, int Tm, int K, cudaStream_t s);
 cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
                                    int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
-                                   uint32_t epoch, cudaStream_t s);
+                                   const uint32_t* epoch_p, cudaStream_t s);
 
 // counts[e] = offsets[e+1] - offsets[e]
 cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s);

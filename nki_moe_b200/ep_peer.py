@@ -39,25 +39,37 @@ class PeerExpertParallelMoE(nn.Module):
     tokens.  Without an initialised process group (or with a group of one)
     it runs as a single rank that sends to itself."""
 
-    def __init__(self, router_w: torch.Tensor, gate_up_local: torch.Tensor, down_local: torch.Tensor,
-                 num_experts: int, top_k: int, max_tokens: int, group=None, router_bias: torch.Tensor | None = None):
+    def __init__(self, router_w: torch.Tensor, gate_up_local: torch.Tensor | None, down_local: torch.Tensor | None,
+                 num_experts: int, top_k: int, max_tokens: int, group=None, router_bias: torch.Tensor | None = None,
+                 device_epochs: bool = False, packed: ops.PackedExperts | None = None):
+        """``gate_up_local [E/P, H, 2I]`` / ``down_local [E/P, I, H]``: this
+        rank's experts in the reference layout; or ``packed``, the same experts
+        already packed (``ops.PackedExperts``), with the two left ``None``."""
         super().__init__()
         distributed = dist.is_available() and dist.is_initialized()
         self.group = (group if group is not None else dist.group.WORLD) if distributed else None
         self.world = dist.get_world_size(self.group) if distributed else 1
         self.rank = dist.get_rank(self.group) if distributed else 0
-        if num_experts % self.world or gate_up_local.shape[0] != num_experts // self.world:
+        local = packed.num_experts if packed is not None else gate_up_local.shape[0]
+        if num_experts % self.world or local != num_experts // self.world:
             raise ValueError("local expert weights do not match num_experts / world size")
         if self.world > 8:
             raise ValueError("at most 8 ranks")
         self.num_experts, self.top_k, self.max_tokens = num_experts, top_k, max_tokens
-        self.device = gate_up_local.device
-        self.hidden = gate_up_local.shape[1]
-        self.inter = gate_up_local.shape[2] // 2
+        if packed is not None:
+            self.device, self.hidden, self.inter = packed.w13.device, packed.hidden, packed.inter
+        else:
+            self.device = gate_up_local.device
+            self.hidden = gate_up_local.shape[1]
+            self.inter = gate_up_local.shape[2] // 2
         self.router_w = router_w.detach().float().contiguous()
         self.router_bias = router_bias.detach().float().contiguous() if router_bias is not None else None
         self.router_split = ops.router_split(self.router_w) if num_experts % 128 == 0 else None
         self.gate_up_local, self.down_local = gate_up_local, down_local
+        self._packed = packed  # packed local weights given by the caller (the originals may be dropped)
+        # device_epochs: every step's epoch is counted on the device (each
+        # rank's buffer holds its count), so a captured step can be replayed
+        self.device_epochs = device_epochs
         self.epoch = 0
         self._own = None
         self._opened = []
@@ -77,6 +89,8 @@ class PeerExpertParallelMoE(nn.Module):
                    router_bias=moe.router_bias)
 
     def packed(self):
+        if self._packed is not None:
+            return self._packed
         return ops.packed_experts(self.gate_up_local, self.down_local, "nxd")
 
     def _setup_buffers(self):
@@ -113,10 +127,11 @@ class PeerExpertParallelMoE(nn.Module):
         ws = ops.workspace(x.device, nbytes)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
         self.epoch = self.epoch % 0xFFFFFFFF + 1  # nonzero, increasing between steps
+        epoch = 0 if self.device_epochs else self.epoch
         bases = (ctypes.c_void_p * P)(*self.bases)
         call("nkimoe_ep_peer_forward", ops._p(x), ops._p(self.router_w), ops._p(self.router_bias),
              ops._p(self.router_split), ops._p(pe.w13), ops._p(pe.w2), ops._p(out), T, H, I, E, K, P, self.rank,
-             self.max_tokens, bases, self.epoch, ops._p(ws), ws.numel(), ops._s(x))
+             self.max_tokens, bases, epoch, ops._p(ws), ws.numel(), ops._s(x))
         if ops.sync_check_enabled():
             ops.read_status(ws)
         return out

@@ -64,12 +64,16 @@ class Qwen3MoEConfig:
 
 
 class _Layer:
-    """One decoder layer's weights in the layouts the kernels take."""
+    """One decoder layer's weights in the layouts the kernels take.  With
+    ``ep`` (an expert-parallel block holding this rank's experts) the MoE runs
+    through it; otherwise ``experts`` holds all experts."""
 
-    def __init__(self, in_norm, qkv_w, q_norm, k_norm, o_w, post_norm, router_w, experts: ops.PackedExperts):
+    def __init__(self, in_norm, qkv_w, q_norm, k_norm, o_w, post_norm, router_w, experts: ops.PackedExperts,
+                 ep=None):
         self.in_norm, self.qkv_w, self.q_norm, self.k_norm = in_norm, qkv_w, q_norm, k_norm
         self.o_w, self.post_norm, self.router_w, self.experts = o_w, post_norm, router_w, experts
-        self.router_split = ops.router_split(router_w) if router_w.shape[0] % 128 == 0 else None
+        self.ep = ep
+        self.router_split = (ops.router_split(router_w) if ep is None and router_w.shape[0] % 128 == 0 else None)
 
 
 class Qwen3MoEStack:
@@ -100,15 +104,34 @@ class Qwen3MoEStack:
     # ------------------------------------------------------------ construction
     @classmethod
     def random_init(cls, cfg: Qwen3MoEConfig, seed: int = 0, device="cuda", max_batch: int = 8,
-                    max_seq: int = 640, std: float = 0.02) -> "Qwen3MoEStack":
+                    max_seq: int = 640, std: float = 0.02, expert_parallel: bool = False,
+                    group=None) -> "Qwen3MoEStack":
         """Random N(0, std) weights (norm weights 1, router fp32), expert weights
         drawn in the reference's ``[E, H, 2I]`` / ``[E, I, H]`` layout and
-        packed once."""
+        packed once.
+
+        ``expert_parallel``: one rank of an expert-parallel stack over the
+        initialised process group (``group``, default WORLD): every rank draws
+        the same weights (same generator sequence as the single-GPU stack),
+        keeps the attention, norms, router and embeddings whole and only its
+        ``E / P`` experts, and runs each layer's MoE as a peer-memory
+        expert-parallel block over its own sequences (``max_batch`` of them,
+        up to ``max_seq`` tokens each).  Every rank must run the same calls
+        (prefill, decode steps) in the same order."""
         dev = torch.device(device)
         g = torch.Generator(device=dev).manual_seed(seed)
         H, hd = cfg.hidden_size, cfg.head_dim
         nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
         E, I = cfg.num_experts, cfg.moe_intermediate_size
+        P, r = 1, 0
+        if expert_parallel:
+            import torch.distributed as dist
+
+            from .ep_peer import PeerExpertParallelMoE
+            P, r = dist.get_world_size(group), dist.get_rank(group)
+            if E % P:
+                raise ValueError(f"{E} experts do not split over {P} ranks")
+        El = E // P
 
         def rnd(*shape, dtype=torch.bfloat16):
             return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * std).to(dtype)
@@ -117,14 +140,27 @@ class Qwen3MoEStack:
         layers = []
         for _ in range(cfg.num_hidden_layers):
             gate_up = rnd(E, H, 2 * I)
-            w13 = ops.pack_gate_up(gate_up, "nxd")
+            w13 = ops.pack_gate_up(gate_up[r * El:(r + 1) * El].contiguous(), "nxd")
             del gate_up
             down = rnd(E, I, H)
-            w2 = ops.pack_down(down, "nxd")
+            w2 = ops.pack_down(down[r * El:(r + 1) * El].contiguous(), "nxd")
             del down
-            layers.append(_Layer(ones(H), rnd((nq + 2 * nkv) * hd, H), ones(hd), ones(hd), rnd(H, nq * hd), ones(H),
-                                 rnd(E, H, dtype=torch.float32), ops.PackedExperts(w13, w2, E, H, I)))
+            experts = ops.PackedExperts(w13, w2, El, H, I)
+            attn = (ones(H), rnd((nq + 2 * nkv) * hd, H), ones(hd), ones(hd), rnd(H, nq * hd), ones(H))
+            router_w = rnd(E, H, dtype=torch.float32)
+            ep = None
+            if expert_parallel:
+                ep = PeerExpertParallelMoE(router_w, None, None, E, cfg.num_experts_per_tok, max_batch * max_seq,
+                                           group=group, device_epochs=True, packed=experts)
+            layers.append(_Layer(*attn, router_w, experts, ep=ep))
         return cls(cfg, rnd(cfg.vocab_size, H), layers, ones(H), rnd(cfg.vocab_size, H), max_batch, max_seq)
+
+    def close(self):
+        """Release the expert-parallel exchange buffers (every rank together)."""
+        self.release_graph()
+        for lyr in self.layers:
+            if lyr.ep is not None:
+                lyr.ep.close()
 
     @classmethod
     def from_hf(cls, model, device="cuda", max_batch: int = 8, max_seq: int = 640) -> "Qwen3MoEStack":
@@ -180,6 +216,8 @@ class Qwen3MoEStack:
 
     # ------------------------------------------------------------ layers
     def _moe(self, lyr: _Layer, x: torch.Tensor) -> torch.Tensor:
+        if lyr.ep is not None:
+            return lyr.ep(x)
         return ops.moe_block(x, lyr.router_w, lyr.experts, self.cfg.num_experts_per_tok,
                              router_w_split=lyr.router_split)
 

@@ -176,3 +176,66 @@ def test_from_safetensors_equals_from_hf(tmp_path, fp8):
     b = Qwen3MoEStack.from_safetensors(str(tmp_path), max_batch=2, max_seq=64)
     ids = torch.randint(0, 1024, (2, 24), generator=torch.Generator().manual_seed(9))
     assert torch.equal(a.prefill(ids, all_logits=True), b.prefill(ids, all_logits=True))
+
+
+def _ep_stack_worker(rank, world, port, out_dir):
+    """One rank of an expert-parallel decoder stack (each rank: its own two
+    sequences, E / P experts) next to a single-GPU stack with the same seed on
+    the same GPU (all experts)."""
+    import datetime
+    import os
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    cfg = Qwen3MoEConfig(vocab_size=1024, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
+                         num_key_value_heads=2, head_dim=128, moe_intermediate_size=128, num_experts=8,
+                         num_experts_per_tok=2)
+    ids = torch.randint(0, 1024, (2 * world, 20), generator=torch.Generator().manual_seed(11))[2 * rank:2 * rank + 2]
+    toks = torch.randint(0, 1024, (2, 4), generator=torch.Generator().manual_seed(12 + rank)).cuda()
+    ep = Qwen3MoEStack.random_init(cfg, seed=5, max_batch=2, max_seq=64, std=0.05, expert_parallel=True)
+    one = Qwen3MoEStack.random_init(cfg, seed=5, max_batch=2, max_seq=64, std=0.05)
+    res = {}
+    for name, st in (("ep", ep), ("one", one)):
+        res[f"{name}_prefill"] = st.prefill(ids, all_logits=True).float().cpu()
+        for graph in (False, True):
+            st.prefill(ids)
+            res[f"{name}_decode_{graph}"] = torch.stack([st.decode(toks[:, i], graph=graph)
+                                                        for i in range(4)], 1).float().cpu()
+        st.release_graph()
+    torch.cuda.synchronize()
+    ep.close()
+    for k, v in res.items():
+        np.save(os.path.join(out_dir, f"{k}_{rank}.npy"), v.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_stack_two_gpus(tmp_path):
+    """Expert-parallel decoder stack on 2 GPUs (peer-memory exchange in every
+    layer, decode step captured in one CUDA graph with device-side epochs)
+    against the single-GPU stack of the same weights: logits within the bars
+    above (the exchange rounds each rank's partial sum to bf16), graph decode
+    bit-identical to eager decode."""
+    import socket
+
+    import numpy as np
+    import torch.multiprocessing as mp
+    sock = socket.socket()
+    sock.bind(("127.0.0.1", 0))
+    port = sock.getsockname()[1]
+    sock.close()
+    world = 2
+    mp.start_processes(_ep_stack_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        ld = lambda k: torch.from_numpy(np.load(tmp_path / f"{k}_{r}.npy"))  # noqa: E731
+        _check(ld("ep_prefill").reshape(-1, 1024), ld("one_prefill").reshape(-1, 1024))
+        _check(ld("ep_decode_False").reshape(-1, 1024), ld("one_decode_False").reshape(-1, 1024))
+        assert torch.equal(ld("ep_decode_True"), ld("ep_decode_False"))
