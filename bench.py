@@ -325,27 +325,39 @@ def measure_stages(torch, fn, steps, evs, graph_of=None):
     return [a / steps for a in acc]
 
 
-def measure_stack(torch):
+def measure_stack(torch, world=1, rank=0):
     """The full-stack configuration: random-init Qwen3-30B-A3B (48 layers),
     batch 8 x 512-token prompts, 128 greedy tokens.  TTFT is the prefill
-    through the first token; decode steps replay one CUDA graph each."""
+    through the first token; decode steps replay one CUDA graph each.  With
+    world > 1 the stack is expert-parallel: every rank holds the attention
+    and E / world experts per layer and serves 8 / world of the sequences; the
+    times are the maximum over ranks."""
     from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
 
     cfg = Qwen3MoEConfig()
     B, S, new = 8, 512, 128
-    st = Qwen3MoEStack.random_init(cfg, seed=0, max_batch=B, max_seq=S + new)
-    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(0))
+    Bl = B // world
+    st = Qwen3MoEStack.random_init(cfg, seed=0, max_batch=Bl, max_seq=S + new, expert_parallel=world > 1)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(0))[rank * Bl:(rank + 1) * Bl]
     st.generate(ids, 8)  # warm-up, graph capture
     _, t = st.generate(ids, new)
-    st.release_graph()
+    ttft, dec = t["ttft_ms"], t["decode_ms"]
+    if world > 1:
+        v = torch.tensor([ttft, dec], device="cuda")
+        torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
+        ttft, dec = float(v[0]), float(v[1])
+    st.close()
     del st
     torch.cuda.empty_cache()
+    steps = t["decode_steps"]
     return {"config": f"Qwen3-30B-A3B decoder stack, {cfg.num_hidden_layers} layers, random-init bf16 weights "
                       f"(router fp32); batch {B} x {S}-token prompts (uniform random ids, seed 0); {new} greedy "
-                      f"tokens", "ttft_ms": t["ttft_ms"], "decode_ms_per_step": t["decode_ms"] / t["decode_steps"],
-            "decode_tok_s": t["decode_tok_s"],
-            "output_tok_s": B * new / ((t["ttft_ms"] + t["decode_ms"]) * 1e-3),
-            "timing": "CUDA events; one CUDA graph replay per decode step", "data": "synthetic"}
+                      f"tokens" + (f"; expert parallel over {world} GPUs, {Bl} sequences per GPU" if world > 1
+                                   else ""),
+            "ttft_ms": ttft, "decode_ms_per_step": dec / steps, "decode_tok_s": B * steps / (dec * 1e-3),
+            "output_tok_s": B * new / ((ttft + dec) * 1e-3),
+            "timing": "CUDA events; one CUDA graph replay per decode step" + (", max over ranks" if world > 1 else ""),
+            "data": "synthetic"}
 
 
 def run_b200(args):
@@ -562,8 +574,8 @@ def run_b200(args):
                           "roofline_block": d.get("roofline_block"), "stages_ms": d["stages_ms"],
                           "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline"),
                           "unique_experts": d["alg"]["unique_experts"]}
-    if world == 1 and not args.no_stack:
-        line["stack"] = measure_stack(torch)
+    if not args.no_stack and (world == 1 or 8 % world == 0):
+        line["stack"] = measure_stack(torch, world, rank)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

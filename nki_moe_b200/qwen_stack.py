@@ -69,10 +69,12 @@ class _Layer:
     through it; otherwise ``experts`` holds all experts."""
 
     def __init__(self, in_norm, qkv_w, q_norm, k_norm, o_w, post_norm, router_w, experts: ops.PackedExperts,
-                 ep=None):
+                 ep=None, ep_decode=None):
         self.in_norm, self.qkv_w, self.q_norm, self.k_norm = in_norm, qkv_w, q_norm, k_norm
         self.o_w, self.post_norm, self.router_w, self.experts = o_w, post_norm, router_w, experts
-        self.ep = ep
+        # expert parallel: one exchange sized for prefill batches, one for a
+        # decode step (the receiver's kernels cover every source's whole region)
+        self.ep, self.ep_decode = ep, ep_decode
         self.router_split = (ops.router_split(router_w) if ep is None and router_w.shape[0] % 128 == 0 else None)
 
 
@@ -148,19 +150,22 @@ class Qwen3MoEStack:
             experts = ops.PackedExperts(w13, w2, El, H, I)
             attn = (ones(H), rnd((nq + 2 * nkv) * hd, H), ones(hd), ones(hd), rnd(H, nq * hd), ones(H))
             router_w = rnd(E, H, dtype=torch.float32)
-            ep = None
+            ep = ep_decode = None
             if expert_parallel:
                 ep = PeerExpertParallelMoE(router_w, None, None, E, cfg.num_experts_per_tok, max_batch * max_seq,
                                            group=group, device_epochs=True, packed=experts)
-            layers.append(_Layer(*attn, router_w, experts, ep=ep))
+                ep_decode = PeerExpertParallelMoE(router_w, None, None, E, cfg.num_experts_per_tok, max_batch,
+                                                  group=group, device_epochs=True, packed=experts)
+            layers.append(_Layer(*attn, router_w, experts, ep=ep, ep_decode=ep_decode))
         return cls(cfg, rnd(cfg.vocab_size, H), layers, ones(H), rnd(cfg.vocab_size, H), max_batch, max_seq)
 
     def close(self):
         """Release the expert-parallel exchange buffers (every rank together)."""
         self.release_graph()
         for lyr in self.layers:
-            if lyr.ep is not None:
-                lyr.ep.close()
+            for blk in (lyr.ep, lyr.ep_decode):
+                if blk is not None:
+                    blk.close()
 
     @classmethod
     def from_hf(cls, model, device="cuda", max_batch: int = 8, max_seq: int = 640) -> "Qwen3MoEStack":
@@ -215,9 +220,9 @@ class Qwen3MoEStack:
                    max_batch, max_seq)
 
     # ------------------------------------------------------------ layers
-    def _moe(self, lyr: _Layer, x: torch.Tensor) -> torch.Tensor:
+    def _moe(self, lyr: _Layer, x: torch.Tensor, decode: bool = False) -> torch.Tensor:
         if lyr.ep is not None:
-            return lyr.ep(x)
+            return lyr.ep_decode(x) if decode else lyr.ep(x)
         return ops.moe_block(x, lyr.router_w, lyr.experts, self.cfg.num_experts_per_tok,
                              router_w_split=lyr.router_split)
 
@@ -235,7 +240,7 @@ class Qwen3MoEStack:
         v = qkv[:, (nq + nkv) * hd:].view(B, S, nkv, hd).transpose(1, 2)
         return q, k, v
 
-    def _layers(self, h: torch.Tensor, attention, linear=F.linear):
+    def _layers(self, h: torch.Tensor, attention, linear=F.linear, decode: bool = False):
         """Run every layer on h [T, H]; ``attention(li, lyr, xn)`` returns the
         attention output [T, nq*hd] before the O projection (``linear``).
         Returns the final norm of the residual stream."""
@@ -251,7 +256,7 @@ class Qwen3MoEStack:
                 xn, res = ops.add_rmsnorm(h, res, lyr.in_norm, eps)
             a = linear(attention(li, lyr, xn), lyr.o_w)
             xn, res = ops.add_rmsnorm(a, res, lyr.post_norm, eps)
-            h = self._moe(lyr, xn)
+            h = self._moe(lyr, xn, decode)
         return ops.add_rmsnorm(h, res, self.final_norm, eps)[0]
 
     # ------------------------------------------------------------ prefill
@@ -299,7 +304,7 @@ class Qwen3MoEStack:
             return ops.decode_attention(qkv, lyr.q_norm, lyr.k_norm, self._pos, self.k_cache[li], self.v_cache[li],
                                         c.num_attention_heads, c.num_key_value_heads, c.rope_theta, c.rms_norm_eps)
 
-        hn = self._layers(h, attention, linear)
+        hn = self._layers(h, attention, linear, decode=True)
         return linear(hn, self.lm_head)
 
     @torch.inference_mode()
