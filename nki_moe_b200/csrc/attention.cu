@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnPara
   const int c = blockIdx.x, j = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;  // MMA fragment row group / column pair
+  pdl_launch_dependents();
+  pdl_wait();
   // the step's query rows (and the key / value row for warps 0 / 1) do not
   // depend on the position: their loads go out first
   const long long row_len = static_cast<long long>(p.nq + 2 * p.nkv) * D;
@@ -391,8 +393,7 @@ cudaError_t decode_attention_launch(const __nv_bfloat16* qkv, const void* qw, co
   p.part = reinterpret_cast<float*>(ws + 256 + counters);
   if (p.grp > kMaxGroup) return cudaErrorInvalidValue;
   const dim3 grid(p.nsplit, n_kv, B);
-  decode_attention_kernel<<<grid, kAttnThreads, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(decode_attention_kernel, grid, dim3(kAttnThreads), 0, s, p);
 }
 
 }  // namespace nkimoe

@@ -65,6 +65,7 @@ std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-co
 std::atomic<int> g_stage_stores{3};  // rows-schedule epilogue staging: bit 0 SwiGLU, bit 1 scaled bf16
 std::atomic<int> g_gather_fused{0};  // GEMM-1 gathers its rows itself: 1 cp.async, 2 TMA gather4
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
+std::atomic<int> g_pdl{1};           // programmatic dependent launch of the decode-path kernels
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
@@ -364,6 +365,8 @@ int device_sm_count() {
   return counts[dev];
 }
 
+bool pdl_enabled() { return g_pdl.load() != 0; }
+
 }  // namespace nkimoe
 
 using namespace nkimoe;
@@ -404,6 +407,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "prefetch" && value >= 0 && value <= 16) {
     g_prefetch = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "pdl" && (value == 0 || value == 1)) {
+    g_pdl = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "router" && value >= 0 && value <= 2) {

@@ -21,6 +21,18 @@ constexpr int kDevErrTmem = 4;          // tensor-memory allocation returned not
 
 constexpr long long kWaitBudgetCycles = 4000000000LL;
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute (launch_pdl) may start while its predecessor
+// in the stream is still running: pdl_wait() blocks until the predecessor
+// grid has completed and its memory is visible, and every such kernel calls
+// it before its first global-memory access (so completion stays transitive
+// along the stream).  pdl_launch_dependents() lets the stream's next kernel be
+// launched early; that kernel still waits in its own pdl_wait().
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -987,6 +987,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_act);
     prefetch_tmap(&tmap_w);
   }
+  // programmatic dependent launch: the prologue above overlaps the previous
+  // kernel; its outputs (offsets, activation rows) are read after this wait
+  pdl_launch_dependents();
+  pdl_wait();
   if (warp == 1) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
   if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BT, feat_tiles);
   tcgen05_fence_before();
@@ -1208,9 +1212,10 @@ cudaError_t ensure_smem_optin(GemmKernel kernel, size_t smem) {
 }
 
 cudaError_t launch_with_smem(GemmKernel kernel, size_t smem, int grid, const CUtensorMap& a, const CUtensorMap& w,
-                             const GroupedGemmParams& p, cudaStream_t s) {
+                             const GroupedGemmParams& p, cudaStream_t s, bool pdl = false) {
   cudaError_t e = ensure_smem_optin(kernel, smem);
   if (e != cudaSuccess) return e;
+  if (pdl) return launch_pdl(kernel, dim3(grid), dim3(kThreads), smem, s, a, w, p);
   kernel<<<grid, kThreads, smem, s>>>(a, w, p);
   return cudaGetLastError();
 }
@@ -1311,11 +1316,14 @@ cudaError_t grouped_gemm_launch(int variant, const CUtensorMap& tmap_act, const 
         return cudaErrorInvalidValue;
       return launch_cluster2(grouped_gemm_tokens2_kernel<6>, tokens2_smem(6), grid, tmap_act, tmap_w, p, s);
     case kWeightsT16:
-      return launch_with_smem(grouped_gemm_weights_kernel<16, 8>, weights_smem(16, 8), grid, tmap_act, tmap_w, p, s);
+      return launch_with_smem(grouped_gemm_weights_kernel<16, 8>, weights_smem(16, 8), grid, tmap_act, tmap_w, p, s,
+                              true);
     case kWeightsT32:
-      return launch_with_smem(grouped_gemm_weights_kernel<32, 8>, weights_smem(32, 8), grid, tmap_act, tmap_w, p, s);
+      return launch_with_smem(grouped_gemm_weights_kernel<32, 8>, weights_smem(32, 8), grid, tmap_act, tmap_w, p, s,
+                              true);
     case kWeightsT64:
-      return launch_with_smem(grouped_gemm_weights_kernel<64, 6>, weights_smem(64, 6), grid, tmap_act, tmap_w, p, s);
+      return launch_with_smem(grouped_gemm_weights_kernel<64, 6>, weights_smem(64, 6), grid, tmap_act, tmap_w, p, s,
+                              true);
   }
   return cudaErrorInvalidValue;
 }

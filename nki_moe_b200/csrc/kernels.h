@@ -18,6 +18,26 @@ constexpr int kI64 = 3;
 
 constexpr int kMaxExperts = 512;
 
+// Launch with programmatic dependent launch (see pdl_wait in common.cuh) when
+// the "pdl" option is on (the default); the kernel must call pdl_wait()
+// before touching global memory.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Stages of a block call, in launch order (for nkimoe_set_stage_events).
 enum Stage : int {
   kStageRouter = 0,

@@ -50,6 +50,8 @@ __global__ void __launch_bounds__(kLinWarps * 32) skinny_linear_kernel(const __n
                                                                       __nv_bfloat16* __restrict__ y, int M, int N,
                                                                       int K) {
   __shared__ float red[kLinWarps][MT][16][9];  // padded: conflict-free column reads
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const long long n0 = static_cast<long long>(blockIdx.x) * 16;
@@ -114,10 +116,9 @@ cudaError_t skinny_linear_launch(const __nv_bfloat16* x, const __nv_bfloat16* w,
   // one CTA per 16 weight rows (a K split over CTA clusters, partials added
   // through distributed shared memory, measured slower at every shape here)
   const unsigned grid = static_cast<unsigned>(N / 16);
-  if (M <= 8)
-    skinny_linear_kernel<1><<<grid, kLinWarps * 32, 0, s>>>(x, w, y, M, N, K);
-  else
-    skinny_linear_kernel<2><<<grid, kLinWarps * 32, 0, s>>>(x, w, y, M, N, K);
+  cudaError_t e = M <= 8 ? launch_pdl(skinny_linear_kernel<1>, dim3(grid), dim3(kLinWarps * 32), 0, s, x, w, y, M, N, K)
+                         : launch_pdl(skinny_linear_kernel<2>, dim3(grid), dim3(kLinWarps * 32), 0, s, x, w, y, M, N, K);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

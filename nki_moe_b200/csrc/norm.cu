@@ -145,6 +145,8 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_row_kernel(const TX* x, c
                                                                   const TW* __restrict__ w, TO* out, int hidden,
                                                                   float eps) {
   __shared__ float red[kRowThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait();
   const long long row = blockIdx.x;
   const int nchunk = hidden >> 3;
   float v[kRowChunks][8], wv[kRowChunks][8];
@@ -208,10 +210,9 @@ template <typename TX, typename TW, typename TO, bool kRes>
 cudaError_t launch_rms(const void* x, const void* res, void* res_out, const void* w, void* out, long long rows,
                        int hidden, float eps, cudaStream_t s) {
   if (rows <= kRowKernelMaxRows && hidden <= kRowChunks * 8 * kRowThreads) {
-    rmsnorm_row_kernel<TX, TW, TO, kRes><<<static_cast<unsigned>(rows), kRowThreads, 0, s>>>(
-        static_cast<const TX*>(x), static_cast<const TX*>(res), static_cast<TX*>(res_out),
-        static_cast<const TW*>(w), static_cast<TO*>(out), hidden, eps);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_row_kernel<TX, TW, TO, kRes>, dim3(static_cast<unsigned>(rows)), dim3(kRowThreads), 0,
+                      s, static_cast<const TX*>(x), static_cast<const TX*>(res), static_cast<TX*>(res_out),
+                      static_cast<const TW*>(w), static_cast<TO*>(out), hidden, eps);
   }
   const int warps = 8;
   const long long blocks = (rows + warps - 1) / warps;

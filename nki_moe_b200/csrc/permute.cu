@@ -158,6 +158,8 @@ __global__ void __launch_bounds__(kPermuteChunk) permute_small_kernel(
   __shared__ int wcnt[kWarps][kMaxExperts];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int TK = T * K;
+  pdl_launch_dependents();
+  pdl_wait();
   for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = 0;
   __syncthreads();
   int ev[kChunks];
@@ -238,6 +240,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* _
                                                           int H) {
   const int chunks = H >> 3;  // 16-byte chunks per row
   const int lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  pdl_wait();
   const long long rows = min(static_cast<long long>(expert_offsets[E]), max_rows);
   const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
@@ -269,6 +273,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ out, int T, int K, int H) {
   const uint32_t chunks = static_cast<uint32_t>(H) >> 3;
   const uint32_t n = static_cast<uint32_t>(T) * chunks;
+  pdl_launch_dependents();
+  pdl_wait();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const uint32_t t = i / chunks;
     const uint32_t c = i - t * chunks;
@@ -435,14 +441,12 @@ cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k
   }
   if (TK <= kPermuteSmall) {
     if (idx_dtype == kI64)
-      permute_small_kernel<long long><<<1, kPermuteChunk, 0, s>>>(static_cast<const long long*>(idx), tokens, top_k,
-                                                                  experts, row_token, row_slot, slot_row,
-                                                                  expert_offsets, slot_weight, row_weight, status);
-    else
-      permute_small_kernel<int32_t><<<1, kPermuteChunk, 0, s>>>(static_cast<const int32_t*>(idx), tokens, top_k,
-                                                                experts, row_token, row_slot, slot_row,
-                                                                expert_offsets, slot_weight, row_weight, status);
-    return cudaGetLastError();
+      return launch_pdl(permute_small_kernel<long long>, dim3(1), dim3(kPermuteChunk), 0, s,
+                        static_cast<const long long*>(idx), tokens, top_k, experts, row_token, row_slot, slot_row,
+                        expert_offsets, slot_weight, row_weight, status);
+    return launch_pdl(permute_small_kernel<int32_t>, dim3(1), dim3(kPermuteChunk), 0, s,
+                      static_cast<const int32_t*>(idx), tokens, top_k, experts, row_token, row_slot, slot_row,
+                      expert_offsets, slot_weight, row_weight, status);
   }
   if (idx_dtype == kI64) {
     permute_count_kernel<long long><<<C, kPermuteChunk, 0, s>>>(static_cast<const long long*>(idx), tokens, top_k,
@@ -469,18 +473,16 @@ cudaError_t permute_launch(const void* idx, int idx_dtype, int tokens, int top_k
 cudaError_t gather_rows_launch(const __nv_bfloat16* x, const int32_t* row_token, const int32_t* expert_offsets,
                                int experts, __nv_bfloat16* x_perm, long long max_rows, int hidden, cudaStream_t s) {
   if (max_rows == 0) return cudaSuccess;
-  gather_rows_kernel<<<grid_for(max_rows * 32, 256), 256, 0, s>>>(x, row_token, expert_offsets, experts, x_perm,
-                                                                    max_rows, hidden);
-  return cudaGetLastError();
+  return launch_pdl(gather_rows_kernel, dim3(grid_for(max_rows * 32, 256)), dim3(256), 0, s, x, row_token,
+                    expert_offsets, experts, x_perm, max_rows, hidden);
 }
 
 cudaError_t combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, const float* slot_weight,
                            __nv_bfloat16* out, int tokens, int top_k, int hidden, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   if (static_cast<long long>(tokens) * (hidden / 8) >= (1LL << 31)) return cudaErrorInvalidValue;
-  combine_kernel<<<grid_for(static_cast<long long>(tokens) * (hidden / 8), 256), 256, 0, s>>>(
-      y, slot_row, slot_weight, out, tokens, top_k, hidden);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, dim3(grid_for(static_cast<long long>(tokens) * (hidden / 8), 256)), dim3(256), 0,
+                    s, y, slot_row, slot_weight, out, tokens, top_k, hidden);
 }
 
 cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s) {

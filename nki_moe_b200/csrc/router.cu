@@ -296,6 +296,8 @@ __global__ void __launch_bounds__(256)
                              int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out, float* partial,
                              int* counters, int kslice) {
   __shared__ int s_last;
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int eb = blockIdx.x, sl = blockIdx.y, gi = blockIdx.z;
   const int e = eb * kRouterExpertsPerCta + warp;
@@ -456,15 +458,16 @@ cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, co
   const int kslice = ((hidden / 128 + slices - 1) / slices) * 128;
   const dim3 grid((experts + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta, slices, groups);
   const int vpt = (experts + 31) / 32;
+  cudaError_t e = cudaSuccess;
 #define NKI_RTS(V)                                                                                           \
-  router_topk_split_kernel<V><<<grid, 256, 0, s>>>(x, wr, bias, logits_out, tokens, hidden, experts, top_k, idx, w, \
-                                                   partial, counters, kslice)
+  e = launch_pdl(router_topk_split_kernel<V>, grid, dim3(256), 0, s, x, wr, bias, logits_out, tokens, hidden,      \
+                 experts, top_k, idx, w, partial, counters, kslice)
   if (vpt <= 1) NKI_RTS(1);
   else if (vpt <= 2) NKI_RTS(2);
   else if (vpt <= 4) NKI_RTS(4);
   else NKI_RTS(8);
 #undef NKI_RTS
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
