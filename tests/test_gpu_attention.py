@@ -34,11 +34,11 @@ def _cuda():
         pytest.skip("no CUDA device")
 
 
-def make_case(B, nq, nkv, max_seq, seed):
+def make_case(B, nq, nkv, max_seq, seed, w_dtype=torch.bfloat16):
     g = torch.Generator().manual_seed(seed)
     qkv = torch.randn(B, (nq + 2 * nkv) * HD, generator=g).bfloat16()
-    qw = (1 + 0.1 * torch.randn(HD, generator=g)).bfloat16()
-    kw = (1 + 0.1 * torch.randn(HD, generator=g)).bfloat16()
+    qw = (1 + 0.1 * torch.randn(HD, generator=g)).to(w_dtype)
+    kw = (1 + 0.1 * torch.randn(HD, generator=g)).to(w_dtype)
     kc = torch.randn(B, nkv, max_seq, HD, generator=g).bfloat16()
     vc = torch.randn(B, nkv, max_seq, HD, generator=g).bfloat16()
     return qkv, qw, kw, kc, vc
@@ -68,8 +68,8 @@ def reference(qkv, qw, kw, positions, kc, vc, nq, nkv, theta=1e6, eps=1e-6):
     return out.view(B, nq * HD), k_new, v_new
 
 
-def run_and_check(B, nq, nkv, max_seq, positions, seed, broadcast=False):
-    qkv, qw, kw, kc, vc = make_case(B, nq, nkv, max_seq, seed)
+def run_and_check(B, nq, nkv, max_seq, positions, seed, broadcast=False, w_dtype=torch.bfloat16):
+    qkv, qw, kw, kc, vc = make_case(B, nq, nkv, max_seq, seed, w_dtype)
     ref, k_new, v_new = reference(qkv, qw, kw, positions, kc, vc, nq, nkv)
     kc_d, vc_d = kc.cuda(), vc.cuda()
     pos_d = torch.tensor([positions[0]] if broadcast else positions, dtype=torch.int64, device="cuda")
@@ -111,6 +111,12 @@ def test_decode_attention_long_cache_and_wide_groups():
     that each CTA stages several 64-position blocks."""
     run_and_check(2, 16, 1, 3000, [2999, 1500], seed=3)
     run_and_check(3, 8, 8, 200, [5, 199, 130], seed=4)
+
+
+def test_decode_attention_single_sequence_fp32_norm_weights():
+    """One sequence, fp32 q/k norm weights, a few positions into a long cache."""
+    run_and_check(1, 32, 4, 4096, [3], seed=9, w_dtype=torch.float32)
+    run_and_check(1, 32, 4, 4096, [4095], seed=10, w_dtype=torch.float32)
 
 
 def test_decode_attention_consecutive_steps():
@@ -159,7 +165,8 @@ def test_decode_attention_in_graph():
         vc[:, :, p] = v_new
 
 
-def test_decode_attention_position_out_of_range_is_reported():
+def test_decode_attention_position_out_of_range_is_reported(monkeypatch):
+    monkeypatch.setenv("NKIMOE_SYNC_CHECK", "0")  # read the status here, not inside the call
     B, nq, nkv, S = 2, 32, 4, 128
     qkv, qw, kw, kc, vc = make_case(B, nq, nkv, S, seed=8)
     kc_d, vc_d = kc.cuda(), vc.cuda()

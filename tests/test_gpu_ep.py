@@ -19,8 +19,14 @@ pytestmark = pytest.mark.gpu
 def _cuda_env():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
+    old = os.environ.get("NKIMOE_SYNC_CHECK")
     os.environ["NKIMOE_SYNC_CHECK"] = "1"
     _lib.load()
+    yield
+    if old is None:
+        os.environ.pop("NKIMOE_SYNC_CHECK", None)
+    else:
+        os.environ["NKIMOE_SYNC_CHECK"] = old
 
 
 @pytest.mark.parametrize("schedule", [0, 1, 2])

@@ -30,11 +30,16 @@ COS_TOL = 0.999
 def _cuda_env():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
+    old = os.environ.get("NKIMOE_SYNC_CHECK")
     os.environ["NKIMOE_SYNC_CHECK"] = "1"
     _lib.load()
     yield
     _lib.set_option("gemm_schedule", 0)
     _lib.set_option("weights_rows", 0)
+    if old is None:
+        os.environ.pop("NKIMOE_SYNC_CHECK", None)
+    else:
+        os.environ["NKIMOE_SYNC_CHECK"] = old
 
 
 def bf(t):
@@ -186,6 +191,33 @@ def test_block_router_paths(c1_inputs, router, T):
         np.testing.assert_allclose(w.cpu().numpy()[ok], rwt[ok], rtol=2e-5, atol=1e-6)
     finally:
         _lib.set_option("router", 0)
+
+
+@pytest.mark.parametrize("T,E,K,H", [(1, 128, 8, 2048), (7, 128, 8, 2048), (9, 128, 8, 2048), (64, 128, 8, 2048),
+                                     (383, 128, 8, 2048), (384, 128, 8, 2048), (385, 128, 8, 2048),
+                                     (40, 256, 8, 2048), (13, 64, 6, 128), (5, 32, 32, 256)])
+def test_decode_router_token_groups(T, E, K, H):
+    """The one-launch decode router (hidden slices, per-8-token-group last-CTA
+    top-k) across token-group counts up to its limit of 48 groups (384
+    tokens; 385 takes the split-K + top-k path), expert counts 32..256 and a
+    router bias: identical routing to the oracle outside near ties, weights
+    to fp32 rounding."""
+    g = torch.Generator().manual_seed(T * 7 + E + K)
+    x = torch.randn(T, H, generator=g)
+    rw = torch.randn(E, H, generator=g) * 0.02
+    bias = torch.randn(E, generator=g) * 0.1
+    xb, xn = bf(x)
+    idx, w = ops.route(xb, rw.cuda(), K, bias=bias.cuda(), tensor_router=False)
+    lg = oracle.router_logits(xn, rw.numpy()) + bias.numpy()
+    ri, rwt = oracle.topk_softmax(lg, K)
+    ties = oracle.near_tie_tokens(lg, K)
+    same = np.all(idx.cpu().numpy() == ri, axis=1)
+    assert np.all(same | ties), f"{(~same & ~ties).sum()} non-tie tokens routed differently"
+    ok = same & ~ties
+    np.testing.assert_allclose(w.cpu().numpy()[ok], rwt[ok], rtol=2e-5, atol=1e-6)
+    # the counters the router leaves behind are zero: a second call routes the same
+    idx2, w2 = ops.route(xb, rw.cuda(), K, bias=bias.cuda(), tensor_router=False)
+    assert torch.equal(idx2, idx) and torch.equal(w2, w)
 
 
 # ---------------------------------------------------------------- K3
