@@ -215,6 +215,20 @@ NKIMOE_API int nkimoe_moe_block(const void* x, const float* router_w, const floa
                      void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
                      int64_t K, void* workspace, size_t workspace_bytes, void* stream);
 
+/* nkimoe_moe_block followed by the decoder's residual add and the next
+ * RMSNorm (qwen_with_nki.py:447-454 with NKIRMSNorm, nki_custom_rmsnorm.py):
+ * residual_out = residual + block(x) (bf16) and norm_out =
+ * rmsnorm(residual_out) * norm_w (bf16), all [T, H]; residual_out may alias
+ * residual; norm_w_dtype F32 or BF16.  Same workspace as nkimoe_moe_block.
+ * Up to 512 tokens the block's combine and the norm run as one kernel; the
+ * results equal nkimoe_moe_block + nkimoe_add_rmsnorm bit for bit. */
+NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w, const float* router_bias,
+                                            const void* router_w_split, const void* w13, const void* w2,
+                                            const void* residual, void* residual_out, const void* norm_w,
+                                            int norm_w_dtype, float eps, void* norm_out, int32_t* topk_idx_out,
+                                            float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* nkimoe_moe_block for callers that cannot allocate GPU memory (a server that
  * reserved all device memory up front, a runtime whose allocator may not be
  * entered where the layer is issued, an embedding that forbids allocation

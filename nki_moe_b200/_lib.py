@@ -51,6 +51,8 @@ SIGNATURES = {
     "nkimoe_moe_experts": (_i, [_vp, _vp, _vp, _vp, _i, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "nkimoe_moe_block": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _sz,
                               _vp]),
+    "nkimoe_moe_block_add_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _vp, _vp, _i64,
+                                          _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "nkimoe_router_split": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_read_status": (_i, [_vp, _vp, _c.POINTER(_i)]),
     "nkimoe_moe_block_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,

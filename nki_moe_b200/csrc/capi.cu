@@ -208,9 +208,13 @@ int check_moe_shapes(long long T, long long H, long long I, long long E, long lo
 
 // logits -> (idx, w): CUDA-core split-K or tensor-core split-fp32 GEMM, then
 // softmax/top-k/renormalise.
+// With `perm`, a decode batch of one token group (8 tokens or fewer) also gets
+// its permutation from the router's last CTA; *permuted then says so.
 int router_impl(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
                 int32_t* idx, float* w, long long T, long long H, long long E, long long K, char* base,
-                const WsLayout& L, int* status, cudaStream_t s) {
+                const WsLayout& L, int* status, cudaStream_t s, const RouterPermOut* perm = nullptr,
+                bool* permuted = nullptr) {
+  if (permuted) *permuted = false;
   float* logits = reinterpret_cast<float*>(base + L.logits);
   const int mode = g_router.load();
   const bool tensor = router_w_split && E % 128 == 0 && (mode == 2 || (mode == 0 && T >= 256));
@@ -230,10 +234,12 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
     // logits and top-k in one launch; the top-k stage marker follows it.  Its
     // per-group counters sit in the status block after the status word, which
     // every caller clears (256 bytes) before the block.
+    const bool fuse_perm = perm && permuted && router_topk_fused_permutes(static_cast<int>(T));
     NKI_CUDA(router_topk_fused_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
                                       static_cast<int>(T), static_cast<int>(H), static_cast<int>(E),
                                       static_cast<int>(K), idx, w, reinterpret_cast<float*>(base + L.partial),
-                                      reinterpret_cast<int*>(base + L.status + 64), s));
+                                      reinterpret_cast<int*>(base + L.status + 64), s, fuse_perm ? perm : nullptr));
+    if (fuse_perm) *permuted = true;
     mark(kStageTopk, s);
   } else {
     float* partial = reinterpret_cast<float*>(base + L.partial);
@@ -257,9 +263,21 @@ struct PeerCombine {
   const uint32_t* epoch_p;
 };
 
+// The decoder's residual add + RMSNorm after the block (qwen_with_nki.py:447-454):
+// residual_out = residual + block output; out = rmsnorm(residual_out) * w.
+struct FusedNorm {
+  const void* residual;
+  void* residual_out;
+  const void* w;
+  int w_dtype;
+  float eps;
+  void* out;
+};
+
 int experts_impl(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype, const float* topk_w,
                  void* out, long long T, long long H, long long I, long long E, long long K, void* ws, size_t ws_bytes,
-                 cudaStream_t s, const PeerCombine* pc = nullptr, int* status_word = nullptr) {
+                 cudaStream_t s, const PeerCombine* pc = nullptr, int* status_word = nullptr,
+                 const FusedNorm* fn = nullptr, bool permuted = false) {
   const WsLayout L = ws_layout(T, H, I, E, K);
   char* base = static_cast<char*>(ws);
   int* status = status_word ? status_word : reinterpret_cast<int*>(base + L.status);
@@ -273,8 +291,9 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
   const long long TK = T * K;
   if (T == 0) return NKIMOE_OK;
   mark(kStagePermute, s);
-  NKI_CUDA(permute_launch(idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
-                          row_slot, slot_row, offsets, base + L.scratch, status, s, topk_w, row_weight));
+  if (!permuted)  // else the router's last CTA has written the permutation
+    NKI_CUDA(permute_launch(idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
+                            row_slot, slot_row, offsets, base + L.scratch, status, s, topk_w, row_weight));
   int rc;
   if (g_gather_fused.load()) {
     // GEMM-1 gathers its activation rows (x[row_token[r]]) in its producer warp
@@ -298,6 +317,18 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
   if (pc) {
     NKI_CUDA(ep_peer_combine_launch(xy, slot_row, static_cast<int>(T), static_cast<int>(K), static_cast<int>(H),
                                     pc->Tm, pc->me, pc->peers, pc->L, pc->P, pc->counter, pc->epoch_p, s));
+  } else if (fn && combine_add_rmsnorm_supported(T, static_cast<int>(H))) {
+    // few rows: the combine and the next residual add + norm in one kernel
+    NKI_CUDA(combine_add_rmsnorm_launch(xy, slot_row, static_cast<int>(K),
+                                        static_cast<const __nv_bfloat16*>(fn->residual),
+                                        static_cast<__nv_bfloat16*>(fn->residual_out), fn->w, fn->w_dtype,
+                                        static_cast<__nv_bfloat16*>(fn->out), T, static_cast<int>(H), fn->eps, s));
+  } else if (fn) {
+    // the block output goes through the SwiGLU buffer, free after GEMM-2
+    NKI_CUDA(combine_launch(xy, slot_row, nullptr, h, static_cast<int>(T), static_cast<int>(K), static_cast<int>(H),
+                            s));
+    NKI_CUDA(add_rmsnorm_launch(h, fn->residual, fn->residual_out, fn->w, fn->w_dtype, fn->out, T,
+                                static_cast<int>(H), fn->eps, s));
   } else {
     NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
                             static_cast<int>(K), static_cast<int>(H), s));
@@ -370,6 +401,51 @@ bool pdl_enabled() { return g_pdl.load() != 0; }
 }  // namespace nkimoe
 
 using namespace nkimoe;
+
+namespace {
+
+int moe_block_impl(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                   const void* w13, const void* w2, void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T,
+                   int64_t H, int64_t I, int64_t E, int64_t K, void* workspace, size_t workspace_bytes, void* stream,
+                   const FusedNorm* fn) {
+  int rc = check_moe_shapes(T, H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
+  NKI_REQUIRE(E <= 256, NKIMOE_ERR_UNSUPPORTED, "router top-k supports up to 256 experts");
+  const size_t need = nkimoe_moe_workspace_bytes(T, H, I, E, K);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  const cudaStream_t s = as_stream(stream);
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(x && router_w && w13 && w2 && (out || fn), NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(x) && aligned16(router_w) && aligned16(w13) && aligned16(w2) && (fn || aligned16(out)),
+              NKIMOE_ERR_INVALID_ARG, "x, weights and out must be 16-byte aligned");
+  if (fn) {
+    NKI_REQUIRE(fn->residual && fn->residual_out && fn->w && fn->out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+    NKI_REQUIRE(aligned16(fn->residual) && aligned16(fn->residual_out) && aligned16(fn->w) && aligned16(fn->out),
+                NKIMOE_ERR_INVALID_ARG, "residual, norm weight and outputs must be 16-byte aligned");
+    NKI_REQUIRE(fn->w_dtype == NKIMOE_F32 || fn->w_dtype == NKIMOE_BF16, NKIMOE_ERR_INVALID_ARG,
+                "bad norm weight dtype");
+    NKI_REQUIRE(H % 8 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden must be a multiple of 8");
+  }
+  NKI_REQUIRE(!router_w_split || aligned16(router_w_split), NKIMOE_ERR_INVALID_ARG, "router_w_split misaligned");
+  const WsLayout L = ws_layout(T, H, I, E, K);
+  char* base = static_cast<char*>(workspace);
+  int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(base + L.idx);
+  float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(base + L.w);
+  int* status = reinterpret_cast<int*>(base + L.status);
+  const RouterPermOut perm{reinterpret_cast<int32_t*>(base + L.row_token), reinterpret_cast<int32_t*>(base + L.row_slot),
+                           reinterpret_cast<int32_t*>(base + L.slot_row), reinterpret_cast<int32_t*>(base + L.offsets),
+                           reinterpret_cast<float*>(base + L.row_weight), status};
+  bool permuted = false;
+  rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, base, L, status, s, &perm,
+                   &permuted);
+  if (rc != NKIMOE_OK) return rc;
+  return experts_impl(x, w13, w2, idx, NKIMOE_I32, w, out, T, H, I, E, K, workspace, workspace_bytes, s, nullptr,
+                      nullptr, fn, permuted);
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -626,27 +702,18 @@ int nkimoe_moe_block(const void* x, const float* router_w, const float* router_b
                      const void* w13, const void* w2, void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T,
                      int64_t H, int64_t I, int64_t E, int64_t K, void* workspace, size_t workspace_bytes,
                      void* stream) {
-  int rc = check_moe_shapes(T, H, I, E, K);
-  if (rc != NKIMOE_OK) return rc;
-  NKI_REQUIRE(E <= 256, NKIMOE_ERR_UNSUPPORTED, "router top-k supports up to 256 experts");
-  const size_t need = nkimoe_moe_workspace_bytes(T, H, I, E, K);
-  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
-  NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
-  const cudaStream_t s = as_stream(stream);
-  NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
-  if (T == 0) return NKIMOE_OK;
-  NKI_REQUIRE(x && router_w && w13 && w2 && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
-  NKI_REQUIRE(aligned16(x) && aligned16(router_w) && aligned16(w13) && aligned16(w2) && aligned16(out),
-              NKIMOE_ERR_INVALID_ARG, "x, weights and out must be 16-byte aligned");
-  NKI_REQUIRE(!router_w_split || aligned16(router_w_split), NKIMOE_ERR_INVALID_ARG, "router_w_split misaligned");
-  const WsLayout L = ws_layout(T, H, I, E, K);
-  char* base = static_cast<char*>(workspace);
-  int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(base + L.idx);
-  float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(base + L.w);
-  rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, base, L,
-                   reinterpret_cast<int*>(base + L.status), s);
-  if (rc != NKIMOE_OK) return rc;
-  return experts_impl(x, w13, w2, idx, NKIMOE_I32, w, out, T, H, I, E, K, workspace, workspace_bytes, s);
+  return moe_block_impl(x, router_w, router_bias, router_w_split, w13, w2, out, topk_idx_out, topk_w_out, T, H, I, E,
+                        K, workspace, workspace_bytes, stream, nullptr);
+}
+
+int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w, const float* router_bias,
+                                 const void* router_w_split, const void* w13, const void* w2, const void* residual,
+                                 void* residual_out, const void* norm_w, int norm_w_dtype, float eps, void* norm_out,
+                                 int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,
+                                 int64_t E, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  const FusedNorm fn{residual, residual_out, norm_w, norm_w_dtype, eps, norm_out};
+  return moe_block_impl(x, router_w, router_bias, router_w_split, w13, w2, nullptr, topk_idx_out, topk_w_out, T, H,
+                        I, E, K, workspace, workspace_bytes, stream, &fn);
 }
 
 int nkimoe_read_status(void* workspace, void* stream, int* status_out) {

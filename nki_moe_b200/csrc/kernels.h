@@ -57,6 +57,13 @@ cudaError_t rmsnorm_launch(const void* x, int x_dtype, const void* w, int w_dtyp
                            long long rows, int hidden, float eps, cudaStream_t s);
 cudaError_t add_rmsnorm_launch(const void* x, const void* residual, void* residual_out, const void* w, int w_dtype,
                                void* out, long long rows, int hidden, float eps, cudaStream_t s);
+// The MoE block's combine (rows of y already scaled by their routing weight)
+// fused with the next residual add + RMSNorm, rows <= 512 (one CTA per row).
+bool combine_add_rmsnorm_supported(long long rows, int hidden);
+cudaError_t combine_add_rmsnorm_launch(const __nv_bfloat16* y, const int32_t* slot_row, int K,
+                                       const __nv_bfloat16* residual, __nv_bfloat16* residual_out, const void* w,
+                                       int w_dtype, __nv_bfloat16* out, long long rows, int hidden, float eps,
+                                       cudaStream_t s);
 cudaError_t qk_norm_rope_launch(const void* qkv_in, void* qkv_out, const void* qw, const void* kw, int w_dtype,
                                 const long long* positions, long long tokens, int n_heads, int n_kv, int head_dim,
                                 float theta, float eps, cudaStream_t s);
@@ -96,9 +103,21 @@ cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, in
 bool router_topk_fused_supported(int hidden, int experts, int top_k);
 int router_topk_slices(int tokens, int hidden, int experts);
 int router_topk_max_groups();
+// Outputs of the permutation (permute_launch's) for the decode router to
+// fill itself when the batch is one token group (8 tokens or fewer).
+struct RouterPermOut {
+  int32_t* row_token;
+  int32_t* row_slot;
+  int32_t* slot_row;
+  int32_t* expert_offsets;
+  float* row_weight;
+  int* status;
+};
+bool router_topk_fused_permutes(int tokens);
 cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                      int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
-                                     float* partial, int* counters, cudaStream_t s);
+                                     float* partial, int* counters, cudaStream_t s,
+                                     const RouterPermOut* perm = nullptr);
 // Same on logits given as `splits` fp32 partial sums [split][T][E] (+ bias[E]);
 // logits_out (nullable) receives the summed logits.
 cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,

@@ -204,6 +204,100 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_row_kernel(const TX* x, c
   }
 }
 
+// The MoE block's combine fused with the decoder's next residual add +
+// RMSNorm, for few rows: per token row (one CTA), h = sum_k y[slot_row[t,k]]
+// in fp32 with k ascending and rounded to bf16 (combine_kernel's arithmetic),
+// then r = h + residual rounded to bf16 and the norm of r, with the reduction
+// order of rmsnorm_row_kernel: bit-identical to combine + add_rmsnorm.
+template <typename TW>
+__global__ void __launch_bounds__(kRowThreads) combine_add_rmsnorm_row_kernel(
+    const __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ slot_row, int K,
+    const __nv_bfloat16* residual, __nv_bfloat16* residual_out, const TW* __restrict__ w,
+    __nv_bfloat16* __restrict__ out, int hidden, float eps) {
+  __shared__ float red[kRowThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const long long row = blockIdx.x;
+  const int nchunk = hidden >> 3;
+  float v[kRowChunks][8], wv[kRowChunks][8], r[kRowChunks][8];
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+      load8(w + c * 8, wv[i]);
+      load8(residual + row * hidden + c * 8, r[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    }
+  }
+  // ascending k, as combine_kernel: 8 slots' row loads in flight per chunk
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c >= nchunk) continue;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      int rr[8];
+      uint4 u[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) rr[q] = k0 + q < K ? slot_row[row * K + k0 + q] : -1;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (rr[q] >= 0) u[q] = *reinterpret_cast<const uint4*>(y + static_cast<long long>(rr[q]) * hidden + c * 8);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (rr[q] < 0) continue;
+        const float2 a = unpack_bf16x2(u[q].x), b = unpack_bf16x2(u[q].y), cc = unpack_bf16x2(u[q].z),
+                     d = unpack_bf16x2(u[q].w);
+        v[i][0] = fmaf(1.f, a.x, v[i][0]);
+        v[i][1] = fmaf(1.f, a.y, v[i][1]);
+        v[i][2] = fmaf(1.f, b.x, v[i][2]);
+        v[i][3] = fmaf(1.f, b.y, v[i][3]);
+        v[i][4] = fmaf(1.f, cc.x, v[i][4]);
+        v[i][5] = fmaf(1.f, cc.y, v[i][5]);
+        v[i][6] = fmaf(1.f, d.x, v[i][6]);
+        v[i][7] = fmaf(1.f, d.y, v[i][7]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+      round_bf16(v[i]);  // the block output h, bf16
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] += r[i][j];
+      round_bf16(v[i]);  // the residual stream, bf16
+      store8(residual_out + row * hidden + c * 8, v[i]);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < kRowThreads / 32; ++q) ss += red[q];
+  const float rinv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+#pragma unroll
+  for (int i = 0; i < kRowChunks; ++i) {
+    const int c = threadIdx.x + i * kRowThreads;
+    if (c < nchunk) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * rinv * wv[i][j];
+      store8(out + row * hidden + c * 8, o);
+    }
+  }
+}
+
 constexpr long long kRowKernelMaxRows = 512;
 
 template <typename TX, typename TW, typename TO, bool kRes>
@@ -236,6 +330,26 @@ cudaError_t rmsnorm_launch(const void* x, int x_dtype, const void* w, int w_dtyp
   if (x_dtype == kF32 && w_dtype == kF32 && out_dtype == kBF16) NKI_RMS(float, float, bf);
   if (x_dtype == kF32 && w_dtype == kBF16 && out_dtype == kF32) NKI_RMS(float, bf, float);
 #undef NKI_RMS
+  return cudaErrorInvalidValue;
+}
+
+bool combine_add_rmsnorm_supported(long long rows, int hidden) {
+  return rows <= kRowKernelMaxRows && hidden % 8 == 0 && hidden <= kRowChunks * 8 * kRowThreads;
+}
+
+cudaError_t combine_add_rmsnorm_launch(const __nv_bfloat16* y, const int32_t* slot_row, int K,
+                                       const __nv_bfloat16* residual, __nv_bfloat16* residual_out, const void* w,
+                                       int w_dtype, __nv_bfloat16* out, long long rows, int hidden, float eps,
+                                       cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  if (!combine_add_rmsnorm_supported(rows, hidden)) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(rows)), block(kRowThreads);
+  if (w_dtype == kF32)
+    return launch_pdl(combine_add_rmsnorm_row_kernel<float>, grid, block, 0, s, y, slot_row, K, residual,
+                      residual_out, static_cast<const float*>(w), out, hidden, eps);
+  if (w_dtype == kBF16)
+    return launch_pdl(combine_add_rmsnorm_row_kernel<__nv_bfloat16>, grid, block, 0, s, y, slot_row, K, residual,
+                      residual_out, static_cast<const __nv_bfloat16*>(w), out, hidden, eps);
   return cudaErrorInvalidValue;
 }
 

@@ -12,23 +12,11 @@
 //               (warp match_any + popc, then per-warp counts).
 // No host synchronisation: the GEMMs read expert_offsets on the device.
 #include "kernels.h"
+#include "permute_small.cuh"
 
 namespace nkimoe {
 
 namespace {
-
-// A negative id marks an empty slot (skipped); an id >= E is an error.
-template <typename IdxT>
-__device__ __forceinline__ int load_expert(const IdxT* idx, long long j, int T, int K, int E, int* status) {
-  const long long k = j / T, t = j % T;
-  const long long e = static_cast<long long>(idx[t * K + k]);
-  if (e < 0) return -1;
-  if (e >= E) {
-    atomicOr(status, kDevErrBadIndex);
-    return -1;
-  }
-  return static_cast<int>(e);
-}
 
 template <typename IdxT>
 __global__ void __launch_bounds__(kPermuteChunk) permute_count_kernel(const IdxT* __restrict__ idx, int T, int K,
@@ -138,96 +126,17 @@ __global__ void __launch_bounds__(kPermuteChunk) permute_scatter_kernel(
   (void)status;
 }
 
-// The same permutation for few assignments (T*K <= kPermuteSmall, decode) in
-// one CTA, so a block call pays one launch instead of three: every thread
-// loads its assignments' expert ids once (assignment j = c * 256 + thread of
-// chunk c, k-major as above), the CTA counts and scans them in shared memory,
-// then walks the chunks in order with the same warp match_any ranking, adding
-// a running per-expert count between chunks.  Bit-identical to the
-// count/scan/scatter kernels.
-constexpr int kPermuteSmall = 8 * kPermuteChunk;
-
+// The permutation for few assignments (T*K <= kPermuteSmall, decode) in one
+// CTA (permute_small.cuh): a block call pays one launch instead of three.
 template <typename IdxT>
 __global__ void __launch_bounds__(kPermuteChunk) permute_small_kernel(
     const IdxT* __restrict__ idx, int T, int K, int E, int32_t* __restrict__ row_token,
     int32_t* __restrict__ row_slot, int32_t* __restrict__ slot_row, int32_t* __restrict__ expert_offsets,
     const float* __restrict__ slot_weight, float* __restrict__ row_weight, int* status) {
-  constexpr int kWarps = kPermuteChunk / 32;
-  constexpr int kChunks = kPermuteSmall / kPermuteChunk;
-  __shared__ int base[kMaxExperts];  // expert offset + rows placed by earlier chunks
-  __shared__ int wcnt[kWarps][kMaxExperts];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int TK = T * K;
   pdl_launch_dependents();
   pdl_wait();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = 0;
-  __syncthreads();
-  int ev[kChunks];
-#pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    const int j = c * kPermuteChunk + threadIdx.x;
-    ev[c] = j < TK ? load_expert(idx, j, T, K, E, status) : -1;
-    if (ev[c] >= 0) atomicAdd(&base[ev[c]], 1);
-  }
-  __syncthreads();
-  if (warp == 0) {  // totals -> exclusive offsets, in place
-    int run = 0;
-    for (int b = 0; b < E; b += 32) {
-      const int e = b + lane;
-      const int v = e < E ? base[e] : 0;
-      int incl = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
-      }
-      if (e < E) {
-        base[e] = run + incl - v;
-        expert_offsets[e] = run + incl - v;
-      }
-      run += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) expert_offsets[E] = run;
-  }
-  for (int i = threadIdx.x; i < kWarps * E; i += blockDim.x) wcnt[i / E][i % E] = 0;
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < kChunks; ++c) {
-    if (c * kPermuteChunk >= TK) break;  // uniform over the CTA
-    const int j = c * kPermuteChunk + threadIdx.x;
-    const int e = ev[c];
-    const unsigned peers = __match_any_sync(0xffffffffu, e);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    if (e >= 0 && rank == 0) wcnt[warp][e] = __popc(peers);
-    __syncthreads();
-    if (j < TK) {
-      const int k = j / T, t = j - k * T;
-      const long long slot = static_cast<long long>(t) * K + k;
-      if (e < 0) {
-        slot_row[slot] = -1;
-      } else {
-        int before = 0;
-        for (int w = 0; w < warp; ++w) before += wcnt[w][e];
-        const int pos = base[e] + before + rank;
-        row_token[pos] = t;
-        row_slot[pos] = static_cast<int32_t>(slot);
-        slot_row[slot] = pos;
-        if (row_weight) row_weight[pos] = slot_weight[slot];
-      }
-    }
-    __syncthreads();
-    // advance the running bases by this chunk's counts; clear the warp counts
-    for (int e2 = threadIdx.x; e2 < E; e2 += blockDim.x) {
-      int add = 0;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        add += wcnt[w][e2];
-        wcnt[w][e2] = 0;
-      }
-      base[e2] += add;
-    }
-    __syncthreads();
-  }
+  permute_small_cta<IdxT>(idx, T, K, E, row_token, row_slot, slot_row, expert_offsets, slot_weight, row_weight,
+                          status);
 }
 
 // x_perm[r] = x[row_token[r]] for r < expert_offsets[E].  One warp per row;

@@ -4,6 +4,7 @@
 #include <algorithm>
 
 #include "kernels.h"
+#include "permute_small.cuh"
 
 namespace nkimoe {
 
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(256)
     router_topk_split_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wr,
                              const float* __restrict__ bias, float* __restrict__ logits_out, int T, int H, int E,
                              int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out, float* partial,
-                             int* counters, int kslice) {
+                             int* counters, int kslice, RouterPermOut perm) {
   __shared__ int s_last;
   pdl_launch_dependents();
   pdl_wait();
@@ -390,6 +391,11 @@ __global__ void __launch_bounds__(256)
     topk_select_warp<VPT>(v, E, K, lane, idx_out + tt * K, w_out + tt * K);
   }
   if (threadIdx.x == 0) counters[gi] = 0;
+  if (perm.row_token != nullptr) {  // one token group: its permutation too
+    __syncthreads();                // the group's idx / w, stored by the 8 warps above
+    permute_small_cta<int32_t>(idx_out, T, K, E, perm.row_token, perm.row_slot, perm.slot_row, perm.expert_offsets,
+                               w_out, perm.row_weight, perm.status);
+  }
 }
 
 }  // namespace
@@ -434,11 +440,11 @@ bool router_topk_fused_supported(int hidden, int experts, int top_k) {
 }
 
 int router_topk_slices(int tokens, int hidden, int experts) {
-  // as many slices as fit one wave of resident CTAs (4 per SM at 256 threads x
-  // 64 registers): a second wave would add a whole round of load latency
+  // as many slices as fit one wave of resident CTAs (3 per SM at 256 threads x
+  // up to 80 registers): a second wave would add a whole round of load latency
   const int groups = (tokens + kRouterTokens - 1) / kRouterTokens;
   const int eblocks = (experts + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta;
-  const int wave = 4 * device_sm_count();
+  const int wave = 3 * device_sm_count();
   const int sl = std::max(1, std::min(kRouterMaxSlices, wave / std::max(1, groups * eblocks)));
   const int blocks = hidden / 128;
   const int per = (blocks + sl - 1) / sl;  // 128-wide blocks per slice
@@ -447,13 +453,19 @@ int router_topk_slices(int tokens, int hidden, int experts) {
 
 int router_topk_max_groups() { return kRouterMaxGroups; }
 
+bool router_topk_fused_permutes(int tokens) {
+  return tokens >= 1 && tokens <= kRouterTokens;  // one token group: its last CTA holds every assignment
+}
+
 cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                      int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
-                                     float* partial, int* counters, cudaStream_t s) {
+                                     float* partial, int* counters, cudaStream_t s, const RouterPermOut* perm) {
   if (tokens == 0) return cudaSuccess;
   if (!router_topk_fused_supported(hidden, experts, top_k)) return cudaErrorInvalidValue;
   const int groups = (tokens + kRouterTokens - 1) / kRouterTokens;
   if (groups > kRouterMaxGroups) return cudaErrorInvalidValue;
+  if (perm && !router_topk_fused_permutes(tokens)) return cudaErrorInvalidValue;
+  const RouterPermOut po = perm ? *perm : RouterPermOut{};
   const int slices = router_topk_slices(tokens, hidden, experts);
   const int kslice = ((hidden / 128 + slices - 1) / slices) * 128;
   const dim3 grid((experts + kRouterExpertsPerCta - 1) / kRouterExpertsPerCta, slices, groups);
@@ -461,7 +473,7 @@ cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, co
   cudaError_t e = cudaSuccess;
 #define NKI_RTS(V)                                                                                           \
   e = launch_pdl(router_topk_split_kernel<V>, grid, dim3(256), 0, s, x, wr, bias, logits_out, tokens, hidden,      \
-                 experts, top_k, idx, w, partial, counters, kslice)
+                 experts, top_k, idx, w, partial, counters, kslice, po)
   if (vpt <= 1) NKI_RTS(1);
   else if (vpt <= 2) NKI_RTS(2);
   else if (vpt <= 4) NKI_RTS(4);

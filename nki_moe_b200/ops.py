@@ -23,6 +23,7 @@ __all__ = [
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
     "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention", "skinny_linear",
+    "moe_block_add_rmsnorm",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -415,6 +416,39 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, t
     if sync_check_enabled():
         read_status(ws)
     return (out, idx, w) if return_routing else out
+
+
+def moe_block_add_rmsnorm(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
+                          residual: torch.Tensor, norm_weight: torch.Tensor, eps: float = 1e-6,
+                          residual_out: torch.Tensor | None = None, router_w_split: torch.Tensor | None = None):
+    """The MoE block on ``x`` followed by the decoder's residual add and the
+    next RMSNorm: returns ``(rmsnorm(r) * norm_weight, r)`` with
+    ``r = residual + moe(x)`` (bf16).  ``residual_out`` may be ``residual``
+    (in place).  Equal bit for bit to :func:`moe_block` + :func:`add_rmsnorm`;
+    up to 512 tokens the block's combine and the norm are one kernel."""
+    x = _contig(_cuda(x, "x"), torch.bfloat16)
+    residual = _contig(_cuda(residual, "residual"), torch.bfloat16)
+    rsplit = None
+    if router_w.shape[0] % 128 == 0:
+        rsplit = router_w_split if router_w_split is not None else router_split(router_w)
+    rw = _contig(_cuda(router_w, "router_w"), torch.float32)
+    wdt = torch.float32 if norm_weight.dtype == torch.float32 else torch.bfloat16
+    nw = _contig(_cuda(norm_weight, "norm_weight"), wdt)
+    T, H = x.shape
+    if residual.shape != x.shape:
+        raise ValueError(f"residual {tuple(residual.shape)} does not match x {tuple(x.shape)}")
+    if residual_out is None:
+        residual_out = torch.empty_like(residual)
+    out = torch.empty_like(x)
+    E, I = experts.num_experts, experts.inter
+    nbytes = size_call("nkimoe_moe_workspace_bytes", T, H, I, E, top_k)
+    ws = workspace(x.device, nbytes)
+    call("nkimoe_moe_block_add_rmsnorm", _p(x), _p(rw), None, _p(rsplit), _p(experts.w13), _p(experts.w2),
+         _p(residual), _p(residual_out), _p(nw), _DT[wdt], float(eps), _p(out), None, None, T, H, I, E, top_k,
+         _p(ws), ws.numel(), _s(x))
+    if sync_check_enabled():
+        read_status(ws)
+    return out, residual_out
 
 
 # ---------------------------------------------------------------- pieces

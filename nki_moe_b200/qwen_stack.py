@@ -220,11 +220,17 @@ class Qwen3MoEStack:
                    max_batch, max_seq)
 
     # ------------------------------------------------------------ layers
-    def _moe(self, lyr: _Layer, x: torch.Tensor, decode: bool = False) -> torch.Tensor:
+    def _moe_add_norm(self, lyr: _Layer, x: torch.Tensor, res: torch.Tensor, norm_w: torch.Tensor,
+                      decode: bool):
+        """The layer's MoE block on ``x``, then the residual add and the next
+        RMSNorm (the next layer's input norm, or the final norm): returns
+        ``(normed, residual)``."""
+        eps = self.cfg.rms_norm_eps
         if lyr.ep is not None:
-            return lyr.ep_decode(x) if decode else lyr.ep(x)
-        return ops.moe_block(x, lyr.router_w, lyr.experts, self.cfg.num_experts_per_tok,
-                             router_w_split=lyr.router_split)
+            h = lyr.ep_decode(x) if decode else lyr.ep(x)
+            return ops.add_rmsnorm(h, res, norm_w, eps)
+        return ops.moe_block_add_rmsnorm(x, lyr.router_w, lyr.experts, self.cfg.num_experts_per_tok, res, norm_w,
+                                         eps, router_w_split=lyr.router_split)
 
     def _qkv(self, lyr: _Layer, xn: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         c = self.cfg
@@ -244,20 +250,16 @@ class Qwen3MoEStack:
         """Run every layer on h [T, H]; ``attention(li, lyr, xn)`` returns the
         attention output [T, nq*hd] before the O projection (``linear``).
         Returns the final norm of the residual stream."""
-        c = self.cfg
-        eps = c.rms_norm_eps
-        res = None
-        xn = None
+        eps = self.cfg.rms_norm_eps
+        res = h
+        xn = ops.rmsnorm(h, self.layers[0].in_norm, eps)
         for li, lyr in enumerate(self.layers):
-            if res is None:
-                res = h
-                xn = ops.rmsnorm(h, lyr.in_norm, eps)
-            else:  # the previous layer's MoE output joins the residual here
-                xn, res = ops.add_rmsnorm(h, res, lyr.in_norm, eps)
             a = linear(attention(li, lyr, xn), lyr.o_w)
             xn, res = ops.add_rmsnorm(a, res, lyr.post_norm, eps)
-            h = self._moe(lyr, xn, decode)
-        return ops.add_rmsnorm(h, res, self.final_norm, eps)[0]
+            # the MoE output joins the residual and feeds the next norm
+            nxt = self.layers[li + 1].in_norm if li + 1 < len(self.layers) else self.final_norm
+            xn, res = self._moe_add_norm(lyr, xn, res, nxt, decode)
+        return xn
 
     # ------------------------------------------------------------ prefill
     @torch.inference_mode()

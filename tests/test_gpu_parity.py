@@ -459,6 +459,43 @@ def test_epilogue_staging_is_bit_identical(staging):
         _lib.set_option("epilogue_staging", 3)
 
 
+@pytest.mark.parametrize("T,in_place,w_dtype", [(1, False, torch.bfloat16), (8, True, torch.bfloat16),
+                                                (64, False, torch.float32), (512, True, torch.bfloat16),
+                                                (513, True, torch.bfloat16), (1000, False, torch.float32)])
+def test_moe_block_add_rmsnorm_equals_unfused(c1_inputs, T, in_place, w_dtype):
+    """The block followed by the decoder's residual add + next RMSNorm
+    (qwen_with_nki.py:447-454) in one call -- one fused combine + norm kernel
+    up to 512 tokens, combine then add + norm above -- equals moe_block +
+    add_rmsnorm bit for bit."""
+    g = torch.Generator().manual_seed(T + 3)
+    xb = torch.randn(T, 2048, generator=g).bfloat16().cuda()
+    res = torch.randn(T, 2048, generator=g).bfloat16().cuda()
+    nw = (1 + 0.1 * torch.randn(2048, generator=g)).to(w_dtype).cuda()
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    h = ops.moe_block(xb, rw, pe, 8)
+    ref_xn, ref_res = ops.add_rmsnorm(h, res, nw, 1e-6)
+    res_in = res.clone()
+    xn, r = ops.moe_block_add_rmsnorm(xb, rw, pe, 8, res_in, nw, 1e-6, residual_out=res_in if in_place else None)
+    assert torch.equal(r, ref_res)
+    assert torch.equal(xn, ref_xn)
+
+
+@pytest.mark.parametrize("T", [1, 5, 8, 9])
+def test_router_permutation_equals_permute_kernel(c1_inputs, T):
+    """Up to 8 tokens the decode router's last CTA also writes the expert
+    permutation (no separate permutation launch): the block's output equals,
+    bit for bit, the experts stage run on the same routing with the
+    permutation kernel (9 tokens: two token groups, the separate kernel)."""
+    g = torch.Generator().manual_seed(40 + T)
+    xb = torch.randn(T, 2048, generator=g).bfloat16().cuda()
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    out, idx, w = ops.moe_block(xb, rw, pe, 8, return_routing=True)
+    ref = ops.moe_experts(xb, pe, idx, w)
+    assert torch.equal(out, ref)
+
+
 def test_moe_block_deterministic(c1_inputs):
     a = _block_case(c1_inputs)[0]
     b = _block_case(c1_inputs)[0]
