@@ -67,7 +67,10 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * 2 with TMA tile::gather4; 0 = separate gather kernel),
  * "epilogue_staging" (prefill GEMM bf16 outputs written through a per-warp
  * shared-memory tile as whole-sector row stores: bit 0 the SwiGLU output,
- * bit 1 the routing-weight-scaled output; default 3).
+ * bit 1 the routing-weight-scaled output; default 3),
+ * "pdl" (1, the default: the decode-path kernels are launched with
+ * programmatic dependent launch, so a kernel's launch and prologue overlap
+ * the previous kernel in the stream; 0 = plain launches).
  * No reference counterpart (NKI tile sizes are compile-time constants,
  * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */
