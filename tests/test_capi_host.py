@@ -39,6 +39,10 @@ def test_version_and_options():
     with pytest.raises(_lib.NKIMoEError) as ei:
         _lib.set_option("no_such_option", 1)
     assert ei.value.code == _lib.ERR_INVALID_ARG
+    _lib.set_option("pdl", 0)
+    _lib.set_option("pdl", 1)
+    with pytest.raises(_lib.NKIMoEError):
+        _lib.set_option("pdl", 2)
 
 
 def test_workspace_sizes_are_host_functions():

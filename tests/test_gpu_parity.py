@@ -496,6 +496,27 @@ def test_router_permutation_equals_permute_kernel(c1_inputs, T):
     assert torch.equal(out, ref)
 
 
+def test_programmatic_dependent_launch_off_is_bit_identical(c1_inputs):
+    """The decode-path kernels launched without programmatic dependent launch
+    (option pdl=0) give the same bits as with it."""
+    g = torch.Generator().manual_seed(77)
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    res = torch.randn(8, 2048, generator=g).bfloat16().cuda()
+    nw = torch.ones(2048, dtype=torch.bfloat16, device="cuda")
+    xs = [torch.randn(T, 2048, generator=g).bfloat16().cuda() for T in (8, 64)]
+    outs = []
+    for pdl in (1, 0):
+        _lib.set_option("pdl", pdl)
+        try:
+            outs.append([ops.moe_block(x, rw, pe, 8) for x in xs] +
+                        list(ops.moe_block_add_rmsnorm(xs[0], rw, pe, 8, res, nw)))
+        finally:
+            _lib.set_option("pdl", 1)
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
 def test_moe_block_deterministic(c1_inputs):
     a = _block_case(c1_inputs)[0]
     b = _block_case(c1_inputs)[0]
