@@ -229,6 +229,13 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
     mark(kStageTopk, s);
     NKI_CUDA(topk_softmax_partials_launch(partial, 3, router_bias, logits, static_cast<int>(T), static_cast<int>(E),
                                           static_cast<int>(K), idx, w, s));
+  } else if (router_topk_fused_supported(static_cast<int>(H), static_cast<int>(E), static_cast<int>(K)) && T > 8 &&
+             T < 256) {
+    // several token groups: 8-CTA clusters (faster than the split router there)
+    NKI_CUDA(router_topk_cluster_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
+                                        static_cast<int>(T), static_cast<int>(H), static_cast<int>(E),
+                                        static_cast<int>(K), idx, w, s));
+    mark(kStageTopk, s);
   } else if (router_topk_fused_supported(static_cast<int>(H), static_cast<int>(E), static_cast<int>(K)) &&
              (T + 7) / 8 <= router_topk_max_groups()) {
     // logits and top-k in one launch; the top-k stage marker follows it.  Its

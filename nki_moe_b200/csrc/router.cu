@@ -398,6 +398,100 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Router + softmax + top-k for a decode batch of more than one token group
+// (9..255 tokens), in one launch: an 8-CTA cluster takes 8 tokens; CTA c computes the fp32 logits of experts
+// [c EG, (c + 1) EG) for those tokens (it reads only its 1/8 of the router
+// weights), keeps them in shared memory, and after a cluster barrier warp 0
+// of CTA c gathers token t0 + c's E logits from the 8 CTAs (distributed
+// shared memory) and selects its top-k.  A logit is one fp32 FMA chain per
+// lane over k = 4 lane + 128 i + j, then a butterfly sum over the lanes.
+constexpr int kRouterCluster = 8;
+
+template <int EG>
+__global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(256)
+    router_topk_cluster_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wr,
+                               const float* __restrict__ bias, float* __restrict__ logits_out, int T, int H, int E,
+                               int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+  extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [8][H]: the cluster's token rows
+  __shared__ float lg[kRouterCluster][EG];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const long long t0 = static_cast<long long>(blockIdx.x / kRouterCluster) * kRouterCluster;
+  // stage the 8 token rows: every thread's loads are issued before its stores
+  const int hc = H >> 3;  // 16-byte chunks per row
+  for (int i0 = threadIdx.x; i0 < kRouterCluster * hc; i0 += 8 * blockDim.x) {
+    uint4 u[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = i0 + q * blockDim.x, r = i / hc, c = i - r * hc;
+      u[q] = make_uint4(0u, 0u, 0u, 0u);
+      if (i < kRouterCluster * hc && t0 + r < T) u[q] = reinterpret_cast<const uint4*>(x + (t0 + r) * H)[c];
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = i0 + q * blockDim.x, r = i / hc, c = i - r * hc;
+      if (i < kRouterCluster * hc) reinterpret_cast<uint4*>(xs + static_cast<long long>(r) * H)[c] = u[q];
+    }
+  }
+  __syncthreads();
+  for (int el = warp; el < EG; el += 8) {
+    const int e = static_cast<int>(rank) * EG + el;
+    float acc[kRouterCluster] = {};
+    if (e < E) {
+      const float* we = wr + static_cast<long long>(e) * H;
+      for (int k0 = 4 * lane; k0 < H; k0 += 16 * 128) {
+        float4 w4[16];  // 16 weight loads in flight per lane
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int k = k0 + 128 * q;
+          w4[q] = k < H ? *reinterpret_cast<const float4*>(we + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int k = k0 + 128 * q;
+          if (k >= H) break;
+#pragma unroll
+          for (int t = 0; t < kRouterCluster; ++t) {
+            const uint2 u = *reinterpret_cast<const uint2*>(xs + static_cast<long long>(t) * H + k);
+            const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+            acc[t] = fmaf(a.x, w4[q].x, acc[t]);
+            acc[t] = fmaf(a.y, w4[q].y, acc[t]);
+            acc[t] = fmaf(b.x, w4[q].z, acc[t]);
+            acc[t] = fmaf(b.y, w4[q].w, acc[t]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterCluster; ++t) {
+      const float sum = warp_sum(acc[t]);
+      if (lane == 0) lg[t][el] = sum;
+    }
+  }
+  cluster_sync();  // every CTA's logits written and visible to the cluster
+  const long long t = t0 + rank;
+  if (warp == 0 && t < T) {
+    constexpr int VPT = (kRouterCluster * EG + 31) / 32;
+    float v[VPT];
+    const uint32_t lg_local = smem_u32(&lg[rank][0]);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int e = lane + 32 * j;
+      v[j] = -INFINITY;
+      if (e < E) {
+        const uint32_t src = mapa_shared(lg_local + static_cast<uint32_t>(e % EG) * 4u, static_cast<uint32_t>(e / EG));
+        float val;
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(val) : "r"(src) : "memory");
+        if (bias) val += bias[e];
+        if (logits_out) logits_out[t * E + e] = val;
+        v[j] = val;
+      }
+    }
+    topk_select_warp<VPT>(v, E, K, lane, idx_out + t * K, w_out + t * K);
+  }
+  cluster_sync();  // no CTA leaves while another still reads its logits
+}
+
 }  // namespace
 
 cudaError_t router_logits_simt_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits,
@@ -480,6 +574,31 @@ cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, co
   else NKI_RTS(8);
 #undef NKI_RTS
   return e;
+}
+
+cudaError_t router_topk_cluster_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
+                                     int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
+                                     cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (!router_topk_fused_supported(hidden, experts, top_k)) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(kRouterCluster) * hidden * sizeof(__nv_bfloat16);
+  const unsigned grid = static_cast<unsigned>((tokens + kRouterCluster - 1) / kRouterCluster) * kRouterCluster;
+  const int eg = (experts + kRouterCluster - 1) / kRouterCluster;
+#define NKI_RTC(EGV)                                                                                         \
+  do {                                                                                                      \
+    auto k = router_topk_cluster_kernel<EGV>;                                                               \
+    if (smem > 48 * 1024) {                                                                                 \
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+      if (e != cudaSuccess) return e;                                                                       \
+    }                                                                                                       \
+    k<<<grid, 256, smem, s>>>(x, wr, bias, logits_out, tokens, hidden, experts, top_k, idx, w);              \
+  } while (0)
+  if (eg <= 4) NKI_RTC(4);
+  else if (eg <= 8) NKI_RTC(8);
+  else if (eg <= 16) NKI_RTC(16);
+  else NKI_RTC(32);
+#undef NKI_RTC
+  return cudaGetLastError();
 }
 
 cudaError_t topk_softmax_launch(const float* logits, int tokens, int experts, int top_k, int32_t* idx, float* w,
