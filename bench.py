@@ -244,8 +244,8 @@ def run_reference(args):
     import torch
 
     from nki_moe_b200.workloads import WORKLOADS, make_moe_inputs
-    wl = WORKLOADS["c3" if args.workload == "prefill" else "c2"]
-    sample = 1024 if args.workload == "prefill" else wl.tokens
+    wl = WORKLOADS[{"prefill": "c3", "decode": "c2", "skewed": "c4"}[args.workload]]
+    sample = wl.tokens if args.workload == "decode" else 1024
     inp = make_moe_inputs(wl, tokens=sample)
     cin = cpu_inputs(inp, torch)
     for _ in range(max(args.warmup, 0)):
@@ -259,8 +259,11 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "moe_block_tokens_per_s", "value": tps, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name, "tokens_per_gpu": wl.tokens, "hidden": wl.hidden, "experts": wl.experts,
+        "higher_is_better": True, "scaling": "strong" if args.workload == "skewed" else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl.name,
+                   "tokens_per_gpu": wl.tokens // args.gpus if args.workload == "skewed" else wl.tokens,
+                   "hidden": wl.hidden, "experts": wl.experts,
                    "top_k": wl.top_k, "intermediate": wl.intermediate, "sample_tokens_per_step": sample},
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{sample} tokens of the {wl.name} workload per step (numpy oracle, fp32)"},
