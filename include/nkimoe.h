@@ -232,6 +232,31 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
                                             float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
                                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Whole block on HOST buffers: NKIMoESimple called on a host tensor
+ * (test_nki_moe.py:146-151 runs the module on hidden_states created on the
+ * host; nki_moe_integrated.py:428-475 is its forward).  x_host [T,H] bf16 in,
+ * out_host [T,H] bf16 out, both page-locked for the copies to overlap
+ * (pageable buffers work, with the copies synchronous); the weights, the
+ * routing outputs (device pointers, may be NULL) and the workspace
+ * (nkimoe_moe_block_host_workspace_bytes) are on the current device.  The
+ * tokens go through in chunks: the copy of chunk c+1 to the device and of
+ * chunk c-1 to the host overlap the block on chunk c (two copy streams of the
+ * library, one per direction and device, ordered against `stream` by events).
+ * chunk_tokens <= 0 picks a quarter of the batch.  Chunks are cut only where
+ * each takes the whole batch's router and GEMM paths (router_w_split given,
+ * 256 tokens or more, more than 48 rows per expert under the auto schedule),
+ * so out equals nkimoe_moe_block's on the whole batch bit for bit; otherwise
+ * one chunk.  Returns once the work is enqueued; `stream` completes with the
+ * last copy to the host, and the host buffers must stay valid until then.
+ * The status word of the workspace (nkimoe_read_status) collects the chunks'
+ * device faults. */
+NKIMOE_API size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
+NKIMOE_API int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float* router_bias,
+                                     const void* router_w_split, const void* w13, const void* w2, void* out_host,
+                                     int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,
+                                     int64_t E, int64_t K, int64_t chunk_tokens, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* nkimoe_moe_block for callers that cannot allocate GPU memory (a server that
  * reserved all device memory up front, a runtime whose allocator may not be
  * entered where the layer is issued, an embedding that forbids allocation

@@ -6,6 +6,7 @@
 //   GEMM-2 (+routing weight)  combine
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -206,6 +207,14 @@ int check_moe_shapes(long long T, long long H, long long I, long long E, long lo
   return NKIMOE_OK;
 }
 
+// The router of a T-token batch runs on the tensor cores (three-plane split of
+// the fp32 weights) when the caller passes the planes and the batch is large
+// enough, unless the "router" option forces one kind.
+bool router_uses_tensor_cores(bool have_split, long long T, long long E) {
+  const int mode = g_router.load();
+  return have_split && E % 128 == 0 && (mode == 2 || (mode == 0 && T >= 256));
+}
+
 // logits -> (idx, w): CUDA-core split-K or tensor-core split-fp32 GEMM, then
 // softmax/top-k/renormalise.
 // With `perm`, a decode batch of one token group (8 tokens or fewer) also gets
@@ -216,8 +225,7 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
                 bool* permuted = nullptr) {
   if (permuted) *permuted = false;
   float* logits = reinterpret_cast<float*>(base + L.logits);
-  const int mode = g_router.load();
-  const bool tensor = router_w_split && E % 128 == 0 && (mode == 2 || (mode == 0 && T >= 256));
+  const bool tensor = router_uses_tensor_cores(router_w_split != nullptr, T, E);
   mark(kStageRouter, s);
   if (tensor) {
     // the three bf16 planes are three "experts" over the same activation rows;
@@ -414,7 +422,7 @@ namespace {
 int moe_block_impl(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
                    const void* w13, const void* w2, void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T,
                    int64_t H, int64_t I, int64_t E, int64_t K, void* workspace, size_t workspace_bytes, void* stream,
-                   const FusedNorm* fn) {
+                   const FusedNorm* fn, bool keep_status = false) {
   int rc = check_moe_shapes(T, H, I, E, K);
   if (rc != NKIMOE_OK) return rc;
   NKI_REQUIRE(E <= 256, NKIMOE_ERR_UNSUPPORTED, "router top-k supports up to 256 experts");
@@ -422,7 +430,10 @@ int moe_block_impl(const void* x, const float* router_w, const float* router_bia
   NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
   NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
   const cudaStream_t s = as_stream(stream);
-  NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
+  if (keep_status)  // a later chunk of one call: the status word keeps the earlier chunks' faults
+    NKI_CUDA(cudaMemsetAsync(static_cast<char*>(workspace) + sizeof(int), 0, 256 - sizeof(int), s));
+  else
+    NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
   if (T == 0) return NKIMOE_OK;
   NKI_REQUIRE(x && router_w && w13 && w2 && (out || fn), NKIMOE_ERR_INVALID_ARG, "null pointer");
   NKI_REQUIRE(aligned16(x) && aligned16(router_w) && aligned16(w13) && aligned16(w2) && (fn || aligned16(out)),
@@ -450,6 +461,80 @@ int moe_block_impl(const void* x, const float* router_w, const float* router_bia
   if (rc != NKIMOE_OK) return rc;
   return experts_impl(x, w13, w2, idx, NKIMOE_I32, w, out, T, H, I, E, K, workspace, workspace_bytes, s, nullptr,
                       nullptr, fn, permuted);
+}
+
+// ---- block on host buffers: token chunks whose copies overlap the block ----
+constexpr int kMaxHostChunks = 16;
+
+// Token chunks of a host-buffer block call.  A chunk is cut only where every
+// chunk takes the path the whole batch takes: the tensor-core router (256
+// tokens or more) and the tile-rows GEMM schedule (more than 48 rows per expert
+// on average, the auto schedule's threshold), so the output is the whole-batch
+// block's bit for bit: each row's router dot products, expert GEMM sums and
+// slot combine do not depend on the other rows of its batch.  requested <= 0:
+// a quarter of the batch (four chunks balance the weight re-reads of more
+// chunks against the unhidden first and last copies of fewer).  The last chunk
+// takes the remainder, merged into the one before it when shorter than the
+// minimum.
+struct HostChunks {
+  long long len, count, longest;
+};
+
+HostChunks host_chunks(long long T, long long E, long long K, bool have_split, long long requested) {
+  HostChunks c{T, 1, T};
+  if (T <= 0 || !router_uses_tensor_cores(have_split, T, E)) return c;
+  long long min_len = 256;
+  const int sched = g_schedule.load();
+  if (sched == 2) return c;  // weight-streaming schedule: its tile height follows the batch
+  if (sched == 0) {
+    if (T * K <= 48 * E) return c;
+    min_len = std::max(min_len, (48 * E) / K + 1);
+  }
+  long long len = requested > 0 ? requested : (T + 3) / 4;
+  len = std::max({len, min_len, (T + kMaxHostChunks - 1) / kMaxHostChunks});
+  if (len >= T) return c;
+  long long n = (T + len - 1) / len;
+  if (T - (n - 1) * len < min_len) --n;  // a short tail joins the chunk before it
+  c.len = len;
+  c.count = n;
+  c.longest = T - (n - 1) * len;
+  if (c.longest < len) c.longest = len;
+  return c;
+}
+
+size_t host_stage_bytes(long long T, long long H) { return round256(sizeof(uint16_t) * T * H); }
+
+// Block workspace of any chunk of a T-token batch: every region of the block
+// workspace grows with the tokens except the router's partial logits (up to 8
+// per logit, more per token for small batches), bounded here by 8 per logit.
+size_t host_block_bytes(long long T, long long H, long long I, long long E, long long K) {
+  return nkimoe_moe_workspace_bytes(T, H, I, E, K) + round256(sizeof(float) * 8 * T * E);
+}
+
+// Per device: a stream for host->device copies, one for device->host copies
+// and the events that order them against the caller's stream.
+struct HostCopyStreams {
+  bool ready = false;
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t start = nullptr, done = nullptr;
+  cudaEvent_t in_done[kMaxHostChunks] = {}, blk_done[kMaxHostChunks] = {};
+};
+constexpr int kHostMaxDevices = 64;
+std::mutex g_host_mu[kHostMaxDevices];
+HostCopyStreams g_host[kHostMaxDevices];
+
+int host_streams_init(HostCopyStreams& h) {
+  if (h.ready) return NKIMOE_OK;
+  NKI_CUDA(cudaStreamCreateWithFlags(&h.in, cudaStreamNonBlocking));
+  NKI_CUDA(cudaStreamCreateWithFlags(&h.out, cudaStreamNonBlocking));
+  NKI_CUDA(cudaEventCreateWithFlags(&h.start, cudaEventDisableTiming));
+  NKI_CUDA(cudaEventCreateWithFlags(&h.done, cudaEventDisableTiming));
+  for (int i = 0; i < kMaxHostChunks; ++i) {
+    NKI_CUDA(cudaEventCreateWithFlags(&h.in_done[i], cudaEventDisableTiming));
+    NKI_CUDA(cudaEventCreateWithFlags(&h.blk_done[i], cudaEventDisableTiming));
+  }
+  h.ready = true;
+  return NKIMOE_OK;
 }
 
 }  // namespace
@@ -721,6 +806,68 @@ int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w, const flo
   const FusedNorm fn{residual, residual_out, norm_w, norm_w_dtype, eps, norm_out};
   return moe_block_impl(x, router_w, router_bias, router_w_split, w13, w2, nullptr, topk_idx_out, topk_w_out, T, H,
                         I, E, K, workspace, workspace_bytes, stream, &fn);
+}
+
+size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K) {
+  if (T < 0 || H <= 0 || E <= 0) return 0;
+  return host_block_bytes(T, H, I, E, K) + 2 * host_stage_bytes(T, H);
+}
+
+int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float* router_bias,
+                          const void* router_w_split, const void* w13, const void* w2, void* out_host,
+                          int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
+                          int64_t K, int64_t chunk_tokens, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_moe_shapes(T, H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
+  const size_t need = nkimoe_moe_block_host_workspace_bytes(T, H, I, E, K);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  const cudaStream_t s = as_stream(stream);
+  if (T == 0) {
+    NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));
+    return NKIMOE_OK;
+  }
+  NKI_REQUIRE(x_host && out_host, NKIMOE_ERR_INVALID_ARG, "null host buffer");
+  const HostChunks ch = host_chunks(T, E, K, router_w_split != nullptr, chunk_tokens);
+  // staging rows after the block workspace, which starts with the status word
+  const size_t blk_bytes = host_block_bytes(T, H, I, E, K);
+  char* xs = static_cast<char*>(workspace) + blk_bytes;
+  char* os = xs + host_stage_bytes(T, H);
+  const size_t row_bytes = sizeof(uint16_t) * static_cast<size_t>(H);
+  int dev = 0;
+  NKI_CUDA(cudaGetDevice(&dev));
+  NKI_REQUIRE(dev >= 0 && dev < kHostMaxDevices, NKIMOE_ERR_UNSUPPORTED, "device %d", dev);
+  std::lock_guard<std::mutex> lock(g_host_mu[dev]);
+  HostCopyStreams& hs = g_host[dev];
+  rc = host_streams_init(hs);
+  if (rc != NKIMOE_OK) return rc;
+  // the copy streams start after the work already on the caller's stream (an
+  // earlier call may still read the staging rows)
+  NKI_CUDA(cudaEventRecord(hs.start, s));
+  NKI_CUDA(cudaStreamWaitEvent(hs.in, hs.start, 0));
+  NKI_CUDA(cudaStreamWaitEvent(hs.out, hs.start, 0));
+  for (long long c = 0; c < ch.count; ++c) {
+    const long long t0 = c * ch.len, n = c + 1 < ch.count ? ch.len : T - t0;
+    NKI_CUDA(cudaMemcpyAsync(xs + t0 * row_bytes, static_cast<const char*>(x_host) + t0 * row_bytes, n * row_bytes,
+                             cudaMemcpyHostToDevice, hs.in));
+    NKI_CUDA(cudaEventRecord(hs.in_done[c], hs.in));
+  }
+  for (long long c = 0; c < ch.count; ++c) {
+    const long long t0 = c * ch.len, n = c + 1 < ch.count ? ch.len : T - t0;
+    NKI_CUDA(cudaStreamWaitEvent(s, hs.in_done[c], 0));
+    rc = moe_block_impl(xs + t0 * row_bytes, router_w, router_bias, router_w_split, w13, w2, os + t0 * row_bytes,
+                        topk_idx_out ? topk_idx_out + t0 * K : nullptr, topk_w_out ? topk_w_out + t0 * K : nullptr, n,
+                        H, I, E, K, workspace, blk_bytes, s, nullptr, c > 0);
+    if (rc != NKIMOE_OK) return rc;
+    NKI_CUDA(cudaEventRecord(hs.blk_done[c], s));
+    NKI_CUDA(cudaStreamWaitEvent(hs.out, hs.blk_done[c], 0));
+    NKI_CUDA(cudaMemcpyAsync(static_cast<char*>(out_host) + t0 * row_bytes, os + t0 * row_bytes, n * row_bytes,
+                             cudaMemcpyDeviceToHost, hs.out));
+  }
+  // the caller's stream completes with the last copy to the host
+  NKI_CUDA(cudaEventRecord(hs.done, hs.out));
+  NKI_CUDA(cudaStreamWaitEvent(s, hs.done, 0));
+  return NKIMOE_OK;
 }
 
 int nkimoe_read_status(void* workspace, void* stream, int* status_out) {

@@ -123,6 +123,14 @@ def _find_top_k(mlp: nn.Module, default: int = 8) -> int:
     return default
 
 
+def _host_batch(x: torch.Tensor, router_w: torch.Tensor) -> bool:
+    """A batch on the host for weights on a GPU (the reference's module test
+    calls the block on host ``hidden_states``, test_nki_moe.py:146-151): the
+    block runs on that GPU with the copies overlapped, the result comes back
+    to the host."""
+    return not x.is_cuda and router_w.is_cuda
+
+
 class NKIMoEWrapper(nn.Module):
     """Runs a wrapped MoE module's weights through the B200 block.
 
@@ -152,7 +160,10 @@ class NKIMoEWrapper(nn.Module):
         rw = _find_router_weight(self.original_mlp)
         gate_up, down, layout = _find_expert_weights(self.original_mlp)
         pe = ops.packed_experts(gate_up, down, layout)
-        out = ops.moe_block(x, rw, pe, self.top_k)
+        if _host_batch(x, rw):
+            out = ops.moe_block_host(x, rw, pe, self.top_k)
+        else:
+            out = ops.moe_block(x, rw, pe, self.top_k)
         return out.to(_out_dtype(hidden_states)).view(shape)
 
 
@@ -185,7 +196,11 @@ class NKIMoESimple(nn.Module):
     def forward(self, hidden_states: torch.Tensor, padding_mask: Optional[torch.Tensor] = None):
         B, S, H = hidden_states.shape
         x = hidden_states.reshape(-1, H)
-        out = ops.moe_block(x, self.router.weight.float(), self.packed(), self.top_k, bias=self.router_bias)
+        rw = self.router.weight.float()
+        if _host_batch(x, rw):
+            out = ops.moe_block_host(x, rw, self.packed(), self.top_k, bias=self.router_bias)
+        else:
+            out = ops.moe_block(x, rw, self.packed(), self.top_k, bias=self.router_bias)
         out = out.to(_out_dtype(hidden_states)).view(B, S, H)
         return (out,) if self.return_tuple else out
 

@@ -418,6 +418,51 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, t
     return (out, idx, w) if return_routing else out
 
 
+def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
+                   bias: torch.Tensor | None = None, out: torch.Tensor | None = None, chunk_tokens: int = 0,
+                   return_routing: bool = False, router_w_split: torch.Tensor | None = None,
+                   non_blocking: bool = False):
+    """:func:`moe_block` on a HOST batch ``x [T, H]`` (bf16; page-locked for
+    the copies to overlap): the tokens cross to the weights' GPU in chunks
+    whose copies overlap the block on the chunk before, and the result comes
+    back to ``out`` (a new page-locked host tensor when None).  Equal to
+    :func:`moe_block` on the whole batch bit for bit (chunks are cut only where
+    each takes the whole batch's router and GEMM paths).  Routing outputs, when
+    asked for, stay on the GPU.  The work runs on the current stream of the
+    weights' device; the call synchronises it unless ``non_blocking``, in which
+    case ``x`` and ``out`` must stay alive and untouched until the stream has
+    completed."""
+    if x.is_cuda:
+        raise ValueError("x must be a host tensor (moe_block takes device tensors)")
+    dev = _cuda(router_w, "router_w").device
+    x = _contig(x, torch.bfloat16)
+    T, H = x.shape
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
+    elif out.is_cuda or out.dtype != torch.bfloat16 or tuple(out.shape) != (T, H) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 host tensor shaped like x")
+    rsplit = None
+    if router_w.shape[0] % 128 == 0:
+        rsplit = router_w_split if router_w_split is not None else router_split(router_w)
+    rw = _contig(router_w, torch.float32)
+    b = _contig(_cuda(bias, "bias"), torch.float32) if bias is not None else None
+    E, I = experts.num_experts, experts.inter
+    idx = w = None
+    if return_routing:
+        idx = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+        w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    nbytes = size_call("nkimoe_moe_block_host_workspace_bytes", T, H, I, E, top_k)
+    with torch.cuda.device(dev):
+        ws = workspace(dev, nbytes)
+        call("nkimoe_moe_block_host", _p(x), _p(rw), _p(b), _p(rsplit), _p(experts.w13), _p(experts.w2), _p(out),
+             _p(idx), _p(w), T, H, I, E, top_k, int(chunk_tokens), _p(ws), ws.numel(), _s(rw))
+        if sync_check_enabled():
+            read_status(ws)
+        elif not non_blocking:
+            torch.cuda.current_stream(dev).synchronize()
+    return (out, idx, w) if return_routing else out
+
+
 def moe_block_add_rmsnorm(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
                           residual: torch.Tensor, norm_weight: torch.Tensor, eps: float = 1e-6,
                           residual_out: torch.Tensor | None = None, router_w_split: torch.Tensor | None = None):

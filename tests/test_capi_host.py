@@ -74,6 +74,27 @@ def test_argument_validation_without_gpu():
     _lib.call("nkimoe_rmsnorm", null, _lib.BF16, null, _lib.F32, null, _lib.BF16, 0, 2048, 1e-6, null)
 
 
+def test_host_block_validation_without_gpu():
+    """The host-buffer block checks its shapes, workspace and host pointers
+    before the first CUDA call."""
+    null = ctypes.c_void_p(0)
+    need = _lib.size_call("nkimoe_moe_block_host_workspace_bytes", 8192, 2048, 768, 128, 8)
+    # the block workspace of any chunk plus the staged input and output rows
+    assert need >= _lib.size_call("nkimoe_moe_workspace_bytes", 8192, 2048, 768, 128, 8) + 2 * 8192 * 2048 * 2
+
+    def host(T, E, ws, ws_bytes, x=null):
+        _lib.call("nkimoe_moe_block_host", x, null, null, null, null, null, null, null, null, T, 2048, 768, E, 8, 0,
+                  ws, ws_bytes, null)
+
+    for args, code in (((64, 600, null, 0), _lib.ERR_UNSUPPORTED),             # 600 experts
+                       ((8192, 128, null, need), _lib.ERR_WORKSPACE),          # no workspace
+                       ((8192, 128, ctypes.c_void_p(256), need - 1), _lib.ERR_WORKSPACE),
+                       ((8192, 128, ctypes.c_void_p(256), need), _lib.ERR_INVALID_ARG)):  # null host rows
+        with pytest.raises(_lib.NKIMoEError) as ei:
+            host(*args)
+        assert ei.value.code == code
+
+
 def test_decode_attention_validation_without_gpu():
     null = ctypes.c_void_p(0)
 

@@ -517,6 +517,46 @@ def test_programmatic_dependent_launch_off_is_bit_identical(c1_inputs):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("T,chunk,pinned", [(2048, 0, True), (2048, 1000, False), (3000, 769, True),
+                                            (300, 0, True), (5, 0, True), (0, 0, True)])
+def test_moe_block_host_equals_device_block(c1_inputs, T, chunk, pinned):
+    """The block on host buffers (copies of token chunks overlapping the block
+    on the chunk before) equals the device call on the whole batch bit for
+    bit: output and routing, two calls in a row.  Chunks hold at least 769
+    tokens here (more than 48 rows per expert at 128 experts, top-8): 2048
+    tokens go as 769 + 1279 (default) or 1000 + 1048 (a short tail merged),
+    3000 as 769 + 769 + 1462; 300 tokens (weight-streaming GEMMs) and 5
+    tokens in one chunk; 0 tokens is a no-op."""
+    g = torch.Generator().manual_seed(T + chunk)
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    for _ in range(2):
+        xh = torch.randn(T, 2048, generator=g).bfloat16()
+        if pinned:
+            xh = xh.pin_memory()
+        ref, ridx, rwt = ops.moe_block(xh.cuda(), rw, pe, 8, return_routing=True)
+        out, idx, w = ops.moe_block_host(xh, rw, pe, 8, chunk_tokens=chunk, return_routing=True)
+        assert not out.is_cuda and out.shape == (T, 2048)
+        assert torch.equal(out.view(torch.int16), ref.cpu().view(torch.int16))
+        assert torch.equal(idx, ridx) and torch.equal(w.view(torch.int32), rwt.view(torch.int32))
+
+
+def test_module_on_host_batch_equals_device_batch(c1_inputs):
+    """NKIMoESimple called on a host tensor (as the reference's module test
+    calls it) runs on the weights' GPU and returns the device call's result on
+    the host."""
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+    moe = NKIMoESimple(2048, 768, 128, 8, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        moe.router.weight.copy_(c1_inputs["router"])
+    xh = torch.randn(2, 1000, 2048, generator=torch.Generator().manual_seed(5)).bfloat16()  # 769 + 1231
+    with torch.no_grad():
+        y_host = moe(xh)
+        y_dev = moe(xh.cuda())
+    assert not y_host.is_cuda
+    assert torch.equal(y_host.view(torch.int16), y_dev.cpu().view(torch.int16))
+
+
 def test_moe_block_deterministic(c1_inputs):
     a = _block_case(c1_inputs)[0]
     b = _block_case(c1_inputs)[0]
