@@ -34,6 +34,10 @@ sys.path.insert(0, REPO)
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernel (GEMM-1), from the ncu captures summarised in
 # profiles/grouped_gemm_prefill_c3_t8192.md and profiles/grouped_gemm_decode_c2_t64.md.
+# Token chunk of the host-buffer e2e calls (nkimoe_moe_block_host): one chunk
+# per batch; the overlap is between successive batches.
+E2E_CHUNK_TOKENS = 1 << 30
+
 NCU_TRAFFIC_BYTES = {"prefill": 1.0739e9 + 92.66e6, "decode": 794.89e6 + 3.64e6}
 
 
@@ -285,7 +289,10 @@ def _cpu_model():
 
 
 # ---------------------------------------------------------------- B200 arm
-def time_steps(torch, fn, steps, warmup, stream, world, evs=None):
+def time_steps(torch, fn, steps, warmup, stream, world, evs=None, finish=None):
+    """Device time per step over `steps` steps (CUDA events on `stream`, max
+    over ranks).  `finish` (optional) runs after the last step, before the end
+    event: it makes `stream` wait for work the steps left on other streams."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -297,6 +304,8 @@ def time_steps(torch, fn, steps, warmup, stream, world, evs=None):
     start.record(stream)
     for _ in range(steps):
         fn()
+    if finish is not None:
+        finish()
     end.record(stream)
     torch.cuda.synchronize()
     ms = start.elapsed_time(end) / steps
@@ -510,23 +519,36 @@ def run_b200(args):
         if not args.no_e2e:
             xh = x.reshape(1, *x.shape).cpu().pin_memory()
             outh = torch.empty_like(xh).pin_memory()
+            # world 1: successive batches through the host-buffer block, each
+            # call's copy in overlapping the previous call's block and its copy
+            # back the next call's block (two output buffers, one completion
+            # event each)
+            outs = [outh[0], torch.empty_like(outh[0]).pin_memory()]
+            dones = [torch.cuda.Event(), torch.cuda.Event()]
+            n_e2e = [0]
 
             def e2e_step():
                 if world == 1:
-                    # the module on a host batch: token chunks whose copies
-                    # overlap the block on the chunk before; the result comes
-                    # back as a page-locked host tensor (outh's size)
-                    moe(xh)
+                    i = n_e2e[0] % 2
+                    n_e2e[0] += 1
+                    ops.moe_block_host(xh[0], moe.router.weight, moe.packed(), wl.top_k, bias=moe.router_bias,
+                                       out=outs[i], chunk_tokens=E2E_CHUNK_TOKENS, done=dones[i])
                     return
                 xd = xh.to("cuda", non_blocking=True)
                 outh.copy_(block(xd[0]).unsqueeze(0), non_blocking=True)
 
-            e_ms, _ = time_steps(torch, e2e_step, args.steps, max(args.warmup, 3), stream, world)
+            def e2e_finish():
+                if world == 1:  # the timed region ends with the last copy back
+                    stream.wait_event(dones[(n_e2e[0] - 1) % 2])
+
+            e_ms, _ = time_steps(torch, e2e_step, args.steps, max(args.warmup, 3), stream, world,
+                                 finish=e2e_finish)
             r["e2e"] = {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
                         "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                         "d2h_bytes_per_step": outh.numel() * outh.element_size(),
-                        "path": ("NKIMoESimple on a page-locked host batch (nkimoe_moe_block_host: token chunks whose "
-                                 "copies overlap the block)" if world == 1 else
+                        "path": ("ops.moe_block_host on page-locked host batches (nkimoe_moe_block_host): each "
+                                 "batch copied in, through the block and copied back, a batch's copies overlapping "
+                                 "its neighbours' blocks" if world == 1 else
                                  "copy to the GPU, expert-parallel block, copy back")}
         if not args.no_cpu_baseline and rank == 0 and world == 1:
             # the whole batch of the workload, repeated to about 10 s of CPU work

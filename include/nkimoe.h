@@ -238,24 +238,33 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
  * out_host [T,H] bf16 out, both page-locked for the copies to overlap
  * (pageable buffers work, with the copies synchronous); the weights, the
  * routing outputs (device pointers, may be NULL) and the workspace
- * (nkimoe_moe_block_host_workspace_bytes) are on the current device.  The
- * tokens go through in chunks: the copy of chunk c+1 to the device and of
- * chunk c-1 to the host overlap the block on chunk c (two copy streams of the
- * library, one per direction and device, ordered against `stream` by events).
- * chunk_tokens <= 0 picks a quarter of the batch.  Chunks are cut only where
- * each takes the whole batch's router and GEMM paths (router_w_split given,
- * 256 tokens or more, more than 48 rows per expert under the auto schedule),
- * so out equals nkimoe_moe_block's on the whole batch bit for bit; otherwise
- * one chunk.  Returns once the work is enqueued; `stream` completes with the
- * last copy to the host, and the host buffers must stay valid until then.
- * The status word of the workspace (nkimoe_read_status) collects the chunks'
- * device faults. */
+ * (nkimoe_moe_block_host_workspace_bytes) are on the current device.
+ * The copies run on two streams of the library (one per direction and
+ * device), ordered against `stream` by events:
+ *  - within a call, the tokens go through in chunks: the copy of chunk c+1
+ *    to the device and of chunk c-1 to the host overlap the block on chunk c.
+ *    chunk_tokens <= 0 picks half the batch; chunk_tokens >= T, one chunk.
+ *    Chunks are cut only where each takes the whole batch's router and GEMM
+ *    paths (router_w_split given, 256 tokens or more, more than 48 rows per
+ *    expert under the auto schedule), so out equals nkimoe_moe_block's on the
+ *    whole batch bit for bit; otherwise one chunk;
+ *  - across calls, the workspace holds two slots of staging rows used by
+ *    alternate calls: a call's copy to the device overlaps the previous
+ *    call's block, and with done_event its copy back overlaps the next call's
+ *    block.
+ * done_event NULL: `stream` completes with the last copy to the host.
+ * done_event (a cudaEvent_t of this device): recorded at the last copy to the
+ * host, which `stream` does not wait for; out_host is ready once the event
+ * has completed.  The host buffers must stay valid until then.  Calls that
+ * share a workspace are issued on one stream.  Returns once the work is
+ * enqueued.  The status word of the workspace (nkimoe_read_status) collects
+ * the call's device faults. */
 NKIMOE_API size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
 NKIMOE_API int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float* router_bias,
                                      const void* router_w_split, const void* w13, const void* w2, void* out_host,
                                      int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,
                                      int64_t E, int64_t K, int64_t chunk_tokens, void* workspace,
-                                     size_t workspace_bytes, void* stream);
+                                     size_t workspace_bytes, void* done_event, void* stream);
 
 /* nkimoe_moe_block for callers that cannot allocate GPU memory (a server that
  * reserved all device memory up front, a runtime whose allocator may not be

@@ -55,7 +55,7 @@ SIGNATURES = {
                                           _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "nkimoe_moe_block_host_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "nkimoe_moe_block_host": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
-                                   _vp, _sz, _vp]),
+                                   _vp, _sz, _vp, _vp]),
     "nkimoe_router_split": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_read_status": (_i, [_vp, _vp, _c.POINTER(_i)]),
     "nkimoe_moe_block_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,

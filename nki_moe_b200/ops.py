@@ -2,7 +2,8 @@
 
 PyTorch is used here only as plumbing: device memory, the current CUDA
 stream and dtype conversions at the boundary.  Every computation runs in
-``libnkimoe.so``; CPU tensors are rejected (no CPU fallback).
+``libnkimoe.so``; CPU tensors are rejected (no CPU fallback), except as the
+host buffers of :func:`moe_block_host`, whose block runs on the GPU.
 """
 
 from __future__ import annotations
@@ -23,7 +24,7 @@ __all__ = [
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
     "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention", "skinny_linear",
-    "moe_block_add_rmsnorm",
+    "moe_block_add_rmsnorm", "moe_block_host",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -421,7 +422,7 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, t
 def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
                    bias: torch.Tensor | None = None, out: torch.Tensor | None = None, chunk_tokens: int = 0,
                    return_routing: bool = False, router_w_split: torch.Tensor | None = None,
-                   non_blocking: bool = False):
+                   non_blocking: bool = False, done: torch.cuda.Event | None = None):
     """:func:`moe_block` on a HOST batch ``x [T, H]`` (bf16; page-locked for
     the copies to overlap): the tokens cross to the weights' GPU in chunks
     whose copies overlap the block on the chunk before, and the result comes
@@ -429,9 +430,15 @@ def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExper
     :func:`moe_block` on the whole batch bit for bit (chunks are cut only where
     each takes the whole batch's router and GEMM paths).  Routing outputs, when
     asked for, stay on the GPU.  The work runs on the current stream of the
-    weights' device; the call synchronises it unless ``non_blocking``, in which
-    case ``x`` and ``out`` must stay alive and untouched until the stream has
-    completed."""
+    weights' device.
+
+    ``done`` None: the stream completes with the copy back, and the call
+    synchronises it unless ``non_blocking``.  ``done`` an event: the copy
+    back's completion is recorded on it and the stream goes on without it, so
+    the next call's block overlaps this call's copy back (and this call's copy
+    in overlaps the previous call's block); ``out`` is ready after
+    ``done.synchronize()``.  Until then ``x`` and ``out`` must stay alive and
+    untouched."""
     if x.is_cuda:
         raise ValueError("x must be a host tensor (moe_block takes device tensors)")
     dev = _cuda(router_w, "router_w").device
@@ -453,12 +460,24 @@ def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExper
         w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
     nbytes = size_call("nkimoe_moe_block_host_workspace_bytes", T, H, I, E, top_k)
     with torch.cuda.device(dev):
+        with _ws_lock:
+            cur = _ws.get((dev.index, torch.cuda.current_stream(dev).cuda_stream))
+        if cur is not None and cur.numel() < nbytes:
+            # the library's copy streams may still read or write the workspace
+            # being replaced (its memory goes back to this stream's pool)
+            torch.cuda.synchronize(dev)
         ws = workspace(dev, nbytes)
+        ev = None
+        if done is not None:
+            done.record(torch.cuda.current_stream(dev))  # creates the CUDA event on this device
+            ev = ctypes.c_void_p(done.cuda_event)
         call("nkimoe_moe_block_host", _p(x), _p(rw), _p(b), _p(rsplit), _p(experts.w13), _p(experts.w2), _p(out),
-             _p(idx), _p(w), T, H, I, E, top_k, int(chunk_tokens), _p(ws), ws.numel(), _s(rw))
+             _p(idx), _p(w), T, H, I, E, top_k, int(chunk_tokens), _p(ws), ws.numel(), ev, _s(rw))
         if sync_check_enabled():
             read_status(ws)
-        elif not non_blocking:
+            if done is not None:
+                done.synchronize()
+        elif not non_blocking and done is None:
             torch.cuda.current_stream(dev).synchronize()
     return (out, idx, w) if return_routing else out
 

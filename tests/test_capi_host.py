@@ -79,12 +79,12 @@ def test_host_block_validation_without_gpu():
     before the first CUDA call."""
     null = ctypes.c_void_p(0)
     need = _lib.size_call("nkimoe_moe_block_host_workspace_bytes", 8192, 2048, 768, 128, 8)
-    # the block workspace of any chunk plus the staged input and output rows
-    assert need >= _lib.size_call("nkimoe_moe_workspace_bytes", 8192, 2048, 768, 128, 8) + 2 * 8192 * 2048 * 2
+    # the block workspace of any chunk plus two slots of staged input and output rows
+    assert need >= _lib.size_call("nkimoe_moe_workspace_bytes", 8192, 2048, 768, 128, 8) + 4 * 8192 * 2048 * 2
 
     def host(T, E, ws, ws_bytes, x=null):
         _lib.call("nkimoe_moe_block_host", x, null, null, null, null, null, null, null, null, T, 2048, 768, E, 8, 0,
-                  ws, ws_bytes, null)
+                  ws, ws_bytes, null, null)
 
     for args, code in (((64, 600, null, 0), _lib.ERR_UNSUPPORTED),             # 600 experts
                        ((8192, 128, null, need), _lib.ERR_WORKSPACE),          # no workspace

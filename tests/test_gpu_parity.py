@@ -524,7 +524,7 @@ def test_moe_block_host_equals_device_block(c1_inputs, T, chunk, pinned):
     on the chunk before) equals the device call on the whole batch bit for
     bit: output and routing, two calls in a row.  Chunks hold at least 769
     tokens here (more than 48 rows per expert at 128 experts, top-8): 2048
-    tokens go as 769 + 1279 (default) or 1000 + 1048 (a short tail merged),
+    tokens go as 1024 + 1024 (default: halves) or 1000 + 1048 (a short tail merged),
     3000 as 769 + 769 + 1462; 300 tokens (weight-streaming GEMMs) and 5
     tokens in one chunk; 0 tokens is a no-op."""
     g = torch.Generator().manual_seed(T + chunk)
@@ -541,6 +541,30 @@ def test_moe_block_host_equals_device_block(c1_inputs, T, chunk, pinned):
         assert torch.equal(idx, ridx) and torch.equal(w.view(torch.int32), rwt.view(torch.int32))
 
 
+@pytest.mark.parametrize("chunk", [0, 1 << 30])
+def test_moe_block_host_overlapped_calls(c1_inputs, chunk):
+    """Successive host-buffer calls with completion events (each call's copy
+    in overlapping the previous call's block, its copy back the next call's
+    block; two output buffers in turn): every batch's output equals the device
+    block's on that batch."""
+    g = torch.Generator().manual_seed(90 + (chunk > 0))
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    xs = [torch.randn(2048, 2048, generator=g).bfloat16().pin_memory() for _ in range(4)]
+    outs = [torch.empty(2048, 2048, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    dones = [torch.cuda.Event() for _ in range(4)]
+    os.environ["NKIMOE_SYNC_CHECK"] = "0"  # no synchronisation inside the calls
+    try:
+        for x, o, d in zip(xs, outs, dones):
+            ops.moe_block_host(x, rw, pe, 8, out=o, chunk_tokens=chunk, done=d)
+    finally:
+        os.environ["NKIMOE_SYNC_CHECK"] = "1"
+    for x, o, d in zip(xs, outs, dones):
+        d.synchronize()
+        ref = ops.moe_block(x.cuda(), rw, pe, 8).cpu()
+        assert torch.equal(o.view(torch.int16), ref.view(torch.int16))
+
+
 def test_module_on_host_batch_equals_device_batch(c1_inputs):
     """NKIMoESimple called on a host tensor (as the reference's module test
     calls it) runs on the weights' GPU and returns the device call's result on
@@ -549,7 +573,7 @@ def test_module_on_host_batch_equals_device_batch(c1_inputs):
     moe = NKIMoESimple(2048, 768, 128, 8, device="cuda", dtype=torch.bfloat16)
     with torch.no_grad():
         moe.router.weight.copy_(c1_inputs["router"])
-    xh = torch.randn(2, 1000, 2048, generator=torch.Generator().manual_seed(5)).bfloat16()  # 769 + 1231
+    xh = torch.randn(2, 1000, 2048, generator=torch.Generator().manual_seed(5)).bfloat16()  # 1000 + 1000
     with torch.no_grad():
         y_host = moe(xh)
         y_dev = moe(xh.cuda())
