@@ -4,8 +4,10 @@
  *
  * Plain pointers and sizes only.  All device pointers are CUDA global memory
  * of the current device; `stream` is a cudaStream_t (NULL = legacy default
- * stream).  Every call is asynchronous and stream-ordered, allocates nothing,
- * and returns NKIMOE_OK or an error code; nkimoe_last_error() gives the
+ * stream).  Every call is asynchronous and stream-ordered, allocates no
+ * memory (nkimoe_moe_block_host creates two copy streams and a few events per
+ * device, and per workspace, when first used), and returns NKIMOE_OK or an
+ * error code; nkimoe_last_error() gives the
  * calling thread's last message.  Device-side faults that cannot be detected
  * at launch (an expert id out of range, a bounded wait that ran out) are
  * accumulated in a status word at the start of the caller's workspace and
