@@ -257,10 +257,12 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
  * done_event NULL: `stream` completes with the last copy to the host.
  * done_event (a cudaEvent_t of this device): recorded at the last copy to the
  * host, which `stream` does not wait for; out_host is ready once the event
- * has completed.  The host buffers must stay valid until then.  Calls that
- * share a workspace are issued on one stream.  Returns once the work is
- * enqueued.  The status word of the workspace (nkimoe_read_status) collects
- * the call's device faults. */
+ * has completed.  The host buffers must stay valid until then, and no other
+ * entry point may be given the workspace before then (the copy back reads
+ * the call's staging rows in it); host-batch calls that share a workspace
+ * are issued on one stream and alternate its two slots safely.  Returns once
+ * the work is enqueued.  The status word of the workspace
+ * (nkimoe_read_status) collects the call's device faults. */
 NKIMOE_API size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
 NKIMOE_API int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float* router_bias,
                                      const void* router_w_split, const void* w13, const void* w2, void* out_host,

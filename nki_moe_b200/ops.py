@@ -419,6 +419,28 @@ def moe_block(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, t
     return (out, idx, w) if return_routing else out
 
 
+_host_ws: dict = {}
+
+
+def _host_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-(device, stream) workspace of the host-batch block, kept apart from
+    :func:`workspace`: with a completion event, the library's copy back still
+    reads a call's staging rows after the stream has moved on, so no device
+    entry point may write them meanwhile."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    with _ws_lock:
+        buf = _host_ws.get(key)
+        if buf is not None and buf.numel() >= nbytes:
+            return buf
+    # the copy streams may still use the buffer being replaced (its memory
+    # goes back to this stream's pool)
+    torch.cuda.synchronize(device)
+    buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+    with _ws_lock:
+        _host_ws[key] = buf
+    return buf
+
+
 def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,
                    bias: torch.Tensor | None = None, out: torch.Tensor | None = None, chunk_tokens: int = 0,
                    return_routing: bool = False, router_w_split: torch.Tensor | None = None,
@@ -460,13 +482,7 @@ def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExper
         w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
     nbytes = size_call("nkimoe_moe_block_host_workspace_bytes", T, H, I, E, top_k)
     with torch.cuda.device(dev):
-        with _ws_lock:
-            cur = _ws.get((dev.index, torch.cuda.current_stream(dev).cuda_stream))
-        if cur is not None and cur.numel() < nbytes:
-            # the library's copy streams may still read or write the workspace
-            # being replaced (its memory goes back to this stream's pool)
-            torch.cuda.synchronize(dev)
-        ws = workspace(dev, nbytes)
+        ws = _host_workspace(dev, nbytes)
         ev = None
         if done is not None:
             done.record(torch.cuda.current_stream(dev))  # creates the CUDA event on this device
