@@ -31,13 +31,13 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernel (GEMM-1), from the ncu captures summarised in
-# profiles/grouped_gemm_prefill_c3_t8192.md and profiles/grouped_gemm_decode_c2_t64.md.
 # Token chunk of the host-buffer e2e calls (nkimoe_moe_block_host): one chunk
 # per batch; the overlap is between successive batches.
 E2E_CHUNK_TOKENS = 1 << 30
 
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernel (GEMM-1), from the ncu captures summarised in
+# profiles/grouped_gemm_prefill_c3_t8192.md and profiles/grouped_gemm_decode_c2_t64.md.
 NCU_TRAFFIC_BYTES = {"prefill": 1.0739e9 + 92.66e6, "decode": 794.89e6 + 3.64e6}
 
 
@@ -526,13 +526,18 @@ def run_b200(args):
             outs = [outh[0], torch.empty_like(outh[0]).pin_memory()]
             dones = [torch.cuda.Event(), torch.cuda.Event()]
             n_e2e = [0]
+            # the packed experts and the router's bf16 planes are made once, as
+            # a serving loop keeps them
+            e_rw = moe.router.weight
+            e_pe = moe.packed()
+            e_split = ops.router_split(e_rw)
 
             def e2e_step():
                 if world == 1:
                     i = n_e2e[0] % 2
                     n_e2e[0] += 1
-                    ops.moe_block_host(xh[0], moe.router.weight, moe.packed(), wl.top_k, bias=moe.router_bias,
-                                       out=outs[i], chunk_tokens=E2E_CHUNK_TOKENS, done=dones[i])
+                    ops.moe_block_host(xh[0], e_rw, e_pe, wl.top_k, bias=moe.router_bias, out=outs[i],
+                                       chunk_tokens=E2E_CHUNK_TOKENS, router_w_split=e_split, done=dones[i])
                     return
                 xd = xh.to("cuda", non_blocking=True)
                 outh.copy_(block(xd[0]).unsqueeze(0), non_blocking=True)
