@@ -529,8 +529,8 @@ def run_b200(args):
             # the packed experts and the router's bf16 planes are made once, as
             # a serving loop keeps them
             e_rw = moe.router.weight
-            e_pe = moe.packed()
-            e_split = ops.router_split(e_rw)
+            e_pe = moe.packed() if world == 1 else None
+            e_split = ops.router_split(e_rw) if world == 1 else None
 
             def e2e_step():
                 if world == 1:
