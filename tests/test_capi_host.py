@@ -128,3 +128,19 @@ def test_reference_module_aliases():
     n = NKIRMSNorm(16)
     with pytest.raises(ValueError):
         n(__import__("torch").ones(16))  # 1-D input: ValueError, as nki_custom_rmsnorm.py:115
+
+
+def test_no_cpu_path_for_host_weights():
+    """The block never computes on the CPU: a host batch is accepted only with
+    the weights on a GPU (the block runs there); host weights raise."""
+    import torch
+    from nki_moe_b200 import ops
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+    moe = NKIMoESimple(128, 64, 4, 2)
+    x = torch.randn(1, 3, 128)
+    with pytest.raises(ValueError, match="CUDA"):
+        moe(x)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.moe_block_host(x[0].bfloat16(), moe.router.weight, None, 2)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.moe_block(x[0].bfloat16(), moe.router.weight, None, 2)
