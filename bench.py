@@ -1,19 +1,29 @@
 """Benchmark of the Qwen3-30B-A3B sparse-MoE block on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload prefill|decode]
+                    [--workload prefill|decode|skewed] [--ep peer|nccl]
 
 A step is one forward of the MoE block (router, softmax/top-8, permute,
 grouped gate/up GEMM + SwiGLU, grouped down GEMM + routing weight, combine)
 over one batch of synthetic tokens:
   prefill (default): 8192 tokens per GPU (4 x 2048), seed 2;
   decode:            64 tokens, seed 1 (also reported as a sub-object of the
-                     prefill line at N=1).
+                     prefill line at N=1);
+  skewed:            16384 tokens in all, split over the GPUs, Zipf(1.2)
+                     router bias (strong scaling).
 Weights are random N(0, 0.02) with the layer's real shapes (hidden 2048, 128
 experts, top-8, intermediate 768); activations N(0, 1); bf16 storage, fp32
 router and accumulation.  At N > 1 the block runs expert-parallel (E/N
-experts per GPU, each GPU with its own 8192 tokens: weak scaling) with NCCL
-all-to-all dispatch and combine.
+experts per GPU, each GPU with its own 8192 tokens: weak scaling) with the
+dispatch and combine exchanged over NVLink peer memory by library kernels
+(--ep peer, default) or by NCCL all-to-all (--ep nccl).
+
+`value`: CUDA-graph replay with the inputs resident.  `e2e`: the same batches
+from page-locked host memory, copied in and back inside the timed region (at
+N=1 through the host-batch block, copies overlapped with neighbouring
+batches' blocks).  The line also carries the GEMM-1 roofline, the SM clocks
+seen during the timed region, the CPU baseline (the oracle, N=1) and the
+48-layer decoder stack's TTFT and decode tokens/s.
 
 Prints ONE JSON line on rank 0.
 """
