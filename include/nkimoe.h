@@ -264,6 +264,11 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
  * the work is enqueued.  The status word of the workspace
  * (nkimoe_read_status) collects the call's device faults. */
 NKIMOE_API size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
+/* How nkimoe_moe_block_host cuts a T-token batch under the current options:
+ * chunks of *chunk_len tokens, *chunk_count of them, the last taking the
+ * remainder (T - (count - 1) * len).  Host-only; no reference counterpart. */
+NKIMOE_API int nkimoe_moe_block_host_plan(int64_t T, int64_t E, int64_t K, int have_router_split,
+                                          int64_t chunk_tokens, int64_t* chunk_len, int64_t* chunk_count);
 NKIMOE_API int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float* router_bias,
                                      const void* router_w_split, const void* w13, const void* w2, void* out_host,
                                      int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,

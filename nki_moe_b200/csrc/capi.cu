@@ -834,6 +834,15 @@ size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, in
   return host_block_bytes(T, H, I, E, K) + 4 * host_stage_bytes(T, H);  // two slots of input + output rows
 }
 
+int nkimoe_moe_block_host_plan(int64_t T, int64_t E, int64_t K, int have_router_split, int64_t chunk_tokens,
+                               int64_t* chunk_len, int64_t* chunk_count) {
+  NKI_REQUIRE(T >= 0 && E > 0 && K > 0 && chunk_len && chunk_count, NKIMOE_ERR_INVALID_ARG, "bad plan arguments");
+  const HostChunks ch = host_chunks(T, E, K, have_router_split != 0, chunk_tokens);
+  *chunk_len = ch.len;
+  *chunk_count = ch.count;
+  return NKIMOE_OK;
+}
+
 int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float* router_bias,
                           const void* router_w_split, const void* w13, const void* w2, void* out_host,
                           int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,

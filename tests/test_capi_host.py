@@ -144,3 +144,41 @@ def test_no_cpu_path_for_host_weights():
         ops.moe_block_host(x[0].bfloat16(), moe.router.weight, None, 2)
     with pytest.raises(ValueError, match="CUDA"):
         ops.moe_block(x[0].bfloat16(), moe.router.weight, None, 2)
+
+
+def _plan(T, E=128, K=8, split=True, chunk=0):
+    n, c = ctypes.c_int64(0), ctypes.c_int64(0)
+    _lib.call("nkimoe_moe_block_host_plan", T, E, K, int(split), chunk, ctypes.byref(n), ctypes.byref(c))
+    lens = [n.value] * (c.value - 1)
+    return lens + [T - sum(lens)]
+
+
+def test_host_batch_chunk_plan():
+    """Chunks of a host-batch call: cut only where every chunk takes the whole
+    batch's path (the tensor-core router at 256 tokens or more with the
+    router planes given; more than 48 rows per expert under the auto GEMM
+    schedule), so the output is the whole-batch block's bit for bit."""
+    assert _plan(8192) == [4096, 4096]                         # default: halves
+    assert _plan(2048) == [1024, 1024]
+    assert _plan(2048, chunk=1000) == [1000, 1048]             # a short tail joins the chunk before
+    assert _plan(3000, chunk=769) == [769, 769, 1462]
+    assert _plan(3000, chunk=500) == [769, 769, 1462]          # at least 48 * 128 / 8 + 1 = 769 tokens
+    assert _plan(8192, chunk=100) == [769] * 9 + [1271]        # at most 16 chunks, tail >= 769
+    assert _plan(8192, chunk=1 << 30) == [8192]
+    assert _plan(1400) == [1400]                               # halves would be shorter than 769
+    assert _plan(300) == [300]                                 # weight-streaming GEMMs: one chunk
+    assert _plan(8192, split=False) == [8192]                  # CUDA-core router: its split-K follows T
+    assert _plan(0) == [0]
+    try:
+        _lib.set_option("router", 1)                           # CUDA-core router forced
+        assert _plan(8192) == [8192]
+        _lib.set_option("router", 0)
+        _lib.set_option("gemm_schedule", 2)                    # weight-streaming GEMMs forced
+        assert _plan(8192) == [8192]
+        _lib.set_option("gemm_schedule", 1)                    # tile-rows GEMMs forced: 256-token minimum
+        assert _plan(2048, chunk=300) == [300] * 5 + [548]
+    finally:
+        _lib.set_option("router", 0)
+        _lib.set_option("gemm_schedule", 0)
+    with pytest.raises(_lib.NKIMoEError):
+        _lib.call("nkimoe_moe_block_host_plan", 10, 0, 8, 1, 0, None, None)
