@@ -46,8 +46,8 @@ sys.path.insert(0, REPO)
 E2E_CHUNK_TOKENS = 1 << 30
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernel (GEMM-1), from the ncu captures summarised in
-# profiles/grouped_gemm_prefill_c3_t8192.md and profiles/grouped_gemm_decode_c2_t64.md.
+# dominant kernel (GEMM-1), from ncu captures of the 8192-token prefill and the
+# 64-token decode workloads.
 NCU_TRAFFIC_BYTES = {"prefill": 1.0739e9 + 92.66e6, "decode": 794.89e6 + 3.64e6}
 
 
@@ -239,6 +239,22 @@ def cpu_inputs(inp, torch):
             else v.float().cpu().numpy() for k, v in inp.items()}
 
 
+def pin_cpu_threads():
+    """Use every host core for the CPU legs, whatever the launcher set
+    (torchrun exports OMP_NUM_THREADS=1): torch's intra-op pool and the BLAS
+    pools numpy loaded."""
+    import numpy as np  # noqa: F401
+    import torch
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
+    except Exception:  # noqa: BLE001 - no threadpoolctl: numpy keeps its pool
+        pass
+    return n
+
+
 def cpu_threads():
     import numpy as np  # noqa: F401
     try:
@@ -259,6 +275,7 @@ def run_reference(args):
 
     from nki_moe_b200.workloads import WORKLOADS, make_moe_inputs
     wl = WORKLOADS[{"prefill": "c3", "decode": "c2", "skewed": "c4"}[args.workload]]
+    pin_cpu_threads()
     sample = wl.tokens if args.workload == "decode" else 1024
     inp = make_moe_inputs(wl, tokens=sample)
     cin = cpu_inputs(inp, torch)

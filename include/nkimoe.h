@@ -55,6 +55,7 @@ extern "C" {
 #define NKIMOE_LAYOUT_HF 1         /* gate_up [E,2I,H], down [E,H,I] (HF Qwen3MoeExperts)       */
 
 #define NKIMOE_IPC_HANDLE_BYTES 64 /* cudaIpcMemHandle_t, for nkimoe_peer_alloc / nkimoe_peer_open */
+#define NKIMOE_NOALLOC_SCRATCH_BYTES (8u << 20) /* scratch array of nkimoe_moe_block_noalloc */
 
 NKIMOE_API int nkimoe_version(void);
 NKIMOE_API const char* nkimoe_last_error(void);
@@ -72,16 +73,22 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * bit 1 the routing-weight-scaled output; default 3),
  * "pdl" (1, the default: the decode-path kernels are launched with
  * programmatic dependent launch, so a kernel's launch and prologue overlap
- * the previous kernel in the stream; 0 = plain launches).
+ * the previous kernel in the stream; 0 = plain launches),
+ * "peer_wait_cycles" (budget of each expert-parallel wait for the peers, in
+ * SM clock cycles, 1000 to 1e12; default 2e10, about 10 s).
  * No reference counterpart (NKI tile sizes are compile-time constants,
  * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */
 NKIMOE_API int nkimoe_set_option(const char* name, long long value);
 
-/* Profiling hook: `events` is an array of `count` (<= 8) cudaEvent_t that the
- * calling thread's later block calls record on their stream at the start of
- * each stage: 0 router, 1 top-k, 2 permute, 3 gather, 4 GEMM-1 (SwiGLU),
- * 5 GEMM-2 (routing weight), 6 combine, 7 end.  count = 0 turns it off.
+/* Profiling hook: `events` is an array of `count` (<= 13) cudaEvent_t that
+ * the calling thread's later block calls record on their stream at the start
+ * of each stage: 0 router, 1 top-k, 2 permute, 3 gather, 4 GEMM-1 (SwiGLU),
+ * 5 GEMM-2 (routing weight), 6 combine, 7 end; the expert-parallel block
+ * (nkimoe_ep_peer_forward) also records 8 send (destinations, sort, stores
+ * to the owners) after 1, 9 wait for the senders (+ mask) before 2, and
+ * after 7 (the receiver's block and the return of its sums): 10 wait for the
+ * partial sums, 11 their sum, 12 end.  count = 0 turns it off.
  * No reference counterpart (the reference times whole graphs, main.py:258-277). */
 NKIMOE_API int nkimoe_set_stage_events(void* const* events, int count);
 
@@ -260,7 +267,10 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
  * has completed.  The host buffers must stay valid until then, and no other
  * entry point may be given the workspace before then (the copy back reads
  * the call's staging rows in it); host-batch calls that share a workspace
- * are issued on one stream and alternate its two slots safely.  Returns once
+ * are issued on one stream and alternate its two slots safely.  The slots'
+ * place in the workspace follows T: a call whose T differs from the previous
+ * call's on the same workspace first waits for the earlier calls' blocks and
+ * copies back (no overlap across that change).  Returns once
  * the work is enqueued.  The status word of the workspace
  * (nkimoe_read_status) collects the call's device faults. */
 NKIMOE_API size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
@@ -280,10 +290,14 @@ NKIMOE_API int nkimoe_moe_block_host(const void* x_host, const float* router_w, 
  * entered where the layer is issued, an embedding that forbids allocation
  * while it records CUDA graphs).  It has no counterpart in the reference.
  * Same arguments and results as nkimoe_moe_block without the workspace: the
- * scratch is a fixed 8 MiB array inside the library, held by every GPU that
- * loads the library until the process exits (enough for up to 168 tokens at
- * H=2048, I=768, E=128, K=8; larger batches return NKIMOE_ERR_WORKSPACE
- * without touching the GPU).  The first call on a device looks up the
+ * scratch is a fixed NKIMOE_NOALLOC_SCRATCH_BYTES (8 MiB) array inside the
+ * library, held by every GPU that loads the library until the process exits.
+ * A batch fits when nkimoe_moe_workspace_bytes(T, H, I, E, K) is at most that
+ * size: up to 175 tokens at H=2048, I=768, E=128, K=8.  Larger batches return
+ * NKIMOE_ERR_WORKSPACE, and bad shapes NKIMOE_ERR_INVALID_ARG or
+ * NKIMOE_ERR_UNSUPPORTED, without touching the GPU.  Device faults (a bounded
+ * wait that ran out, an expert id out of range) land in the array's status
+ * word: read it with nkimoe_noalloc_read_status.  The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress) and should come before any
  * stream capture.  All calls on a device share the array, which keeps the
  * last call's contents (each call clears what must start at zero): two calls
@@ -293,6 +307,10 @@ NKIMOE_API int nkimoe_moe_block_noalloc(const void* x, const float* router_w, co
                                         const void* router_w_split, const void* w13, const void* w2, void* out,
                                         int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,
                                         int64_t E, int64_t K, void* stream);
+/* Reads and clears the status word of nkimoe_moe_block_noalloc's scratch
+ * array on the current device (synchronises the stream; allocates nothing).
+ * Same returns as nkimoe_read_status.  No reference counterpart. */
+NKIMOE_API int nkimoe_noalloc_read_status(void* stream, int* status_out);
 
 /* Reads and clears the device status word of a workspace (synchronises the
  * stream).  Returns NKIMOE_OK, NKIMOE_ERR_DEVICE (status in *status_out), or
@@ -398,10 +416,13 @@ NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I
  * own counter + 1 per call), so that a step captured in a CUDA graph can be
  * replayed -- a caller uses one mode for the buffer's lifetime.  A peer that
  * never arrives sets NKIMOE_DEV_TIMEOUT in the status word
- * (nkimoe_read_status) after a bounded wait (~10 s). */
+ * (nkimoe_read_status) after a bounded wait (~10 s; option
+ * "peer_wait_cycles").  topk_idx_out / topk_w_out (device, [T, K], may be
+ * NULL): the routing of this rank's tokens, as nkimoe_moe_block returns it. */
 NKIMOE_API int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias,
                                       const void* router_w_split, const void* w13_local, const void* w2_local,
-                                      void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                      void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H,
+                                      int64_t I, int64_t E, int64_t K,
                                       int64_t num_ranks, int64_t rank, int64_t max_tokens, void* const* peer_buffers,
                                       uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
 

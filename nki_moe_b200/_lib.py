@@ -59,6 +59,7 @@ SIGNATURES = {
                                    _vp, _sz, _vp, _vp]),
     "nkimoe_router_split": (_i, [_vp, _vp, _i64, _i64, _vp]),
     "nkimoe_read_status": (_i, [_vp, _vp, _c.POINTER(_i)]),
+    "nkimoe_noalloc_read_status": (_i, [_vp, _c.POINTER(_i)]),
     "nkimoe_moe_block_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                       _vp]),
     "nkimoe_grouped_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
@@ -75,8 +76,8 @@ SIGNATURES = {
     "nkimoe_peer_close": (_i, [_vp]),
     "nkimoe_peer_free": (_i, [_vp]),
     "nkimoe_ep_peer_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64]),
-    "nkimoe_ep_peer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
-                                    _i64, _c.POINTER(_vp), _c.c_uint32, _vp, _sz, _vp]),
+    "nkimoe_ep_peer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                    _i64, _i64, _c.POINTER(_vp), _c.c_uint32, _vp, _sz, _vp]),
     "nkimoe_ep_dispatch_workspace_bytes": (_sz, [_i64, _i64]),
     "nkimoe_ep_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                 _vp]),

@@ -24,7 +24,7 @@ BUILD = os.path.join(REPO, "_build")
 LIB = os.path.join(PKG, "libnkimoe.so")
 SOURCES = ["norm.cu", "router.cu", "permute.cu", "pack.cu", "grouped_gemm.cu", "ep_peer.cu", "capi.cu",
            "noalloc.cu", "attention.cu", "linear.cu"]
-HEADERS = ["common.cuh", "kernels.h", "rope.cuh"]
+HEADERS = ["common.cuh", "kernels.h", "rope.cuh", "permute_small.cuh"]
 
 
 def nvcc() -> str:

@@ -68,6 +68,10 @@ std::atomic<int> g_stage_stores{3};  // rows-schedule epilogue staging: bit 0 Sw
 std::atomic<int> g_gather_fused{0};  // GEMM-1 gathers its rows itself: 1 cp.async, 2 TMA gather4
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
 std::atomic<int> g_pdl{1};           // programmatic dependent launch of the decode-path kernels
+// Budget of the expert-parallel waits for peers, in SM clock cycles (~10 s at
+// 2 GHz by default): a peer that has not reached the step by then is reported
+// as a timeout in the status word.
+std::atomic<long long> g_peer_wait_cycles{20000000000LL};
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
@@ -195,16 +199,6 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   long long grid = std::min<long long>(max_tiles, device_sm_count());
   if (pair) grid = 2 * std::max<long long>(1, std::min<long long>(max_tiles, device_sm_count() / 2));
   NKI_CUDA(grouped_gemm_launch(variant, ta, tw, p, static_cast<int>(std::max<long long>(grid, 1)), s));
-  return NKIMOE_OK;
-}
-
-int check_moe_shapes(long long T, long long H, long long I, long long E, long long K) {
-  NKI_REQUIRE(T >= 0 && H > 0 && I > 0 && E > 0 && K > 0, NKIMOE_ERR_INVALID_ARG, "non-positive dimension");
-  NKI_REQUIRE(E <= kMaxExperts, NKIMOE_ERR_UNSUPPORTED, "num_experts %lld > %d", E, kMaxExperts);
-  NKI_REQUIRE(K <= 32 && K <= E, NKIMOE_ERR_UNSUPPORTED, "top_k %lld must be <= 32 and <= num_experts", K);
-  NKI_REQUIRE(H % 128 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden %lld must be a multiple of 128", H);
-  NKI_REQUIRE(I % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "intermediate %lld must be a multiple of 64", I);
-  NKI_REQUIRE(T * K < (1LL << 31), NKIMOE_ERR_UNSUPPORTED, "T*K too large");
   return NKIMOE_OK;
 }
 
@@ -377,6 +371,16 @@ PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, 
 
 }  // namespace
 
+int check_moe_shapes(long long T, long long H, long long I, long long E, long long K) {
+  NKI_REQUIRE(T >= 0 && H > 0 && I > 0 && E > 0 && K > 0, NKIMOE_ERR_INVALID_ARG, "non-positive dimension");
+  NKI_REQUIRE(E <= kMaxExperts, NKIMOE_ERR_UNSUPPORTED, "num_experts %lld > %d", E, kMaxExperts);
+  NKI_REQUIRE(K <= 32 && K <= E, NKIMOE_ERR_UNSUPPORTED, "top_k %lld must be <= 32 and <= num_experts", K);
+  NKI_REQUIRE(H % 128 == 0, NKIMOE_ERR_UNSUPPORTED, "hidden %lld must be a multiple of 128", H);
+  NKI_REQUIRE(I % 64 == 0, NKIMOE_ERR_UNSUPPORTED, "intermediate %lld must be a multiple of 64", I);
+  NKI_REQUIRE(T * K < (1LL << 31), NKIMOE_ERR_UNSUPPORTED, "T*K too large");
+  return NKIMOE_OK;
+}
+
 bool make_tmap_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, int box_rows) {
   auto fn = encode_fn();
   if (!fn || rows <= 0 || cols <= 0 || (cols * 2) % 16 != 0 || !aligned16(base)) return false;
@@ -520,6 +524,7 @@ size_t host_block_bytes(long long T, long long H, long long I, long long E, long
 // block of the call before or after it.
 struct HostSlots {
   unsigned calls = 0;
+  long long last_tokens = -1;  // batch size of the previous call (its staging layout)
   cudaEvent_t x_free[2] = {}, out_free[2] = {};
 };
 struct HostCopyStreams {
@@ -604,6 +609,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "router" && value >= 0 && value <= 2) {
     g_router = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "peer_wait_cycles" && value >= 1000 && value <= 1000000000000LL) {
+    g_peer_wait_cycles = value;
     return NKIMOE_OK;
   }
   return fail(NKIMOE_ERR_INVALID_ARG, "unknown option %s=%lld", name, value);
@@ -878,6 +887,19 @@ int nkimoe_moe_block_host(const void* x_host, const float* router_w, const float
   char* xs = static_cast<char*>(workspace) + blk_bytes + k * 2 * host_stage_bytes(T, H);
   char* os = xs + host_stage_bytes(T, H);
   const size_t row_bytes = sizeof(uint16_t) * static_cast<size_t>(H);
+  // The staging slots sit after the block workspace, whose size follows T, so
+  // with the same T a slot only overlaps its own previous use.  When T changes
+  // this call's rows may lie on the previous calls' block scratch or staging
+  // rows: its copies in then wait for both slots' blocks and copies back, and
+  // its block for both copies back.
+  if (sl->last_tokens >= 0 && sl->last_tokens != T) {
+    for (int i = 0; i < 2; ++i) {
+      NKI_CUDA(cudaStreamWaitEvent(hs.in, sl->x_free[i], 0));
+      NKI_CUDA(cudaStreamWaitEvent(hs.in, sl->out_free[i], 0));
+      NKI_CUDA(cudaStreamWaitEvent(s, sl->out_free[i], 0));
+    }
+  }
+  sl->last_tokens = T;
   // input rows: after the block of this slot's previous call has read them
   NKI_CUDA(cudaStreamWaitEvent(hs.in, sl->x_free[k], 0));
   for (long long c = 0; c < ch.count; ++c) {
@@ -1146,7 +1168,8 @@ size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E
 }
 
 int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
-                           const void* w13_local, const void* w2_local, void* out, int64_t T, int64_t H, int64_t I,
+                           const void* w13_local, const void* w2_local, void* out, int32_t* topk_idx_out,
+                           float* topk_w_out, int64_t T, int64_t H, int64_t I,
                            int64_t E, int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
                            void* const* peer_buffers, uint32_t epoch, void* workspace, size_t workspace_bytes,
                            void* stream) {
@@ -1178,8 +1201,8 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   const WsLayout R = ws_layout(T, H, I, E, K);
   char* rb = b + W.route;
   int* status = reinterpret_cast<int*>(rb + R.status);
-  int32_t* idx = reinterpret_cast<int32_t*>(rb + R.idx);
-  float* w = reinterpret_cast<float*>(rb + R.w);
+  int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(rb + R.idx);
+  float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(rb + R.w);
   unsigned* counters = reinterpret_cast<unsigned*>(b + W.counters);
   NKI_CUDA(cudaMemsetAsync(status, 0, 256, s));  // status word and router counters
   NKI_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned), s));
@@ -1199,6 +1222,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   void* scratch = row_slot + round256(sizeof(int32_t) * T * P) / sizeof(int32_t);
   int32_t* slot_in = reinterpret_cast<int32_t*>(b + W.slot_in);
   int32_t* slot_out = reinterpret_cast<int32_t*>(b + W.slot_out);
+  mark(kStageEpSend, s);
   if (T > 0)
     NKI_CUDA(ep_dest_launch(idx, static_cast<int>(T), static_cast<int>(K), static_cast<int>(P), static_cast<int>(El),
                             dest, s));
@@ -1210,8 +1234,9 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
                                static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), static_cast<int>(rank),
                                peers, PL, counters, epoch_p, s));
   char* own = peers.base[rank];
+  mark(kStageEpWait, s);
   NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.disp_flag), static_cast<int>(P), epoch_p,
-                               status, s));
+                               status, g_peer_wait_cycles.load(), s));
   int32_t* recv_slots = reinterpret_cast<int32_t*>(own + PL.recv_slots);
   NKI_CUDA(ep_peer_mask_launch(recv_slots, reinterpret_cast<const int32_t*>(own + PL.counts), static_cast<int>(P),
                                static_cast<int>(Tm), static_cast<int>(K), s));
@@ -1222,12 +1247,15 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
                     reinterpret_cast<const float*>(own + PL.recv_w), nullptr, P * Tm, H, I, El, K, b + W.recv,
                     workspace_bytes - W.recv, s, &pc, status);
   if (rc != NKIMOE_OK) return rc;
+  mark(kStageEpReturnWait, s);
   NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.res_flag), static_cast<int>(P), epoch_p,
-                               status, s));
+                               status, g_peer_wait_cycles.load(), s));
+  mark(kStageEpSum, s);
   if (T > 0)
     NKI_CUDA(combine_launch(reinterpret_cast<const __nv_bfloat16*>(own + PL.ret_y), slot_out, nullptr,
                             static_cast<__nv_bfloat16*>(out), static_cast<int>(T), static_cast<int>(P),
                             static_cast<int>(H), s));
+  mark(kStageEpEnd, s);
   return NKIMOE_OK;
 }
 

@@ -28,9 +28,6 @@ namespace nkimoe {
 
 namespace {
 
-// ~10 s at 2 GHz: a peer that has not reached this step by then is reported
-constexpr long long kPeerWaitBudgetCycles = 20000000000LL;
-
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -150,15 +147,18 @@ __global__ void __launch_bounds__(256) ep_peer_send_kernel(
   }
 }
 
-// Poll this rank's P flags until each holds the step's epoch (bounded).  One warp.
-__global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status) {
+// Poll this rank's P flags until each holds the step's epoch, for at most
+// `budget` SM clock cycles; a flag still behind then sets the timeout bit of the
+// status word and the kernel returns.  One warp.
+__global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status,
+                                    long long budget) {
   const uint32_t epoch = *epoch_p;
   const int lane = threadIdx.x;
   bool ok = true;
   if (lane < P) {
     const long long t0 = clock64();
     while (static_cast<int>(ld_acquire_sys(flags + lane) - epoch) < 0) {
-      if (clock64() - t0 > kPeerWaitBudgetCycles) {
+      if (clock64() - t0 > budget) {
         ok = false;
         break;
       }
@@ -305,8 +305,9 @@ cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s) 
   return cudaGetLastError();
 }
 
-cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status, cudaStream_t s) {
-  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, P, epoch_p, status);
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status,
+                                long long budget_cycles, cudaStream_t s) {
+  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, P, epoch_p, status, budget_cycles);
   return cudaGetLastError();
 }
 

@@ -48,7 +48,13 @@ enum Stage : int {
   kStageGemm2 = 5,
   kStageCombine = 6,
   kStageEnd = 7,
-  kNumStageEvents = 8,
+  // expert-parallel block only: the exchange around the receiver's block
+  kStageEpSend = 8,        // destinations, (token, rank) sort and the rows' stores to their owners
+  kStageEpWait = 9,        // wait for the senders, mask of unused region rows
+  kStageEpReturnWait = 10, // after the receiver's block: wait for the partial sums
+  kStageEpSum = 11,        // sum of the partial sums
+  kStageEpEnd = 12,
+  kNumStageEvents = 13,
 };
 constexpr int kPermuteChunk = 256;  // assignments per block in the permutation kernels
 
@@ -160,7 +166,8 @@ cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, cons
                                 const uint32_t* epoch_p, cudaStream_t s);
 // epoch := value when nonzero, else epoch + 1 (device-side step count)
 cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s);
-cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status, cudaStream_t s);
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status,
+                                long long budget_cycles, cudaStream_t s);
 cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, int Tm, int K, cudaStream_t s);
 cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
                                    int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
@@ -253,5 +260,7 @@ int device_sm_count();
 
 // Sets the calling thread's message returned by nkimoe_last_error().
 void set_last_error(const char* msg);
+// Shape rules of the MoE block entry points (sets the last error on failure).
+int check_moe_shapes(long long T, long long H, long long I, long long E, long long K);
 
 }  // namespace nkimoe

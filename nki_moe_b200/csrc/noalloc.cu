@@ -24,7 +24,7 @@
 namespace nkimoe {
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+constexpr size_t kNoAllocScratchBytes = NKIMOE_NOALLOC_SCRATCH_BYTES;  // 8 MiB
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -58,6 +58,9 @@ int nkimoe_moe_block_noalloc(const void* x, const float* router_w, const float* 
                              const void* router_w_split, const void* w13, const void* w2, void* out,
                              int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
                              int64_t K, void* stream) {
+  // shapes first: a negative T would otherwise show up as a huge scratch need
+  const int rc = nkimoe::check_moe_shapes(T, H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
   const size_t need = nkimoe_moe_workspace_bytes(T, H, I, E, K);
   if (need > nkimoe::kNoAllocScratchBytes) {
     char msg[256];
@@ -75,6 +78,18 @@ int nkimoe_moe_block_noalloc(const void* x, const float* router_w, const float* 
   }
   return nkimoe_moe_block(x, router_w, router_bias, router_w_split, w13, w2, out, topk_idx_out, topk_w_out, T, H, I,
                           E, K, scratch, nkimoe::kNoAllocScratchBytes, stream);
+}
+
+// The device status word of the no-allocation entry point sits at the start of
+// the library's scratch array, which its callers cannot name: this reads and
+// clears it for them, as nkimoe_read_status does for a workspace.
+int nkimoe_noalloc_read_status(void* stream, int* status_out) {
+  void* scratch = nullptr;
+  if (nkimoe::noalloc_scratch(&scratch) != NKIMOE_OK) {
+    nkimoe::set_last_error("nkimoe_noalloc_read_status: cudaGetSymbolAddress of the scratch array failed");
+    return NKIMOE_ERR_CUDA;
+  }
+  return nkimoe_read_status(scratch, stream, status_out);
 }
 
 }  // extern "C"

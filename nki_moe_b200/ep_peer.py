@@ -116,7 +116,10 @@ class PeerExpertParallelMoE(nn.Module):
                 bases.append(p.value)
         return bases
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, return_routing: bool = False):
+        """``out`` (optional): a contiguous bf16 ``[T, H]`` device tensor for
+        the result.  With ``return_routing`` also returns this rank's routing
+        ``(idx int32 [T, K], weights fp32 [T, K])``."""
         x = ops._contig(ops._cuda(x, "x"), torch.bfloat16)
         T, H = x.shape
         if T > self.max_tokens or H != self.hidden:
@@ -125,16 +128,24 @@ class PeerExpertParallelMoE(nn.Module):
         pe = self.packed()
         nbytes = size_call("nkimoe_ep_peer_workspace_bytes", T, H, I, E, K, P, self.max_tokens)
         ws = ops.workspace(x.device, nbytes)
-        out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.bfloat16, device=x.device)
+        elif out.dtype != torch.bfloat16 or tuple(out.shape) != (T, H) or not out.is_contiguous() or \
+                out.device != x.device:
+            raise ValueError("out must be a contiguous bf16 [T, H] tensor on x's device")
+        idx = w = None
+        if return_routing:
+            idx = torch.empty(T, K, dtype=torch.int32, device=x.device)
+            w = torch.empty(T, K, dtype=torch.float32, device=x.device)
         self.epoch = self.epoch % 0xFFFFFFFF + 1  # nonzero, increasing between steps
         epoch = 0 if self.device_epochs else self.epoch
         bases = (ctypes.c_void_p * P)(*self.bases)
         call("nkimoe_ep_peer_forward", ops._p(x), ops._p(self.router_w), ops._p(self.router_bias),
-             ops._p(self.router_split), ops._p(pe.w13), ops._p(pe.w2), ops._p(out), T, H, I, E, K, P, self.rank,
-             self.max_tokens, bases, epoch, ops._p(ws), ws.numel(), ops._s(x))
+             ops._p(self.router_split), ops._p(pe.w13), ops._p(pe.w2), ops._p(out), ops._p(idx), ops._p(w), T, H, I,
+             E, K, P, self.rank, self.max_tokens, bases, epoch, ops._p(ws), ws.numel(), ops._s(x))
         if ops.sync_check_enabled():
             ops.read_status(ws)
-        return out
+        return (out, idx, w) if return_routing else out
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (after every rank is

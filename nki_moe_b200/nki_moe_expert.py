@@ -55,10 +55,16 @@ def nki_grouped_expert_gemm(input_tokens, expert_weights, expert_ids, num_expert
     M, H = input_tokens.shape
     E, _, N = expert_weights.shape
     ids = expert_ids.reshape(M, 1)
-    row_token, _, _, offsets = ops.permute(ids, num_experts)
-    a_perm = input_tokens.to(torch.bfloat16)[row_token.long()]
-    w_packed = expert_weights.to(torch.bfloat16).transpose(1, 2).contiguous()  # [E, N, H]
-    out = ops.grouped_gemm(a_perm, w_packed, offsets, out_row_map=row_token, out_rows=M)
+    # rows grouped by expert (library permutation + gather), one slot per row
+    ones = torch.ones(M, 1, dtype=torch.float32, device=input_tokens.device)
+    a_perm, _, slot_row, counts = ops.dispatch(input_tokens.to(torch.bfloat16), ids, ones, num_experts)
+    offsets = torch.zeros(num_experts + 1, dtype=torch.int32, device=input_tokens.device)
+    offsets[1:] = counts.cumsum(0)
+    # [E, N, H] K-major copy, made once per weight tensor and cached
+    w_packed = ops.kmajor_weights(expert_weights, k_multiple=64, n_multiple=128)
+    out_perm = ops.grouped_gemm(a_perm, w_packed, offsets)
+    # back to token order: a one-slot combine copies row slot_row[m] to m
+    out = ops.combine(out_perm, slot_row, M, 1)[:, :N]
     dt = input_tokens.dtype if input_tokens.dtype in (torch.float32, torch.bfloat16, torch.float16) else torch.bfloat16
     return out.to(dt)
 

@@ -43,18 +43,17 @@ def _out_dtype(t: torch.Tensor):
 def nki_matmul_tiled(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """``a[M,K] @ b[K,N]`` with fp32 accumulation on the tensor cores (one
     expert segment of the grouped GEMM).  K and N are zero-padded to the
-    kernel's 64 / 128 granularity when needed."""
+    kernel's 64 / 128 granularity when needed.  ``b`` is the weight operand:
+    its K-major, padded bf16 copy is made once and cached while ``b`` lives
+    unmodified (``ops.kmajor_weights``), so repeated calls with one weight
+    re-lay it out once."""
     M, K = a.shape
     N = b.shape[1]
-    Kp, Np = -(-K // 64) * 64, -(-N // 128) * 128
+    Kp = -(-K // 64) * 64
     a16 = a.to(torch.bfloat16)
-    bt = b.to(torch.bfloat16).t()
     if Kp != K:
         a16 = torch.nn.functional.pad(a16, (0, Kp - K))
-        bt = torch.nn.functional.pad(bt, (0, Kp - K))
-    if Np != N:
-        bt = torch.nn.functional.pad(bt, (0, 0, 0, Np - N))
-    w = bt.contiguous().reshape(1, Np, Kp)
+    w = ops.kmajor_weights(b, k_multiple=64, n_multiple=128)
     offsets = torch.tensor([0, M], dtype=torch.int32, device=a.device)
     out = ops.grouped_gemm(a16.contiguous(), w, offsets)
     return out[:, :N].to(_out_dtype(a))
@@ -227,22 +226,31 @@ def enable_nki_moe(model):
 
 
 def replace_with_nki_moe(model, config):
-    """Replace every layer's MoE with ``NKIMoESimple`` carrying the same weights."""
-    for layer in model.model.layers:
-        moe = NKIMoESimple(hidden_size=config.hidden_size, intermediate_size=config.moe_intermediate_size,
-                           num_experts=config.num_experts, top_k=config.num_experts_per_tok, return_tuple=True)
+    """Replace every layer's MoE with ``NKIMoESimple`` carrying the same weights.
+
+    Raises ``AttributeError`` (naming the layer) when a layer's MoE holds no
+    weights this function can find: the reference (nki_moe_integrated.py:545-563)
+    then silently leaves randomly initialised experts in place, which this
+    package does not do.  No layer is replaced unless every layer's weights
+    were found."""
+    new_mlps = []
+    for i, layer in enumerate(model.model.layers):
         original = layer.mlp
         try:
             gate_up, down, layout = _find_expert_weights(original)
             rw = _find_router_weight(original)
-            with torch.no_grad():
-                if layout == "hf":
-                    gate_up = gate_up.transpose(1, 2)
-                    down = down.transpose(1, 2)
-                moe.gate_up_proj.data = gate_up.detach().contiguous()
-                moe.down_proj.data = down.detach().contiguous()
-                moe.router.weight.data = rw.detach().float().contiguous()
-        except AttributeError:
-            pass
+        except AttributeError as e:
+            raise AttributeError(f"replace_with_nki_moe: layer {i}: {e}") from e
+        moe = NKIMoESimple(hidden_size=config.hidden_size, intermediate_size=config.moe_intermediate_size,
+                           num_experts=config.num_experts, top_k=config.num_experts_per_tok, return_tuple=True)
+        with torch.no_grad():
+            if layout == "hf":
+                gate_up = gate_up.transpose(1, 2)
+                down = down.transpose(1, 2)
+            moe.gate_up_proj.data = gate_up.detach().contiguous()
+            moe.down_proj.data = down.detach().contiguous()
+            moe.router.weight.data = rw.detach().float().contiguous()
+        new_mlps.append(moe)
+    for layer, moe in zip(model.model.layers, new_mlps):
         layer.mlp = moe
     return model

@@ -24,7 +24,8 @@ __all__ = [
     "pack_gate_up", "pack_down", "PackedExperts", "packed_experts", "moe_experts", "moe_block",
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
     "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention", "skinny_linear",
-    "moe_block_add_rmsnorm", "moe_block_host",
+    "moe_block_add_rmsnorm", "moe_block_host", "kmajor_weights",
+    "release_captured_workspaces",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -60,19 +61,49 @@ def _contig(t: torch.Tensor, dtype=None) -> torch.Tensor:
 # ---------------------------------------------------------------- workspace
 _ws_lock = threading.Lock()
 _ws: dict = {}
+# Buffers that a CUDA graph captured and that a later, larger call replaced:
+# the graph still writes them on every replay, so they stay alive until the
+# caller says its graphs are gone (release_captured_workspaces).
+_ws_retired: list = []
+
+
+def _grow(table: dict, key, device: torch.device, nbytes: int, zero: bool) -> torch.Tensor:
+    """The buffer of ``table[key]``, replaced by a larger one when it is
+    smaller than ``nbytes``.  A buffer handed out while the current stream
+    is being captured is marked, and a marked buffer that gets replaced is
+    kept in ``_ws_retired`` instead of going back to the allocator."""
+    capturing = torch.cuda.is_current_stream_capturing()
+    with _ws_lock:
+        buf = table.get(key)
+        if buf is None or buf.numel() < nbytes:
+            if buf is not None and getattr(buf, "_nkimoe_captured", False):
+                _ws_retired.append(buf)
+            n = max(nbytes, 1 << 20 if not zero else 1 << 16)
+            buf = torch.zeros(n, dtype=torch.uint8, device=device) if zero else \
+                torch.empty(n, dtype=torch.uint8, device=device)
+            table[key] = buf
+        if capturing:
+            buf._nkimoe_captured = True
+        return buf
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """A per-(device, stream) scratch buffer from the torch caching allocator,
-    grown on demand and reused by later calls on the same stream."""
-    stream = torch.cuda.current_stream(device).cuda_stream
-    key = (device.index, stream)
+    grown on demand and reused by later calls on the same stream.  A buffer
+    that a CUDA graph captured outlives its replacement by a larger call
+    (streams from torch's pool reuse their handles), until
+    :func:`release_captured_workspaces`."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    return _grow(_ws, key, device, nbytes, zero=False)
+
+
+def release_captured_workspaces() -> int:
+    """Drop the replaced workspaces kept for captured CUDA graphs (call after
+    those graphs are destroyed).  Returns how many were released."""
     with _ws_lock:
-        buf = _ws.get(key)
-        if buf is None or buf.numel() < nbytes:
-            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-            _ws[key] = buf
-        return buf
+        n = len(_ws_retired)
+        _ws_retired.clear()
+    return n
 
 
 def read_status(ws: torch.Tensor) -> int:
@@ -143,15 +174,10 @@ _attn_ws: dict = {}
 
 def _attention_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Zero-filled per-(device, stream) workspace of the decode attention
-    (its split counters must start at zero; every call leaves them at zero)."""
-    stream = torch.cuda.current_stream(device).cuda_stream
-    key = (device.index, stream)
-    with _ws_lock:
-        buf = _attn_ws.get(key)
-        if buf is None or buf.numel() < nbytes:
-            buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
-            _attn_ws[key] = buf
-        return buf
+    (its split counters must start at zero; every call leaves them at zero).
+    Kept for captured graphs as :func:`workspace` is."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    return _grow(_attn_ws, key, device, nbytes, zero=True)
 
 
 def decode_attention(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, positions: torch.Tensor,
@@ -337,6 +363,40 @@ def packed_experts(gate_up: torch.Tensor, down: torch.Tensor, layout: str = "nxd
         while len(_pack_cache) > _PACK_CACHE_MAX:
             _pack_cache.popitem(last=False)
     return pe
+
+
+_kmajor_cache: "OrderedDict[int, tuple]" = OrderedDict()
+
+
+def kmajor_weights(w: torch.Tensor, k_multiple: int = 64, n_multiple: int = 128) -> torch.Tensor:
+    """Weights ``w [E, K, N]`` (or ``[K, N]``, taken as one expert) as the
+    grouped GEMM's K-major bf16 operand ``[E, N', K']``, K and N zero-padded to
+    the given multiples.  The transpose runs in the library (``nkimoe_pack_down``)
+    once per weight tensor and is cached while ``w`` lives unmodified (weak
+    reference + pointer/version stamp, as :func:`packed_experts`)."""
+    key = id(w)
+    with _pack_lock:
+        hit = _kmajor_cache.get(key)
+        if hit is not None and hit[0]() is w and hit[1] == _stamp(w) and hit[2] == (k_multiple, n_multiple):
+            _kmajor_cache.move_to_end(key)
+            return hit[3]
+    src = _contig(_cuda(w, "w").detach(), torch.bfloat16)
+    if src.dim() == 2:
+        src = src.unsqueeze(0)
+    E, K, N = src.shape
+    Kp, Np = -(-K // k_multiple) * k_multiple, -(-N // n_multiple) * n_multiple
+    if (Kp, Np) != (K, N):
+        src = torch.nn.functional.pad(src, (0, Np - N, 0, Kp - K)).contiguous()
+    out = torch.empty(E, Np, Kp, dtype=torch.bfloat16, device=src.device)
+    # pack_down's plain transpose: [E, I, H] -> [E, H, I] with I = K', H = N'
+    call("nkimoe_pack_down", _p(src), LAYOUT_NXD, _p(out), E, Np, Kp, _s(src))
+    with _pack_lock:
+        for k in [k for k, v in _kmajor_cache.items() if v[0]() is None]:
+            del _kmajor_cache[k]
+        _kmajor_cache[key] = (weakref.ref(w), _stamp(w), (k_multiple, n_multiple), out)
+        while len(_kmajor_cache) > _PACK_CACHE_MAX:
+            _kmajor_cache.popitem(last=False)
+    return out
 
 
 # ---------------------------------------------------------------- MoE block

@@ -76,7 +76,7 @@ def run_simple(mod, x, router, gate_up, down, top_k):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="directory holding the reference sources")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     install_neuron_stub()

@@ -182,3 +182,33 @@ def test_host_batch_chunk_plan():
         _lib.set_option("gemm_schedule", 0)
     with pytest.raises(_lib.NKIMoEError):
         _lib.call("nkimoe_moe_block_host_plan", 10, 0, 8, 1, 0, None, None)
+
+
+def test_replace_with_nki_moe_raises_when_weights_are_missing():
+    """The reference leaves randomly initialised experts in place when it cannot
+    find a layer's weights (nki_moe_integrated.py:545-563); this package
+    raises and replaces no layer."""
+    import types
+
+    import torch.nn as nn
+    from nki_moe_b200.nki_moe_integrated import replace_with_nki_moe
+
+    class NoWeights(nn.Module):
+        pass
+
+    layers = [types.SimpleNamespace(mlp=NoWeights()) for _ in range(2)]
+    model = types.SimpleNamespace(model=types.SimpleNamespace(layers=layers))
+    cfg = types.SimpleNamespace(hidden_size=128, moe_intermediate_size=64, num_experts=4, num_experts_per_tok=2)
+    with pytest.raises(AttributeError, match="layer 0"):
+        replace_with_nki_moe(model, cfg)
+    assert all(isinstance(layer.mlp, NoWeights) for layer in layers)
+
+
+def test_peer_wait_budget_option():
+    """The expert-parallel waits' budget is settable; values outside
+    [1000, 1e12] cycles are rejected."""
+    _lib.set_option("peer_wait_cycles", 2_000_000)
+    _lib.set_option("peer_wait_cycles", 20_000_000_000)
+    for bad in (0, 999, 10 ** 13):
+        with pytest.raises(_lib.NKIMoEError):
+            _lib.set_option("peer_wait_cycles", bad)

@@ -213,3 +213,66 @@ def test_expert_parallel_two_gpus_matches_single_gpu(tmp_path):
         # exchange computes (same rows, same order, same sums)
         assert np.array_equal(np.load(tmp_path / f"peer{r}.npy"), d), f"rank {r}: peer != dedup"
         assert np.array_equal(np.load(tmp_path / f"peer2_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
+
+
+def test_peer_wait_runs_out_when_a_peer_never_joins():
+    """Rank 0 of two whose peer never reaches the step (host-side fault: the
+    second rank's buffer is a local buffer that nobody serves).  Both of rank
+    0's bounded waits run out after the short budget set here; the kernels
+    return, the timeout bit lands in the status word and the host raises.  The
+    next step on the same workspace (a single rank, sending to itself) then
+    runs clean and equals the single-GPU block."""
+    import ctypes
+
+    from nki_moe_b200.ep_peer import PeerExpertParallelMoE
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+
+    wl = WORKLOADS["c3"]
+    T, P, El = 256, 2, wl.experts // 2
+    inp = make_moe_inputs(wl, device="cuda", tokens=T)
+    moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        moe.router.weight.copy_(inp["router"])
+        moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
+        moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+    x = inp["x"].to(torch.bfloat16)
+    rw = moe.router.weight.detach().float().contiguous()
+    pe_local = ops.packed_experts(moe.gate_up_proj.detach()[:El].contiguous(),
+                                  moe.down_proj.detach()[:El].contiguous(), "nxd")
+    H, I, E, K = wl.hidden, wl.intermediate, wl.experts, wl.top_k
+    nbuf = _lib.size_call("nkimoe_ep_peer_buffer_bytes", P, T, H, K)
+    bufs = []
+    for _ in range(P):
+        p = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.call("nkimoe_peer_alloc", nbuf, ctypes.byref(p), handle)
+        bufs.append(p.value)
+    ws = ops.workspace(x.device, _lib.size_call("nkimoe_ep_peer_workspace_bytes", T, H, I, E, K, P, T))
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    _lib.set_option("peer_wait_cycles", 2_000_000)  # ~1 ms
+    try:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        _lib.call("nkimoe_ep_peer_forward", ops._p(x), ops._p(rw), None, None, ops._p(pe_local.w13),
+                  ops._p(pe_local.w2), ops._p(out), None, None, T, H, I, E, K, P, 0, T, (ctypes.c_void_p * P)(*bufs), 1,
+                  ops._p(ws), ws.numel(), ops._s(x))
+        t1.record()
+        with pytest.raises(_lib.NKIMoEError) as ei:
+            ops.read_status(ws)
+        assert ei.value.code == _lib.ERR_DEVICE
+        assert "0x1" in str(ei.value)  # NKIMOE_DEV_TIMEOUT
+        assert t0.elapsed_time(t1) < 1000.0  # the budget, not the ~10 s default, ended the waits
+    finally:
+        _lib.set_option("peer_wait_cycles", 20_000_000_000)
+        torch.cuda.synchronize()
+        for b in bufs:
+            _lib.call("nkimoe_peer_free", ctypes.c_void_p(b))
+    # the status word was cleared by the read; the next step is clean
+    peer = PeerExpertParallelMoE.from_dense(moe, max_tokens=T)
+    try:
+        y = peer(x)
+        assert ops.read_status(ops.workspace(x.device, 1)) == 0
+        assert torch.equal(y, ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k))
+    finally:
+        peer.close()

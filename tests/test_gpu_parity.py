@@ -620,6 +620,10 @@ def test_grouped_expert_gemm_and_single_expert():
     out = nki_grouped_expert_gemm(xb, wb, ids.cuda(), E).float().cpu().numpy()
     ref = np.stack([xn[m] @ wn[ids[m]] for m in range(M)])
     assert_block_close(out, ref, tol=1e-2)
+    # the weight re-layout is made once per weight tensor, then reused
+    assert ops.kmajor_weights(wb, 64, 128) is ops.kmajor_weights(wb, 64, 128)
+    out2 = nki_grouped_expert_gemm(xb, wb, ids.cuda(), E).float().cpu().numpy()
+    assert np.array_equal(out, out2)
     # single expert: w[t] * FFN(x[t])
     I = 128
     gu = torch.randn(H, 2 * I, generator=g) * 0.05
