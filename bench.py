@@ -63,6 +63,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-measurement")
+    ap.add_argument("--no-skewed", action="store_true", help="skip the skewed-routing sub-measurement")
     ap.add_argument("--profile-once", action="store_true", help="one warm step only (for ncu launch lists)")
     ap.add_argument("--no-stack", action="store_true", help="skip the 48-layer decoder-stack TTFT / decode run")
     ap.add_argument("--stack-profile-layers", type=int, default=0,
@@ -178,14 +179,16 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- helpers
-def algorithmic(wl, idx_np=None):
-    """FLOPs and bytes of one block and of its GEMM-1 launch."""
+def algorithmic(wl, idx_np=None, tokens=None):
+    """FLOPs and bytes of one block (``tokens`` of the workload, default all of
+    them) and of its GEMM-1 launch."""
     import numpy as np
-    T, H, I, E, K = wl.tokens, wl.hidden, wl.intermediate, wl.experts, wl.top_k
+    T = wl.tokens if tokens is None else tokens
+    H, I, E, K = wl.hidden, wl.intermediate, wl.experts, wl.top_k
     R = T * K
     u = len(np.unique(idx_np)) if idx_np is not None else E
     return {
-        "block_flops": wl.flops,
+        "block_flops": wl.flops * T / wl.tokens,
         "gemm1_flops": 2.0 * R * H * 2 * I,
         "gemm2_flops": 2.0 * R * I * H,
         # bytes that must move at least once: touched expert weights + activations in/out
@@ -197,7 +200,7 @@ def algorithmic(wl, idx_np=None):
 
 
 def stage_events(torch):
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(13)]
     for e in evs:  # torch creates the CUDA event lazily, on its first record
         e.record()
     torch.cuda.synchronize()
@@ -215,7 +218,13 @@ def set_stage_events(evs):
     _lib.call("nkimoe_set_stage_events", arr, len(evs))
 
 
+# Stage events the library records (nkimoe_set_stage_events), in time order,
+# and the names of the intervals between consecutive ones.
+STAGE_ORDER = [0, 1, 2, 3, 4, 5, 6, 7]
 STAGES = ["router", "topk", "permute", "gather", "gemm1_swiglu", "gemm2_scale", "combine"]
+EP_STAGE_ORDER = [0, 1, 8, 9, 2, 3, 4, 5, 6, 10, 11, 12]
+EP_STAGES = ["router", "topk", "ep_send", "ep_wait", "permute", "gather", "gemm1_swiglu", "gemm2_scale",
+             "combine_return", "ep_return_wait", "ep_sum"]
 
 
 def cpu_oracle_tokens_per_s(inp_cpu, wl, sample_tokens, repeat=1):
@@ -343,22 +352,24 @@ def time_steps(torch, fn, steps, warmup, stream, world, evs=None, finish=None):
     return ms, stage_ms
 
 
-def measure_stages(torch, fn, steps, evs, graph_of=None):
+def measure_stages(torch, fn, steps, evs, graph_of=None, order=None):
     """Per-kernel durations from CUDA events that the library records between
-    its launches on the launching stream, averaged over `steps` steps.  With
-    `graph_of`, the step is captured into a CUDA graph together with its event
-    records and replayed, so the durations exclude CPU launch gaps."""
+    its launches on the launching stream, averaged over `steps` steps: the
+    intervals between consecutive events of `order`.  With `graph_of`, the
+    step is captured into a CUDA graph together with its event records and
+    replayed, so the durations exclude CPU launch gaps."""
+    order = order or STAGE_ORDER
     set_stage_events(evs)
     try:
         run = fn
         if graph_of is not None:
             run = graph_of(fn).replay
-        acc = [0.0] * len(STAGES)
+        acc = [0.0] * (len(order) - 1)
         for _ in range(steps):
             run()
             torch.cuda.synchronize()
-            for i in range(len(STAGES)):
-                acc[i] += evs[i].elapsed_time(evs[i + 1])
+            for i in range(len(order) - 1):
+                acc[i] += evs[order[i]].elapsed_time(evs[order[i + 1]])
     finally:
         set_stage_events(None)
     return [a / steps for a in acc]
@@ -399,6 +410,45 @@ def measure_stack(torch, world=1, rank=0):
             "data": "synthetic"}
 
 
+def ep_exchange_counts(torch, idx, world, rank, experts):
+    """(token, rank) rows and (token, slot) pairs between the ranks of an
+    expert-parallel step, from every rank's routing: rows[s][d] = tokens of
+    rank s with an expert on rank d (each sent once), pairs[s][d] = their
+    (token, slot) pairs."""
+    import torch.distributed as dist
+    el = experts // world
+    dr = idx.long() // el
+    hit = torch.zeros(idx.shape[0], world, dtype=torch.bool, device=idx.device)
+    hit.scatter_(1, dr, True)
+    mine = torch.stack([hit.sum(0), torch.bincount(dr.flatten(), minlength=world)]).to(torch.int64)
+    allv = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allv, mine)
+    m = torch.stack(allv).cpu()  # [src, 2, dst]
+    return m[:, 0, :], m[:, 1, :]
+
+
+def block_parity(torch, y, ref, idx=None, ref_idx=None, world=1):
+    """Normwise error and cosine of an output against the single-GPU block's
+    on the same tokens, and the tokens whose routing differs; max / min / sum
+    over the ranks."""
+    a, b = y.float(), ref.float()
+    err = ((a - b).abs().max() / b.abs().max().clamp_min(1e-30)).reshape(1)
+    cos = (torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)).reshape(1)
+    mis = torch.zeros(1, device=y.device)
+    if idx is not None and ref_idx is not None:
+        mis[0] = (idx != ref_idx).any(dim=1).sum().float()
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        cos = -cos
+        dist.all_reduce(cos, op=dist.ReduceOp.MAX)
+        cos = -cos
+        dist.all_reduce(mis, op=dist.ReduceOp.SUM)
+    return {"normwise_max": float(err), "cosine_min": float(cos),
+            "routing_mismatch_tokens": int(mis) if idx is not None else None,
+            "pass": bool(float(err) <= 2e-2 and float(cos) >= 0.999 and (idx is None or int(mis) == 0))}
+
+
 def run_b200(args):
     import numpy as np
     import torch
@@ -435,6 +485,7 @@ def run_b200(args):
     hbm_gbs, tf_burst, tf_sus, peak_src = peaks()
     sampler = ClockSampler(local)
     sampler.start()
+    ep_peer = world > 1 and args.ep == "peer"
 
     def setup(wl):
         inp = make_moe_inputs(wl, device="cuda")
@@ -466,136 +517,199 @@ def run_b200(args):
             fn()
         return g
 
+    def max_over_ranks(vals):
+        if world == 1:
+            return list(vals)
+        t = torch.tensor(list(vals), device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return t.tolist()
+
+    def gather_ranks(v):
+        if world == 1:
+            return [v]
+        t = torch.tensor([float(v)], device="cuda", dtype=torch.float64)
+        out = [torch.empty_like(t) for _ in range(world)]
+        torch.distributed.all_gather(out, t)
+        return [float(o) for o in out]
+
     result = {}
     workloads = [args.workload]
     if args.workload == "prefill" and world == 1 and not args.no_decode:
         workloads.append("decode")
+    if args.workload == "prefill" and not args.no_skewed:
+        workloads.append("skewed")
     wl_key = {"prefill": "c3", "decode": "c2", "skewed": "c4"}
     for which in workloads:
         wl = WORKLOADS[wl_key[which]]
         inp, moe, x = setup(wl)
+        T_local = x.shape[0]
+        pe = moe.packed()
+        rw, rb = moe.router.weight, moe.router_bias
+        stream = torch.cuda.current_stream()
+        # the single-GPU block on this rank's batch: routing (the algorithmic
+        # byte count) and, at N > 1, the parity reference of the EP output
+        y_one, idx_one, _ = ops.moe_block(x, rw, pe, wl.top_k, bias=rb, return_routing=True)
+        alg = algorithmic(wl, idx_one.cpu().numpy(), tokens=T_local)
         block = None
         if world > 1:
-            if args.ep == "peer":
+            if ep_peer:
                 from nki_moe_b200.ep_peer import PeerExpertParallelMoE
-                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=x.shape[0])
+                # epochs counted on the device: the step replays as a CUDA graph
+                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=T_local, device_epochs=True)
             else:
                 from nki_moe_b200.ep import ExpertParallelMoE
                 block = ExpertParallelMoE.from_dense(moe, torch.distributed.group.WORLD)
             fwd = lambda: block(x)  # noqa: E731
         else:
-            pe = moe.packed()
-            rw = moe.router.weight
-            rb = moe.router_bias
             fwd = lambda: ops.moe_block(x, rw, pe, wl.top_k, bias=rb)  # noqa: E731
-        stream = torch.cuda.current_stream()
-        # routing of this batch (for the algorithmic byte count) and warm-up
-        _, idx, _ = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k, bias=moe.router_bias,
-                                  return_routing=True)
-        alg = algorithmic(wl, idx.cpu().numpy())
-        if which == "skewed":
-            # hottest rank's (token, slot) rows against the mean: the imbalance
-            # that caps an expert-parallel step
-            ep = max(world, 1)
-            per_rank = np.bincount((idx.cpu().numpy().ravel() // (wl.experts // ep)), minlength=ep)
-            alg["rank_rows_max_over_mean"] = float(per_rank.max() / per_rank.mean())
         if args.profile_once:
             fwd()
             torch.cuda.synchronize()
             return
-        run = fwd
-        use_graph = world == 1
-        if use_graph:
-            g = graph_of(fwd)
-            run = g.replay
+        # the NCCL exchange synchronises with the host (split sizes): eager
+        use_graph = world == 1 or ep_peer
+        run = graph_of(fwd).replay if use_graph else fwd
         if which == workloads[0]:  # clocks over the headline measurement's timed region
             sampler.mark(True)
         ms, _ = time_steps(torch, run, args.steps, max(args.warmup, 3), stream, world)
         if which == workloads[0]:
             sampler.mark(False)
-        st = (measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch), graph_of)
-              if world == 1 else None)
-        # skewed: the workload's tokens are split over the ranks (strong scaling)
-        per_rank_share = 1.0 / world if which == "skewed" else 1.0
-        tokens_total = x.shape[0] * world
+        order, names = (EP_STAGE_ORDER, EP_STAGES) if ep_peer else (STAGE_ORDER, STAGES)
+        st = None
+        if world == 1 or ep_peer:
+            st = measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch),
+                                graph_of if use_graph else None, order)
+        tokens_total = T_local * world
         r = {"ms_per_step": ms, "tokens_per_s": tokens_total / (ms * 1e-3),
-             "block_tflops": alg["block_flops"] * per_rank_share * world / (ms * 1e-3) / 1e12,
-             "block_gbs": alg["block_bytes"] * per_rank_share * world / (ms * 1e-3) / 1e9, "alg": alg,
-             "stages_ms": None}
+             "block_tflops": alg["block_flops"] * world / (ms * 1e-3) / 1e12,
+             "block_gbs": alg["block_bytes"] * world / (ms * 1e-3) / 1e9, "alg": alg, "stages_ms": None}
+        i1, i2 = names.index("gemm1_swiglu"), names.index("gemm2_scale")
         if st is not None:
-            r["stages_ms"] = dict(zip(STAGES, [round(v, 4) for v in st]))
-            if which in ("prefill", "skewed"):
-                t = st[4] * 1e-3
-                r["roofline"] = {"bound": "tensor", "kernel": "grouped_gemm_rows (gate/up + SwiGLU)",
-                                 "achieved": alg["gemm1_flops"] / t / 1e12, "peak": tf_burst, "unit": "TFLOP/s",
-                                 "frac": alg["gemm1_flops"] / t / 1e12 / tf_burst,
-                                 "traffic": NCU_TRAFFIC_BYTES["prefill"],
-                                 "peak_source": f"{peak_src} bf16 burst"}
-                t2 = st[5] * 1e-3
-                r["roofline_gemm2"] = {"bound": "tensor", "achieved": alg["gemm2_flops"] / t2 / 1e12,
-                                       "frac": alg["gemm2_flops"] / t2 / 1e12 / tf_burst}
+            st_max = max_over_ranks(st)
+            r["stages_ms"] = dict(zip(names, [round(v, 4) for v in st_max]))
+            if world > 1:
+                r["stages_ms_note"] = "per stage, the maximum over ranks of the rank's mean over steps"
+        if world > 1:
+            rows, pairs = ep_exchange_counts(torch, idx_one, world, rank, wl.experts)
+            pairs_in = int(pairs[:, rank].sum())
+            rows_out_remote = int(rows[rank].sum() - rows[rank, rank])
+            rows_in_remote = int(rows[:, rank].sum() - rows[rank, rank])
+            r["alg"]["gemm1_flops"] = 2.0 * pairs_in * wl.hidden * 2 * wl.intermediate
+            r["alg"]["gemm2_flops"] = 2.0 * pairs_in * wl.intermediate * wl.hidden
+            r["rank_rows_max_over_mean"] = float(pairs.sum(0).max() / pairs.sum(0).float().mean())
+            if st is not None:
+                d_bytes = rows_out_remote * (2 * wl.hidden + 8 * wl.top_k)
+                r_bytes = rows_in_remote * 2 * wl.hidden
+                t_send, t_ret = st[names.index("ep_send")], st[names.index("combine_return")]
+                send_gbs = gather_ranks(d_bytes / (t_send * 1e-3) / 1e9)
+                ret_gbs = gather_ranks(r_bytes / (t_ret * 1e-3) / 1e9)
+                exposed = max_over_ranks([st[names.index("ep_send")] + st[names.index("ep_wait")] +
+                                          st[names.index("ep_return_wait")] + st[names.index("ep_sum")]])[0]
+                r["exchange"] = {
+                    "dispatch_bytes_out_rank0": d_bytes, "return_bytes_out_rank0": r_bytes,
+                    "send_gbs_min_over_ranks": min(send_gbs), "send_gbs_rank0": send_gbs[0],
+                    "return_gbs_min_over_ranks": min(ret_gbs), "return_gbs_rank0": ret_gbs[0],
+                    "nvlink_gbs_per_direction": 770.0,
+                    "exposed_ms_max_over_ranks": exposed,
+                    "note": "stores to peers over NVLink by the library's send and return-combine kernels; the "
+                            "send stage also holds the destination sort, the return stage the local rows' sums"}
+        if st is not None and which in ("prefill", "skewed"):
+            ach = gather_ranks(r["alg"]["gemm1_flops"] / (st[i1] * 1e-3) / 1e12)
+            r["roofline"] = {"bound": "tensor", "kernel": "grouped_gemm_rows (gate/up + SwiGLU)",
+                             "achieved": ach[0], "peak": tf_burst, "unit": "TFLOP/s", "frac": ach[0] / tf_burst,
+                             "traffic": NCU_TRAFFIC_BYTES["prefill"] if world == 1 else None,
+                             "peak_source": f"{peak_src} bf16 burst"}
+            if world > 1:
+                r["roofline"]["frac_min_over_ranks"] = min(ach) / tf_burst
+                r["roofline"]["note"] = "rank 0's GEMM-1 over the (token, slot) pairs it received, per-GPU peak"
+                step_flops = alg["block_flops"] * world
+                r["roofline_step"] = {"achieved": step_flops / (ms * 1e-3) / 1e12, "peak": tf_burst * world,
+                                      "frac": step_flops / (ms * 1e-3) / 1e12 / (tf_burst * world),
+                                      "unit": "TFLOP/s", "note": "whole step, all ranks, against N x per-GPU peak"}
+            a2 = gather_ranks(r["alg"]["gemm2_flops"] / (st[i2] * 1e-3) / 1e12)
+            r["roofline_gemm2"] = {"bound": "tensor", "achieved": a2[0], "frac": a2[0] / tf_burst}
+        elif st is not None:
+            t = st[i1] * 1e-3
+            r["roofline"] = {"bound": "hbm", "kernel": "grouped_gemm_weights (gate/up + SwiGLU)",
+                             "achieved": alg["gemm1_bytes"] / t / 1e9, "peak": hbm_gbs, "unit": "GB/s",
+                             "frac": alg["gemm1_bytes"] / t / 1e9 / hbm_gbs,
+                             "traffic": NCU_TRAFFIC_BYTES["decode"], "peak_source": f"{peak_src} HBM copy"}
+            blk = alg["block_bytes"] / (ms * 1e-3) / 1e9
+            r["roofline_block"] = {"bound": "hbm", "achieved": blk, "frac": blk / hbm_gbs, "unit": "GB/s"}
+        if which == "skewed" and world == 1:
+            per_rank = np.bincount(idx_one.cpu().numpy().ravel() // (wl.experts // 8), minlength=8)
+            r["rank_rows_max_over_mean_at_8"] = float(per_rank.max() / per_rank.mean())
+        # parity of the expert-parallel output against the single-GPU block on
+        # the same tokens (after the timed region; every rank takes part)
+        if world > 1:
+            if ep_peer:
+                y_ep, idx_ep, _ = block(x, return_routing=True)
             else:
-                t = st[4] * 1e-3
-                r["roofline"] = {"bound": "hbm", "kernel": "grouped_gemm_weights (gate/up + SwiGLU)",
-                                 "achieved": alg["gemm1_bytes"] / t / 1e9, "peak": hbm_gbs, "unit": "GB/s",
-                                 "frac": alg["gemm1_bytes"] / t / 1e9 / hbm_gbs,
-                                 "traffic": NCU_TRAFFIC_BYTES["decode"], "peak_source": f"{peak_src} HBM copy"}
-                blk = alg["block_bytes"] / (ms * 1e-3) / 1e9
-                r["roofline_block"] = {"bound": "hbm", "achieved": blk, "frac": blk / hbm_gbs, "unit": "GB/s"}
-        # e2e through the public module API with pinned host buffers
+                y_ep, idx_ep = block(x), None
+            r["parity"] = block_parity(torch, y_ep, y_one, idx_ep, idx_one if idx_ep is not None else None, world)
+            r["parity"].update(vs="single-GPU nkimoe_moe_block on each rank's own batch", tokens=tokens_total,
+                               bars="normwise <= 2e-2, cosine >= 0.999, no token routed differently")
+            del y_ep
+        # e2e through the public module API with pinned host buffers: successive
+        # batches, each call's copy in overlapping the previous call's block and
+        # its copy back the next call's block (two output buffers, one completion
+        # event each)
         if not args.no_e2e:
             xh = x.reshape(1, *x.shape).cpu().pin_memory()
             outh = torch.empty_like(xh).pin_memory()
-            # world 1: successive batches through the host-buffer block, each
-            # call's copy in overlapping the previous call's block and its copy
-            # back the next call's block (two output buffers, one completion
-            # event each)
             outs = [outh[0], torch.empty_like(outh[0]).pin_memory()]
             dones = [torch.cuda.Event(), torch.cuda.Event()]
             n_e2e = [0]
             # the packed experts and the router's bf16 planes are made once, as
             # a serving loop keeps them
-            e_rw = moe.router.weight
-            e_pe = moe.packed() if world == 1 else None
-            e_split = ops.router_split(e_rw) if world == 1 else None
+            e_split = ops.router_split(rw) if world == 1 else None
 
             def e2e_step():
+                i = n_e2e[0] % 2
+                n_e2e[0] += 1
                 if world == 1:
-                    i = n_e2e[0] % 2
-                    n_e2e[0] += 1
-                    ops.moe_block_host(xh[0], e_rw, e_pe, wl.top_k, bias=moe.router_bias, out=outs[i],
+                    ops.moe_block_host(xh[0], rw, pe, wl.top_k, bias=rb, out=outs[i],
                                        chunk_tokens=E2E_CHUNK_TOKENS, router_w_split=e_split, done=dones[i])
-                    return
-                xd = xh.to("cuda", non_blocking=True)
-                outh.copy_(block(xd[0]).unsqueeze(0), non_blocking=True)
+                elif ep_peer:
+                    block.forward_host(xh[0], out=outs[i], done=dones[i])
+                else:
+                    xd = xh.to("cuda", non_blocking=True)
+                    outs[i].copy_(block(xd[0]), non_blocking=True)
+                    dones[i].record(stream)
 
-            def e2e_finish():
-                if world == 1:  # the timed region ends with the last copy back
-                    stream.wait_event(dones[(n_e2e[0] - 1) % 2])
+            def e2e_finish():  # the timed region ends with the last copy back
+                stream.wait_event(dones[(n_e2e[0] - 1) % 2])
 
             e_ms, _ = time_steps(torch, e2e_step, args.steps, max(args.warmup, 3), stream, world,
                                  finish=e2e_finish)
             r["e2e"] = {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
-                        "h2d_bytes_per_step": xh.numel() * xh.element_size(),
-                        "d2h_bytes_per_step": outh.numel() * outh.element_size(),
-                        "path": ("ops.moe_block_host on page-locked host batches (nkimoe_moe_block_host): each "
-                                 "batch copied in, through the block and copied back, a batch's copies overlapping "
-                                 "its neighbours' blocks" if world == 1 else
-                                 "copy to the GPU, expert-parallel block, copy back")}
-        if not args.no_cpu_baseline and rank == 0 and world == 1:
-            # the whole batch of the workload, repeated to about 10 s of CPU work
-            sample = wl.tokens
+                        "h2d_bytes_per_step": xh.numel() * xh.element_size() * world,
+                        "d2h_bytes_per_step": outh.numel() * outh.element_size() * world,
+                        "path": ("ops.moe_block_host (nkimoe_moe_block_host)" if world == 1 else
+                                 "PeerExpertParallelMoE.forward_host" if ep_peer else
+                                 "copy in, ExpertParallelMoE, copy back") +
+                                " on page-locked host batches: each batch copied in, through the block and copied "
+                                "back, a batch's copies overlapping its neighbours' blocks"}
+        if not args.no_cpu_baseline and rank == 0:
+            # the oracle on this rank's whole batch, repeated to about 10 s of
+            # CPU work (3 s for the sub-workloads), on every host core
+            pin_cpu_threads()
             cin = cpu_inputs(inp, torch)
-            _, one = cpu_oracle_tokens_per_s(cin, wl, sample)
-            rep = max(1, min(int(10.0 / max(one, 1e-3)) + 1, int(30.0 / max(one, 1e-3))))
-            tps, dt = cpu_oracle_tokens_per_s(cin, wl, sample, repeat=rep)
+            cin["x"] = x.float().cpu().numpy()
+            target = 10.0 if which == workloads[0] else 3.0
+            _, one = cpu_oracle_tokens_per_s(cin, wl, T_local)
+            rep = max(1, min(int(target / max(one, 1e-3)) + 1, int(30.0 / max(one, 1e-3))))
+            tps, dt = cpu_oracle_tokens_per_s(cin, wl, T_local, repeat=rep)
             r["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
-                                 "sample": f"the {sample}-token {wl.name} batch x {rep} (numpy oracle, fp32), "
+                                 "sample": f"the {T_local}-token {wl.name} batch"
+                                           f"{' of rank 0' if world > 1 else ''} x {rep} (numpy oracle, fp32), "
                                            f"{dt * rep:.1f} s"}
+        if world > 1:
+            torch.distributed.barrier()
         result[which] = r
         if block is not None and hasattr(block, "close"):
             block.close()
-        del moe, inp, x, block
+        del moe, inp, x, block, y_one, idx_one
         torch.cuda.empty_cache()
 
     sampler.stop()
@@ -603,11 +717,13 @@ def run_b200(args):
     main_key = workloads[0]
     m = result[main_key]
     wl = WORKLOADS[wl_key[main_key]]
-    # this library's kernels per step: single GPU 9 (router, top-k, 3 permutation,
-    # gather, 2 GEMMs, combine); EP over peer memory 18 (+ rank sort, send,
-    # 2 waits, mask, receiver permutation, final sum); EP over NCCL 17 of ours
-    # (NCCL's own kernels not counted)
-    launches_per_step = 9 if world == 1 else (18 if args.ep == "peer" else 17)
+    # this library's kernels per step: single GPU 9 (router GEMM, top-k, 3
+    # permutation, gather, 2 GEMMs, combine); EP over peer memory 19 (+ epoch,
+    # destinations, 3 rank-sort, send, 2 waits, mask, final sum); EP over NCCL
+    # 17 of ours (NCCL's own kernels not counted)
+    launches_per_step = 9 if world == 1 else (19 if ep_peer else 17)
+    timing = ("CUDA graph replay, CUDA events" + (", max over ranks" if world > 1 else "")) if (world == 1 or ep_peer) \
+        else "eager, CUDA events, max over ranks"
     line = {
         "metric": "moe_block_tokens_per_s", "value": m["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": m["ms_per_step"],
@@ -619,7 +735,7 @@ def run_b200(args):
                    "top_k": wl.top_k, "intermediate": wl.intermediate,
                    "parallelism": f"ep{world}-{args.ep}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.21 GB of expert weights read per step)",
-                   "timing": "CUDA graph replay, CUDA events" if world == 1 else "eager, CUDA events, max over ranks"},
+                   "timing": timing},
         "roofline": m.get("roofline"),
         "cpu_baseline": m.get("cpu_baseline"),
         "e2e": m.get("e2e"),
@@ -628,10 +744,11 @@ def run_b200(args):
         "block_tflops": m["block_tflops"],
         "stages_ms": m["stages_ms"],
     }
-    if "roofline_gemm2" in m:
-        line["roofline_gemm2"] = m["roofline_gemm2"]
-    if main_key == "skewed":
-        line["rank_rows_max_over_mean"] = m["alg"]["rank_rows_max_over_mean"]
+    for k in ("roofline_gemm2", "roofline_step", "exchange", "parity", "stages_ms_note"):
+        if k in m:
+            line[k] = m[k]
+    if "rank_rows_max_over_mean" in m:
+        line["rank_rows_max_over_mean"] = m["rank_rows_max_over_mean"]
     if "decode" in result and main_key != "decode":
         d = result["decode"]
         line["decode"] = {"workload": WORKLOADS["c2"].name, "tokens_per_s": d["tokens_per_s"],
@@ -639,6 +756,17 @@ def run_b200(args):
                           "roofline_block": d.get("roofline_block"), "stages_ms": d["stages_ms"],
                           "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline"),
                           "unique_experts": d["alg"]["unique_experts"]}
+    if "skewed" in result and main_key != "skewed":
+        d = result["skewed"]
+        line["skewed"] = {"workload": WORKLOADS["c4"].name, "tokens_total": WORKLOADS["c4"].tokens,
+                          "tokens_per_gpu": WORKLOADS["c4"].tokens // world, "scaling": "strong",
+                          "tokens_per_s": d["tokens_per_s"], "ms_per_step": d["ms_per_step"],
+                          "block_tflops": d["block_tflops"],
+                          "frac_of_n_x_peak": d["block_tflops"] / (tf_burst * world),
+                          "rank_rows_max_over_mean": d.get("rank_rows_max_over_mean",
+                                                           d.get("rank_rows_max_over_mean_at_8")),
+                          "roofline": d.get("roofline"), "stages_ms": d["stages_ms"], "parity": d.get("parity"),
+                          "exchange": d.get("exchange"), "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline")}
     if not args.no_stack and (world == 1 or 8 % world == 0):
         line["stack"] = measure_stack(torch, world, rank)
     if rank == 0:

@@ -76,7 +76,7 @@ class PeerExpertParallelMoE(nn.Module):
         self.bases = self._setup_buffers()
 
     @classmethod
-    def from_dense(cls, moe, max_tokens: int, group=None):
+    def from_dense(cls, moe, max_tokens: int, group=None, device_epochs: bool = False):
         """Slice this rank's experts out of an ``NKIMoESimple`` holding all of them."""
         distributed = dist.is_available() and dist.is_initialized()
         g = (group if group is not None else dist.group.WORLD) if distributed else None
@@ -86,7 +86,7 @@ class PeerExpertParallelMoE(nn.Module):
         lo, hi = rank * el, (rank + 1) * el
         return cls(moe.router.weight, moe.gate_up_proj.detach()[lo:hi].contiguous(),
                    moe.down_proj.detach()[lo:hi].contiguous(), moe.num_experts, moe.top_k, max_tokens, group=g,
-                   router_bias=moe.router_bias)
+                   router_bias=moe.router_bias, device_epochs=device_epochs)
 
     def packed(self):
         if self._packed is not None:
@@ -146,6 +146,71 @@ class PeerExpertParallelMoE(nn.Module):
         if ops.sync_check_enabled():
             ops.read_status(ws)
         return (out, idx, w) if return_routing else out
+
+    def forward_host(self, x: torch.Tensor, out: torch.Tensor | None = None,
+                     done: torch.cuda.Event | None = None) -> torch.Tensor:
+        """The block on a HOST batch ``x [T, H]`` (bf16, page-locked for the
+        copies to overlap), the result returned into ``out`` (a new page-locked
+        host tensor when None).  The copies run on two side streams of this
+        module (one per direction) and use two device staging slots in turn,
+        so a call's copy in overlaps the previous call's block and, with
+        ``done``, its copy back overlaps the next call's block.
+
+        ``done`` None: the current stream waits for the copy back.  ``done``
+        an event: recorded when the copy back has completed; the current
+        stream goes on without waiting, and ``out`` is ready after
+        ``done.synchronize()`` (until then ``x`` and ``out`` must stay alive and
+        untouched).  As with :meth:`forward`, every rank makes the call once per
+        step.  The reference runs its block on host tensors in its module test
+        (test_nki_moe.py:146-151)."""
+        if x.is_cuda:
+            raise ValueError("x must be a host tensor (forward takes device tensors)")
+        x = ops._contig(x, torch.bfloat16)
+        T, H = x.shape
+        if T > self.max_tokens or H != self.hidden:
+            raise ValueError(f"x [{T}, {H}] does not fit max_tokens {self.max_tokens} / hidden {self.hidden}")
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.bfloat16, pin_memory=True)
+        elif out.is_cuda or out.dtype != torch.bfloat16 or tuple(out.shape) != (T, H) or not out.is_contiguous():
+            raise ValueError("out must be a contiguous bf16 host tensor shaped like x")
+        with torch.cuda.device(self.device):
+            st = self._host_state()
+            k = st["calls"] & 1
+            st["calls"] += 1
+            main = torch.cuda.current_stream(self.device)
+            xd, yd = st["x"][k][:T], st["y"][k][:T]
+            # copy in: after the block that last read this slot's rows
+            st["in"].wait_event(st["x_free"][k])
+            with torch.cuda.stream(st["in"]):
+                xd.copy_(x, non_blocking=True)
+                st["in_done"][k].record(st["in"])
+            # block: after its rows arrived and this slot's last copy back
+            main.wait_event(st["in_done"][k])
+            main.wait_event(st["out_free"][k])
+            self.forward(xd, out=yd)
+            st["x_free"][k].record(main)
+            # copy back, after the block
+            st["out"].wait_event(st["x_free"][k])
+            with torch.cuda.stream(st["out"]):
+                out.copy_(yd, non_blocking=True)
+                st["out_free"][k].record(st["out"])
+            if done is not None:
+                done.record(st["out"])
+            else:
+                main.wait_event(st["out_free"][k])
+        return out
+
+    def _host_state(self):
+        st = getattr(self, "_host", None)
+        if st is None:
+            Tm, H = self.max_tokens, self.hidden
+            st = {"calls": 0, "in": torch.cuda.Stream(self.device), "out": torch.cuda.Stream(self.device),
+                  "x": [torch.empty(Tm, H, dtype=torch.bfloat16, device=self.device) for _ in range(2)],
+                  "y": [torch.empty(Tm, H, dtype=torch.bfloat16, device=self.device) for _ in range(2)],
+                  "x_free": [torch.cuda.Event() for _ in range(2)], "out_free": [torch.cuda.Event() for _ in range(2)],
+                  "in_done": [torch.cuda.Event() for _ in range(2)]}
+            self._host = st
+        return st
 
     def close(self):
         """Unmap the peers' buffers and free this rank's (after every rank is

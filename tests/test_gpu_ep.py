@@ -276,3 +276,39 @@ def test_peer_wait_runs_out_when_a_peer_never_joins():
         assert torch.equal(y, ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k))
     finally:
         peer.close()
+
+
+def test_peer_ep_host_batches_equal_device_batches():
+    """The expert-parallel block on host batches (two staging slots, copies on
+    side streams, completion events so that neighbouring calls overlap) equals
+    the device call on the same batch bit for bit, over calls of changing
+    size."""
+    from nki_moe_b200.ep_peer import PeerExpertParallelMoE
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+
+    wl = WORKLOADS["c3"]
+    inp = make_moe_inputs(wl, device="cuda", tokens=1024)
+    moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        moe.router.weight.copy_(inp["router"])
+        moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
+        moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+    peer = PeerExpertParallelMoE.from_dense(moe, max_tokens=1024)
+    g = torch.Generator().manual_seed(31)
+    sizes = (1024, 700, 1024, 300)
+    xs = [torch.randn(T, wl.hidden, generator=g).bfloat16().pin_memory() for T in sizes]
+    outs = [torch.empty(T, wl.hidden, dtype=torch.bfloat16).pin_memory() for T in sizes]
+    dones = [torch.cuda.Event() for _ in sizes]
+    old = os.environ.get("NKIMOE_SYNC_CHECK")
+    os.environ["NKIMOE_SYNC_CHECK"] = "0"
+    try:
+        for x, o, d in zip(xs, outs, dones):
+            peer.forward_host(x, out=o, done=d)
+        for x, o, d in zip(xs, outs, dones):
+            d.synchronize()
+            ref = peer(x.cuda()).cpu()
+            assert torch.equal(o.view(torch.int16), ref.view(torch.int16)), f"{x.shape[0]} tokens"
+        assert ops.read_status(ops.workspace(torch.device("cuda", 0), 1)) == 0
+    finally:
+        os.environ["NKIMOE_SYNC_CHECK"] = old if old is not None else "1"
+        peer.close()

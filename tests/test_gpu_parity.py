@@ -565,6 +565,65 @@ def test_moe_block_host_overlapped_calls(c1_inputs, chunk):
         assert torch.equal(o.view(torch.int16), ref.view(torch.int16))
 
 
+def test_moe_block_host_overlapped_calls_of_changing_size(c1_inputs):
+    """Successive host-buffer calls with completion events whose batch size
+    changes from call to call (2048, 1000, 2048, 600, 2048 tokens) on one
+    workspace: the staging rows' place follows the batch size, so a call
+    after a change must not overwrite rows an earlier call's block or copy back
+    still uses.  Every output equals the device block's bit for bit."""
+    g = torch.Generator().manual_seed(97)
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    sizes = (2048, 1000, 2048, 600, 2048)
+    xs = [torch.randn(T, 2048, generator=g).bfloat16().pin_memory() for T in sizes]
+    outs = [torch.empty(T, 2048, dtype=torch.bfloat16).pin_memory() for T in sizes]
+    dones = [torch.cuda.Event() for _ in sizes]
+    os.environ["NKIMOE_SYNC_CHECK"] = "0"  # no synchronisation inside the calls
+    try:
+        for x, o, d in zip(xs, outs, dones):
+            ops.moe_block_host(x, rw, pe, 8, out=o, done=d)
+    finally:
+        os.environ["NKIMOE_SYNC_CHECK"] = "1"
+    for x, o, d in zip(xs, outs, dones):
+        d.synchronize()
+        ref = ops.moe_block(x.cuda(), rw, pe, 8).cpu()
+        assert torch.equal(o.view(torch.int16), ref.view(torch.int16)), f"{x.shape[0]} tokens"
+
+
+def test_workspace_captured_by_a_graph_survives_a_larger_call(c1_inputs):
+    """A CUDA graph that captured the block keeps its workspace alive after a
+    later, larger call on the same stream replaced it: replaying the graph
+    still gives the eager result."""
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    g = torch.Generator().manual_seed(98)
+    x = torch.randn(64, 2048, generator=g).bfloat16().cuda()
+    big = torch.randn(4096, 2048, generator=g).bfloat16().cuda()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    os.environ["NKIMOE_SYNC_CHECK"] = "0"
+    try:
+        with torch.cuda.stream(s):
+            ops.release_captured_workspaces()
+            ops._ws.pop((x.device.index, s.cuda_stream), None)  # start this stream small
+            ops.moe_block(x, rw, pe, 8)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                y = ops.moe_block(x, rw, pe, 8)
+            ops.moe_block(big, rw, pe, 8)  # grows (replaces) this stream's workspace
+            assert len(ops._ws_retired) >= 1
+            torch.cuda.synchronize()
+            y.zero_()
+            graph.replay()
+        torch.cuda.synchronize()
+    finally:
+        os.environ["NKIMOE_SYNC_CHECK"] = "1"
+    ref = ops.moe_block(x, rw, pe, 8)
+    assert torch.equal(y, ref)
+    del graph
+    ops.release_captured_workspaces()
+
+
 def test_module_on_host_batch_equals_device_batch(c1_inputs):
     """NKIMoESimple called on a host tensor (as the reference's module test
     calls it) runs on the weights' GPU and returns the device call's result on
