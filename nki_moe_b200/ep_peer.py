@@ -147,6 +147,21 @@ class PeerExpertParallelMoE(nn.Module):
             ops.read_status(ws)
         return (out, idx, w) if return_routing else out
 
+    def resync(self):
+        """After a step that failed on some ranks (a rank that left a step, a
+        wait that ran out), bring the ranks' step counters together again: every
+        rank calls this between steps, with none of its exchange kernels in
+        flight, and the next step runs with a fresh epoch on all of them.  Flags
+        a failed step left in the buffers hold older epochs, so they are not
+        taken for the next step's.  Host-counted epochs only."""
+        if self.device_epochs:
+            raise RuntimeError("resync needs host-counted epochs (device_epochs=False)")
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            t = torch.tensor([self.epoch], dtype=torch.int64, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            self.epoch = int(t.item())
+
     def forward_host(self, x: torch.Tensor, out: torch.Tensor | None = None,
                      done: torch.cuda.Event | None = None) -> torch.Tensor:
         """The block on a HOST batch ``x [T, H]`` (bf16, page-locked for the

@@ -182,6 +182,27 @@ def _ep_worker(rank, world, port, out_dir):
     assert ops.read_status(ops.workspace(x.device, 1)) == 0  # no bounded wait ran out
     y_dedup2 = ExpertParallelMoE.from_dense(moe, dedup=True)(x2)
     torch.cuda.synchronize()
+    # rank 1 leaves a step (host side, between steps): rank 0's waits run out
+    # after a short budget and its step raises; after a resync both ranks'
+    # next step is correct again
+    timed_out = 0
+    if rank == 0:
+        _lib.set_option("peer_wait_cycles", 4_000_000)
+        try:
+            peer(x)
+            ops.read_status(ops.workspace(x.device, 1))
+        except _lib.NKIMoEError as e:
+            timed_out = int(e.code == _lib.ERR_DEVICE and "0x1" in str(e))
+        finally:
+            _lib.set_option("peer_wait_cycles", 20_000_000_000)
+    torch.cuda.synchronize()
+    dist.barrier()
+    peer.resync()
+    y_peer3 = peer(x2)
+    assert ops.read_status(ops.workspace(x.device, 1)) == 0
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"peer3_{rank}.npy"), y_peer3.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"timeout{rank}.npy"), np.array([timed_out]))
     peer.close()
     np.save(os.path.join(out_dir, f"peer{rank}.npy"), y_peer1.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"peer2_{rank}.npy"), y_peer2.float().cpu().numpy())
@@ -213,6 +234,9 @@ def test_expert_parallel_two_gpus_matches_single_gpu(tmp_path):
         # exchange computes (same rows, same order, same sums)
         assert np.array_equal(np.load(tmp_path / f"peer{r}.npy"), d), f"rank {r}: peer != dedup"
         assert np.array_equal(np.load(tmp_path / f"peer2_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
+        # after rank 1 left a step and the ranks resynchronised
+        assert np.array_equal(np.load(tmp_path / f"peer3_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
+    assert int(np.load(tmp_path / "timeout0.npy")[0]) == 1  # rank 0's step raised the wait timeout
 
 
 def test_peer_wait_runs_out_when_a_peer_never_joins():
