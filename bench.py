@@ -69,6 +69,9 @@ def parse():
     ap.add_argument("--stack-profile-layers", type=int, default=0,
                     help="with --profile-once: build a decoder stack of this many layers, prefill batch 8 x 512 "
                          "and run one eager decode step inside the NVTX range 'decode_step' (for ncu launch lists)")
+    ap.add_argument("--ep-overlap", type=int, default=1, choices=[0, 1],
+                    help="N > 1, peer exchange: 1 overlapped schedule (default), 0 one block after all rows arrived")
+    ap.add_argument("--ep-groups", type=int, default=0, help="N > 1, overlapped schedule: remote region groups (0 auto)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: exchange over peer memory (library kernels) or NCCL all-to-all")
     return ap.parse_args()
@@ -222,9 +225,12 @@ def set_stage_events(evs):
 # and the names of the intervals between consecutive ones.
 STAGE_ORDER = [0, 1, 2, 3, 4, 5, 6, 7]
 STAGES = ["router", "topk", "permute", "gather", "gemm1_swiglu", "gemm2_scale", "combine"]
-EP_STAGE_ORDER = [0, 1, 8, 9, 2, 3, 4, 5, 6, 10, 11, 12]
-EP_STAGES = ["router", "topk", "ep_send", "ep_wait", "permute", "gather", "gemm1_swiglu", "gemm2_scale",
-             "combine_return", "ep_return_wait", "ep_sum"]
+EP_STAGE_ORDER = [0, 1, 8, 9, 2, 3, 4, 5, 6, 10, 11, 12]  # one-block schedule (option ep_overlap 0)
+EP_STAGES = ["router", "topk_and_rank_sort", "ep_send", "ep_wait", "permute", "gather", "gemm1_swiglu",
+             "gemm2_scale", "combine_return", "ep_return_wait", "ep_sum"]
+EPO_STAGE_ORDER = [0, 1, 2, 8, 9, 10, 11, 12]  # overlapped schedule (the default)
+EPO_STAGES = ["router", "topk", "rank_sort", "own_tokens_first_half", "remote_groups",
+              "own_tokens_second_half_and_return_wait", "ep_sum"]
 
 
 def cpu_oracle_tokens_per_s(inp_cpu, wl, sample_tokens, repeat=1):
@@ -466,6 +472,8 @@ def run_b200(args):
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     _lib.load()
+    _lib.set_option("ep_overlap", args.ep_overlap)
+    _lib.set_option("ep_groups", args.ep_groups)
     if args.profile_once and args.stack_profile_layers > 0:
         from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
 
@@ -575,10 +583,21 @@ def run_b200(args):
         if which == workloads[0]:
             sampler.mark(False)
         order, names = (EP_STAGE_ORDER, EP_STAGES) if ep_peer else (STAGE_ORDER, STAGES)
-        st = None
-        if world == 1 or ep_peer:
-            st = measure_stages(torch, fwd, max(5, min(args.steps, 20)), stage_events(torch),
-                                graph_of if use_graph else None, order)
+        st = st_o = None
+        n_stage_steps = max(5, min(args.steps, 20))
+        if ep_peer:
+            # the timed (overlapped) schedule's stages; then the one-block
+            # schedule, whose stages isolate each kernel (GEMM-1 roofline,
+            # exchange rates) -- every rank takes the same steps
+            if args.ep_overlap:
+                st_o = measure_stages(torch, fwd, n_stage_steps, stage_events(torch), graph_of, EPO_STAGE_ORDER)
+            _lib.set_option("ep_overlap", 0)
+            try:
+                st = measure_stages(torch, fwd, n_stage_steps, stage_events(torch), graph_of, order)
+            finally:
+                _lib.set_option("ep_overlap", args.ep_overlap)
+        elif world == 1:
+            st = measure_stages(torch, fwd, n_stage_steps, stage_events(torch), graph_of if use_graph else None, order)
         tokens_total = T_local * world
         r = {"ms_per_step": ms, "tokens_per_s": tokens_total / (ms * 1e-3),
              "block_tflops": alg["block_flops"] * world / (ms * 1e-3) / 1e12,
@@ -589,6 +608,13 @@ def run_b200(args):
             r["stages_ms"] = dict(zip(names, [round(v, 4) for v in st_max]))
             if world > 1:
                 r["stages_ms_note"] = "per stage, the maximum over ranks of the rank's mean over steps"
+        if st_o is not None:
+            r["stages_ms_one_block"] = r["stages_ms"]
+            r["stages_ms"] = dict(zip(EPO_STAGES, [round(v, 4) for v in max_over_ranks(st_o)]))
+            r["stages_ms_note"] = ("per stage, the maximum over ranks of the rank's mean over steps; stages_ms: the "
+                                   "timed overlapped schedule (sends and returns on a side stream beside the expert "
+                                   "GEMMs); stages_ms_one_block: the one-block schedule, whose stages isolate the "
+                                   "kernels (the roofline and exchange figures come from it)")
         if world > 1:
             rows, pairs = ep_exchange_counts(torch, idx_one, world, rank, wl.experts)
             pairs_in = int(pairs[:, rank].sum())
@@ -611,8 +637,9 @@ def run_b200(args):
                     "return_gbs_min_over_ranks": min(ret_gbs), "return_gbs_rank0": ret_gbs[0],
                     "nvlink_gbs_per_direction": 770.0,
                     "exposed_ms_max_over_ranks": exposed,
-                    "note": "stores to peers over NVLink by the library's send and return-combine kernels; the "
-                            "send stage also holds the destination sort, the return stage the local rows' sums"}
+                        "note": "stores to peers over NVLink by the library's send and return-combine kernels, timed "
+                            "in the one-block schedule (exposed_ms: its send, waits and final sum); the return stage "
+                            "also holds the local rows' sums"}
         if st is not None and which in ("prefill", "skewed"):
             ach = gather_ranks(r["alg"]["gemm1_flops"] / (st[i1] * 1e-3) / 1e12)
             r["roofline"] = {"bound": "tensor", "kernel": "grouped_gemm_rows (gate/up + SwiGLU)",
@@ -733,7 +760,8 @@ def run_b200(args):
                    "tokens_per_gpu": wl.tokens // world if main_key == "skewed" else wl.tokens,
                    "hidden": wl.hidden, "experts": wl.experts,
                    "top_k": wl.top_k, "intermediate": wl.intermediate,
-                   "parallelism": f"ep{world}-{args.ep}" if world > 1 else "single",
+                   "parallelism": (f"ep{world}-{args.ep}" + ("-overlapped" if ep_peer and args.ep_overlap else ""))
+                   if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.21 GB of expert weights read per step)",
                    "timing": timing},
         "roofline": m.get("roofline"),
@@ -744,7 +772,7 @@ def run_b200(args):
         "block_tflops": m["block_tflops"],
         "stages_ms": m["stages_ms"],
     }
-    for k in ("roofline_gemm2", "roofline_step", "exchange", "parity", "stages_ms_note"):
+    for k in ("roofline_gemm2", "roofline_step", "exchange", "parity", "stages_ms_note", "stages_ms_one_block"):
         if k in m:
             line[k] = m[k]
     if "rank_rows_max_over_mean" in m:
@@ -765,7 +793,8 @@ def run_b200(args):
                           "frac_of_n_x_peak": d["block_tflops"] / (tf_burst * world),
                           "rank_rows_max_over_mean": d.get("rank_rows_max_over_mean",
                                                            d.get("rank_rows_max_over_mean_at_8")),
-                          "roofline": d.get("roofline"), "stages_ms": d["stages_ms"], "parity": d.get("parity"),
+                          "roofline": d.get("roofline"), "stages_ms": d["stages_ms"],
+                          "stages_ms_one_block": d.get("stages_ms_one_block"), "parity": d.get("parity"),
                           "exchange": d.get("exchange"), "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline")}
     if not args.no_stack and (world == 1 or 8 % world == 0):
         line["stack"] = measure_stack(torch, world, rank)

@@ -75,7 +75,13 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * programmatic dependent launch, so a kernel's launch and prologue overlap
  * the previous kernel in the stream; 0 = plain launches),
  * "peer_wait_cycles" (budget of each expert-parallel wait for the peers, in
- * SM clock cycles, 1000 to 1e12; default 2e10, about 10 s).
+ * SM clock cycles, 1000 to 1e12; default 2e10, about 10 s),
+ * "ep_overlap" (1, the default: nkimoe_ep_peer_forward sends, computes and
+ * returns in an overlapped schedule; 0: one expert block after every row has
+ * arrived), "ep_groups" (remote regions taken in this many groups by the
+ * overlapped schedule, 1 to 7; 0 = auto, min(ranks - 1, 3)),
+ * "ep_side_ctas" (grid bound of the send and return kernels that run beside
+ * the expert GEMMs; 0 = the SM count).
  * No reference counterpart (NKI tile sizes are compile-time constants,
  * nki_moe_expert.py:545-556).  Returns NKIMOE_OK or
  * NKIMOE_ERR_INVALID_ARG for an unknown name/value. */
@@ -84,11 +90,14 @@ NKIMOE_API int nkimoe_set_option(const char* name, long long value);
 /* Profiling hook: `events` is an array of `count` (<= 13) cudaEvent_t that
  * the calling thread's later block calls record on their stream at the start
  * of each stage: 0 router, 1 top-k, 2 permute, 3 gather, 4 GEMM-1 (SwiGLU),
- * 5 GEMM-2 (routing weight), 6 combine, 7 end; the expert-parallel block
- * (nkimoe_ep_peer_forward) also records 8 send (destinations, sort, stores
- * to the owners) after 1, 9 wait for the senders (+ mask) before 2, and
- * after 7 (the receiver's block and the return of its sums): 10 wait for the
- * partial sums, 11 their sum, 12 end.  count = 0 turns it off.
+ * 5 GEMM-2 (routing weight), 6 combine, 7 end.  The expert-parallel block
+ * (nkimoe_ep_peer_forward) records 0 and 1, then 2 at the (token, rank)
+ * sort and 8 once the sends are issued; one-block schedule ("ep_overlap" 0):
+ * 9 wait for the senders, 2-7 of the receiver's block (7 after the return
+ * of its sums), 10 wait for the partial sums, 11 their sum, 12 end;
+ * overlapped schedule: 9 after the own tokens' first half of the experts,
+ * 10 after the remote groups, 11 after the second half, the returns and the
+ * wait for the partial sums, 12 end.  count = 0 turns it off.
  * No reference counterpart (the reference times whole graphs, main.py:258-277). */
 NKIMOE_API int nkimoe_set_stage_events(void* const* events, int count);
 
@@ -414,7 +423,15 @@ NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I
  * rank calls this once per step with the same epoch, increasing between
  * steps; epoch 0 lets each rank's buffer count the steps on the device (its
  * own counter + 1 per call), so that a step captured in a CUDA graph can be
- * replayed -- a caller uses one mode for the buffer's lifetime.  A peer that
+ * replayed -- a caller uses one mode for the buffer's lifetime.  The default
+ * overlapped schedule (option "ep_overlap") issues the sends, one
+ * destination after another nearest first, on a side stream of the library
+ * while this rank's experts run over its own tokens; it takes the remote rows
+ * in groups as they arrive and returns each group's sums from the side
+ * stream while the next group computes; the call's work on the side stream
+ * is joined back into `stream` before the final sum (capturable; the first
+ * call on a device creates the side stream and should come before any
+ * capture).  Calls on one device share the side stream.  A peer that
  * never arrives sets NKIMOE_DEV_TIMEOUT in the status word
  * (nkimoe_read_status) after a bounded wait (~10 s; option
  * "peer_wait_cycles").  topk_idx_out / topk_w_out (device, [T, K], may be

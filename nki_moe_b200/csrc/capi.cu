@@ -72,6 +72,12 @@ std::atomic<int> g_pdl{1};           // programmatic dependent launch of the dec
 // 2 GHz by default): a peer that has not reached the step by then is reported
 // as a timeout in the status word.
 std::atomic<long long> g_peer_wait_cycles{20000000000LL};
+// Expert-parallel schedule: 1 overlapped (the default), 0 one block after all
+// rows arrived; groups of remote regions (0 auto); the grid bound of the send
+// and return kernels that run beside the expert GEMMs (0: the SM count).
+std::atomic<int> g_ep_overlap{1};
+std::atomic<int> g_ep_groups{0};
+std::atomic<int> g_ep_side_ctas{0};
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
@@ -146,13 +152,14 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
              const int32_t* row_slot, const int32_t* out_row_map, const float* col_bias, int* status,
              cudaStream_t s, long long kd_act = 0, bool shared_a = false, const float* row_weight = nullptr,
              long long weight_experts = 0, int weight_mod = 0, const int32_t* a_row_map = nullptr,
-             long long problem_rows = 0) {
+             long long problem_rows = 0, long long choose_rows = 0, long long choose_experts = 0) {
   if (act_rows == 0) return NKIMOE_OK;
   if (kd_act == 0) kd_act = kd;
   // with shared activation rows every expert has act_rows rows; with gathered
   // rows the problem has problem_rows rows taken from the act_rows of `act`
   const long long rows_total = a_row_map ? problem_rows : (shared_a ? act_rows * E : act_rows);
-  int variant = choose_variant(rows_total, E, N);
+  // a GEMM over part of a routing's experts takes the schedule of the whole
+  int variant = choose_variant(choose_rows ? choose_rows : rows_total, choose_experts ? choose_experts : E, N);
   // the SM-pair kernels load A by TMA tiles only; the tokens kernel has no fp32 epilogue
   if ((variant == kRows2BN256 || variant == kTokens2) && (a_row_map || epilogue == kEpiStoreF32))
     variant = kRowsBN256;
@@ -269,6 +276,8 @@ struct PeerCombine {
   EpPeerPtrs peers;
   EpPeerLayout L;
   int P, me, Tm;
+  int q0, nq;      // the rows are those of regions q0 .. q0 + nq - 1
+  int max_ctas;    // grid bound of the return kernel (0: none)
   unsigned* counter;
   const uint32_t* epoch_p;
 };
@@ -284,49 +293,89 @@ struct FusedNorm {
   void* out;
 };
 
-int experts_impl(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype, const float* topk_w,
-                 void* out, long long T, long long H, long long I, long long E, long long K, void* ws, size_t ws_bytes,
-                 cudaStream_t s, const PeerCombine* pc = nullptr, int* status_word = nullptr,
-                 const FusedNorm* fn = nullptr, bool permuted = false) {
-  const WsLayout L = ws_layout(T, H, I, E, K);
-  char* base = static_cast<char*>(ws);
-  int* status = status_word ? status_word : reinterpret_cast<int*>(base + L.status);
-  int32_t* offsets = reinterpret_cast<int32_t*>(base + L.offsets);
-  int32_t* row_token = reinterpret_cast<int32_t*>(base + L.row_token);
-  int32_t* row_slot = reinterpret_cast<int32_t*>(base + L.row_slot);
-  int32_t* slot_row = reinterpret_cast<int32_t*>(base + L.slot_row);
-  float* row_weight = reinterpret_cast<float*>(base + L.row_weight);
-  __nv_bfloat16* xy = reinterpret_cast<__nv_bfloat16*>(base + L.xy);
-  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(base + L.h);
-  const long long TK = T * K;
-  if (T == 0) return NKIMOE_OK;
-  mark(kStagePermute, s);
+// The expert FFNs of a given routing over a workspace (ws_layout), in phases
+// so that a caller can put other work between them: prep (permutation and row
+// gather), GEMMs over a range of experts, finish (combine).
+struct ExpertsRun {
+  const void* x;
+  const void* w13;
+  const void* w2;
+  const void* idx;
+  int idx_dtype;
+  const float* topk_w;
+  long long T, H, I, E, K;
+  char* base;
+  WsLayout L;
+  int* status;
+};
+
+ExpertsRun experts_run(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype,
+                       const float* topk_w, long long T, long long H, long long I, long long E, long long K, void* ws,
+                       int* status_word) {
+  ExpertsRun r{x, w13, w2, idx, idx_dtype, topk_w, T, H, I, E, K, static_cast<char*>(ws), ws_layout(T, H, I, E, K),
+               nullptr};
+  r.status = status_word ? status_word : reinterpret_cast<int*>(r.base + r.L.status);
+  return r;
+}
+
+int experts_prep(const ExpertsRun& r, cudaStream_t s, bool permuted, bool marks) {
+  if (r.T == 0) return NKIMOE_OK;
+  const WsLayout& L = r.L;
+  int32_t* offsets = reinterpret_cast<int32_t*>(r.base + L.offsets);
+  int32_t* row_token = reinterpret_cast<int32_t*>(r.base + L.row_token);
+  if (marks) mark(kStagePermute, s);
   if (!permuted)  // else the router's last CTA has written the permutation
-    NKI_CUDA(permute_launch(idx, idx_dtype, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), row_token,
-                            row_slot, slot_row, offsets, base + L.scratch, status, s, topk_w, row_weight));
+    NKI_CUDA(permute_launch(r.idx, r.idx_dtype, static_cast<int>(r.T), static_cast<int>(r.K), static_cast<int>(r.E),
+                            row_token, reinterpret_cast<int32_t*>(r.base + L.row_slot),
+                            reinterpret_cast<int32_t*>(r.base + L.slot_row), offsets, r.base + L.scratch, r.status, s,
+                            r.topk_w, reinterpret_cast<float*>(r.base + L.row_weight)));
+  if (marks) mark(kStageGather, s);
+  if (!g_gather_fused.load())
+    NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(r.x), row_token, offsets, static_cast<int>(r.E),
+                                reinterpret_cast<__nv_bfloat16*>(r.base + L.xy), r.T * r.K, static_cast<int>(r.H), s));
+  return NKIMOE_OK;
+}
+
+// GEMM-1 (+SwiGLU) and GEMM-2 (+routing weight) of experts [e_lo, e_hi).  The
+// tile schedule is the one the whole routing would get.
+int experts_gemms(const ExpertsRun& r, long long e_lo, long long e_hi, cudaStream_t s, bool marks) {
+  if (r.T == 0 || e_hi <= e_lo) return NKIMOE_OK;
+  const WsLayout& L = r.L;
+  const long long TK = r.T * r.K, H = r.H, I = r.I, E = e_hi - e_lo;
+  const int32_t* offsets = reinterpret_cast<const int32_t*>(r.base + L.offsets) + e_lo;
+  const char* w13 = static_cast<const char*>(r.w13) + sizeof(uint16_t) * e_lo * 2 * I * H;
+  const char* w2 = static_cast<const char*>(r.w2) + sizeof(uint16_t) * e_lo * H * I;
+  __nv_bfloat16* xy = reinterpret_cast<__nv_bfloat16*>(r.base + L.xy);
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(r.base + L.h);
   int rc;
+  if (marks) mark(kStageGemm1, s);
   if (g_gather_fused.load()) {
     // GEMM-1 gathers its activation rows (x[row_token[r]]) in its producer warp
-    mark(kStageGather, s);
-    mark(kStageGemm1, s);
-    rc = run_gemm(x, T, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s, 0,
-                  false, nullptr, 0, 0, row_token, TK);
+    rc = run_gemm(r.x, r.T, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, r.status,
+                  s, 0, false, nullptr, 0, 0, reinterpret_cast<const int32_t*>(r.base + L.row_token), TK, TK, r.E);
   } else {
-    mark(kStageGather, s);
-    NKI_CUDA(gather_rows_launch(static_cast<const __nv_bfloat16*>(x), row_token, offsets, static_cast<int>(E), xy, TK,
-                                static_cast<int>(H), s));
-    mark(kStageGemm1, s);
-    rc = run_gemm(xy, TK, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, status, s);
+    rc = run_gemm(xy, TK, w13, E, 2 * I, H, offsets, kEpiSwiGLU, h, I, nullptr, nullptr, nullptr, nullptr, r.status, s,
+                  0, false, nullptr, 0, 0, nullptr, 0, TK, r.E);
   }
   if (rc != NKIMOE_OK) return rc;
-  mark(kStageGemm2, s);
-  rc = run_gemm(h, TK, w2, E, H, I, offsets, kEpiScaleBf16, xy, H, topk_w, row_slot, nullptr, nullptr, status, s, 0,
-                false, row_weight);
-  if (rc != NKIMOE_OK) return rc;
-  mark(kStageCombine, s);
+  if (marks) mark(kStageGemm2, s);
+  return run_gemm(h, TK, w2, E, H, I, offsets, kEpiScaleBf16, xy, H, r.topk_w,
+                  reinterpret_cast<const int32_t*>(r.base + L.row_slot), nullptr, nullptr, r.status, s, 0, false,
+                  reinterpret_cast<const float*>(r.base + L.row_weight), 0, 0, nullptr, 0, TK, r.E);
+}
+
+int experts_finish(const ExpertsRun& r, void* out, const PeerCombine* pc, const FusedNorm* fn, cudaStream_t s,
+                   bool marks) {
+  if (r.T == 0) return NKIMOE_OK;
+  const WsLayout& L = r.L;
+  const long long T = r.T, K = r.K, H = r.H;
+  const __nv_bfloat16* xy = reinterpret_cast<const __nv_bfloat16*>(r.base + L.xy);
+  const int32_t* slot_row = reinterpret_cast<const int32_t*>(r.base + L.slot_row);
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(r.base + L.h);
+  if (marks) mark(kStageCombine, s);
   if (pc) {
-    NKI_CUDA(ep_peer_combine_launch(xy, slot_row, static_cast<int>(T), static_cast<int>(K), static_cast<int>(H),
-                                    pc->Tm, pc->me, pc->peers, pc->L, pc->P, pc->counter, pc->epoch_p, s));
+    NKI_CUDA(ep_peer_combine_launch(xy, slot_row, pc->q0, pc->nq, static_cast<int>(K), static_cast<int>(H), pc->Tm,
+                                    pc->me, pc->peers, pc->L, pc->P, pc->counter, pc->epoch_p, pc->max_ctas, s));
   } else if (fn && combine_add_rmsnorm_supported(T, static_cast<int>(H))) {
     // few rows: the combine and the next residual add + norm in one kernel
     NKI_CUDA(combine_add_rmsnorm_launch(xy, slot_row, static_cast<int>(K),
@@ -343,18 +392,51 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
     NKI_CUDA(combine_launch(xy, slot_row, nullptr, static_cast<__nv_bfloat16*>(out), static_cast<int>(T),
                             static_cast<int>(K), static_cast<int>(H), s));
   }
-  mark(kStageEnd, s);
+  if (marks) mark(kStageEnd, s);
   return NKIMOE_OK;
 }
 
+int experts_impl(const void* x, const void* w13, const void* w2, const void* idx, int idx_dtype, const float* topk_w,
+                 void* out, long long T, long long H, long long I, long long E, long long K, void* ws, size_t ws_bytes,
+                 cudaStream_t s, const PeerCombine* pc = nullptr, int* status_word = nullptr,
+                 const FusedNorm* fn = nullptr, bool permuted = false) {
+  (void)ws_bytes;
+  if (T == 0) return NKIMOE_OK;
+  const ExpertsRun r = experts_run(x, w13, w2, idx, idx_dtype, topk_w, T, H, I, E, K, ws, status_word);
+  int rc = experts_prep(r, s, permuted, true);
+  if (rc == NKIMOE_OK) rc = experts_gemms(r, 0, E, s, true);
+  if (rc == NKIMOE_OK) rc = experts_finish(r, out, pc, fn, s, true);
+  return rc;
+}
+
 // Workspace of nkimoe_ep_peer_forward: routing of the local tokens, the
-// (token, rank) sort, the row map of the final sum, two completion counters,
-// and the receiver's expert block over all P * max_tokens region rows.
+// (token, rank) sort, the row map of the final sum, completion counters, then
+// the receiver's expert blocks.  The one-block schedule runs one block over
+// all P * max_tokens region rows; the overlapped schedule runs one block over
+// the rank's own tokens (their own-expert slots in self_idx / self_w) and one
+// per group of remote regions.  The workspace holds the larger of the two.
 struct PeerWs {
-  size_t route, disp, slot_in, slot_out, counters, recv, total;
+  size_t route, disp, slot_in, slot_out, counters, self_idx, self_w, recv, total;
 };
 
 size_t ep_dispatch_ws_bytes(long long T, long long P);
+
+// Regions q >= 1 cut into `groups` groups of consecutive regions, nearly equal,
+// the later groups taking the remainder: group g is [q0(g), q0(g + 1)).
+inline long long group_q0(long long P, long long groups, long long g) {
+  const long long n = P - 1, base = n / groups, extra = n % groups;
+  return 1 + g * base + std::max<long long>(0, g - (groups - extra));
+}
+
+size_t overlapped_recv_bytes(long long T, long long H, long long I, long long El, long long K, long long P,
+                             long long Tm, long long groups) {
+  size_t o = round256(ws_layout(T, H, I, El, K).total);  // own tokens
+  for (long long g = 0; g < groups; ++g) {
+    const long long nq = group_q0(P, groups, g + 1) - group_q0(P, groups, g);
+    o += round256(ws_layout(nq * Tm, H, I, El, K).total);
+  }
+  return o;
+}
 
 PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, long long P, long long Tm) {
   PeerWs W{};
@@ -364,7 +446,12 @@ PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, 
   W.slot_in = o; o += round256(sizeof(int32_t) * T * P);
   W.slot_out = o; o += round256(sizeof(int32_t) * T * P);
   W.counters = o; o += 256;
-  W.recv = o; o += ws_layout(P * Tm, H, I, E / P, K).total;
+  W.self_idx = o; o += round256(sizeof(int32_t) * T * K);
+  W.self_w = o; o += round256(sizeof(float) * T * K);
+  W.recv = o;
+  size_t recv = ws_layout(P * Tm, H, I, E / P, K).total;
+  for (long long g = 1; g < P; ++g) recv = std::max(recv, overlapped_recv_bytes(T, H, I, E / P, K, P, Tm, g));
+  o += recv;
   W.total = o;
   return W;
 }
@@ -563,6 +650,28 @@ int host_slots_for(HostCopyStreams& h, void* workspace, HostSlots** out) {
   return NKIMOE_OK;
 }
 
+// Per device: the side stream of the expert-parallel block (sends and returns
+// beside the expert GEMMs) and the events that fork it from and join it to
+// the caller's stream.  Calls on one device share it (and its lock).
+constexpr int kEpMaxDevices = 64;
+struct EpSideStream {
+  bool ready = false;
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr, group[kMaxPeers] = {};
+};
+std::mutex g_ep_mu[kEpMaxDevices];
+EpSideStream g_ep[kEpMaxDevices];
+
+int ep_side_init(EpSideStream& es) {
+  if (es.ready) return NKIMOE_OK;
+  NKI_CUDA(cudaStreamCreateWithFlags(&es.side, cudaStreamNonBlocking));
+  NKI_CUDA(cudaEventCreateWithFlags(&es.fork, cudaEventDisableTiming));
+  NKI_CUDA(cudaEventCreateWithFlags(&es.join, cudaEventDisableTiming));
+  for (int g = 0; g < kMaxPeers; ++g) NKI_CUDA(cudaEventCreateWithFlags(&es.group[g], cudaEventDisableTiming));
+  es.ready = true;
+  return NKIMOE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -613,6 +722,18 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "peer_wait_cycles" && value >= 1000 && value <= 1000000000000LL) {
     g_peer_wait_cycles = value;
+    return NKIMOE_OK;
+  }
+  if (n == "ep_overlap" && (value == 0 || value == 1)) {
+    g_ep_overlap = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "ep_groups" && value >= 0 && value < kMaxPeers) {
+    g_ep_groups = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "ep_side_ctas" && value >= 0 && value <= 4096) {
+    g_ep_side_ctas = static_cast<int>(value);
     return NKIMOE_OK;
   }
   return fail(NKIMOE_ERR_INVALID_ARG, "unknown option %s=%lld", name, value);
@@ -1196,6 +1317,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   const cudaStream_t s = as_stream(stream);
   const EpPeerLayout PL = ep_peer_layout(P, Tm, H, K);
   const long long El = E / P;
+  const int me = static_cast<int>(rank);
   char* b = static_cast<char*>(workspace);
   // routing of the local tokens (its status word is the call's status word)
   const WsLayout R = ws_layout(T, H, I, E, K);
@@ -1203,9 +1325,10 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   int* status = reinterpret_cast<int*>(rb + R.status);
   int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(rb + R.idx);
   float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(rb + R.w);
+  // completion counters: [0, P) sends, [P, 2P) returns
   unsigned* counters = reinterpret_cast<unsigned*>(b + W.counters);
   NKI_CUDA(cudaMemsetAsync(status, 0, 256, s));  // status word and router counters
-  NKI_CUDA(cudaMemsetAsync(counters, 0, 2 * sizeof(unsigned), s));
+  NKI_CUDA(cudaMemsetAsync(counters, 0, 256, s));
   // this step's epoch: the caller's, or this rank's device-side count + 1
   uint32_t* epoch_p = reinterpret_cast<uint32_t*>(peers.base[rank] + PL.step);
   NKI_CUDA(ep_peer_step_launch(epoch_p, epoch, s));
@@ -1214,6 +1337,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     if (rc != NKIMOE_OK) return rc;
   }
   // (token, rank) pairs grouped by rank, tokens ascending
+  mark(kStagePermute, s);
   char* db = b + W.disp;
   int32_t* offsets = reinterpret_cast<int32_t*>(db + 256);
   int32_t* dest = offsets + round256(sizeof(int32_t) * (P + 1)) / sizeof(int32_t);
@@ -1222,34 +1346,114 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   void* scratch = row_slot + round256(sizeof(int32_t) * T * P) / sizeof(int32_t);
   int32_t* slot_in = reinterpret_cast<int32_t*>(b + W.slot_in);
   int32_t* slot_out = reinterpret_cast<int32_t*>(b + W.slot_out);
-  mark(kStageEpSend, s);
   if (T > 0)
     NKI_CUDA(ep_dest_launch(idx, static_cast<int>(T), static_cast<int>(K), static_cast<int>(P), static_cast<int>(El),
                             dest, s));
   NKI_CUDA(permute_launch(dest, NKIMOE_I32, static_cast<int>(T), static_cast<int>(P), static_cast<int>(P), row_token,
                           row_slot, slot_in, offsets, scratch, status, s));
-  // rows to their owners' buffers, then this rank's incoming rows
-  NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets, slot_in,
-                               slot_out, static_cast<int>(T), static_cast<int>(H), static_cast<int>(K),
-                               static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), static_cast<int>(rank),
-                               peers, PL, counters, epoch_p, s));
   char* own = peers.base[rank];
-  mark(kStageEpWait, s);
-  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.disp_flag), static_cast<int>(P), epoch_p,
-                               status, g_peer_wait_cycles.load(), s));
   int32_t* recv_slots = reinterpret_cast<int32_t*>(own + PL.recv_slots);
-  NKI_CUDA(ep_peer_mask_launch(recv_slots, reinterpret_cast<const int32_t*>(own + PL.counts), static_cast<int>(P),
-                               static_cast<int>(Tm), static_cast<int>(K), s));
-  // this rank's experts over every region; sums go back to the sources
-  const PeerCombine pc{peers, PL, static_cast<int>(P), static_cast<int>(rank), static_cast<int>(Tm), counters + 1,
-                       epoch_p};
-  rc = experts_impl(own + PL.recv_x, w13_local, w2_local, recv_slots, NKIMOE_I32,
-                    reinterpret_cast<const float*>(own + PL.recv_w), nullptr, P * Tm, H, I, El, K, b + W.recv,
-                    workspace_bytes - W.recv, s, &pc, status);
-  if (rc != NKIMOE_OK) return rc;
-  mark(kStageEpReturnWait, s);
-  NKI_CUDA(ep_peer_wait_launch(reinterpret_cast<const uint32_t*>(own + PL.res_flag), static_cast<int>(P), epoch_p,
-                               status, g_peer_wait_cycles.load(), s));
+  const float* recv_w = reinterpret_cast<const float*>(own + PL.recv_w);
+  const char* recv_x = own + PL.recv_x;
+  const int32_t* counts = reinterpret_cast<const int32_t*>(own + PL.counts);
+  const uint32_t* disp_flag = reinterpret_cast<const uint32_t*>(own + PL.disp_flag);
+  const uint32_t* res_flag = reinterpret_cast<const uint32_t*>(own + PL.res_flag);
+  const long long budget = g_peer_wait_cycles.load();
+  const bool overlapped = g_ep_overlap.load() != 0;
+
+  if (!overlapped) {
+    // ---- one block: every row (own included) through the buffers, then all
+    // of this rank's experts over all P regions
+    NKI_CUDA(ep_peer_local_launch(idx, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
+                                  static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), me, false, slot_out,
+                                  nullptr, nullptr, s));
+    mark(kStageEpSend, s);
+    NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+                                 static_cast<int>(T), static_cast<int>(H), static_cast<int>(K), static_cast<int>(P),
+                                 static_cast<int>(El), static_cast<int>(Tm), me, 0, static_cast<int>(P), peers, PL,
+                                 counters, epoch_p, 0, s));
+    mark(kStageEpWait, s);
+    NKI_CUDA(ep_peer_wait_launch(disp_flag, static_cast<int>(P), epoch_p, status, budget, s));
+    NKI_CUDA(ep_peer_mask_launch(recv_slots, counts, 0, static_cast<int>(P), static_cast<int>(Tm),
+                                 static_cast<int>(K), s));
+    const PeerCombine pc{peers, PL, static_cast<int>(P), me, static_cast<int>(Tm), 0, static_cast<int>(P), 0,
+                         counters + P, epoch_p};
+    rc = experts_impl(recv_x, w13_local, w2_local, recv_slots, NKIMOE_I32, recv_w, nullptr, P * Tm, H, I, El, K,
+                      b + W.recv, workspace_bytes - W.recv, s, &pc, status);
+    if (rc != NKIMOE_OK) return rc;
+    mark(kStageEpReturnWait, s);
+    NKI_CUDA(ep_peer_wait_launch(res_flag, static_cast<int>(P), epoch_p, status, budget, s));
+  } else {
+    // ---- overlapped: the sends to the other ranks and the returns of their
+    // sums run on a side stream of the library beside the expert GEMMs.  The
+    // own tokens' share goes straight from x; remote regions are taken in
+    // groups, nearest sources first (each source sends to its nearest
+    // destination first), each group's sums returned while the next computes.
+    int32_t* self_idx = reinterpret_cast<int32_t*>(b + W.self_idx);
+    float* self_w = reinterpret_cast<float*>(b + W.self_w);
+    NKI_CUDA(ep_peer_local_launch(idx, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
+                                  static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), me, true, slot_out,
+                                  self_idx, self_w, s));
+    int dev = 0;
+    NKI_CUDA(cudaGetDevice(&dev));
+    NKI_REQUIRE(dev >= 0 && dev < kEpMaxDevices, NKIMOE_ERR_UNSUPPORTED, "device %d", dev);
+    std::lock_guard<std::mutex> lock(g_ep_mu[dev]);
+    EpSideStream& es = g_ep[dev];
+    rc = ep_side_init(es);
+    if (rc != NKIMOE_OK) return rc;
+    const int side_ctas = g_ep_side_ctas.load() > 0 ? g_ep_side_ctas.load() : device_sm_count();
+    long long groups = g_ep_groups.load() > 0 ? g_ep_groups.load() : std::min<long long>(P - 1, 3);
+    groups = std::min<long long>(groups, P - 1);  // 0 for a single rank: no remote regions
+    mark(kStageEpSend, s);
+    NKI_CUDA(cudaEventRecord(es.fork, s));
+    NKI_CUDA(cudaStreamWaitEvent(es.side, es.fork, 0));
+    for (long long q = 1; q < P; ++q) {  // one launch per destination, nearest first
+      const int d = static_cast<int>((rank + q) % P);
+      NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+                                   static_cast<int>(T), static_cast<int>(H), static_cast<int>(K), static_cast<int>(P),
+                                   static_cast<int>(El), static_cast<int>(Tm), me, d, 1, peers, PL, counters + q,
+                                   epoch_p, side_ctas, es.side));
+    }
+    // own tokens: prep and the first half of the experts before the remote
+    // rows are needed, the second half after them (covering the last returns)
+    char* sb = b + W.recv;
+    const ExpertsRun self = experts_run(x, w13_local, w2_local, self_idx, NKIMOE_I32, self_w, T, H, I, El, K, sb,
+                                        status);
+    const long long split = (T * K > 48 * El * P && El >= 2) ? El / 2 : El;
+    rc = experts_prep(self, s, false, false);
+    if (rc == NKIMOE_OK) rc = experts_gemms(self, 0, split, s, false);
+    if (rc != NKIMOE_OK) return rc;
+    mark(kStageEpWait, s);
+    char* gb = sb + round256(ws_layout(T, H, I, El, K).total);
+    for (long long g = 0; g < groups; ++g) {
+      const long long q0 = group_q0(P, groups, g), nq = group_q0(P, groups, g + 1) - q0;
+      NKI_CUDA(ep_peer_wait_launch(disp_flag + q0, static_cast<int>(nq), epoch_p, status, budget, s));
+      NKI_CUDA(ep_peer_mask_launch(recv_slots + q0 * Tm * K, counts, static_cast<int>(q0), static_cast<int>(nq),
+                                   static_cast<int>(Tm), static_cast<int>(K), s));
+      const ExpertsRun grp = experts_run(recv_x + q0 * Tm * H * sizeof(uint16_t), w13_local, w2_local,
+                                         recv_slots + q0 * Tm * K, NKIMOE_I32, recv_w + q0 * Tm * K, nq * Tm, H, I,
+                                         El, K, gb, status);
+      rc = experts_prep(grp, s, false, false);
+      if (rc == NKIMOE_OK) rc = experts_gemms(grp, 0, El, s, false);
+      if (rc != NKIMOE_OK) return rc;
+      // the group's sums go back to their sources from the side stream
+      NKI_CUDA(cudaEventRecord(es.group[g], s));
+      NKI_CUDA(cudaStreamWaitEvent(es.side, es.group[g], 0));
+      const PeerCombine pc{peers, PL, static_cast<int>(P), me, static_cast<int>(Tm), static_cast<int>(q0),
+                           static_cast<int>(nq), side_ctas, counters + P + g, epoch_p};
+      rc = experts_finish(grp, nullptr, &pc, nullptr, es.side, false);
+      if (rc != NKIMOE_OK) return rc;
+      gb += round256(ws_layout(nq * Tm, H, I, El, K).total);
+    }
+    mark(kStageEpReturnWait, s);
+    rc = experts_gemms(self, split, El, s, false);
+    if (rc == NKIMOE_OK) rc = experts_finish(self, own + PL.ret_y, nullptr, nullptr, s, false);
+    if (rc != NKIMOE_OK) return rc;
+    if (P > 1) NKI_CUDA(ep_peer_wait_launch(res_flag + 1, static_cast<int>(P - 1), epoch_p, status, budget, s));
+    // the side stream's work belongs to this call
+    NKI_CUDA(cudaEventRecord(es.join, es.side));
+    NKI_CUDA(cudaStreamWaitEvent(s, es.join, 0));
+  }
   mark(kStageEpSum, s);
   if (T > 0)
     NKI_CUDA(combine_launch(reinterpret_cast<const __nv_bfloat16*>(own + PL.ret_y), slot_out, nullptr,

@@ -8,12 +8,18 @@
 //   counts[P]                  i32 rows sent by each source this step
 //   recv_slots [P][Tm][K]      i32 local expert ids (-1: empty slot)
 //   recv_w     [P][Tm][K]      f32 routing weights
-//   recv_x     [P][Tm][H]      bf16 token rows, region s written by source s
-//   ret_y      [P][Tm][H]      bf16 partial sums, region d written by rank d
-// Source s sends token t to rank d once when any of t's experts lives on d
-// (the de-duplicated dispatch) as row j of region s of d's buffer; rank d runs
-// its local experts over all regions (empty slots skipped) and writes row j's
-// weighted sum into region d of s's ret_y; s adds its P partial sums.
+//   recv_x     [P][Tm][H]      bf16 token rows
+//   ret_y      [P][Tm][H]      bf16 partial sums
+// Regions, flags and counts are indexed by the distance between the two
+// ranks: region q of rank d's recv_* (and flag / count q) holds what rank
+// d - q (mod P) sent; region q of rank s's ret_y (and res_flag q) holds what
+// rank s + q returned.  Region 0 is the rank's own.  Source s sends token t
+// to rank d once when any of t's experts lives on d (the de-duplicated
+// dispatch) as row j of region q = d - s of d's buffer; d runs its local
+// experts over the rows (empty slots skipped) and writes row j's weighted sum
+// into row j of region q of s's ret_y; s adds its P partial sums.  Indexing by
+// distance keeps the regions a receiver takes in arrival order (sources send
+// to the nearest destination first) contiguous.
 //
 // Publication: each CTA of a sending kernel fences its peer stores at system
 // scope, the last CTA to finish (a counter in local memory) publishes the
@@ -76,34 +82,39 @@ __device__ __forceinline__ bool last_block_done(unsigned* counter) {
 }
 
 // Source side: send row r (token row_token[r], destination d = row_slot[r] % P,
-// j = r - rank_offsets[d]) to region src of d's buffer: the token row, its K
-// slots as d sees them and their weights.  Also rewrites slot_row for the final
-// sum: (t, d) -> d * Tm + j in this rank's ret_y.  One warp per pair of rows:
-// both rows' metadata, then both rows' 4 KB of loads, are in flight before the
-// stores (the stores to a peer are posted; the loads set the pace).
+// j = r - rank_offsets[d]) of destinations [d_first, d_first + d_count) to
+// region (d - src) mod P of d's buffer: the token row, its K slots as d sees
+// them and their weights.  One warp per pair of rows: both rows' metadata,
+// then both rows' 4 KB of loads, are in flight before the stores (the stores
+// to a peer are posted; the loads set the pace).  The last CTA publishes each
+// destination's count and raises its dispatch flag.
 __global__ void __launch_bounds__(256) ep_peer_send_kernel(
     const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx, const float* __restrict__ w,
     const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
-    const int32_t* __restrict__ rank_offsets, const int32_t* __restrict__ slot_row_in,
-    int32_t* __restrict__ slot_row_out, int T, int H, int K, int P, int El, int Tm, int src, EpPeerPtrs peers,
-    EpPeerLayout L, unsigned* counter, const uint32_t* epoch_p) {
+    const int32_t* __restrict__ rank_offsets, int H, int K, int P, int El, int Tm, int src, int d_first, int d_count,
+    EpPeerPtrs peers, EpPeerLayout L, unsigned* counter, const uint32_t* epoch_p) {
   constexpr int kRowsPerWarp = 2;
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  const long long rows = rank_offsets[P];
+  const long long r_begin = rank_offsets[d_first];
+  const long long rows = rank_offsets[d_first + d_count] - r_begin;
   const int chunks = H >> 3;
-  for (long long r0 = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kRowsPerWarp;
-       r0 < rows; r0 += nw * kRowsPerWarp) {
+  for (long long i0 = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kRowsPerWarp;
+       i0 < rows; i0 += nw * kRowsPerWarp) {
+    const long long r0 = r_begin + i0;
     int t[kRowsPerWarp], d[kRowsPerWarp];
     long long dst_row[kRowsPerWarp];
 #pragma unroll
     for (int q = 0; q < kRowsPerWarp; ++q) {
-      const long long r = r0 + q < rows ? r0 + q : r0;
+      const long long r = i0 + q < rows ? r0 + q : r0;
       t[q] = row_token[r];
       d[q] = row_slot[r] % P;
     }
 #pragma unroll
-    for (int q = 0; q < kRowsPerWarp; ++q) dst_row[q] = static_cast<long long>(src) * Tm + (r0 + q - rank_offsets[d[q]]);
+    for (int q = 0; q < kRowsPerWarp; ++q) {
+      const int region = (d[q] - src + P) % P;
+      dst_row[q] = static_cast<long long>(region) * Tm + (r0 + q - rank_offsets[d[q]]);
+    }
     for (int c0 = lane; c0 < chunks; c0 += 256) {
       uint4 v[kRowsPerWarp][8];
 #pragma unroll
@@ -115,7 +126,7 @@ __global__ void __launch_bounds__(256) ep_peer_send_kernel(
       }
 #pragma unroll
       for (int q = 0; q < kRowsPerWarp; ++q) {
-        if (r0 + q >= rows) break;
+        if (i0 + q >= rows) break;
         uint4* d4 = reinterpret_cast<uint4*>(view_of(peers.base[d[q]], L).recv_x + dst_row[q] * H);
 #pragma unroll
         for (int u = 0; u < 8; ++u)
@@ -124,7 +135,7 @@ __global__ void __launch_bounds__(256) ep_peer_send_kernel(
     }
 #pragma unroll
     for (int q = 0; q < kRowsPerWarp; ++q) {
-      if (r0 + q >= rows || lane >= K) continue;
+      if (i0 + q >= rows || lane >= K) continue;
       const EpPeerView pv = view_of(peers.base[d[q]], L);
       const int e = idx[static_cast<long long>(t[q]) * K + lane];
       const bool mine = e >= d[q] * El && e < (d[q] + 1) * El;
@@ -132,30 +143,54 @@ __global__ void __launch_bounds__(256) ep_peer_send_kernel(
       pv.recv_w[dst_row[q] * K + lane] = mine ? w[static_cast<long long>(t[q]) * K + lane] : 0.f;
     }
   }
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < static_cast<long long>(T) * P;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int d = static_cast<int>(i % P);
-    const int sr = slot_row_in[i];
-    slot_row_out[i] = sr >= 0 ? d * Tm + (sr - rank_offsets[d]) : -1;
-  }
-  if (last_block_done(counter) && threadIdx.x < P) {
-    const int d = threadIdx.x;
+  if (last_block_done(counter) && threadIdx.x < d_count) {
+    const int d = d_first + threadIdx.x;
+    const int region = (d - src + P) % P;
     const EpPeerView pv = view_of(peers.base[d], L);
-    pv.counts[src] = rank_offsets[d + 1] - rank_offsets[d];
+    pv.counts[region] = rank_offsets[d + 1] - rank_offsets[d];
     __threadfence_system();
-    st_release_sys(pv.disp_flag + src, *epoch_p);
+    st_release_sys(pv.disp_flag + region, *epoch_p);
   }
 }
 
-// Poll this rank's P flags until each holds the step's epoch, for at most
-// `budget` SM clock cycles; a flag still behind then sets the timeout bit of the
-// status word and the kernel returns.  One warp.
-__global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status,
+// Source-side bookkeeping: slot_out[t * P + d] = the row of ret_y that will
+// hold the partial sum of token t from rank d (region (d - src) mod P, at the
+// row t was sent to; region 0 at row t when self_direct), -1 when t has no
+// expert on d; and with self_idx, t's slots as this rank sees them.
+__global__ void ep_peer_local_kernel(const int32_t* __restrict__ idx, const float* __restrict__ w,
+                                     const int32_t* __restrict__ slot_in, const int32_t* __restrict__ rank_offsets,
+                                     int T, int K, int P, int El, int Tm, int src, int self_direct,
+                                     int32_t* __restrict__ slot_out, int32_t* __restrict__ self_idx,
+                                     float* __restrict__ self_w) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (long long i = i0; i < static_cast<long long>(T) * P; i += stride) {
+    const int d = static_cast<int>(i % P);
+    const int sr = slot_in[i];
+    const int region = (d - src + P) % P;
+    int row = -1;
+    if (sr >= 0) row = (self_direct && d == src) ? static_cast<int>(i / P) : region * Tm + (sr - rank_offsets[d]);
+    slot_out[i] = row;
+  }
+  if (self_idx) {
+    for (long long i = i0; i < static_cast<long long>(T) * K; i += stride) {
+      const int e = idx[i];
+      const bool mine = e >= src * El && e < (src + 1) * El;
+      self_idx[i] = mine ? e - src * El : -1;
+      self_w[i] = mine ? w[i] : 0.f;
+    }
+  }
+}
+
+// Poll flags[0 .. n) until each holds the step's epoch, for at most `budget`
+// SM clock cycles; a flag still behind then sets the timeout bit of the status
+// word and the kernel returns.  One warp.
+__global__ void ep_peer_wait_kernel(const uint32_t* flags, int n, const uint32_t* epoch_p, int* status,
                                     long long budget) {
   const uint32_t epoch = *epoch_p;
   const int lane = threadIdx.x;
   bool ok = true;
-  if (lane < P) {
+  if (lane < n) {
     const long long t0 = clock64();
     while (static_cast<int>(ld_acquire_sys(flags + lane) - epoch) < 0) {
       if (clock64() - t0 > budget) {
@@ -169,42 +204,45 @@ __global__ void ep_peer_wait_kernel(const uint32_t* flags, int P, const uint32_t
 }
 
 // Receiver: rows past each source's count get empty slots (the region holds
-// whatever an earlier step left there).
-__global__ void ep_peer_mask_kernel(int32_t* __restrict__ slots, const int32_t* __restrict__ counts, int P, int Tm,
-                                    int K) {
-  const long long n = static_cast<long long>(P) * Tm * K;
+// whatever an earlier step left there).  `slots` starts at region q0.
+__global__ void ep_peer_mask_kernel(int32_t* __restrict__ slots, const int32_t* __restrict__ counts, int q0, int nq,
+                                    int Tm, int K) {
+  const long long n = static_cast<long long>(nq) * Tm * K;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long row = i / K;
-    const int s = static_cast<int>(row / Tm);
-    const long long j = row - static_cast<long long>(s) * Tm;
-    if (j >= counts[s]) slots[i] = -1;
+    const int q = static_cast<int>(row / Tm);
+    const long long j = row - static_cast<long long>(q) * Tm;
+    if (j >= counts[q0 + q]) slots[i] = -1;
   }
 }
 
 // Receiver: the routing-weighted sum of row r's K expert outputs (fp32, k
-// ascending, as combine_kernel), stored straight into region `me` of the
-// source's ret_y (source s = r / Tm, row j = r % Tm).  Rows without a local
+// ascending, as combine_kernel), stored straight into the source's ret_y: row
+// r is row j = r % Tm of region q = q0 + r / Tm, from source s = me - q, and
+// its sum goes to row j of region q of s's ret_y.  Rows without a local
 // expert are skipped.  One warp per row: its K output-row indices come in one
 // load, then each present slot's whole 4 KB row is loaded (8 x 16 bytes per
 // lane in flight) and added; the sum leaves as 4 KB of contiguous stores.  The
-// last CTA raises every source's result flag.
+// last CTA raises the result flags of the regions' sources.
 __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat16* __restrict__ y,
-                                                              const int32_t* __restrict__ slot_row, int rows, int K,
-                                                              int H, int Tm, int me, EpPeerPtrs peers,
+                                                              const int32_t* __restrict__ slot_row, int q0, int nq,
+                                                              int K, int H, int Tm, int me, EpPeerPtrs peers,
                                                               EpPeerLayout L, int P, unsigned* counter,
                                                               const uint32_t* epoch_p) {
   const int lane = threadIdx.x & 31;
   const int chunks = H >> 3;
+  const long long rows = static_cast<long long>(nq) * Tm;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
        r += nw) {
     const int my_yr = lane < K ? slot_row[r * K + lane] : -1;
     const unsigned present = __ballot_sync(0xffffffffu, my_yr >= 0);
     if (present == 0u) continue;
-    const int s = static_cast<int>(r / Tm);
-    const long long j = r - static_cast<long long>(s) * Tm;
-    uint4* dst = reinterpret_cast<uint4*>(view_of(peers.base[s], L).ret_y + (static_cast<long long>(me) * Tm + j) * H);
+    const int q = q0 + static_cast<int>(r / Tm);
+    const long long j = r % Tm;
+    const int s = (me - q + P) % P;
+    uint4* dst = reinterpret_cast<uint4*>(view_of(peers.base[s], L).ret_y + (static_cast<long long>(q) * Tm + j) * H);
     for (int c0 = lane; c0 < chunks; c0 += 256) {
       float acc[8][8] = {};
       for (unsigned m = present; m != 0u; m &= m - 1u) {  // slots in ascending k
@@ -212,38 +250,39 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
         const uint4* src = reinterpret_cast<const uint4*>(y + static_cast<long long>(yr) * H);
         uint4 u[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (c0 + 32 * q < chunks) u[q] = __ldcs(src + c0 + 32 * q);
+        for (int qq = 0; qq < 8; ++qq)
+          if (c0 + 32 * qq < chunks) u[qq] = __ldcs(src + c0 + 32 * qq);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (c0 + 32 * q >= chunks) break;
-          const float2 a = unpack_bf16x2(u[q].x), b = unpack_bf16x2(u[q].y);
-          const float2 cc = unpack_bf16x2(u[q].z), dd = unpack_bf16x2(u[q].w);
-          acc[q][0] += a.x;
-          acc[q][1] += a.y;
-          acc[q][2] += b.x;
-          acc[q][3] += b.y;
-          acc[q][4] += cc.x;
-          acc[q][5] += cc.y;
-          acc[q][6] += dd.x;
-          acc[q][7] += dd.y;
+        for (int qq = 0; qq < 8; ++qq) {
+          if (c0 + 32 * qq >= chunks) break;
+          const float2 a = unpack_bf16x2(u[qq].x), b = unpack_bf16x2(u[qq].y);
+          const float2 cc = unpack_bf16x2(u[qq].z), dd = unpack_bf16x2(u[qq].w);
+          acc[qq][0] += a.x;
+          acc[qq][1] += a.y;
+          acc[qq][2] += b.x;
+          acc[qq][3] += b.y;
+          acc[qq][4] += cc.x;
+          acc[qq][5] += cc.y;
+          acc[qq][6] += dd.x;
+          acc[qq][7] += dd.y;
         }
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (c0 + 32 * q >= chunks) break;
+      for (int qq = 0; qq < 8; ++qq) {
+        if (c0 + 32 * qq >= chunks) break;
         uint4 o;
-        o.x = pack_bf16x2(acc[q][0], acc[q][1]);
-        o.y = pack_bf16x2(acc[q][2], acc[q][3]);
-        o.z = pack_bf16x2(acc[q][4], acc[q][5]);
-        o.w = pack_bf16x2(acc[q][6], acc[q][7]);
-        dst[c0 + 32 * q] = o;
+        o.x = pack_bf16x2(acc[qq][0], acc[qq][1]);
+        o.y = pack_bf16x2(acc[qq][2], acc[qq][3]);
+        o.z = pack_bf16x2(acc[qq][4], acc[qq][5]);
+        o.w = pack_bf16x2(acc[qq][6], acc[qq][7]);
+        dst[c0 + 32 * qq] = o;
       }
     }
   }
-  if (last_block_done(counter) && threadIdx.x < P) {
-    const EpPeerView pv = view_of(peers.base[threadIdx.x], L);
-    st_release_sys(pv.res_flag + me, *epoch_p);
+  if (last_block_done(counter) && threadIdx.x < nq) {
+    const int q = q0 + threadIdx.x;
+    const EpPeerView pv = view_of(peers.base[(me - q + P) % P], L);
+    st_release_sys(pv.res_flag + q, *epoch_p);
   }
 }
 
@@ -288,15 +327,27 @@ EpPeerLayout ep_peer_layout(long long P, long long Tm, long long H, long long K)
 }
 
 cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
-                                const int32_t* row_slot, const int32_t* rank_offsets, const int32_t* slot_row_in,
-                                int32_t* slot_row_out, int T, int H, int K, int P, int El, int Tm, int src,
-                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter,
-                                const uint32_t* epoch_p, cudaStream_t s) {
-  // one warp per send row (at most T * P rows); at least one CTA so that the
-  // flags are raised even when nothing is sent
-  const unsigned grid = grid_cap(static_cast<long long>(T) * P * 32, 256);
-  ep_peer_send_kernel<<<grid, 256, 0, s>>>(x, idx, w, row_token, row_slot, rank_offsets, slot_row_in, slot_row_out, T,
-                                           H, K, P, El, Tm, src, peers, L, counter, epoch_p);
+                                const int32_t* row_slot, const int32_t* rank_offsets, int T, int H, int K, int P,
+                                int El, int Tm, int src, int d_first, int d_count, const EpPeerPtrs& peers,
+                                const EpPeerLayout& L, unsigned* counter, const uint32_t* epoch_p, int max_ctas,
+                                cudaStream_t s) {
+  if (d_first < 0 || d_count < 1 || d_first + d_count > P || d_count > 256) return cudaErrorInvalidValue;
+  // one warp per two send rows (at most T rows per destination); at least one
+  // CTA so that the flags are raised even when nothing is sent
+  unsigned grid = grid_cap(static_cast<long long>(T) * d_count * 16, 256);
+  if (max_ctas > 0 && grid > static_cast<unsigned>(max_ctas)) grid = static_cast<unsigned>(max_ctas);
+  ep_peer_send_kernel<<<grid, 256, 0, s>>>(x, idx, w, row_token, row_slot, rank_offsets, H, K, P, El, Tm, src,
+                                           d_first, d_count, peers, L, counter, epoch_p);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_local_launch(const int32_t* idx, const float* w, const int32_t* slot_in,
+                                 const int32_t* rank_offsets, int T, int K, int P, int El, int Tm, int src,
+                                 bool self_direct, int32_t* slot_out, int32_t* self_idx, float* self_w, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  const long long work = static_cast<long long>(T) * (P > K ? P : K);
+  ep_peer_local_kernel<<<grid_cap(work, 256), 256, 0, s>>>(idx, w, slot_in, rank_offsets, T, K, P, El, Tm, src,
+                                                           self_direct ? 1 : 0, slot_out, self_idx, self_w);
   return cudaGetLastError();
 }
 
@@ -305,22 +356,26 @@ cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s) 
   return cudaGetLastError();
 }
 
-cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status,
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int n, const uint32_t* epoch_p, int* status,
                                 long long budget_cycles, cudaStream_t s) {
-  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, P, epoch_p, status, budget_cycles);
+  if (n < 1 || n > 32) return cudaErrorInvalidValue;
+  ep_peer_wait_kernel<<<1, 32, 0, s>>>(flags, n, epoch_p, status, budget_cycles);
   return cudaGetLastError();
 }
 
-cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, int Tm, int K, cudaStream_t s) {
-  ep_peer_mask_kernel<<<grid_cap(static_cast<long long>(P) * Tm * K, 256), 256, 0, s>>>(slots, counts, P, Tm, K);
+cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int q0, int nq, int Tm, int K, cudaStream_t s) {
+  ep_peer_mask_kernel<<<grid_cap(static_cast<long long>(nq) * Tm * K, 256), 256, 0, s>>>(slots, counts, q0, nq, Tm,
+                                                                                        K);
   return cudaGetLastError();
 }
 
-cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
-                                   int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
-                                   const uint32_t* epoch_p, cudaStream_t s) {
-  const unsigned grid = grid_cap(static_cast<long long>(rows) * 32, 256);  // one warp per row
-  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, rows, K, H, Tm, me, peers, L, P, counter, epoch_p);
+cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int q0, int nq, int K, int H,
+                                   int Tm, int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P,
+                                   unsigned* counter, const uint32_t* epoch_p, int max_ctas, cudaStream_t s) {
+  if (nq < 1 || q0 < 0 || q0 + nq > P) return cudaErrorInvalidValue;
+  unsigned grid = grid_cap(static_cast<long long>(nq) * Tm * 32, 256);  // one warp per row
+  if (max_ctas > 0 && grid > static_cast<unsigned>(max_ctas)) grid = static_cast<unsigned>(max_ctas);
+  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, q0, nq, K, H, Tm, me, peers, L, P, counter, epoch_p);
   return cudaGetLastError();
 }
 

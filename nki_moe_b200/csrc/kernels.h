@@ -159,19 +159,42 @@ struct EpPeerLayout {  // byte offsets inside an exchange buffer (ep_peer.cu)
   size_t step, disp_flag, res_flag, counts, recv_slots, recv_w, recv_x, ret_y, total;
 };
 EpPeerLayout ep_peer_layout(long long P, long long max_tokens, long long H, long long K);
+// Regions of an exchange buffer are indexed by the distance q = (receiver -
+// source) mod P: region q of rank d holds the rows sent by rank d - q, and
+// region q of rank s's ret_y the partial sums returned by rank s + q.  Flags
+// and counts are indexed the same way.  Region 0 is the rank's own.
+//
+// Rows (sorted by destination rank: rank_offsets[P + 1]) for the destinations
+// d_first .. d_first + d_count - 1 go to region (d - src) mod P of d's
+// buffer; the last CTA publishes their counts and raises their dispatch flags.
+// max_ctas bounds the grid (0: as many as the rows need).
 cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
-                                const int32_t* row_slot, const int32_t* rank_offsets, const int32_t* slot_row_in,
-                                int32_t* slot_row_out, int T, int H, int K, int P, int El, int Tm, int src,
-                                const EpPeerPtrs& peers, const EpPeerLayout& L, unsigned* counter,
-                                const uint32_t* epoch_p, cudaStream_t s);
+                                const int32_t* row_slot, const int32_t* rank_offsets, int T, int H, int K, int P,
+                                int El, int Tm, int src, int d_first, int d_count, const EpPeerPtrs& peers,
+                                const EpPeerLayout& L, unsigned* counter, const uint32_t* epoch_p, int max_ctas,
+                                cudaStream_t s);
+// Source-side bookkeeping of a step: the row of every (token t, rank d) partial
+// sum in this rank's ret_y (slot_out[t * P + d], -1: no expert of t on d) and,
+// when self_idx is given, this rank's own share of its tokens as a given
+// routing (self_idx[t][k] = local expert id or -1, self_w the weight or 0);
+// with self_direct the own partial sums sit in region 0 at row t, otherwise at
+// the row the token was sent to.
+cudaError_t ep_peer_local_launch(const int32_t* idx, const float* w, const int32_t* slot_in,
+                                 const int32_t* rank_offsets, int T, int K, int P, int El, int Tm, int src,
+                                 bool self_direct, int32_t* slot_out, int32_t* self_idx, float* self_w, cudaStream_t s);
 // epoch := value when nonzero, else epoch + 1 (device-side step count)
 cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s);
-cudaError_t ep_peer_wait_launch(const uint32_t* flags, int P, const uint32_t* epoch_p, int* status,
+// Waits (bounded by budget_cycles) until flags[0 .. n) all hold the epoch.
+cudaError_t ep_peer_wait_launch(const uint32_t* flags, int n, const uint32_t* epoch_p, int* status,
                                 long long budget_cycles, cudaStream_t s);
-cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int P, int Tm, int K, cudaStream_t s);
-cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int rows, int K, int H, int Tm,
-                                   int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P, unsigned* counter,
-                                   const uint32_t* epoch_p, cudaStream_t s);
+// Regions q0 .. q0 + nq - 1 (slots from region q0 on): rows past counts[q] get empty slots.
+cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int q0, int nq, int Tm, int K, cudaStream_t s);
+// Receiver: the weighted sums of rows [0, nq * Tm) of regions q0 .. q0 + nq - 1
+// (row r: region q0 + r / Tm, row r % Tm) stored into the sources' ret_y, and
+// their result flags raised.
+cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int q0, int nq, int K, int H,
+                                   int Tm, int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P,
+                                   unsigned* counter, const uint32_t* epoch_p, int max_ctas, cudaStream_t s);
 
 // counts[e] = offsets[e+1] - offsets[e]
 cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s);

@@ -114,10 +114,13 @@ def test_given_routing_block_skips_empty_slots():
     assert oracle.normwise_rel_err(out, ref) < 2e-2 and oracle.cosine(out, ref) > 0.999
 
 
-def test_peer_ep_single_rank_equals_block():
-    """The peer-memory EP block as a single rank (rows sent to itself, epoch
-    flags, masking of rows left from an earlier, larger step) equals the
-    single-GPU block bit for bit, step after step."""
+@pytest.mark.parametrize("overlap", [1, 0])
+def test_peer_ep_single_rank_equals_block(overlap):
+    """The peer-memory EP block as a single rank equals the single-GPU block bit
+    for bit, step after step: in the overlapped schedule (its own tokens'
+    block straight from x) and in the one-block schedule (rows sent to itself,
+    epoch flags, masking of rows left from an earlier, larger step)."""
+    _lib.set_option("ep_overlap", overlap)
     from nki_moe_b200.ep_peer import PeerExpertParallelMoE
     from nki_moe_b200.nki_moe_integrated import NKIMoESimple
 
@@ -139,6 +142,7 @@ def test_peer_ep_single_rank_equals_block():
             assert torch.equal(y, ref), f"step {step}: max diff {(y.float() - ref.float()).abs().max().item()}"
     finally:
         peer.close()
+        _lib.set_option("ep_overlap", 1)
 
 
 def _free_port():
@@ -180,6 +184,14 @@ def _ep_worker(rank, world, port, out_dir):
     y_peer1 = peer(x)
     y_peer2 = peer(x2)
     assert ops.read_status(ops.workspace(x.device, 1)) == 0  # no bounded wait ran out
+    # the one-block schedule, then back to the overlapped one; a rank may take
+    # either schedule whatever the other takes
+    _lib.set_option("ep_overlap", 0)
+    y_peer1b = peer(x)
+    _lib.set_option("ep_overlap", rank % 2)
+    y_peer2b = peer(x2)
+    _lib.set_option("ep_overlap", 1)
+    assert ops.read_status(ops.workspace(x.device, 1)) == 0
     y_dedup2 = ExpertParallelMoE.from_dense(moe, dedup=True)(x2)
     torch.cuda.synchronize()
     # rank 1 leaves a step (host side, between steps): rank 0's waits run out
@@ -202,6 +214,8 @@ def _ep_worker(rank, world, port, out_dir):
     assert ops.read_status(ops.workspace(x.device, 1)) == 0
     torch.cuda.synchronize()
     np.save(os.path.join(out_dir, f"peer3_{rank}.npy"), y_peer3.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"peer1b_{rank}.npy"), y_peer1b.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"peer2b_{rank}.npy"), y_peer2b.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"timeout{rank}.npy"), np.array([timed_out]))
     peer.close()
     np.save(os.path.join(out_dir, f"peer{rank}.npy"), y_peer1.float().cpu().numpy())
@@ -234,6 +248,9 @@ def test_expert_parallel_two_gpus_matches_single_gpu(tmp_path):
         # exchange computes (same rows, same order, same sums)
         assert np.array_equal(np.load(tmp_path / f"peer{r}.npy"), d), f"rank {r}: peer != dedup"
         assert np.array_equal(np.load(tmp_path / f"peer2_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
+        # the one-block schedule and a mix of schedules across the ranks
+        assert np.array_equal(np.load(tmp_path / f"peer1b_{r}.npy"), d)
+        assert np.array_equal(np.load(tmp_path / f"peer2b_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
         # after rank 1 left a step and the ranks resynchronised
         assert np.array_equal(np.load(tmp_path / f"peer3_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
     assert int(np.load(tmp_path / "timeout0.npy")[0]) == 1  # rank 0's step raised the wait timeout
