@@ -64,6 +64,7 @@ inline void mark(int stage, cudaStream_t s) {
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
+std::atomic<int> g_router_fused{1};  // tensor-core router: logits + top-k in one kernel (0: two kernels)
 std::atomic<int> g_stage_stores{3};  // rows-schedule epilogue staging: bit 0 SwiGLU, bit 1 scaled bf16
 std::atomic<int> g_gather_fused{0};  // GEMM-1 gathers its rows itself: 1 cp.async, 2 TMA gather4
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
@@ -229,7 +230,17 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
   float* logits = reinterpret_cast<float*>(base + L.logits);
   const bool tensor = router_uses_tensor_cores(router_w_split != nullptr, T, E);
   mark(kStageRouter, s);
-  if (tensor) {
+  if (tensor && g_router_fused.load() && router_topk_tc_supported(T, static_cast<int>(H), static_cast<int>(E),
+                                                                   static_cast<int>(K), false)) {
+    // logits, softmax and top-k in one tensor-core kernel (the same MMAs and
+    // sums as the two-kernel form below)
+    CUtensorMap tx, tw;
+    NKI_REQUIRE(make_tmap_bf16(&tx, x, T, H, 128) && make_tmap_bf16(&tw, router_w_split, 3 * E, H, 128),
+                NKIMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the router operands");
+    NKI_CUDA(router_topk_tc_launch(tx, tw, nullptr, nullptr, 0, 0.f, nullptr, router_bias, logits, T,
+                                   static_cast<int>(H), static_cast<int>(K), idx, w, status, s));
+    mark(kStageTopk, s);
+  } else if (tensor) {
     // the three bf16 planes are three "experts" over the same activation rows;
     // their fp32 partial logits [3][T][E] are added (hi + mid + lo) by top-k
     float* partial = reinterpret_cast<float*>(base + L.partial);
@@ -718,6 +729,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "router" && value >= 0 && value <= 2) {
     g_router = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "router_fused" && (value == 0 || value == 1)) {
+    g_router_fused = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "peer_wait_cycles" && value >= 1000 && value <= 1000000000000LL) {

@@ -274,6 +274,290 @@ __global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restri
   topk_select_warp<VPT>(v, E, K, lane, idx_out + t * K, w_out + t * K);
 }
 
+// Router + softmax + top-k of a prefill batch in one tensor-core kernel, with
+// an optional RMSNorm of the rows in front of it.  CTA = 128 rows; the fp32
+// router weights are three exact bf16 planes (hi, mid, lo; router_split_kernel)
+// and each plane has its own TMEM accumulator (3 x 128 columns).  The MMAs are
+// the ones of the separate router GEMM (M128 N128 K16, K ascending, one
+// accumulator per plane) and the logits the same ((hi + mid) + lo) + bias sums
+// topk_softmax_kernel forms, so idx, w and logits equal the separate kernels'
+// bit for bit.  With the norm, the A operand of every 64-wide K block is the
+// row block normalised by the CTA itself (rmsnorm_kernel's arithmetic: the
+// lane-chunk fp32 sum of squares of a warp per row, (x * rsqrt) * w rounded to
+// bf16), written to shared memory in the TMA 128-byte swizzle and to x_out for
+// the expert gather, so the normalised rows are produced once and consumed by
+// the router in the same pass (the reference's fused post-attention norm,
+// qwen_with_nki.py:379-382, :451-452).
+//   warps 0-3: row workers (norm, A blocks), then the epilogue (TMEM lanes
+//              32 w .. 32 w + 31 = rows; logits to shared memory; one warp-
+//              cooperative top-k per row)
+//   warp 4:    TMA producer (router planes; the x block without the norm)
+//   warp 5:    MMA issuer, TMEM owner
+constexpr int kRtRows = 128, kRtBK = 64, kRtE = 128, kRtStages = 3, kRtThreads = 192;
+constexpr uint32_t kRtABytes = kRtRows * kRtBK * 2;      // 16 KB
+constexpr uint32_t kRtBBytes = 3 * kRtE * kRtBK * 2;     // 48 KB: three planes
+constexpr uint32_t kRtStageBytes = kRtABytes + kRtBBytes;
+
+struct RtCtl {
+  uint64_t full[kRtStages], empty[kRtStages], afull[kRtStages];
+  uint64_t acc_full, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  float rinv[kRtRows];
+};
+
+__device__ __forceinline__ float rt_weight(const void* w, int w_dtype, int k) {
+  return w_dtype == 0 ? static_cast<const float*>(w)[k] : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[k]);
+}
+
+template <bool kNorm>
+__global__ void __launch_bounds__(kRtThreads, 1)
+    router_topk_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                          const __nv_bfloat16* __restrict__ h, const void* __restrict__ norm_w, int norm_w_dtype,
+                          float eps, __nv_bfloat16* __restrict__ x_out, const float* __restrict__ bias,
+                          float* __restrict__ logits_out, int T, int H, int K, int32_t* __restrict__ idx_out,
+                          float* __restrict__ w_out, int* status) {
+  extern __shared__ uint8_t rt_smem_raw[];
+  __shared__ RtCtl ctl;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row0 = static_cast<long long>(blockIdx.x) * kRtRows;
+  const int kblocks = H / kRtBK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRtStages; ++s) {
+      mbar_init(&ctl.full[s], 1);
+      mbar_init(&ctl.empty[s], 1);
+      mbar_init(&ctl.afull[s], 4 * 32);
+    }
+    mbar_init(&ctl.acc_full, 1);
+    mbar_init(&ctl.drain, 1);
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tmap_w);
+    if (!kNorm) prefetch_tmap(&tmap_x);
+  }
+  if (warp == 5) tmem_alloc(&ctl.tmem_base, 512);
+  if (kNorm && warp < 4) {
+    // sum of squares of each row as rmsnorm_kernel forms it: lane l adds the
+    // squares of chunks l + 32 i (8 bf16 each) in order, then a butterfly
+    for (int rl = warp; rl < kRtRows; rl += 4) {
+      const long long row = row0 + rl;
+      float ss = 0.f;
+      if (row < T) {
+        const __nv_bfloat16* xr = h + row * H;
+        float v[8][8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = lane + i * 32;
+          if (c < (H >> 3)) {
+            const uint4 u = *reinterpret_cast<const uint4*>(xr + c * 8);
+            const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), cc = unpack_bf16x2(u.z),
+                         d = unpack_bf16x2(u.w);
+            v[i][0] = a.x; v[i][1] = a.y; v[i][2] = b.x; v[i][3] = b.y;
+            v[i][4] = cc.x; v[i][5] = cc.y; v[i][6] = d.x; v[i][7] = d.y;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int c = lane + i * 32;
+          if (c < (H >> 3)) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+          }
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) ctl.rinv[rl] = rsqrtf(ss / static_cast<float>(H) + eps);
+    }
+  }
+  tcgen05_fence_before();
+  __syncthreads();
+  tcgen05_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued = 0, last = 0;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + stage * kRtStageBytes;
+        mbar_arrive_expect_tx(&ctl.full[stage], kNorm ? kRtBBytes : kRtStageBytes);
+        if (!kNorm) tma_load_2d(st, &tmap_x, &ctl.full[stage], kb * kRtBK, static_cast<int>(row0));
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+          tma_load_2d(st + kRtABytes + p * (kRtE * kRtBK * 2), &tmap_w, &ctl.full[stage], kb * kRtBK, p * kRtE);
+        issued |= 1u << stage;
+        last = (last & ~(1u << stage)) | (phase << stage);
+        if (++stage == kRtStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok)  // let copies in flight land before the CTA exits
+        for (int s = 0; s < kRtStages; ++s)
+          if ((issued >> s) & 1u) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&ctl.full[s], (last >> s) & 1u))
+              if (clock64() - t0 > kWaitBudgetCycles / 8) break;
+          }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(kRtRows, kRtE);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, any = false;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&ctl.full[stage], phase, &ctl.abort_flag, status) ||
+            (kNorm && !mbar_wait(&ctl.afull[stage], phase, &ctl.abort_flag, status))) {
+          ok = false;
+          break;
+        }
+        tcgen05_fence_after();
+        uint8_t* st = smem + stage * kRtStageBytes;
+        const uint64_t da = umma_desc_sw128(smem_u32(st));
+#pragma unroll
+        for (int p = 0; p < 3; ++p) {
+          const uint64_t db = umma_desc_sw128(smem_u32(st + kRtABytes + p * (kRtE * kRtBK * 2)));
+#pragma unroll
+          for (int kk = 0; kk < kRtBK / 16; ++kk)
+            umma_bf16(tmem_base + p * kRtE, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&ctl.empty[stage]);
+        any = true;
+        if (++stage == kRtStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) {
+        umma_commit(&ctl.acc_full);
+      } else if (any) {  // wait for issued MMAs before TMEM is released
+        umma_commit(&ctl.drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&ctl.drain, 0))
+          if (clock64() - t0 > kWaitBudgetCycles / 8) break;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ row workers
+    bool ok = true;
+    if (kNorm) {
+      // A block kb: thread t fills 16-byte chunk t % 8 of rows t / 8 + 16 i
+      const int c = threadIdx.x & 7;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int kb = 0; kb < kblocks && ok; ++kb) {
+        bool got = true;
+        if (lane == 0) got = mbar_wait(&ctl.empty[stage], phase ^ 1u, &ctl.abort_flag, status);
+        if (__shfl_sync(0xffffffffu, got ? 1 : 0, 0) == 0) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * kRtStageBytes;
+        const int k0 = kb * kRtBK + c * 8;
+        float wv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[j] = rt_weight(norm_w, norm_w_dtype, k0 + j);
+        uint4 in[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rl = (threadIdx.x >> 3) + 16 * i;
+          const long long row = row0 + rl;
+          in[i] = row < T ? *reinterpret_cast<const uint4*>(h + row * H + k0) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rl = (threadIdx.x >> 3) + 16 * i;
+          const long long row = row0 + rl;
+          uint4 o = make_uint4(0, 0, 0, 0);
+          if (row < T) {
+            const float r = ctl.rinv[rl];
+            const float2 a = unpack_bf16x2(in[i].x), b = unpack_bf16x2(in[i].y), cc = unpack_bf16x2(in[i].z),
+                         d = unpack_bf16x2(in[i].w);
+            o.x = pack_bf16x2(a.x * r * wv[0], a.y * r * wv[1]);
+            o.y = pack_bf16x2(b.x * r * wv[2], b.y * r * wv[3]);
+            o.z = pack_bf16x2(cc.x * r * wv[4], cc.y * r * wv[5]);
+            o.w = pack_bf16x2(d.x * r * wv[6], d.y * r * wv[7]);
+            *reinterpret_cast<uint4*>(x_out + row * H + k0) = o;
+          }
+          *reinterpret_cast<uint4*>(sa + rl * 128 + ((c ^ (rl & 7)) << 4)) = o;
+        }
+        fence_proxy_async_shared();  // generic-proxy writes -> tensor-core reads
+        mbar_arrive(&ctl.afull[stage]);
+        if (++stage == kRtStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // ------------------------------------------------------------ epilogue
+    bool got = ok;
+    if (got && lane == 0) got = mbar_wait(&ctl.acc_full, 0, &ctl.abort_flag, status);
+    got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+    if (got) {
+      tcgen05_fence_after();
+      // every MMA has completed: the stages are free; logits staged as
+      // [128 rows][129] fp32 (padded: conflict-free row and column access)
+      float* stg = reinterpret_cast<float*>(smem);
+      const int rl = warp * 32 + lane;
+      const long long row = row0 + rl;
+      const uint32_t tl = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < kRtE; c0 += 32) {
+        uint32_t a[32], b[32], d[32];
+        tmem_ld_32x32b_x32(tl + c0, a);
+        tmem_ld_32x32b_x32(tl + kRtE + c0, b);
+        tmem_ld_32x32b_x32(tl + 2 * kRtE + c0, d);
+        tmem_ld_wait();
+        float lg[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float acc = __uint_as_float(a[j]);
+          acc += __uint_as_float(b[j]);
+          acc += __uint_as_float(d[j]);
+          if (bias) acc += bias[c0 + j];
+          lg[j] = acc;
+          stg[rl * (kRtE + 1) + c0 + j] = acc;
+        }
+        if (logits_out && row < T) {
+          float4* dst = reinterpret_cast<float4*>(logits_out + row * kRtE + c0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) dst[q] = make_float4(lg[4 * q], lg[4 * q + 1], lg[4 * q + 2], lg[4 * q + 3]);
+        }
+      }
+      __syncwarp();
+      // one warp-cooperative top-k per row of this warp (topk_softmax_kernel's)
+      for (int i = 0; i < 32; ++i) {
+        const long long t = row0 + warp * 32 + i;
+        if (t >= T) break;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = stg[(warp * 32 + i) * (kRtE + 1) + lane + 32 * j];
+        topk_select_warp<4>(v, kRtE, K, lane, idx_out + t * K, w_out + t * K);
+      }
+    }
+  }
+  tcgen05_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tcgen05_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
 // Router + softmax + top-k for few tokens (decode), in one launch spread over
 // many SMs (the work is 2*T*H*E FLOP on E*H*4 bytes of weights, so a handful
 // of SMs would be compute-bound).  CTA (eb, s, g) computes fp32 partial
@@ -622,6 +906,48 @@ cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const
   else if (vpt <= 4) NKI_TOPK(4);
   else NKI_TOPK(8);
 #undef NKI_TOPK
+  return cudaGetLastError();
+}
+
+
+size_t router_topk_tc_smem_bytes() { return static_cast<size_t>(kRtStages) * kRtStageBytes + 1024; }
+
+bool router_topk_tc_supported(long long T, int H, int E, int K, bool norm) {
+  return E == kRtE && K >= 1 && K <= 32 && H % kRtBK == 0 && H >= kRtBK && T > 0 &&
+         (!norm || H <= 8 * 32 * 8);
+}
+
+cudaError_t router_topk_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
+                                  const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out,
+                                  const float* bias, float* logits_out, long long T, int H, int K, int32_t* idx,
+                                  float* w, int* status, cudaStream_t s) {
+  const bool norm = h != nullptr;
+  if (!router_topk_tc_supported(T, H, kRtE, K, norm) || (norm && (!norm_w || !x_out))) return cudaErrorInvalidValue;
+  const size_t smem = router_topk_tc_smem_bytes();
+  const unsigned grid = static_cast<unsigned>((T + kRtRows - 1) / kRtRows);
+  if (norm) {
+    static bool attr = false;
+    if (!attr) {
+      cudaError_t e = cudaFuncSetAttribute(router_topk_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      attr = true;
+    }
+    router_topk_tc_kernel<true><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out,
+                                                                bias, logits_out, static_cast<int>(T), H, K, idx, w,
+                                                                status);
+  } else {
+    static bool attr = false;
+    if (!attr) {
+      cudaError_t e = cudaFuncSetAttribute(router_topk_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      attr = true;
+    }
+    router_topk_tc_kernel<false><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr,
+                                                                 bias, logits_out, static_cast<int>(T), H, K, idx, w,
+                                                                 status);
+  }
   return cudaGetLastError();
 }
 

@@ -702,3 +702,26 @@ def test_invalid_shapes_raise():
     assert ei.value.code == _lib.ERR_UNSUPPORTED
     with pytest.raises(ValueError):
         ops.rmsnorm(torch.zeros(4, 128), torch.ones(128))  # CPU tensors: no CPU path
+
+
+@pytest.mark.parametrize("T", [256, 300, 8192])
+def test_fused_tensor_core_router_equals_two_kernels(T):
+    """The one-kernel tensor-core router (logits, softmax and top-k with the
+    logits kept in shared memory) issues the same MMAs and sums as the router
+    GEMM + top-k kernels: routing indices and weights identical bit for bit,
+    with and without a router bias, on full and ragged row tiles."""
+    g = torch.Generator().manual_seed(T)
+    x = torch.randn(T, 2048, generator=g).bfloat16().cuda()
+    rw = (torch.randn(128, 2048, generator=g) * 0.02).cuda()
+    bias = (torch.randn(128, generator=g) * 0.1).cuda()
+    for b in (None, bias):
+        outs = []
+        for fused in (1, 0):
+            _lib.set_option("router_fused", fused)
+            try:
+                outs.append(ops.route(x, rw, 8, bias=b))
+            finally:
+                _lib.set_option("router_fused", 1)
+        (i1, w1), (i0, w0) = outs
+        assert torch.equal(i1, i0)
+        assert torch.equal(w1.view(torch.int32), w0.view(torch.int32))
