@@ -71,6 +71,8 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * "epilogue_staging" (prefill GEMM bf16 outputs written through a per-warp
  * shared-memory tile as whole-sector row stores: bit 0 the SwiGLU output,
  * bit 1 the routing-weight-scaled output; default 3),
+ * "router_fused" (1, the default: the tensor-core router computes logits,
+ * softmax and top-k in one kernel; 0: router GEMM, then the top-k kernel),
  * "pdl" (1, the default: the decode-path kernels are launched with
  * programmatic dependent launch, so a kernel's launch and prologue overlap
  * the previous kernel in the stream; 0 = plain launches),
@@ -249,6 +251,25 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
                                             int norm_w_dtype, float eps, void* norm_out, int32_t* topk_idx_out,
                                             float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
                                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* The block with the post-attention RMSNorm inside it: x = rmsnorm(h) *
+ * norm_w (bf16, as nkimoe_rmsnorm), then nkimoe_moe_block on x.  This is the
+ * reference's fused-norm MoE (qwen_with_nki.py:379-382 passes
+ * post_attention_layernorm into the MoE module when moe_fused_nki_kernel_enabled,
+ * and :451-452 then skips the decoder's own norm call).  For prefill batches
+ * (more than 512 tokens, router_w_split given, 128 experts) the norm, the router
+ * logits and the top-k run as one tensor-core kernel that writes the
+ * normalised rows once and routes them in the same pass; smaller batches run
+ * the RMSNorm kernel and then the router.  Either way the results equal
+ * nkimoe_rmsnorm + nkimoe_moe_block bit for bit.  x_out [T, H] bf16 (device,
+ * may be NULL: the rows then stay in the workspace); norm_w_dtype F32 or
+ * BF16; workspace nkimoe_moe_block_rmsnorm_workspace_bytes. */
+NKIMOE_API size_t nkimoe_moe_block_rmsnorm_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K);
+NKIMOE_API int nkimoe_moe_block_rmsnorm(const void* h, const void* norm_w, int norm_w_dtype, float eps, void* x_out,
+                                        const float* router_w, const float* router_bias, const void* router_w_split,
+                                        const void* w13, const void* w2, void* out, int32_t* topk_idx_out,
+                                        float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* Whole block on HOST buffers: NKIMoESimple called on a host tensor
  * (test_nki_moe.py:146-151 runs the module on hidden_states created on the

@@ -53,6 +53,9 @@ SIGNATURES = {
                               _vp]),
     "nkimoe_moe_block_add_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _f, _vp, _vp, _vp, _i64,
                                           _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "nkimoe_moe_block_rmsnorm_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "nkimoe_moe_block_rmsnorm": (_i, [_vp, _vp, _i, _f, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                      _i64, _i64, _vp, _sz, _vp]),
     "nkimoe_moe_block_host_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "nkimoe_moe_block_host_plan": (_i, [_i64, _i64, _i64, _i, _i64, _vp, _vp]),
     "nkimoe_moe_block_host": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,

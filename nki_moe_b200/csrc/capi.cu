@@ -974,6 +974,61 @@ int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w, const flo
                         I, E, K, workspace, workspace_bytes, stream, &fn);
 }
 
+size_t nkimoe_moe_block_rmsnorm_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K) {
+  if (T < 0 || H <= 0) return 0;
+  return nkimoe_moe_workspace_bytes(T, H, I, E, K) + round256(sizeof(uint16_t) * T * H);
+}
+
+int nkimoe_moe_block_rmsnorm(const void* h, const void* norm_w, int norm_w_dtype, float eps, void* x_out,
+                             const float* router_w, const float* router_bias, const void* router_w_split,
+                             const void* w13, const void* w2, void* out, int32_t* topk_idx_out, float* topk_w_out,
+                             int64_t T, int64_t H, int64_t I, int64_t E, int64_t K, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  int rc = check_moe_shapes(T, H, I, E, K);
+  if (rc != NKIMOE_OK) return rc;
+  NKI_REQUIRE(E <= 256, NKIMOE_ERR_UNSUPPORTED, "router top-k supports up to 256 experts");
+  const size_t need = nkimoe_moe_block_rmsnorm_workspace_bytes(T, H, I, E, K);
+  NKI_REQUIRE(workspace && workspace_bytes >= need, NKIMOE_ERR_WORKSPACE, "workspace %zu < %zu", workspace_bytes, need);
+  NKI_REQUIRE(aligned16(workspace), NKIMOE_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  NKI_REQUIRE(norm_w_dtype == NKIMOE_F32 || norm_w_dtype == NKIMOE_BF16, NKIMOE_ERR_INVALID_ARG,
+              "norm weight dtype must be F32 or BF16");
+  const cudaStream_t s = as_stream(stream);
+  NKI_CUDA(cudaMemsetAsync(workspace, 0, 256, s));  // status word and router counters
+  if (T == 0) return NKIMOE_OK;
+  NKI_REQUIRE(h && norm_w && router_w && w13 && w2 && out, NKIMOE_ERR_INVALID_ARG, "null pointer");
+  NKI_REQUIRE(aligned16(h) && aligned16(norm_w) && aligned16(router_w) && aligned16(w13) && aligned16(w2) &&
+                  aligned16(out) && (!x_out || aligned16(x_out)) && (!router_w_split || aligned16(router_w_split)),
+              NKIMOE_ERR_INVALID_ARG, "pointers must be 16-byte aligned");
+  const WsLayout L = ws_layout(T, H, I, E, K);
+  char* base = static_cast<char*>(workspace);
+  void* x = x_out ? x_out : base + nkimoe_moe_workspace_bytes(T, H, I, E, K);
+  int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(base + L.idx);
+  float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(base + L.w);
+  int* status = reinterpret_cast<int*>(base + L.status);
+  // Prefill batches on the tensor-core router: the norm, the logits and the
+  // top-k in one kernel that writes the normalised rows once.  (Up to 512 rows
+  // RMSNorm runs its one-CTA-per-row kernel, whose reduction order differs, so
+  // the fused kernel starts above that and stays bit-identical to the unfused
+  // calls.)  Otherwise: the RMSNorm kernel, then the router.
+  const bool fused = router_uses_tensor_cores(router_w_split != nullptr, T, E) && g_router_fused.load() && T > 512 &&
+                     router_topk_tc_supported(T, static_cast<int>(H), static_cast<int>(E), static_cast<int>(K), true);
+  if (fused) {
+    CUtensorMap tw;
+    NKI_REQUIRE(make_tmap_bf16(&tw, router_w_split, 3 * E, H, 128), NKIMOE_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed for the router planes");
+    mark(kStageRouter, s);
+    NKI_CUDA(router_topk_tc_launch(tw, tw, static_cast<const __nv_bfloat16*>(h), norm_w, norm_w_dtype, eps,
+                                   static_cast<__nv_bfloat16*>(x), router_bias, reinterpret_cast<float*>(base + L.logits),
+                                   T, static_cast<int>(H), static_cast<int>(K), idx, w, status, s));
+    mark(kStageTopk, s);
+  } else {
+    NKI_CUDA(rmsnorm_launch(h, NKIMOE_BF16, norm_w, norm_w_dtype, x, NKIMOE_BF16, T, static_cast<int>(H), eps, s));
+    rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, base, L, status, s);
+    if (rc != NKIMOE_OK) return rc;
+  }
+  return experts_impl(x, w13, w2, idx, NKIMOE_I32, w, out, T, H, I, E, K, workspace, workspace_bytes, s);
+}
+
 size_t nkimoe_moe_block_host_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K) {
   if (T < 0 || H <= 0 || E <= 0) return 0;
   return host_block_bytes(T, H, I, E, K) + 4 * host_stage_bytes(T, H);  // two slots of input + output rows

@@ -188,6 +188,18 @@ class NKIMoESimple(nn.Module):
                                 nn.Parameter(torch.randn(num_experts, intermediate_size, hidden_size, **kw)))
         # optional per-expert logit bias (synthetic skewed-routing workloads)
         self.router_bias: Optional[torch.Tensor] = None
+        # optional post-attention RMSNorm run inside the block (fuse_rmsnorm)
+        self.rmsnorm: Optional[nn.Module] = None
+
+    def fuse_rmsnorm(self, norm: nn.Module):
+        """Run ``norm`` (an ``NKIRMSNorm`` or any module with ``weight`` and
+        ``eps``/``variance_epsilon``) inside the block, as the reference's
+        fused MoE kernel takes ``post_attention_layernorm``
+        (qwen_with_nki.py:379-382; the decoder then skips its own norm call,
+        :451-452): ``forward(h)`` computes ``moe(norm(h))``.  Prefill batches
+        run the norm, the router and the top-k in one kernel."""
+        self.rmsnorm = norm
+        return self
 
     def packed(self) -> ops.PackedExperts:
         return ops.packed_experts(self.gate_up_proj, self.down_proj, "nxd")
@@ -196,6 +208,12 @@ class NKIMoESimple(nn.Module):
         B, S, H = hidden_states.shape
         x = hidden_states.reshape(-1, H)
         rw = self.router.weight.float()
+        if self.rmsnorm is not None:
+            eps = getattr(self.rmsnorm, "eps", getattr(self.rmsnorm, "variance_epsilon", 1e-6))
+            out = ops.moe_block_rmsnorm(ops._cuda(x, "hidden_states"), self.rmsnorm.weight, rw, self.packed(),
+                                        self.top_k, eps=float(eps), bias=self.router_bias)
+            out = out.to(_out_dtype(hidden_states)).view(B, S, H)
+            return (out,) if self.return_tuple else out
         if _host_batch(x, rw):
             out = ops.moe_block_host(x, rw, self.packed(), self.top_k, bias=self.router_bias)
         else:

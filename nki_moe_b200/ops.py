@@ -25,7 +25,7 @@ __all__ = [
     "grouped_gemm", "swiglu", "aggregate", "read_status", "workspace", "sync_check_enabled", "router_split",
     "route", "dispatch", "segment_experts", "combine", "ep_dispatch", "decode_attention", "skinny_linear",
     "moe_block_add_rmsnorm", "moe_block_host", "kmajor_weights",
-    "release_captured_workspaces",
+    "release_captured_workspaces", "moe_block_rmsnorm",
 ]
 
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.int32: I32, torch.int64: I64}
@@ -556,6 +556,45 @@ def moe_block_host(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExper
         elif not non_blocking and done is None:
             torch.cuda.current_stream(dev).synchronize()
     return (out, idx, w) if return_routing else out
+
+
+def moe_block_rmsnorm(h: torch.Tensor, norm_weight: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts,
+                      top_k: int, eps: float = 1e-6, bias: torch.Tensor | None = None, return_x: bool = False,
+                      return_routing: bool = False, router_w_split: torch.Tensor | None = None):
+    """The block with the RMSNorm in front of it inside the call:
+    ``moe_block(rmsnorm(h) * norm_weight)``, equal bit for bit to
+    :func:`rmsnorm` + :func:`moe_block`.  For prefill batches (more than 512
+    tokens, 128 experts) the norm, router logits and top-k are one
+    tensor-core kernel that writes the normalised rows once.  With
+    ``return_x`` also returns the normalised rows (bf16)."""
+    h = _contig(_cuda(h, "h"), torch.bfloat16)
+    rsplit = None
+    if router_w.shape[0] % 128 == 0:
+        rsplit = router_w_split if router_w_split is not None else router_split(router_w)
+    rw = _contig(_cuda(router_w, "router_w"), torch.float32)
+    wdt = torch.float32 if norm_weight.dtype == torch.float32 else torch.bfloat16
+    nw = _contig(_cuda(norm_weight, "norm_weight"), wdt)
+    b = _contig(bias, torch.float32) if bias is not None else None
+    T, H = h.shape
+    E, I = experts.num_experts, experts.inter
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=h.device)
+    x = torch.empty_like(h) if return_x else None
+    idx = w = None
+    if return_routing:
+        idx = torch.empty(T, top_k, dtype=torch.int32, device=h.device)
+        w = torch.empty(T, top_k, dtype=torch.float32, device=h.device)
+    nbytes = size_call("nkimoe_moe_block_rmsnorm_workspace_bytes", T, H, I, E, top_k)
+    ws = workspace(h.device, nbytes)
+    call("nkimoe_moe_block_rmsnorm", _p(h), _p(nw), _DT[wdt], float(eps), _p(x), _p(rw), _p(b), _p(rsplit),
+         _p(experts.w13), _p(experts.w2), _p(out), _p(idx), _p(w), T, H, I, E, top_k, _p(ws), ws.numel(), _s(h))
+    if sync_check_enabled():
+        read_status(ws)
+    res = (out,)
+    if return_x:
+        res += (x,)
+    if return_routing:
+        res += (idx, w)
+    return res if len(res) > 1 else out
 
 
 def moe_block_add_rmsnorm(x: torch.Tensor, router_w: torch.Tensor, experts: PackedExperts, top_k: int,

@@ -725,3 +725,40 @@ def test_fused_tensor_core_router_equals_two_kernels(T):
         (i1, w1), (i0, w0) = outs
         assert torch.equal(i1, i0)
         assert torch.equal(w1.view(torch.int32), w0.view(torch.int32))
+
+
+@pytest.mark.parametrize("T", [300, 2048, 8192])
+@pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16])
+def test_moe_block_with_fused_rmsnorm_equals_separate_calls(c1_inputs, T, wdt):
+    """The block with the post-attention RMSNorm inside the call equals
+    rmsnorm + block bit for bit: the normalised rows, the routing and the
+    output.  Above 512 tokens the norm, router logits and top-k are one
+    tensor-core kernel; at 300 tokens the norm kernel runs first."""
+    g = torch.Generator().manual_seed(T + 7)
+    h = (torch.randn(T, 2048, generator=g) * 3).bfloat16().cuda()
+    nw = (torch.rand(2048, generator=g) + 0.5).to(wdt).cuda()
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    out, x, idx, w = ops.moe_block_rmsnorm(h, nw, rw, pe, 8, eps=1e-6, return_x=True, return_routing=True)
+    x_ref = ops.rmsnorm(h, nw, 1e-6, out_dtype=torch.bfloat16)
+    ref, ridx, rwt = ops.moe_block(x_ref, rw, pe, 8, return_routing=True)
+    assert torch.equal(x, x_ref)
+    assert torch.equal(idx, ridx) and torch.equal(w.view(torch.int32), rwt.view(torch.int32))
+    assert torch.equal(out, ref)
+
+
+def test_module_with_fused_post_attention_norm(c1_inputs):
+    """NKIMoESimple.fuse_rmsnorm(norm): forward(h) = moe(norm(h)), as the
+    reference's fused MoE module receives post_attention_layernorm."""
+    from nki_moe_b200.nki_custom_rmsnorm import NKIRMSNorm
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+    moe = NKIMoESimple(2048, 768, 128, 8, device="cuda", dtype=torch.bfloat16)
+    norm = NKIRMSNorm(2048).cuda()
+    with torch.no_grad():
+        moe.router.weight.copy_(c1_inputs["router"])
+        norm.weight.copy_(torch.rand(2048, generator=torch.Generator().manual_seed(3)) + 0.5)
+    h = torch.randn(2, 1024, 2048, generator=torch.Generator().manual_seed(8)).bfloat16().cuda()
+    with torch.no_grad():
+        ref = moe(norm(h).bfloat16())
+        fused = moe.fuse_rmsnorm(norm)(h)
+    assert torch.equal(fused, ref)
