@@ -5,6 +5,8 @@
 //     qwen_with_nki.py:447-452).
 // K6: per-head q/k RMSNorm + rotate-half RoPE on a fused [Q | K | V] row
 //     (qwen_with_nki.py:330-350 with the HF Qwen3-MoE order: norm, then RoPE).
+#include <type_traits>
+
 #include "kernels.h"
 #include "rope.cuh"
 
@@ -46,6 +48,108 @@ __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
 // Rows of up to kMaxChunks*8*32 elements are held in registers (one pass over
 // HBM); longer rows are re-read from L2 for the second pass.
 constexpr int kMaxChunks = 8;  // 2048 elements per row in registers
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+
+// bf16 rows: the register-held part of a row stays packed (4 registers per 8
+// elements instead of 8), so more warps fit on an SM and more of the rows'
+// loads are in flight; the arithmetic and its order are those of the generic
+// kernel below.
+template <typename TW, typename TO, bool kResidual>
+__global__ void __launch_bounds__(256, 3) rmsnorm_bf16_kernel(const __nv_bfloat16* x, const __nv_bfloat16* residual,
+                                                           __nv_bfloat16* residual_out, const TW* __restrict__ w,
+                                                           TO* out, long long rows, int hidden, float eps) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nchunk = hidden >> 3;
+  const __nv_bfloat16* xr = x + row * hidden;
+  uint4 p[kMaxChunks];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) p[i] = *reinterpret_cast<const uint4*>(xr + c * 8);
+  }
+  if constexpr (kResidual) {
+    uint4 q[kMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = lane + i * 32;
+      if (c < nchunk) q[i] = *reinterpret_cast<const uint4*>(residual + row * hidden + c * 8);
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxChunks; ++i) {
+      const int c = lane + i * 32;
+      if (c < nchunk) {
+        float v[8], r[8];
+        unpack8(p[i], v);
+        unpack8(q[i], r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += r[j];
+        // the sum is rounded to the residual stream's dtype before the norm
+        p[i].x = pack_bf16x2(v[0], v[1]);
+        p[i].y = pack_bf16x2(v[2], v[3]);
+        p[i].z = pack_bf16x2(v[4], v[5]);
+        p[i].w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(residual_out + row * hidden + c * 8) = p[i];
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) {
+      float v[8];
+      unpack8(p[i], v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+    }
+  }
+  for (int c = lane + kMaxChunks * 32; c < nchunk; c += 32) {
+    float t[8];
+    if constexpr (kResidual) {
+      float r[8];
+      load8(xr + c * 8, t);
+      load8(residual + row * hidden + c * 8, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] += r[j];
+      round_bf16(t);
+      store8(residual_out + row * hidden + c * 8, t);
+    } else {
+      load8(xr + c * 8, t);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(t[j], t[j], ss);
+  }
+  ss = warp_sum(ss);
+  const float rinv = rsqrtf(ss / static_cast<float>(hidden) + eps);
+  TO* orow = out + row * hidden;
+#pragma unroll
+  for (int i = 0; i < kMaxChunks; ++i) {
+    const int c = lane + i * 32;
+    if (c < nchunk) {
+      float v[8], wv[8], o[8];
+      unpack8(p[i], v);
+      load8(w + c * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[j] * rinv * wv[j];
+      store8(orow + c * 8, o);
+    }
+  }
+  const __nv_bfloat16* src = kResidual ? residual_out + row * hidden : xr;
+  for (int c = lane + kMaxChunks * 32; c < nchunk; c += 32) {
+    float t[8], wv[8];
+    load8(src + c * 8, t);
+    load8(w + c * 8, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = t[j] * rinv * wv[j];
+    store8(orow + c * 8, t);
+  }
+}
 
 template <typename TX, typename TW, typename TO, bool kResidual>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const TX* x, const TX* residual, TX* residual_out,
@@ -310,6 +414,12 @@ cudaError_t launch_rms(const void* x, const void* res, void* res_out, const void
   }
   const int warps = 8;
   const long long blocks = (rows + warps - 1) / warps;
+  if constexpr (std::is_same<TX, __nv_bfloat16>::value) {
+    rmsnorm_bf16_kernel<TW, TO, kRes><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(
+        static_cast<const TX*>(x), static_cast<const TX*>(res), static_cast<TX*>(res_out),
+        static_cast<const TW*>(w), static_cast<TO*>(out), rows, hidden, eps);
+    return cudaGetLastError();
+  }
   rmsnorm_kernel<TX, TW, TO, kRes><<<static_cast<unsigned>(blocks), warps * 32, 0, s>>>(
       static_cast<const TX*>(x), static_cast<const TX*>(res), static_cast<TX*>(res_out),
       static_cast<const TW*>(w), static_cast<TO*>(out), rows, hidden, eps);
@@ -368,27 +478,44 @@ cudaError_t add_rmsnorm_launch(const void* x, const void* residual, void* residu
 // [4l, 4l+4); its rotate-half partner lives in lane l ^ 16.
 namespace {
 
+// One warp per token: the RoPE cos / sin of the lane's 4 elements are computed
+// once (powf + sincosf are the kernel's costly part) and serve all the
+// token's q and k heads; heads are loaded kAhead at a time so their loads are
+// in flight together.  Each head's arithmetic is norm_rope_head128's.
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, const void* qw,
                                                            const void* kw, int w_dtype,
                                                            const long long* __restrict__ positions, long long tokens,
                                                            int n_heads, int n_kv, float theta, float eps) {
   constexpr int D = kHeadDim;
+  constexpr int kAhead = 4;
   const int lane = threadIdx.x & 31;
   const int heads_total = n_heads + 2 * n_kv;
-  const long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (gw >= tokens * heads_total) return;
-  const long long t = gw / heads_total;
-  const int h = static_cast<int>(gw % heads_total);
-  const long long base = t * heads_total * D + static_cast<long long>(h) * D + lane * 4;
-  float v[4];
-  head_load4(in + base, v);
-  if (h >= n_heads + n_kv) {  // V head: pass through
-    if (in != out) *reinterpret_cast<uint2*>(out + base) = *reinterpret_cast<const uint2*>(in + base);
-    return;
+  const long long t = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  const long long row = t * heads_total * D + lane * 4;
+  float cs[4], sn[4];
+  rope_cs_lane(static_cast<float>(positions[t]), theta, lane, cs, sn);
+  for (int h0 = 0; h0 < heads_total; h0 += kAhead) {
+    uint2 raw[kAhead];
+#pragma unroll
+    for (int a = 0; a < kAhead; ++a)
+      if (h0 + a < heads_total) raw[a] = *reinterpret_cast<const uint2*>(in + row + static_cast<long long>(h0 + a) * D);
+#pragma unroll
+    for (int a = 0; a < kAhead; ++a) {
+      const int h = h0 + a;
+      if (h >= heads_total) break;
+      __nv_bfloat16* dst = out + row + static_cast<long long>(h) * D;
+      if (h >= n_heads + n_kv) {  // V head: pass through
+        if (in != out) *reinterpret_cast<uint2*>(dst) = raw[a];
+        continue;
+      }
+      const float2 x0 = unpack_bf16x2(raw[a].x), x1 = unpack_bf16x2(raw[a].y);
+      const float v[4] = {x0.x, x0.y, x1.x, x1.y};
+      float o[4];
+      norm_rope_head128_cs(v, h < n_heads ? qw : kw, w_dtype, eps, lane, cs, sn, o);
+      head_store4(dst, o);
+    }
   }
-  float o[4];
-  norm_rope_head128(v, h < n_heads ? qw : kw, w_dtype, static_cast<float>(positions[t]), theta, eps, lane, o);
-  head_store4(out + base, o);
 }
 
 }  // namespace
@@ -398,9 +525,8 @@ cudaError_t qk_norm_rope_launch(const void* qkv_in, void* qkv_out, const void* q
                                 float theta, float eps, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   if (head_dim != 128) return cudaErrorInvalidValue;
-  const long long warps_total = tokens * (n_heads + 2 * n_kv);
-  const int wpb = 8;
-  const long long blocks = (warps_total + wpb - 1) / wpb;
+  const int wpb = 8;  // one warp per token
+  const long long blocks = (tokens + wpb - 1) / wpb;
   qk_norm_rope_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, s>>>(
       static_cast<const __nv_bfloat16*>(qkv_in), static_cast<__nv_bfloat16*>(qkv_out), qw, kw, w_dtype, positions,
       tokens, n_heads, n_kv, theta, eps);

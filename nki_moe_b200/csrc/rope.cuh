@@ -57,15 +57,29 @@ __device__ __forceinline__ void head_rope(const float (&v)[4], const float (&cs)
   }
 }
 
+// cos / sin of this lane's 4 elements at position `pos` (the same for every
+// head of a token).
+__device__ __forceinline__ void rope_cs_lane(float pos, float theta, int lane, float (&cs)[4], float (&sn)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) rope_cs(pos, (lane * 4 + j) & (kHeadDim / 2 - 1), theta, cs[j], sn[j]);
+}
+
+// norm_rope_head128 with the lane's cos / sin given (computed once per token).
+__device__ __forceinline__ void norm_rope_head128_cs(const float (&v_in)[4], const void* w, int w_dtype, float eps,
+                                                     int lane, const float (&cs)[4], const float (&sn)[4],
+                                                     float (&o)[4]) {
+  float v[4];
+  head_rmsnorm(v_in, w, w_dtype, eps, lane, v);
+  head_rope(v, cs, sn, lane, o);
+}
+
 // v: this lane's 4 elements of one head; returns the normalised, weighted and
 // rotated values in o.  All 32 lanes of the warp must call it.
 __device__ __forceinline__ void norm_rope_head128(const float (&v_in)[4], const void* w, int w_dtype, float pos,
                                                   float theta, float eps, int lane, float (&o)[4]) {
-  float v[4], cs[4], sn[4];
-  head_rmsnorm(v_in, w, w_dtype, eps, lane, v);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) rope_cs(pos, (lane * 4 + j) & (kHeadDim / 2 - 1), theta, cs[j], sn[j]);
-  head_rope(v, cs, sn, lane, o);
+  float cs[4], sn[4];
+  rope_cs_lane(pos, theta, lane, cs, sn);
+  norm_rope_head128_cs(v_in, w, w_dtype, eps, lane, cs, sn, o);
 }
 
 __device__ __forceinline__ void head_store4(__nv_bfloat16* p, const float (&o)[4]) {

@@ -310,6 +310,70 @@ __device__ __forceinline__ float rt_weight(const void* w, int w_dtype, int k) {
   return w_dtype == 0 ? static_cast<const float*>(w)[k] : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[k]);
 }
 
+// topk_select_warp for one row held by one thread (the row's 128 logits in
+// shared memory): the same maximum, the same per-lane sums of exp(v - max)
+// over experts l, l + 32, l + 64, l + 96 added by the same butterfly, the same
+// selection (by logit, ties to the lower id) and the same butterfly sum of the
+// K probabilities, so idx and w are bit-identical to the warp version.
+__device__ __forceinline__ float rt_butterfly32(float (&t)[32]) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float u[32];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) u[l] = t[l] + t[l ^ o];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) t[l] = u[l];
+  }
+  return t[0];
+}
+
+__device__ __forceinline__ void rt_topk_row(const float* lg, int K, int32_t* idx_row, float* w_row) {
+  float m = -INFINITY;
+  for (int e = 0; e < kRtE; ++e) m = fmaxf(m, lg[e]);
+  float t[32];
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    float sl = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRtE / 32; ++j) sl += expf(lg[l + 32 * j] - m);
+    t[l] = sl;
+  }
+  const float ssum = rt_butterfly32(t);
+  uint32_t taken[kRtE / 32] = {};
+  float p[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) p[r] = 0.f;
+  for (int r = 0; r < K; ++r) {
+    uint32_t best = 0u;
+    int win = 0;
+    for (int e = 0; e < kRtE; ++e) {
+      if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
+      const uint32_t k = order_key(lg[e]);
+      if (k > best) {  // ascending ids: an equal key keeps the lower id
+        best = k;
+        win = e;
+      }
+    }
+    taken[win >> 5] |= 1u << (win & 31);
+    const uint32_t bits = (best & 0x80000000u) ? (best & 0x7fffffffu) : ~best;
+    idx_row[r] = win;
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q == r) p[q] = expf(__uint_as_float(bits) - m) / ssum;
+  }
+  float tt[32];
+#pragma unroll
+  for (int q = 0; q < 32; ++q) tt[q] = p[q];
+  const float tot = rt_butterfly32(tt);
+  for (int r = 0; r < K; ++r) {
+    float pr = 0.f;
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q == r) pr = p[q];
+    w_row[r] = pr / tot;
+  }
+}
+
 template <bool kNorm>
 __global__ void __launch_bounds__(kRtThreads, 1)
     router_topk_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -539,15 +603,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
         }
       }
       __syncwarp();
-      // one warp-cooperative top-k per row of this warp (topk_softmax_kernel's)
-      for (int i = 0; i < 32; ++i) {
-        const long long t = row0 + warp * 32 + i;
-        if (t >= T) break;
-        float v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = stg[(warp * 32 + i) * (kRtE + 1) + lane + 32 * j];
-        topk_select_warp<4>(v, kRtE, K, lane, idx_out + t * K, w_out + t * K);
-      }
+      if (row < T) rt_topk_row(stg + rl * (kRtE + 1), K, idx_out + row * K, w_out + row * K);
     }
   }
   tcgen05_fence_before();
