@@ -339,39 +339,53 @@ __device__ __forceinline__ void rt_topk_row(const float* lg, int K, int32_t* idx
     t[l] = sl;
   }
   const float ssum = rt_butterfly32(t);
-  uint32_t taken[kRtE / 32] = {};
-  float p[32];
+  // the K largest (by logit, ties to the lower id): one pass over the experts
+  // in ascending id keeping a sorted list; a new key goes in front of the
+  // first strictly smaller one, so equal keys keep ascending ids
+  constexpr int kList = 8;
+  uint32_t lk[kList];
+  int li[kList];
 #pragma unroll
-  for (int r = 0; r < 32; ++r) p[r] = 0.f;
-  for (int r = 0; r < K; ++r) {
-    uint32_t best = 0u;
-    int win = 0;
-    for (int e = 0; e < kRtE; ++e) {
-      if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
-      const uint32_t k = order_key(lg[e]);
-      if (k > best) {  // ascending ids: an equal key keeps the lower id
-        best = k;
-        win = e;
+  for (int q = 0; q < kList; ++q) {
+    lk[q] = 0u;
+    li[q] = 0;
+  }
+  const int kk = K < kList ? K : kList;
+  for (int e = 0; e < kRtE; ++e) {
+    uint32_t k = order_key(lg[e]);
+    if (k <= lk[kk - 1]) continue;
+    int id = e;
+#pragma unroll
+    for (int q = 0; q < kList; ++q) {
+      if (q < kk && k > lk[q]) {
+        const uint32_t tk = lk[q];
+        const int ti = li[q];
+        lk[q] = k;
+        li[q] = id;
+        k = tk;
+        id = ti;
       }
     }
-    taken[win >> 5] |= 1u << (win & 31);
-    const uint32_t bits = (best & 0x80000000u) ? (best & 0x7fffffffu) : ~best;
-    idx_row[r] = win;
+  }
+  float p[32];
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (q == r) p[q] = expf(__uint_as_float(bits) - m) / ssum;
+  for (int q = 0; q < 32; ++q) {
+    p[q] = 0.f;
+    if (q < kk) {
+      const uint32_t bits = (lk[q] & 0x80000000u) ? (lk[q] & 0x7fffffffu) : ~lk[q];
+      p[q] = expf(__uint_as_float(bits) - m) / ssum;
+    }
   }
   float tt[32];
 #pragma unroll
   for (int q = 0; q < 32; ++q) tt[q] = p[q];
   const float tot = rt_butterfly32(tt);
-  for (int r = 0; r < K; ++r) {
-    float pr = 0.f;
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (q == r) pr = p[q];
-    w_row[r] = pr / tot;
-  }
+  for (int q = 0; q < kList; ++q)
+    if (q < kk) {
+      idx_row[q] = li[q];
+      w_row[q] = p[q] / tot;
+    }
 }
 
 template <bool kNorm>
@@ -969,7 +983,7 @@ cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const
 size_t router_topk_tc_smem_bytes() { return static_cast<size_t>(kRtStages) * kRtStageBytes + 1024; }
 
 bool router_topk_tc_supported(long long T, int H, int E, int K, bool norm) {
-  return E == kRtE && K >= 1 && K <= 32 && H % kRtBK == 0 && H >= kRtBK && T > 0 &&
+  return E == kRtE && K >= 1 && K <= 8 && H % kRtBK == 0 && H >= kRtBK && T > 0 &&
          (!norm || H <= 8 * 32 * 8);
 }
 
