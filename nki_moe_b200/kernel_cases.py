@@ -62,10 +62,13 @@ def run_norms(device):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all", choices=["block", "norms", "all"])
+    ap.add_argument("--router-fused", type=int, default=1, choices=[0, 1],
+                    help="tensor-core router: logits + top-k in one kernel (1) or two (0)")
     a = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("needs a CUDA device")
     _lib.load()
+    _lib.set_option("router_fused", a.router_fused)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     if a.case in ("block", "all"):
