@@ -71,8 +71,10 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * "epilogue_staging" (prefill GEMM bf16 outputs written through a per-warp
  * shared-memory tile as whole-sector row stores: bit 0 the SwiGLU output,
  * bit 1 the routing-weight-scaled output; default 3),
- * "router_fused" (1, the default: the tensor-core router computes logits,
- * softmax and top-k in one kernel; 0: router GEMM, then the top-k kernel),
+ * "router_fused" (1, the default: the tensor-core router forms the summed
+ * fp32 logits of its three weight planes in one kernel before the top-k;
+ * 0: the grouped GEMM writes the three planes' partials, which the top-k
+ * kernel adds),
  * "pdl" (1, the default: the decode-path kernels are launched with
  * programmatic dependent launch, so a kernel's launch and prologue overlap
  * the previous kernel in the stream; 0 = plain launches),
@@ -257,10 +259,10 @@ NKIMOE_API int nkimoe_moe_block_add_rmsnorm(const void* x, const float* router_w
  * reference's fused-norm MoE (qwen_with_nki.py:379-382 passes
  * post_attention_layernorm into the MoE module when moe_fused_nki_kernel_enabled,
  * and :451-452 then skips the decoder's own norm call).  For prefill batches
- * (more than 512 tokens, router_w_split given, 128 experts) the norm, the router
- * logits and the top-k run as one tensor-core kernel that writes the
- * normalised rows once and routes them in the same pass; smaller batches run
- * the RMSNorm kernel and then the router.  Either way the results equal
+ * (more than 512 tokens, router_w_split given, 128 experts) the norm and the
+ * router logits run as one tensor-core kernel that writes the normalised rows
+ * once and routes them in the same pass (the top-k kernel follows); smaller
+ * batches run the RMSNorm kernel and then the router.  Either way the results equal
  * nkimoe_rmsnorm + nkimoe_moe_block bit for bit.  x_out [T, H] bf16 (device,
  * may be NULL: the rows then stay in the workspace); norm_w_dtype F32 or
  * BF16; workspace nkimoe_moe_block_rmsnorm_workspace_bytes. */

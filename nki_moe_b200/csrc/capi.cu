@@ -64,7 +64,7 @@ inline void mark(int stage, cudaStream_t s) {
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
-std::atomic<int> g_router_fused{1};  // tensor-core router: logits + top-k in one kernel (0: two kernels)
+std::atomic<int> g_router_fused{1};  // tensor-core router: summed logits in one kernel (0: GEMM partials)
 std::atomic<int> g_stage_stores{3};  // rows-schedule epilogue staging: bit 0 SwiGLU, bit 1 scaled bf16
 std::atomic<int> g_gather_fused{0};  // GEMM-1 gathers its rows itself: 1 cp.async, 2 TMA gather4
 std::atomic<int> g_prefetch{0};      // L2 prefetch distance of the rows-schedule GEMMs, in k-blocks
@@ -230,16 +230,17 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
   float* logits = reinterpret_cast<float*>(base + L.logits);
   const bool tensor = router_uses_tensor_cores(router_w_split != nullptr, T, E);
   mark(kStageRouter, s);
-  if (tensor && g_router_fused.load() && router_topk_tc_supported(T, static_cast<int>(H), static_cast<int>(E),
-                                                                   static_cast<int>(K), false)) {
-    // logits, softmax and top-k in one tensor-core kernel (the same MMAs and
-    // sums as the two-kernel form below)
+  if (tensor && g_router_fused.load() && router_tc_supported(T, static_cast<int>(H), static_cast<int>(E), false)) {
+    // the three planes' logits summed in one tensor-core kernel (the same MMAs
+    // and sums as the router GEMM + partials form below), then the top-k
     CUtensorMap tx, tw;
     NKI_REQUIRE(make_tmap_bf16(&tx, x, T, H, 128) && make_tmap_bf16(&tw, router_w_split, 3 * E, H, 128),
                 NKIMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the router operands");
-    NKI_CUDA(router_topk_tc_launch(tx, tw, nullptr, nullptr, 0, 0.f, nullptr, router_bias, logits, T,
-                                   static_cast<int>(H), static_cast<int>(K), idx, w, status, s));
+    NKI_CUDA(router_tc_launch(tx, tw, nullptr, nullptr, 0, 0.f, nullptr, router_bias, logits, T, static_cast<int>(H),
+                              status, s));
     mark(kStageTopk, s);
+    NKI_CUDA(topk_softmax_partials_launch(logits, 1, nullptr, nullptr, static_cast<int>(T), static_cast<int>(E),
+                                          static_cast<int>(K), idx, w, s));
   } else if (tensor) {
     // the three bf16 planes are three "experts" over the same activation rows;
     // their fp32 partial logits [3][T][E] are added (hi + mid + lo) by top-k
@@ -1005,22 +1006,24 @@ int nkimoe_moe_block_rmsnorm(const void* h, const void* norm_w, int norm_w_dtype
   int32_t* idx = topk_idx_out ? topk_idx_out : reinterpret_cast<int32_t*>(base + L.idx);
   float* w = topk_w_out ? topk_w_out : reinterpret_cast<float*>(base + L.w);
   int* status = reinterpret_cast<int*>(base + L.status);
-  // Prefill batches on the tensor-core router: the norm, the logits and the
-  // top-k in one kernel that writes the normalised rows once.  (Up to 512 rows
+  // Prefill batches on the tensor-core router: the norm and the logits in one
+  // kernel that writes the normalised rows once, then the top-k.  (Up to 512 rows
   // RMSNorm runs its one-CTA-per-row kernel, whose reduction order differs, so
   // the fused kernel starts above that and stays bit-identical to the unfused
   // calls.)  Otherwise: the RMSNorm kernel, then the router.
   const bool fused = router_uses_tensor_cores(router_w_split != nullptr, T, E) && g_router_fused.load() && T > 512 &&
-                     router_topk_tc_supported(T, static_cast<int>(H), static_cast<int>(E), static_cast<int>(K), true);
+                     router_tc_supported(T, static_cast<int>(H), static_cast<int>(E), true);
   if (fused) {
     CUtensorMap tw;
     NKI_REQUIRE(make_tmap_bf16(&tw, router_w_split, 3 * E, H, 128), NKIMOE_ERR_CUDA,
                 "cuTensorMapEncodeTiled failed for the router planes");
+    float* logits = reinterpret_cast<float*>(base + L.logits);
     mark(kStageRouter, s);
-    NKI_CUDA(router_topk_tc_launch(tw, tw, static_cast<const __nv_bfloat16*>(h), norm_w, norm_w_dtype, eps,
-                                   static_cast<__nv_bfloat16*>(x), router_bias, reinterpret_cast<float*>(base + L.logits),
-                                   T, static_cast<int>(H), static_cast<int>(K), idx, w, status, s));
+    NKI_CUDA(router_tc_launch(tw, tw, static_cast<const __nv_bfloat16*>(h), norm_w, norm_w_dtype, eps,
+                              static_cast<__nv_bfloat16*>(x), router_bias, logits, T, static_cast<int>(H), status, s));
     mark(kStageTopk, s);
+    NKI_CUDA(topk_softmax_partials_launch(logits, 1, nullptr, nullptr, static_cast<int>(T), static_cast<int>(E),
+                                          static_cast<int>(K), idx, w, s));
   } else {
     NKI_CUDA(rmsnorm_launch(h, NKIMOE_BF16, norm_w, norm_w_dtype, x, NKIMOE_BF16, T, static_cast<int>(H), eps, s));
     rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, base, L, status, s);

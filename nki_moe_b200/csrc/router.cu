@@ -274,23 +274,24 @@ __global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restri
   topk_select_warp<VPT>(v, E, K, lane, idx_out + t * K, w_out + t * K);
 }
 
-// Router + softmax + top-k of a prefill batch in one tensor-core kernel, with
-// an optional RMSNorm of the rows in front of it.  CTA = 128 rows; the fp32
+// Router logits of a prefill batch in one tensor-core kernel, with an
+// optional RMSNorm of the rows in front of it.  CTA = 128 rows; the fp32
 // router weights are three exact bf16 planes (hi, mid, lo; router_split_kernel)
 // and each plane has its own TMEM accumulator (3 x 128 columns).  The MMAs are
-// the ones of the separate router GEMM (M128 N128 K16, K ascending, one
-// accumulator per plane) and the logits the same ((hi + mid) + lo) + bias sums
-// topk_softmax_kernel forms, so idx, w and logits equal the separate kernels'
-// bit for bit.  With the norm, the A operand of every 64-wide K block is the
-// row block normalised by the CTA itself (rmsnorm_kernel's arithmetic: the
-// lane-chunk fp32 sum of squares of a warp per row, (x * rsqrt) * w rounded to
-// bf16), written to shared memory in the TMA 128-byte swizzle and to x_out for
-// the expert gather, so the normalised rows are produced once and consumed by
-// the router in the same pass (the reference's fused post-attention norm,
+// the ones of the router GEMM (M128 N128 K16, K ascending, one accumulator per
+// plane) and the epilogue adds the planes as topk_softmax_kernel adds split
+// partials, ((hi + mid) + lo) + bias, so the logits it writes give the same
+// top-k bit for bit; the top-k itself stays a separate kernel (spread over the
+// whole GPU it is several times faster than in these 64-128 CTAs' epilogues).
+// With the norm, the A operand of every 64-wide K block is the row block
+// normalised by the CTA itself (rmsnorm_kernel's arithmetic: the lane-chunk
+// fp32 sum of squares of a warp per row, (x * rsqrt) * w rounded to bf16),
+// written to shared memory in the TMA 128-byte swizzle and to x_out for the
+// expert gather, so the normalised rows are produced once and consumed by the
+// router in the same pass (the reference's fused post-attention norm,
 // qwen_with_nki.py:379-382, :451-452).
 //   warps 0-3: row workers (norm, A blocks), then the epilogue (TMEM lanes
-//              32 w .. 32 w + 31 = rows; logits to shared memory; one warp-
-//              cooperative top-k per row)
+//              32 w .. 32 w + 31 = rows; fp32 logits rows to global memory)
 //   warp 4:    TMA producer (router planes; the x block without the norm)
 //   warp 5:    MMA issuer, TMEM owner
 constexpr int kRtRows = 128, kRtBK = 64, kRtE = 128, kRtStages = 3, kRtThreads = 192;
@@ -310,91 +311,12 @@ __device__ __forceinline__ float rt_weight(const void* w, int w_dtype, int k) {
   return w_dtype == 0 ? static_cast<const float*>(w)[k] : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[k]);
 }
 
-// topk_select_warp for one row held by one thread (the row's 128 logits in
-// shared memory): the same maximum, the same per-lane sums of exp(v - max)
-// over experts l, l + 32, l + 64, l + 96 added by the same butterfly, the same
-// selection (by logit, ties to the lower id) and the same butterfly sum of the
-// K probabilities, so idx and w are bit-identical to the warp version.
-__device__ __forceinline__ float rt_butterfly32(float (&t)[32]) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    float u[32];
-#pragma unroll
-    for (int l = 0; l < 32; ++l) u[l] = t[l] + t[l ^ o];
-#pragma unroll
-    for (int l = 0; l < 32; ++l) t[l] = u[l];
-  }
-  return t[0];
-}
-
-__device__ __forceinline__ void rt_topk_row(const float* lg, int K, int32_t* idx_row, float* w_row) {
-  float m = -INFINITY;
-  for (int e = 0; e < kRtE; ++e) m = fmaxf(m, lg[e]);
-  float t[32];
-#pragma unroll
-  for (int l = 0; l < 32; ++l) {
-    float sl = 0.f;
-#pragma unroll
-    for (int j = 0; j < kRtE / 32; ++j) sl += expf(lg[l + 32 * j] - m);
-    t[l] = sl;
-  }
-  const float ssum = rt_butterfly32(t);
-  // the K largest (by logit, ties to the lower id): one pass over the experts
-  // in ascending id keeping a sorted list; a new key goes in front of the
-  // first strictly smaller one, so equal keys keep ascending ids
-  constexpr int kList = 8;
-  uint32_t lk[kList];
-  int li[kList];
-#pragma unroll
-  for (int q = 0; q < kList; ++q) {
-    lk[q] = 0u;
-    li[q] = 0;
-  }
-  const int kk = K < kList ? K : kList;
-  for (int e = 0; e < kRtE; ++e) {
-    uint32_t k = order_key(lg[e]);
-    if (k <= lk[kk - 1]) continue;
-    int id = e;
-#pragma unroll
-    for (int q = 0; q < kList; ++q) {
-      if (q < kk && k > lk[q]) {
-        const uint32_t tk = lk[q];
-        const int ti = li[q];
-        lk[q] = k;
-        li[q] = id;
-        k = tk;
-        id = ti;
-      }
-    }
-  }
-  float p[32];
-#pragma unroll
-  for (int q = 0; q < 32; ++q) {
-    p[q] = 0.f;
-    if (q < kk) {
-      const uint32_t bits = (lk[q] & 0x80000000u) ? (lk[q] & 0x7fffffffu) : ~lk[q];
-      p[q] = expf(__uint_as_float(bits) - m) / ssum;
-    }
-  }
-  float tt[32];
-#pragma unroll
-  for (int q = 0; q < 32; ++q) tt[q] = p[q];
-  const float tot = rt_butterfly32(tt);
-#pragma unroll
-  for (int q = 0; q < kList; ++q)
-    if (q < kk) {
-      idx_row[q] = li[q];
-      w_row[q] = p[q] / tot;
-    }
-}
-
 template <bool kNorm>
 __global__ void __launch_bounds__(kRtThreads, 1)
-    router_topk_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                          const __nv_bfloat16* __restrict__ h, const void* __restrict__ norm_w, int norm_w_dtype,
-                          float eps, __nv_bfloat16* __restrict__ x_out, const float* __restrict__ bias,
-                          float* __restrict__ logits_out, int T, int H, int K, int32_t* __restrict__ idx_out,
-                          float* __restrict__ w_out, int* status) {
+    router_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                     const __nv_bfloat16* __restrict__ h, const void* __restrict__ norm_w, int norm_w_dtype,
+                     float eps, __nv_bfloat16* __restrict__ x_out, const float* __restrict__ bias,
+                     float* __restrict__ logits_out, int T, int H, int* status) {
   extern __shared__ uint8_t rt_smem_raw[];
   __shared__ RtCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_smem_raw) + 1023) &
@@ -587,11 +509,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
     got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
     if (got) {
       tcgen05_fence_after();
-      // every MMA has completed: the stages are free; logits staged as
-      // [128 rows][129] fp32 (padded: conflict-free row and column access)
-      float* stg = reinterpret_cast<float*>(smem);
-      const int rl = warp * 32 + lane;
-      const long long row = row0 + rl;
+      const long long row = row0 + warp * 32 + lane;
       const uint32_t tl = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll 1
       for (int c0 = 0; c0 < kRtE; c0 += 32) {
@@ -608,16 +526,13 @@ __global__ void __launch_bounds__(kRtThreads, 1)
           acc += __uint_as_float(d[j]);
           if (bias) acc += bias[c0 + j];
           lg[j] = acc;
-          stg[rl * (kRtE + 1) + c0 + j] = acc;
         }
-        if (logits_out && row < T) {
+        if (row < T) {
           float4* dst = reinterpret_cast<float4*>(logits_out + row * kRtE + c0);
 #pragma unroll
           for (int q = 0; q < 8; ++q) dst[q] = make_float4(lg[4 * q], lg[4 * q + 1], lg[4 * q + 2], lg[4 * q + 3]);
         }
       }
-      __syncwarp();
-      if (row < T) rt_topk_row(stg + rl * (kRtE + 1), K, idx_out + row * K, w_out + row * K);
     }
   }
   tcgen05_fence_before();
@@ -980,45 +895,41 @@ cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const
 }
 
 
-size_t router_topk_tc_smem_bytes() { return static_cast<size_t>(kRtStages) * kRtStageBytes + 1024; }
+size_t router_tc_smem_bytes() { return static_cast<size_t>(kRtStages) * kRtStageBytes + 1024; }
 
-bool router_topk_tc_supported(long long T, int H, int E, int K, bool norm) {
-  return E == kRtE && K >= 1 && K <= 8 && H % kRtBK == 0 && H >= kRtBK && T > 0 &&
-         (!norm || H <= 8 * 32 * 8);
+bool router_tc_supported(long long T, int H, int E, bool norm) {
+  return E == kRtE && H % kRtBK == 0 && H >= kRtBK && T > 0 && (!norm || H <= 8 * 32 * 8);
 }
 
-cudaError_t router_topk_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
-                                  const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out,
-                                  const float* bias, float* logits_out, long long T, int H, int K, int32_t* idx,
-                                  float* w, int* status, cudaStream_t s) {
+cudaError_t router_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
+                             const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out, const float* bias,
+                             float* logits_out, long long T, int H, int* status, cudaStream_t s) {
   const bool norm = h != nullptr;
-  if (!router_topk_tc_supported(T, H, kRtE, K, norm) || (norm && (!norm_w || !x_out))) return cudaErrorInvalidValue;
-  const size_t smem = router_topk_tc_smem_bytes();
+  if (!router_tc_supported(T, H, kRtE, norm) || !logits_out || (norm && (!norm_w || !x_out)))
+    return cudaErrorInvalidValue;
+  const size_t smem = router_tc_smem_bytes();
   const unsigned grid = static_cast<unsigned>((T + kRtRows - 1) / kRtRows);
   if (norm) {
     static bool attr = false;
     if (!attr) {
-      cudaError_t e = cudaFuncSetAttribute(router_topk_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       attr = true;
     }
-    router_topk_tc_kernel<true><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out,
-                                                                bias, logits_out, static_cast<int>(T), H, K, idx, w,
-                                                                status);
+    router_tc_kernel<true><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out, bias,
+                                                           logits_out, static_cast<int>(T), H, status);
   } else {
     static bool attr = false;
     if (!attr) {
-      cudaError_t e = cudaFuncSetAttribute(router_topk_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
       if (e != cudaSuccess) return e;
       attr = true;
     }
-    router_topk_tc_kernel<false><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr,
-                                                                 bias, logits_out, static_cast<int>(T), H, K, idx, w,
-                                                                 status);
+    router_tc_kernel<false><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr, bias,
+                                                            logits_out, static_cast<int>(T), H, status);
   }
   return cudaGetLastError();
 }
-
 }  // namespace nkimoe

@@ -63,7 +63,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all", choices=["block", "norms", "all"])
     ap.add_argument("--router-fused", type=int, default=1, choices=[0, 1],
-                    help="tensor-core router: logits + top-k in one kernel (1) or two (0)")
+                    help="tensor-core router: the planes' summed logits in one kernel (1) or the GEMM's partials (0)")
     a = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("needs a CUDA device")

@@ -197,7 +197,7 @@ class NKIMoESimple(nn.Module):
         fused MoE kernel takes ``post_attention_layernorm``
         (qwen_with_nki.py:379-382; the decoder then skips its own norm call,
         :451-452): ``forward(h)`` computes ``moe(norm(h))``.  Prefill batches
-        run the norm, the router and the top-k in one kernel."""
+        run the norm and the router logits in one kernel."""
         self.rmsnorm = norm
         return self
 

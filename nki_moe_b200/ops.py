@@ -564,8 +564,8 @@ def moe_block_rmsnorm(h: torch.Tensor, norm_weight: torch.Tensor, router_w: torc
     """The block with the RMSNorm in front of it inside the call:
     ``moe_block(rmsnorm(h) * norm_weight)``, equal bit for bit to
     :func:`rmsnorm` + :func:`moe_block`.  For prefill batches (more than 512
-    tokens, 128 experts) the norm, router logits and top-k are one
-    tensor-core kernel that writes the normalised rows once.  With
+    tokens, 128 experts) the norm and the router logits are one tensor-core
+    kernel that writes the normalised rows once.  With
     ``return_x`` also returns the normalised rows (bf16)."""
     h = _contig(_cuda(h, "h"), torch.bfloat16)
     rsplit = None

@@ -706,10 +706,10 @@ def test_invalid_shapes_raise():
 
 @pytest.mark.parametrize("T", [256, 300, 8192])
 def test_fused_tensor_core_router_equals_two_kernels(T):
-    """The one-kernel tensor-core router (logits, softmax and top-k with the
-    logits kept in shared memory) issues the same MMAs and sums as the router
-    GEMM + top-k kernels: routing indices and weights identical bit for bit,
-    with and without a router bias, on full and ragged row tiles."""
+    """The one-kernel tensor-core router logits (the three weight planes
+    summed in the epilogue) issue the same MMAs and sums as the router GEMM's
+    partials added by the top-k kernel: routing indices and weights identical
+    bit for bit, with and without a router bias, on full and ragged row tiles."""
     g = torch.Generator().manual_seed(T)
     x = torch.randn(T, 2048, generator=g).bfloat16().cuda()
     rw = (torch.randn(128, 2048, generator=g) * 0.02).cuda()
@@ -732,7 +732,7 @@ def test_fused_tensor_core_router_equals_two_kernels(T):
 def test_moe_block_with_fused_rmsnorm_equals_separate_calls(c1_inputs, T, wdt):
     """The block with the post-attention RMSNorm inside the call equals
     rmsnorm + block bit for bit: the normalised rows, the routing and the
-    output.  Above 512 tokens the norm, router logits and top-k are one
+    output.  Above 512 tokens the norm and the router logits are one
     tensor-core kernel; at 300 tokens the norm kernel runs first."""
     g = torch.Generator().manual_seed(T + 7)
     h = (torch.randn(T, 2048, generator=g) * 3).bfloat16().cuda()
