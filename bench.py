@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--ep-overlap", type=int, default=1, choices=[0, 1],
                     help="N > 1, peer exchange: 1 overlapped schedule (default), 0 one block after all rows arrived")
     ap.add_argument("--ep-groups", type=int, default=0, help="N > 1, overlapped schedule: remote region groups (0 auto)")
+    ap.add_argument("--ep-side-ctas", type=int, default=0,
+                    help="N > 1, overlapped schedule: CTAs of the send / return kernels beside the GEMMs (0: library "
+                         "default)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: exchange over peer memory (library kernels) or NCCL all-to-all")
     return ap.parse_args()
@@ -474,6 +477,8 @@ def run_b200(args):
     _lib.load()
     _lib.set_option("ep_overlap", args.ep_overlap)
     _lib.set_option("ep_groups", args.ep_groups)
+    if args.ep_side_ctas:
+        _lib.set_option("ep_side_ctas", args.ep_side_ctas)
     if args.profile_once and args.stack_profile_layers > 0:
         from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
 
