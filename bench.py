@@ -69,8 +69,9 @@ def parse():
     ap.add_argument("--stack-profile-layers", type=int, default=0,
                     help="with --profile-once: build a decoder stack of this many layers, prefill batch 8 x 512 "
                          "and run one eager decode step inside the NVTX range 'decode_step' (for ncu launch lists)")
-    ap.add_argument("--ep-overlap", type=int, default=1, choices=[0, 1],
-                    help="N > 1, peer exchange: 1 overlapped schedule (default), 0 one block after all rows arrived")
+    ap.add_argument("--ep-overlap", type=int, default=1, choices=[0, 1, 2],
+                    help="N > 1, peer exchange: 0 one block after all rows arrived; 1 overlapped, SM stores on a side "
+                         "stream; 2 overlapped, copy engines")
     ap.add_argument("--ep-groups", type=int, default=0, help="N > 1, overlapped schedule: remote region groups (0 auto)")
     ap.add_argument("--ep-side-ctas", type=int, default=0,
                     help="N > 1, overlapped schedule: CTAs of the send / return kernels beside the GEMMs (0: library "

@@ -428,7 +428,9 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
 // the rank's own tokens (their own-expert slots in self_idx / self_w) and one
 // per group of remote regions.  The workspace holds the larger of the two.
 struct PeerWs {
-  size_t route, disp, slot_in, slot_out, counters, self_idx, self_w, recv, total;
+  size_t route, disp, slot_in, slot_out, counters, self_idx, self_w, recv;
+  // copy-engine schedule: outgoing rows per destination and returned sums per region
+  size_t stage_x, stage_slots, stage_w, stage_counts, ret_stage, total;
 };
 
 size_t ep_dispatch_ws_bytes(long long T, long long P);
@@ -463,7 +465,12 @@ PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, 
   W.recv = o;
   size_t recv = ws_layout(P * Tm, H, I, E / P, K).total;
   for (long long g = 1; g < P; ++g) recv = std::max(recv, overlapped_recv_bytes(T, H, I, E / P, K, P, Tm, g));
-  o += recv;
+  o += round256(recv);
+  W.stage_x = o; o += round256(sizeof(uint16_t) * P * Tm * H);
+  W.stage_slots = o; o += round256(sizeof(int32_t) * P * Tm * K);
+  W.stage_w = o; o += round256(sizeof(float) * P * Tm * K);
+  W.stage_counts = o; o += 256;
+  W.ret_stage = o; o += round256(sizeof(uint16_t) * P * Tm * H);
   W.total = o;
   return W;
 }
@@ -740,7 +747,7 @@ int nkimoe_set_option(const char* name, long long value) {
     g_peer_wait_cycles = value;
     return NKIMOE_OK;
   }
-  if (n == "ep_overlap" && (value == 0 || value == 1)) {
+  if (n == "ep_overlap" && value >= 0 && value <= 2) {
     g_ep_overlap = static_cast<int>(value);
     return NKIMOE_OK;
   }
@@ -1457,11 +1464,17 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     mark(kStageEpReturnWait, s);
     NKI_CUDA(ep_peer_wait_launch(res_flag, static_cast<int>(P), epoch_p, status, budget, s));
   } else {
-    // ---- overlapped: the sends to the other ranks and the returns of their
-    // sums run on a side stream of the library beside the expert GEMMs.  The
-    // own tokens' share goes straight from x; remote regions are taken in
-    // groups, nearest sources first (each source sends to its nearest
+    // ---- overlapped: the transfers to the other ranks run on a side stream
+    // of the library beside the expert GEMMs.  Schedule 1: the send and
+    // return kernels store over NVLink from that stream; schedule 2: the rows
+    // and sums are gathered into local staging regions on the main stream and
+    // the copy engines move each destination's whole region (cudaMemcpyAsync
+    // to the peer's mapped buffer, then a one-thread kernel publishes the
+    // count and the flag), so the transfers take no SM time from the GEMMs.
+    // The own tokens' share goes straight from x; remote regions are taken
+    // in groups, nearest sources first (each source sends to its nearest
     // destination first), each group's sums returned while the next computes.
+    const bool copy_engines = g_ep_overlap.load() == 2;
     int32_t* self_idx = reinterpret_cast<int32_t*>(b + W.self_idx);
     float* self_w = reinterpret_cast<float*>(b + W.self_w);
     NKI_CUDA(ep_peer_local_launch(idx, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
@@ -1477,15 +1490,39 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     const int side_ctas = g_ep_side_ctas.load() > 0 ? g_ep_side_ctas.load() : device_sm_count();
     long long groups = g_ep_groups.load() > 0 ? g_ep_groups.load() : std::min<long long>(P - 1, 3);
     groups = std::min<long long>(groups, P - 1);  // 0 for a single rank: no remote regions
+    __nv_bfloat16* stage_x = reinterpret_cast<__nv_bfloat16*>(b + W.stage_x);
+    int32_t* stage_slots = reinterpret_cast<int32_t*>(b + W.stage_slots);
+    float* stage_w = reinterpret_cast<float*>(b + W.stage_w);
+    int32_t* stage_counts = reinterpret_cast<int32_t*>(b + W.stage_counts);
+    __nv_bfloat16* ret_stage = reinterpret_cast<__nv_bfloat16*>(b + W.ret_stage);
+    const size_t region_x = sizeof(uint16_t) * Tm * H, region_k = sizeof(int32_t) * Tm * K;
+    if (copy_engines)
+      NKI_CUDA(ep_peer_stage_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+                                    static_cast<int>(T), static_cast<int>(H), static_cast<int>(K), static_cast<int>(P),
+                                    static_cast<int>(El), static_cast<int>(Tm), me, stage_x, stage_slots, stage_w,
+                                    stage_counts, s));
     mark(kStageEpSend, s);
     NKI_CUDA(cudaEventRecord(es.fork, s));
     NKI_CUDA(cudaStreamWaitEvent(es.side, es.fork, 0));
-    for (long long q = 1; q < P; ++q) {  // one launch per destination, nearest first
+    for (long long q = 1; q < P; ++q) {  // one destination after another, nearest first
       const int d = static_cast<int>((rank + q) % P);
-      NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
-                                   static_cast<int>(T), static_cast<int>(H), static_cast<int>(K), static_cast<int>(P),
-                                   static_cast<int>(El), static_cast<int>(Tm), me, d, 1, peers, PL, counters + q,
-                                   epoch_p, side_ctas, es.side));
+      if (copy_engines) {
+        char* pd = peers.base[d];
+        NKI_CUDA(cudaMemcpyAsync(pd + PL.recv_x + q * region_x, reinterpret_cast<char*>(stage_x) + d * region_x,
+                                 region_x, cudaMemcpyDeviceToDevice, es.side));
+        NKI_CUDA(cudaMemcpyAsync(pd + PL.recv_slots + q * region_k,
+                                 reinterpret_cast<char*>(stage_slots) + d * region_k, region_k,
+                                 cudaMemcpyDeviceToDevice, es.side));
+        NKI_CUDA(cudaMemcpyAsync(pd + PL.recv_w + q * region_k, reinterpret_cast<char*>(stage_w) + d * region_k,
+                                 region_k, cudaMemcpyDeviceToDevice, es.side));
+        NKI_CUDA(ep_peer_publish_launch(reinterpret_cast<int32_t*>(pd + PL.counts) + q, stage_counts + d,
+                                        reinterpret_cast<uint32_t*>(pd + PL.disp_flag) + q, epoch_p, es.side));
+      } else {
+        NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(K),
+                                     static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), me, d, 1, peers,
+                                     PL, counters + q, epoch_p, side_ctas, es.side));
+      }
     }
     // own tokens: prep and the first half of the experts before the remote
     // rows are needed, the second half after them (covering the last returns)
@@ -1509,13 +1546,32 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
       rc = experts_prep(grp, s, false, false);
       if (rc == NKIMOE_OK) rc = experts_gemms(grp, 0, El, s, false);
       if (rc != NKIMOE_OK) return rc;
-      // the group's sums go back to their sources from the side stream
-      NKI_CUDA(cudaEventRecord(es.group[g], s));
-      NKI_CUDA(cudaStreamWaitEvent(es.side, es.group[g], 0));
-      const PeerCombine pc{peers, PL, static_cast<int>(P), me, static_cast<int>(Tm), static_cast<int>(q0),
-                           static_cast<int>(nq), side_ctas, counters + P + g, epoch_p};
-      rc = experts_finish(grp, nullptr, &pc, nullptr, es.side, false);
-      if (rc != NKIMOE_OK) return rc;
+      if (copy_engines) {
+        // the group's sums into the local return regions, then each region
+        // copied to its source from the side stream
+        NKI_CUDA(ep_peer_combine_launch(reinterpret_cast<const __nv_bfloat16*>(gb + grp.L.xy),
+                                        reinterpret_cast<const int32_t*>(gb + grp.L.slot_row), static_cast<int>(q0),
+                                        static_cast<int>(nq), static_cast<int>(K), static_cast<int>(H),
+                                        static_cast<int>(Tm), me, peers, PL, static_cast<int>(P), nullptr, epoch_p, 0,
+                                        s, ret_stage));
+        NKI_CUDA(cudaEventRecord(es.group[g], s));
+        NKI_CUDA(cudaStreamWaitEvent(es.side, es.group[g], 0));
+        for (long long q = q0; q < q0 + nq; ++q) {
+          char* ps = peers.base[(rank - q + P) % P];
+          NKI_CUDA(cudaMemcpyAsync(ps + PL.ret_y + q * region_x, reinterpret_cast<char*>(ret_stage) + q * region_x,
+                                   region_x, cudaMemcpyDeviceToDevice, es.side));
+          NKI_CUDA(ep_peer_publish_launch(nullptr, nullptr, reinterpret_cast<uint32_t*>(ps + PL.res_flag) + q,
+                                          epoch_p, es.side));
+        }
+      } else {
+        // the group's sums go back to their sources from the side stream
+        NKI_CUDA(cudaEventRecord(es.group[g], s));
+        NKI_CUDA(cudaStreamWaitEvent(es.side, es.group[g], 0));
+        const PeerCombine pc{peers, PL, static_cast<int>(P), me, static_cast<int>(Tm), static_cast<int>(q0),
+                             static_cast<int>(nq), side_ctas, counters + P + g, epoch_p};
+        rc = experts_finish(grp, nullptr, &pc, nullptr, es.side, false);
+        if (rc != NKIMOE_OK) return rc;
+      }
       gb += round256(ws_layout(nq * Tm, H, I, El, K).total);
     }
     mark(kStageEpReturnWait, s);

@@ -229,7 +229,8 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
                                                               const int32_t* __restrict__ slot_row, int q0, int nq,
                                                               int K, int H, int Tm, int me, EpPeerPtrs peers,
                                                               EpPeerLayout L, int P, unsigned* counter,
-                                                              const uint32_t* epoch_p) {
+                                                              const uint32_t* epoch_p,
+                                                              __nv_bfloat16* __restrict__ local_ret) {
   const int lane = threadIdx.x & 31;
   const int chunks = H >> 3;
   const long long rows = static_cast<long long>(nq) * Tm;
@@ -242,7 +243,8 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
     const int q = q0 + static_cast<int>(r / Tm);
     const long long j = r % Tm;
     const int s = (me - q + P) % P;
-    uint4* dst = reinterpret_cast<uint4*>(view_of(peers.base[s], L).ret_y + (static_cast<long long>(q) * Tm + j) * H);
+    __nv_bfloat16* ret = local_ret ? local_ret : view_of(peers.base[s], L).ret_y;
+    uint4* dst = reinterpret_cast<uint4*>(ret + (static_cast<long long>(q) * Tm + j) * H);
     for (int c0 = lane; c0 < chunks; c0 += 256) {
       float acc[8][8] = {};
       for (unsigned m = present; m != 0u; m &= m - 1u) {  // slots in ascending k
@@ -279,11 +281,58 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
       }
     }
   }
+  if (local_ret) return;
   if (last_block_done(counter) && threadIdx.x < nq) {
     const int q = q0 + threadIdx.x;
     const EpPeerView pv = view_of(peers.base[(me - q + P) % P], L);
     st_release_sys(pv.res_flag + q, *epoch_p);
   }
+}
+
+// Copy-engine send, local half: rows of the destinations d != src to this
+// rank's staging regions (row j of destination d at d * Tm + j), the rows'
+// slots as d sees them and their weights; stage_counts[d] = d's row count.
+__global__ void __launch_bounds__(256) ep_peer_stage_kernel(
+    const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx, const float* __restrict__ w,
+    const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
+    const int32_t* __restrict__ rank_offsets, int H, int K, int P, int El, int Tm, int src,
+    __nv_bfloat16* __restrict__ stage_x, int32_t* __restrict__ stage_slots, float* __restrict__ stage_w,
+    int32_t* __restrict__ stage_counts) {
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long rows = rank_offsets[P];
+  const int chunks = H >> 3;
+  if (blockIdx.x == 0 && threadIdx.x < P) stage_counts[threadIdx.x] = rank_offsets[threadIdx.x + 1] - rank_offsets[threadIdx.x];
+  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    const int d = row_slot[r] % P;
+    if (d == src) continue;  // the own tokens' share is computed from x directly
+    const int t = row_token[r];
+    const long long dst_row = static_cast<long long>(d) * Tm + (r - rank_offsets[d]);
+    const uint4* s4 = reinterpret_cast<const uint4*>(x + static_cast<long long>(t) * H);
+    uint4* d4 = reinterpret_cast<uint4*>(stage_x + dst_row * H);
+    for (int c0 = lane; c0 < chunks; c0 += 256) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + 32 * u < chunks) v[u] = s4[c0 + 32 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + 32 * u < chunks) d4[c0 + 32 * u] = v[u];
+    }
+    if (lane < K) {
+      const int e = idx[static_cast<long long>(t) * K + lane];
+      const bool mine = e >= d * El && e < (d + 1) * El;
+      stage_slots[dst_row * K + lane] = mine ? e - d * El : -1;
+      stage_w[dst_row * K + lane] = mine ? w[static_cast<long long>(t) * K + lane] : 0.f;
+    }
+  }
+}
+
+__global__ void ep_peer_publish_kernel(int32_t* count_dst, const int32_t* count_src, uint32_t* flag,
+                                       const uint32_t* epoch_p) {
+  if (count_src) *count_dst = *count_src;
+  __threadfence_system();
+  st_release_sys(flag, *epoch_p);
 }
 
 // The step's epoch in this rank's own buffer: `value` when nonzero (the
@@ -371,11 +420,30 @@ cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int q0, i
 
 cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int q0, int nq, int K, int H,
                                    int Tm, int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P,
-                                   unsigned* counter, const uint32_t* epoch_p, int max_ctas, cudaStream_t s) {
+                                   unsigned* counter, const uint32_t* epoch_p, int max_ctas, cudaStream_t s,
+                                   __nv_bfloat16* local_ret) {
   if (nq < 1 || q0 < 0 || q0 + nq > P) return cudaErrorInvalidValue;
   unsigned grid = grid_cap(static_cast<long long>(nq) * Tm * 32, 256);  // one warp per row
   if (max_ctas > 0 && grid > static_cast<unsigned>(max_ctas)) grid = static_cast<unsigned>(max_ctas);
-  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, q0, nq, K, H, Tm, me, peers, L, P, counter, epoch_p);
+  ep_peer_combine_kernel<<<grid, 256, 0, s>>>(y, slot_row, q0, nq, K, H, Tm, me, peers, L, P, counter, epoch_p,
+                                              local_ret);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_stage_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
+                                 const int32_t* row_slot, const int32_t* rank_offsets, int T, int H, int K, int P,
+                                 int El, int Tm, int src, __nv_bfloat16* stage_x, int32_t* stage_slots,
+                                 float* stage_w, int32_t* stage_counts, cudaStream_t s) {
+  if (P > 256) return cudaErrorInvalidValue;
+  const unsigned grid = grid_cap(static_cast<long long>(T) * P * 32, 256);  // one warp per row
+  ep_peer_stage_kernel<<<grid, 256, 0, s>>>(x, idx, w, row_token, row_slot, rank_offsets, H, K, P, El, Tm, src,
+                                            stage_x, stage_slots, stage_w, stage_counts);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_peer_publish_launch(int32_t* count_dst, const int32_t* count_src, uint32_t* flag,
+                                   const uint32_t* epoch_p, cudaStream_t s) {
+  ep_peer_publish_kernel<<<1, 1, 0, s>>>(count_dst, count_src, flag, epoch_p);
   return cudaGetLastError();
 }
 

@@ -193,6 +193,19 @@ cudaError_t ep_peer_send_launch(const __nv_bfloat16* x, const int32_t* idx, cons
 cudaError_t ep_peer_local_launch(const int32_t* idx, const float* w, const int32_t* slot_in,
                                  const int32_t* rank_offsets, int T, int K, int P, int El, int Tm, int src,
                                  bool self_direct, int32_t* slot_out, int32_t* self_idx, float* self_w, cudaStream_t s);
+// Copy-engine form of the send: the rows of every destination d != src, in
+// the order ep_peer_send_launch gives them, written to this rank's staging
+// [P][Tm] rows (stage_x, stage_slots, stage_w, stage_counts[d]) instead of
+// the peers' buffers; the library then copies each destination's whole
+// staging region to it and raises its flag with ep_peer_publish_launch.
+cudaError_t ep_peer_stage_launch(const __nv_bfloat16* x, const int32_t* idx, const float* w, const int32_t* row_token,
+                                 const int32_t* row_slot, const int32_t* rank_offsets, int T, int H, int K, int P,
+                                 int El, int Tm, int src, __nv_bfloat16* stage_x, int32_t* stage_slots,
+                                 float* stage_w, int32_t* stage_counts, cudaStream_t s);
+// One thread: *count_dst = *count_src (when count_src is given), then, after a
+// system-scope fence, *flag = the step's epoch with release semantics.
+cudaError_t ep_peer_publish_launch(int32_t* count_dst, const int32_t* count_src, uint32_t* flag,
+                                   const uint32_t* epoch_p, cudaStream_t s);
 // epoch := value when nonzero, else epoch + 1 (device-side step count)
 cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s);
 // Waits (bounded by budget_cycles) until flags[0 .. n) all hold the epoch.
@@ -203,9 +216,12 @@ cudaError_t ep_peer_mask_launch(int32_t* slots, const int32_t* counts, int q0, i
 // Receiver: the weighted sums of rows [0, nq * Tm) of regions q0 .. q0 + nq - 1
 // (row r: region q0 + r / Tm, row r % Tm) stored into the sources' ret_y, and
 // their result flags raised.
+// With local_ret non-null the sums go to local_ret [regions][Tm][H] (row j of
+// region q at (q * Tm + j) * H) and no flag is raised.
 cudaError_t ep_peer_combine_launch(const __nv_bfloat16* y, const int32_t* slot_row, int q0, int nq, int K, int H,
                                    int Tm, int me, const EpPeerPtrs& peers, const EpPeerLayout& L, int P,
-                                   unsigned* counter, const uint32_t* epoch_p, int max_ctas, cudaStream_t s);
+                                   unsigned* counter, const uint32_t* epoch_p, int max_ctas, cudaStream_t s,
+                                   __nv_bfloat16* local_ret = nullptr);
 
 // counts[e] = offsets[e+1] - offsets[e]
 cudaError_t offsets_to_counts_launch(const int32_t* offsets, int32_t* counts, int n, cudaStream_t s);

@@ -114,7 +114,7 @@ def test_given_routing_block_skips_empty_slots():
     assert oracle.normwise_rel_err(out, ref) < 2e-2 and oracle.cosine(out, ref) > 0.999
 
 
-@pytest.mark.parametrize("overlap", [1, 0])
+@pytest.mark.parametrize("overlap", [1, 0, 2])
 def test_peer_ep_single_rank_equals_block(overlap):
     """The peer-memory EP block as a single rank equals the single-GPU block bit
     for bit, step after step: in the overlapped schedule (its own tokens'
@@ -188,8 +188,10 @@ def _ep_worker(rank, world, port, out_dir):
     # either schedule whatever the other takes
     _lib.set_option("ep_overlap", 0)
     y_peer1b = peer(x)
-    _lib.set_option("ep_overlap", rank % 2)
+    _lib.set_option("ep_overlap", 2 * (rank % 2))
     y_peer2b = peer(x2)
+    _lib.set_option("ep_overlap", 2)
+    y_peer2c = peer(x2)
     _lib.set_option("ep_overlap", 1)
     assert ops.read_status(ops.workspace(x.device, 1)) == 0
     y_dedup2 = ExpertParallelMoE.from_dense(moe, dedup=True)(x2)
@@ -216,6 +218,7 @@ def _ep_worker(rank, world, port, out_dir):
     np.save(os.path.join(out_dir, f"peer3_{rank}.npy"), y_peer3.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"peer1b_{rank}.npy"), y_peer1b.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"peer2b_{rank}.npy"), y_peer2b.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"peer2c_{rank}.npy"), y_peer2c.float().cpu().numpy())
     np.save(os.path.join(out_dir, f"timeout{rank}.npy"), np.array([timed_out]))
     peer.close()
     np.save(os.path.join(out_dir, f"peer{rank}.npy"), y_peer1.float().cpu().numpy())
@@ -251,6 +254,7 @@ def test_expert_parallel_two_gpus_matches_single_gpu(tmp_path):
         # the one-block schedule and a mix of schedules across the ranks
         assert np.array_equal(np.load(tmp_path / f"peer1b_{r}.npy"), d)
         assert np.array_equal(np.load(tmp_path / f"peer2b_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
+        assert np.array_equal(np.load(tmp_path / f"peer2c_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
         # after rank 1 left a step and the ranks resynchronised
         assert np.array_equal(np.load(tmp_path / f"peer3_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
     assert int(np.load(tmp_path / "timeout0.npy")[0]) == 1  # rank 0's step raised the wait timeout
