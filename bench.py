@@ -69,9 +69,9 @@ def parse():
     ap.add_argument("--stack-profile-layers", type=int, default=0,
                     help="with --profile-once: build a decoder stack of this many layers, prefill batch 8 x 512 "
                          "and run one eager decode step inside the NVTX range 'decode_step' (for ncu launch lists)")
-    ap.add_argument("--ep-overlap", type=int, default=1, choices=[0, 1, 2],
-                    help="N > 1, peer exchange: 0 one block after all rows arrived; 1 overlapped, SM stores on a side "
-                         "stream; 2 overlapped, copy engines")
+    ap.add_argument("--ep-overlap", type=int, default=-1, choices=[-1, 0, 1, 2],
+                    help="N > 1, peer exchange: -1 the library's choice (copy engines for prefill batches); 0 one block "
+                         "after all rows arrived; 1 overlapped, SM stores on a side stream; 2 overlapped, copy engines")
     ap.add_argument("--ep-groups", type=int, default=0, help="N > 1, overlapped schedule: remote region groups (0 auto)")
     ap.add_argument("--ep-side-ctas", type=int, default=0,
                     help="N > 1, overlapped schedule: CTAs of the send / return kernels beside the GEMMs (0: library "
@@ -595,7 +595,7 @@ def run_b200(args):
             # the timed (overlapped) schedule's stages; then the one-block
             # schedule, whose stages isolate each kernel (GEMM-1 roofline,
             # exchange rates) -- every rank takes the same steps
-            if args.ep_overlap:
+            if args.ep_overlap != 0 and (args.ep_overlap > 0 or T_local >= 1024):
                 st_o = measure_stages(torch, fwd, n_stage_steps, stage_events(torch), graph_of, EPO_STAGE_ORDER)
             _lib.set_option("ep_overlap", 0)
             try:
@@ -766,8 +766,9 @@ def run_b200(args):
                    "tokens_per_gpu": wl.tokens // world if main_key == "skewed" else wl.tokens,
                    "hidden": wl.hidden, "experts": wl.experts,
                    "top_k": wl.top_k, "intermediate": wl.intermediate,
-                   "parallelism": (f"ep{world}-{args.ep}" + ("-overlapped" if ep_peer and args.ep_overlap else ""))
-                   if world > 1 else "single",
+                   "parallelism": (f"ep{world}-{args.ep}" + ({-1: "-auto", 0: "-one-block", 1: "-overlapped-sm",
+                                                             2: "-overlapped-copy-engines"}[args.ep_overlap]
+                                                            if ep_peer else "")) if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.21 GB of expert weights read per step)",
                    "timing": timing},
         "roofline": m.get("roofline"),

@@ -81,11 +81,12 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * "peer_wait_cycles" (budget of each expert-parallel wait for the peers, in
  * SM clock cycles, 1000 to 1e12; default 2e10, about 10 s),
  * "ep_overlap" (schedule of nkimoe_ep_peer_forward: 0 one expert block after
- * every row has arrived; 1 (the default) sends, computes and returns
- * overlapped, the send and return kernels storing over NVLink from a side
- * stream; 2 the same with the rows and sums gathered into local staging and
- * moved by the copy engines), "ep_groups" (remote regions taken in this many groups by the
- * overlapped schedule, 1 to 7; 0 = auto, min(ranks - 1, 3)),
+ * every row has arrived; 1 sends, computes and returns overlapped, the send
+ * and return kernels storing over NVLink from a side stream; 2 the same with
+ * the rows and sums gathered into local staging and moved by the copy
+ * engines; -1, the default, picks 2 when max_tokens >= 1024 and 0 below),
+ * "ep_groups" (remote regions taken in this many groups by the overlapped
+ * schedules, 1 to 7; 0 = auto, min(ranks - 1, 2)),
  * "ep_side_ctas" (grid bound of the send and return kernels that run beside
  * the expert GEMMs; 0 = the SM count).
  * No reference counterpart (NKI tile sizes are compile-time constants,

@@ -73,10 +73,12 @@ std::atomic<int> g_pdl{1};           // programmatic dependent launch of the dec
 // 2 GHz by default): a peer that has not reached the step by then is reported
 // as a timeout in the status word.
 std::atomic<long long> g_peer_wait_cycles{20000000000LL};
-// Expert-parallel schedule: 1 overlapped (the default), 0 one block after all
-// rows arrived; groups of remote regions (0 auto); the grid bound of the send
-// and return kernels that run beside the expert GEMMs (0: the SM count).
-std::atomic<int> g_ep_overlap{1};
+// Expert-parallel schedule: -1 auto (the default: copy engines from 1024
+// tokens on, one block below), 0 one block after all rows arrived, 1
+// overlapped with SM stores, 2 overlapped with copy engines; groups of remote
+// regions (0 auto); the grid bound of the send and return kernels that run
+// beside the expert GEMMs (0: the SM count).
+std::atomic<int> g_ep_overlap{-1};
 std::atomic<int> g_ep_groups{0};
 std::atomic<int> g_ep_side_ctas{0};
 
@@ -747,7 +749,7 @@ int nkimoe_set_option(const char* name, long long value) {
     g_peer_wait_cycles = value;
     return NKIMOE_OK;
   }
-  if (n == "ep_overlap" && value >= 0 && value <= 2) {
+  if (n == "ep_overlap" && value >= -1 && value <= 2) {
     g_ep_overlap = static_cast<int>(value);
     return NKIMOE_OK;
   }
@@ -1439,7 +1441,13 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   const uint32_t* disp_flag = reinterpret_cast<const uint32_t*>(own + PL.disp_flag);
   const uint32_t* res_flag = reinterpret_cast<const uint32_t*>(own + PL.res_flag);
   const long long budget = g_peer_wait_cycles.load();
-  const bool overlapped = g_ep_overlap.load() != 0;
+  // auto: overlap pays where the transfers are long (prefill-sized batches);
+  // a decode step is a handful of rows, where the one block's few launches win.
+  // Each rank decides for itself: every schedule writes the same buffers the
+  // same way, only the order of the work differs.
+  int schedule = g_ep_overlap.load();
+  if (schedule < 0) schedule = (P > 1 && Tm >= 1024) ? 2 : 0;
+  const bool overlapped = schedule != 0;
 
   if (!overlapped) {
     // ---- one block: every row (own included) through the buffers, then all
@@ -1474,7 +1482,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     // The own tokens' share goes straight from x; remote regions are taken
     // in groups, nearest sources first (each source sends to its nearest
     // destination first), each group's sums returned while the next computes.
-    const bool copy_engines = g_ep_overlap.load() == 2;
+    const bool copy_engines = schedule == 2;
     int32_t* self_idx = reinterpret_cast<int32_t*>(b + W.self_idx);
     float* self_w = reinterpret_cast<float*>(b + W.self_w);
     NKI_CUDA(ep_peer_local_launch(idx, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
@@ -1488,7 +1496,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     rc = ep_side_init(es);
     if (rc != NKIMOE_OK) return rc;
     const int side_ctas = g_ep_side_ctas.load() > 0 ? g_ep_side_ctas.load() : device_sm_count();
-    long long groups = g_ep_groups.load() > 0 ? g_ep_groups.load() : std::min<long long>(P - 1, 3);
+    long long groups = g_ep_groups.load() > 0 ? g_ep_groups.load() : std::min<long long>(P - 1, 2);
     groups = std::min<long long>(groups, P - 1);  // 0 for a single rank: no remote regions
     __nv_bfloat16* stage_x = reinterpret_cast<__nv_bfloat16*>(b + W.stage_x);
     int32_t* stage_slots = reinterpret_cast<int32_t*>(b + W.stage_slots);

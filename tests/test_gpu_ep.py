@@ -142,7 +142,7 @@ def test_peer_ep_single_rank_equals_block(overlap):
             assert torch.equal(y, ref), f"step {step}: max diff {(y.float() - ref.float()).abs().max().item()}"
     finally:
         peer.close()
-        _lib.set_option("ep_overlap", 1)
+        _lib.set_option("ep_overlap", -1)
 
 
 def _free_port():
@@ -192,7 +192,7 @@ def _ep_worker(rank, world, port, out_dir):
     y_peer2b = peer(x2)
     _lib.set_option("ep_overlap", 2)
     y_peer2c = peer(x2)
-    _lib.set_option("ep_overlap", 1)
+    _lib.set_option("ep_overlap", -1)
     assert ops.read_status(ops.workspace(x.device, 1)) == 0
     y_dedup2 = ExpertParallelMoE.from_dense(moe, dedup=True)(x2)
     torch.cuda.synchronize()
