@@ -84,36 +84,56 @@ __device__ __forceinline__ bool last_block_done(unsigned* counter) {
 // Source side: send row r (token row_token[r], destination d = row_slot[r] % P,
 // j = r - rank_offsets[d]) of destinations [d_first, d_first + d_count) to
 // region (d - src) mod P of d's buffer: the token row, its K slots as d sees
-// them and their weights.  One warp per pair of rows: both rows' metadata,
-// then both rows' 4 KB of loads, are in flight before the stores (the stores
-// to a peer are posted; the loads set the pace).  The last CTA publishes each
-// destination's count and raises its dispatch flag.
+// them and their weights.  The grid walks the destinations by distance from
+// src (src + 1 first, src itself last), so that while every rank sends, each
+// destination is being written by one source at a time instead of all ranks
+// writing to the same destination (their rows are sorted by destination rank
+// alike).  One warp per pair of rows: both rows' metadata, then both rows'
+// 4 KB of loads, are in flight before the stores (the stores to a peer are
+// posted; the loads set the pace).  The last CTA publishes each destination's
+// count and raises its dispatch flag.
 __global__ void __launch_bounds__(256) ep_peer_send_kernel(
     const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ idx, const float* __restrict__ w,
     const int32_t* __restrict__ row_token, const int32_t* __restrict__ row_slot,
     const int32_t* __restrict__ rank_offsets, int H, int K, int P, int El, int Tm, int src, int d_first, int d_count,
     EpPeerPtrs peers, EpPeerLayout L, unsigned* counter, const uint32_t* epoch_p) {
   constexpr int kRowsPerWarp = 2;
+  // destinations in walking order and where each starts in the walk
+  __shared__ int s_dest[kMaxPeers + 1], s_start[kMaxPeers + 1];
+  if (threadIdx.x == 0) {
+    int n = 0, o = 0;
+    for (int q = 1; q <= P; ++q) {
+      const int d = (src + q) % P;
+      if (d < d_first || d >= d_first + d_count) continue;
+      s_dest[n] = d;
+      s_start[n] = o;
+      o += rank_offsets[d + 1] - rank_offsets[d];
+      ++n;
+    }
+    s_start[n] = o;
+    s_dest[n] = n;  // number of destinations walked
+  }
+  __syncthreads();
+  const int nd = s_dest[d_count];
   const int lane = threadIdx.x & 31;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  const long long r_begin = rank_offsets[d_first];
-  const long long rows = rank_offsets[d_first + d_count] - r_begin;
+  const long long rows = s_start[nd];
   const int chunks = H >> 3;
   for (long long i0 = (static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kRowsPerWarp;
        i0 < rows; i0 += nw * kRowsPerWarp) {
-    const long long r0 = r_begin + i0;
     int t[kRowsPerWarp], d[kRowsPerWarp];
     long long dst_row[kRowsPerWarp];
 #pragma unroll
     for (int q = 0; q < kRowsPerWarp; ++q) {
-      const long long r = i0 + q < rows ? r0 + q : r0;
+      const long long i = i0 + q < rows ? i0 + q : i0;
+      int k = 0;
+      while (k + 1 < nd && s_start[k + 1] <= i) ++k;
+      d[q] = s_dest[k];
+      const long long jrow = i - s_start[k];
+      const long long r = rank_offsets[d[q]] + jrow;
       t[q] = row_token[r];
-      d[q] = row_slot[r] % P;
-    }
-#pragma unroll
-    for (int q = 0; q < kRowsPerWarp; ++q) {
       const int region = (d[q] - src + P) % P;
-      dst_row[q] = static_cast<long long>(region) * Tm + (r0 + q - rank_offsets[d[q]]);
+      dst_row[q] = static_cast<long long>(region) * Tm + jrow;
     }
     for (int c0 = lane; c0 < chunks; c0 += 256) {
       uint4 v[kRowsPerWarp][8];
