@@ -84,7 +84,8 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * every row has arrived; 1 sends, computes and returns overlapped, the send
  * and return kernels storing over NVLink from a side stream; 2 the same with
  * the rows and sums gathered into local staging and moved by the copy
- * engines; -1, the default, picks 2 when max_tokens >= 1024 and 0 below),
+ * engines; -1, the default, picks 2 on 2 to 4 ranks when max_tokens >= 1024
+ * and 0 otherwise),
  * "ep_groups" (remote regions taken in this many groups by the overlapped
  * schedules, 1 to 7; 0 = auto, min(ranks - 1, 2)),
  * "ep_side_ctas" (grid bound of the send and return kernels that run beside

@@ -1441,12 +1441,15 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   const uint32_t* disp_flag = reinterpret_cast<const uint32_t*>(own + PL.disp_flag);
   const uint32_t* res_flag = reinterpret_cast<const uint32_t*>(own + PL.res_flag);
   const long long budget = g_peer_wait_cycles.load();
-  // auto: overlap pays where the transfers are long (prefill-sized batches);
-  // a decode step is a handful of rows, where the one block's few launches win.
-  // Each rank decides for itself: every schedule writes the same buffers the
-  // same way, only the order of the work differs.
+  // auto: the copy-engine overlap for prefill-sized batches on 2 to 4 ranks
+  // (measured at 8192 tokens per rank: 4 ranks 0.99 ms against 1.12 ms in one
+  // block, 2 ranks on par); one block on more ranks, where the whole-region
+  // copies of every pair of ranks outlast the expert work (8 ranks: 1.75 ms
+  // against 1.55), and for decode steps (a handful of rows, where the one
+  // block's few launches win).  Each rank decides for itself: every schedule
+  // writes the same buffers the same way, only the order of the work differs.
   int schedule = g_ep_overlap.load();
-  if (schedule < 0) schedule = (P > 1 && Tm >= 1024) ? 2 : 0;
+  if (schedule < 0) schedule = (P > 1 && P <= 4 && Tm >= 1024) ? 2 : 0;
   const bool overlapped = schedule != 0;
 
   if (!overlapped) {
