@@ -589,13 +589,15 @@ def run_b200(args):
         if which == workloads[0]:
             sampler.mark(False)
         order, names = (EP_STAGE_ORDER, EP_STAGES) if ep_peer else (STAGE_ORDER, STAGES)
-        st = st_o = None
+        st = st_o = ep_schedule = None
         n_stage_steps = max(5, min(args.steps, 20))
         if ep_peer:
             # the timed (overlapped) schedule's stages; then the one-block
             # schedule, whose stages isolate each kernel (GEMM-1 roofline,
             # exchange rates) -- every rank takes the same steps
-            if args.ep_overlap != 0 and (args.ep_overlap > 0 or T_local >= 1024):
+            schedule = _lib.size_call("nkimoe_ep_peer_schedule", world, T_local)
+            ep_schedule = {0: "one block", 1: "overlapped, SM stores", 2: "overlapped, copy engines"}[schedule]
+            if schedule != 0:
                 st_o = measure_stages(torch, fwd, n_stage_steps, stage_events(torch), graph_of, EPO_STAGE_ORDER)
             _lib.set_option("ep_overlap", 0)
             try:
@@ -608,6 +610,8 @@ def run_b200(args):
         r = {"ms_per_step": ms, "tokens_per_s": tokens_total / (ms * 1e-3),
              "block_tflops": alg["block_flops"] * world / (ms * 1e-3) / 1e12,
              "block_gbs": alg["block_bytes"] * world / (ms * 1e-3) / 1e9, "alg": alg, "stages_ms": None}
+        if ep_schedule is not None:
+            r["ep_schedule"] = ep_schedule
         i1, i2 = names.index("gemm1_swiglu"), names.index("gemm2_scale")
         if st is not None:
             st_max = max_over_ranks(st)
@@ -779,7 +783,8 @@ def run_b200(args):
         "block_tflops": m["block_tflops"],
         "stages_ms": m["stages_ms"],
     }
-    for k in ("roofline_gemm2", "roofline_step", "exchange", "parity", "stages_ms_note", "stages_ms_one_block"):
+    for k in ("roofline_gemm2", "roofline_step", "exchange", "parity", "stages_ms_note", "stages_ms_one_block",
+              "ep_schedule"):
         if k in m:
             line[k] = m[k]
     if "rank_rows_max_over_mean" in m:
@@ -801,7 +806,8 @@ def run_b200(args):
                           "rank_rows_max_over_mean": d.get("rank_rows_max_over_mean",
                                                            d.get("rank_rows_max_over_mean_at_8")),
                           "roofline": d.get("roofline"), "stages_ms": d["stages_ms"],
-                          "stages_ms_one_block": d.get("stages_ms_one_block"), "parity": d.get("parity"),
+                          "stages_ms_one_block": d.get("stages_ms_one_block"), "ep_schedule": d.get("ep_schedule"),
+                          "parity": d.get("parity"),
                           "exchange": d.get("exchange"), "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline")}
     if not args.no_stack and (world == 1 or 8 % world == 0):
         line["stack"] = measure_stack(torch, world, rank)

@@ -463,6 +463,11 @@ NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I
  * (nkimoe_read_status) after a bounded wait (~10 s; option
  * "peer_wait_cycles").  topk_idx_out / topk_w_out (device, [T, K], may be
  * NULL): the routing of this rank's tokens, as nkimoe_moe_block returns it. */
+/* The schedule nkimoe_ep_peer_forward takes for num_ranks ranks and buffers of
+ * max_tokens rows under the current "ep_overlap" option: 0 one block, 1
+ * overlapped with SM stores, 2 overlapped with copy engines.  Host-only; no
+ * reference counterpart. */
+NKIMOE_API int nkimoe_ep_peer_schedule(int64_t num_ranks, int64_t max_tokens);
 NKIMOE_API int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias,
                                       const void* router_w_split, const void* w13_local, const void* w2_local,
                                       void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H,

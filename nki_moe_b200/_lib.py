@@ -79,6 +79,7 @@ SIGNATURES = {
     "nkimoe_peer_close": (_i, [_vp]),
     "nkimoe_peer_free": (_i, [_vp]),
     "nkimoe_ep_peer_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "nkimoe_ep_peer_schedule": (_i, [_i64, _i64]),
     "nkimoe_ep_peer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _c.POINTER(_vp), _c.c_uint32, _vp, _sz, _vp]),
     "nkimoe_ep_dispatch_workspace_bytes": (_sz, [_i64, _i64]),

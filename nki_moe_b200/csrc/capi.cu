@@ -1370,6 +1370,12 @@ size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E
   return peer_ws(T, H, I, E, K, num_ranks, max_tokens).total;
 }
 
+int nkimoe_ep_peer_schedule(int64_t num_ranks, int64_t max_tokens) {
+  const int schedule = g_ep_overlap.load();
+  if (schedule >= 0) return schedule;
+  return (num_ranks > 1 && num_ranks <= 4 && max_tokens >= 1024) ? 2 : 0;
+}
+
 int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
                            const void* w13_local, const void* w2_local, void* out, int32_t* topk_idx_out,
                            float* topk_w_out, int64_t T, int64_t H, int64_t I,
@@ -1448,8 +1454,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   // against 1.55), and for decode steps (a handful of rows, where the one
   // block's few launches win).  Each rank decides for itself: every schedule
   // writes the same buffers the same way, only the order of the work differs.
-  int schedule = g_ep_overlap.load();
-  if (schedule < 0) schedule = (P > 1 && P <= 4 && Tm >= 1024) ? 2 : 0;
+  const int schedule = nkimoe_ep_peer_schedule(P, Tm);
   const bool overlapped = schedule != 0;
 
   if (!overlapped) {
