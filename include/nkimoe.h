@@ -60,7 +60,9 @@ extern "C" {
 NKIMOE_API int nkimoe_version(void);
 NKIMOE_API const char* nkimoe_last_error(void);
 /* Process-wide tuning knobs: "gemm_schedule" (0 auto, 1 rows on one SM,
- * 2 weights, 3 rows on an SM pair, 4 features x rows on an SM pair),
+ * 2 weights, 3 rows on an SM pair, 4 features x rows on an SM pair, 5 rows
+ * on an SM pair over each expert's whole 256-row blocks and on one SM past
+ * them),
  * "weights_rows" (16, 32 or 64 rows per decode tile), "router" (0 auto,
  * 1 CUDA-core fp32, 2 tensor-core split-fp32), "prefetch" (64-wide K blocks
  * of a prefill GEMM CTA's next tile pulled into L2 when it starts a tile;

@@ -141,7 +141,7 @@ int choose_variant(long long rows_total, long long E, long long N) {
   // the SM-pair schedule is selected only on request: measured slower than the
   // 1-SM schedule on B200 for these shapes (TMA completions in the pair run at
   // about a third of the 1-SM rate)
-  if (N % 256 == 0 && sched == 3) return kRows2BN256;
+  if (N % 256 == 0 && (sched == 3 || sched == 5)) return kRows2BN256;
   if (N % 256 == 0 && sched == 4) return kTokens2;
   return (N % 256 == 0) ? kRowsBN256 : kRowsBN128;
 }
@@ -208,7 +208,22 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   const long long max_tiles = (rows_total / rpt + E) * (N / fpt);
   long long grid = std::min<long long>(max_tiles, device_sm_count());
   if (pair) grid = 2 * std::max<long long>(1, std::min<long long>(max_tiles, device_sm_count() / 2));
+  // schedule 5: the SM pair over each expert's whole 256-row blocks (no padded
+  // rows), then the 1-SM kernel over the rows past them
+  const bool split = variant == kRows2BN256 && g_schedule.load() == 5 && !shared_a && offsets;
+  if (split) p.row_split = 1;
   NKI_CUDA(grouped_gemm_launch(variant, ta, tw, p, static_cast<int>(std::max<long long>(grid, 1)), s));
+  if (split) {
+    const int v2 = kRowsBN256;
+    NKI_REQUIRE(make_tmap_bf16(&ta, act, act_rows, kd_act, grouped_gemm_box_rows_act(v2)) &&
+                    make_tmap_bf16(&tw, w, weight_experts * N, kd, grouped_gemm_box_rows_w(v2)),
+                NKIMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the remainder rows' operands");
+    p.row_split = 2;
+    // at most one 128-row block of remainder per 128 rows and per expert
+    const long long tiles2 = (std::min<long long>(rows_total, E * 255) / 128 + E) * (N / 256);
+    const long long grid2 = std::max<long long>(1, std::min<long long>(tiles2, device_sm_count()));
+    NKI_CUDA(grouped_gemm_launch(v2, ta, tw, p, static_cast<int>(grid2), s));
+  }
   return NKIMOE_OK;
 }
 
@@ -713,7 +728,7 @@ const char* nkimoe_last_error(void) { return g_err.c_str(); }
 int nkimoe_set_option(const char* name, long long value) {
   if (!name) return fail(NKIMOE_ERR_INVALID_ARG, "null option name");
   const std::string n(name);
-  if (n == "gemm_schedule" && value >= 0 && value <= 4) {
+  if (n == "gemm_schedule" && value >= 0 && value <= 5) {
     g_schedule = static_cast<int>(value);
     return NKIMOE_OK;
   }

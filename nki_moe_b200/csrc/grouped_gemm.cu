@@ -48,9 +48,15 @@ struct SharedCtl {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  int seg[kMaxExperts + 1];         // expert row offsets
+  int seg[kMaxExperts + 1];         // first row of each expert's rows in this launch
+  int seg_end[kMaxExperts];         // one past its last row
   int tile_start[kMaxExperts + 1];  // first tile of each expert
 };
+
+// Row split between the SM-pair kernel and the 1-SM kernel (row_split 1 / 2
+// in GroupedGemmParams): the pair takes each expert's whole blocks of this
+// many rows, the 1-SM kernel the rows past them.
+constexpr int kSplitRows = 256;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -74,7 +80,7 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 
 // Per-expert tile table in smem.  tiles(e) = ceil(rows_e / rows_per_tile) * feat_tiles.
 __device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int dense_rows, int E, int rows_per_tile,
-                                 int feat_tiles) {
+                                 int feat_tiles, int row_split = 0) {
   const int lane = threadIdx.x & 31;
   int run = 0;
   for (int b = 0; b < E; b += 32) {
@@ -83,6 +89,12 @@ __device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int dense_
     if (e < E) {
       s0 = offs ? offs[e] : e * dense_rows;
       cnt = offs ? offs[e + 1] - s0 : dense_rows;
+      if (row_split == 1) {
+        cnt -= cnt % kSplitRows;  // whole blocks only
+      } else if (row_split == 2) {
+        s0 += cnt - cnt % kSplitRows;  // the rows past the whole blocks
+        cnt %= kSplitRows;
+      }
     }
     const int tiles = ((cnt + rows_per_tile - 1) / rows_per_tile) * feat_tiles;
     int incl = tiles;
@@ -94,6 +106,7 @@ __device__ void build_tile_table(SharedCtl& ctl, const int32_t* offs, int dense_
     if (e < E) {
       ctl.tile_start[e] = run + incl - tiles;
       ctl.seg[e] = s0;
+      ctl.seg_end[e] = s0 + cnt;
     }
     run += __shfl_sync(0xffffffffu, incl, 31);
   }
@@ -327,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_w);
   }
   if (warp == 1) tmem_alloc(&ctl.tmem_base, TMEM_COLS);
-  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BM, feat_tiles);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BM, feat_tiles, p.row_split);
   tcgen05_fence_before();
   __syncthreads();
   tcgen05_fence_after();
@@ -353,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // accumulator rows are never stored)
         int src_row[BM / 32];
         if (gather_a) {
-          const int seg_end = ctl.seg[tc.e + 1];
+          const int seg_end = ctl.seg_end[tc.e];
           const int first = p.a_row_map[row0];
 #pragma unroll
           for (int j = 0; j < BM / 32; ++j) {
@@ -475,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord tc = decode_tile(ctl, E, tile, BM, feat_tiles);
       const int acc = t_local & 1;
       const uint32_t acc_phase = (t_local >> 1) & 1;
-      const int seg_end = ctl.seg[tc.e + 1];
+      const int seg_end = ctl.seg_end[tc.e];
       const int r = ctl.seg[tc.e] + tc.rblk * BM + row_in_tile;
       const bool valid = r < seg_end;
       // per-row loads issued before the accumulator wait so their latency overlaps it
@@ -553,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmap_w);
   }
   if (warp == 1) tmem_alloc_2sm(&ctl.tmem_base, TMEM_COLS);
-  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BM2, feat_tiles);
+  if (warp == 2) build_tile_table(ctl, p.expert_offsets, p.dense_rows, E, BM2, feat_tiles, p.row_split);
   tcgen05_fence_before();
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
   tcgen05_fence_after();
@@ -662,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord tc = decode_tile(ctl, E, tile, BM2, feat_tiles);
       const int acc = t_local & 1;
       const uint32_t acc_phase = (t_local >> 1) & 1;
-      const int seg_end = ctl.seg[tc.e + 1];
+      const int seg_end = ctl.seg_end[tc.e];
       const int r = ctl.seg[tc.e] + tc.rblk * BM2 + row_in_tile;
       const bool valid = r < seg_end;
       const long long orow = valid ? (p.out_row_map ? p.out_row_map[r] : r) : 0;
@@ -764,7 +777,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = pair; ok && tile < total_tiles; tile += npairs) {
         const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
         const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
-        const int nt = min(BT, ctl.seg[tc.e + 1] - row0);
+        const int nt = min(BT, ctl.seg_end[tc.e] - row0);
         const int half = ((nt + 15) & ~15) >> 1;  // rows of the MMA's N supplied by each CTA
         const int brow = (p.shared_a ? tc.rblk * BT : row0) + static_cast<int>(rank) * half;
         const int wrow = (p.weight_mod ? tc.e % p.weight_mod : tc.e) * p.n + tc.fblk * BF + static_cast<int>(rank) * BM;
@@ -809,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int t_local = 0;
       for (int tile = pair; ok && tile < total_tiles; tile += npairs, ++t_local) {
         const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
-        const int nt = min(BT, ctl.seg[tc.e + 1] - ctl.seg[tc.e] - tc.rblk * BT);
+        const int nt = min(BT, ctl.seg_end[tc.e] - ctl.seg[tc.e] - tc.rblk * BT);
         const uint32_t idesc = umma_idesc_bf16_f32(BF, (nt + 15) & ~15);
         const int acc = t_local & 1;
         const uint32_t acc_phase = (t_local >> 1) & 1;
@@ -857,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int acc = t_local & 1;
       const uint32_t acc_phase = (t_local >> 1) & 1;
       const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
-      const int nt = min(BT, ctl.seg[tc.e + 1] - row0);
+      const int nt = min(BT, ctl.seg_end[tc.e] - row0);
       bool ok = true;
       if (lane == 0) ok = mbar_wait_cluster(&ctl.acc_full[acc], acc_phase, &ctl.abort_flag, p.status);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -1018,14 +1031,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         int src_row[(BT + 31) / 32];
         int g4[4];
         if (gather_cp) {
-          const int seg_end = ctl.seg[tc.e + 1];
+          const int seg_end = ctl.seg_end[tc.e];
 #pragma unroll
           for (int j = 0; j < (BT + 31) / 32; ++j) {
             const int r = row0 + lane + 32 * j;
             src_row[j] = (lane + 32 * j < BT && r < seg_end) ? p.a_row_map[r] : -1;
           }
         } else if (gather_a) {
-          const int seg_end = ctl.seg[tc.e + 1];
+          const int seg_end = ctl.seg_end[tc.e];
           const int first = p.a_row_map[row0];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -1136,7 +1149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (named_bar_any(1, 128, !ok)) break;
       tcgen05_fence_after();
       const int r0 = ctl.seg[tc.e] + tc.rblk * BT;
-      const int nvalid = min(BT, ctl.seg[tc.e + 1] - r0);
+      const int nvalid = min(BT, ctl.seg_end[tc.e] - r0);
       float v[BT];
       tmem_ld_cols<BT>(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BT, v);
       tcgen05_fence_before();

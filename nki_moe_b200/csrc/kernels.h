@@ -284,6 +284,8 @@ struct GroupedGemmParams {
   const int32_t* out_row_map; // optional: output row of permuted row r
   const float* col_bias;      // kEpiStoreF32 optional
   int* status;
+  int row_split;              // rows schedules: 0 every row; 1 each expert's whole blocks of 256 rows
+                              // (the SM-pair kernel); 2 the rows past them (the 1-SM kernel)
 };
 
 // Tile shape choices exposed to the host.

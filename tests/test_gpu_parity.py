@@ -262,7 +262,7 @@ def test_bad_expert_id_is_reported():
 
 # ---------------------------------------------------------------- K4/K5
 @pytest.mark.parametrize("counts", [(5, 0, 130, 64, 1), (300, 17, 0, 256, 513, 16)])
-@pytest.mark.parametrize("schedule,rows", [(1, 0), (2, 16), (2, 32), (2, 64), (3, 0), (4, 0)])
+@pytest.mark.parametrize("schedule,rows", [(1, 0), (2, 16), (2, 32), (2, 64), (3, 0), (4, 0), (5, 0)])
 def test_grouped_gemm(schedule, rows, counts):
     """Ragged segments: empty, one-row, exact multiples of the tile and
     partial last tiles (300 = 256 + 44 rows) for every schedule."""
@@ -290,7 +290,7 @@ def test_grouped_gemm(schedule, rows, counts):
         _lib.set_option("weights_rows", 0)
 
 
-@pytest.mark.parametrize("schedule,rows", [(0, 0), (1, 0), (2, 16), (2, 32), (2, 64), (3, 0), (4, 0)])
+@pytest.mark.parametrize("schedule,rows", [(0, 0), (1, 0), (2, 16), (2, 32), (2, 64), (3, 0), (4, 0), (5, 0)])
 def test_moe_experts_tiny(golden_dir, schedule, rows):
     """The reference test's module case (H=256, I=512, E=4, top-2) given routing."""
     _lib.set_option("gemm_schedule", schedule)
@@ -337,7 +337,7 @@ def _oracle_block(xn, gun, dn, rwn, bias, idx_gpu, w_gpu):
     return oracle.experts_forward(xn, gun, dn, idx_gpu, w_gpu)
 
 
-@pytest.mark.parametrize("schedule", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("schedule", [0, 1, 2, 3, 4, 5])
 def test_moe_block_c1(c1_inputs, golden_dir, schedule):
     _lib.set_option("gemm_schedule", schedule)
     try:
@@ -363,7 +363,7 @@ def test_moe_block_c2_decode():
     assert len(np.unique(idx)) > 100  # natural routing touches ~all experts
 
 
-@pytest.mark.parametrize("schedule", [0, 1, 4])
+@pytest.mark.parametrize("schedule", [0, 1, 4, 5])
 def test_moe_block_c3_prefill_sampled_tokens(schedule):
     """Full prefill size (8192 tokens); each token's output depends only on
     that token, so 256 sampled tokens are checked against the oracle."""
@@ -384,7 +384,7 @@ def test_moe_block_c3_prefill_sampled_tokens(schedule):
     assert np.isfinite(out).all()
 
 
-@pytest.mark.parametrize("schedule", [0, 4])
+@pytest.mark.parametrize("schedule", [0, 4, 5])
 def test_moe_block_skewed_routing(schedule):
     wl = WORKLOADS["c4"]
     inp = make_moe_inputs(wl, tokens=2048)
@@ -762,3 +762,21 @@ def test_module_with_fused_post_attention_norm(c1_inputs):
         ref = moe(norm(h).bfloat16())
         fused = moe.fuse_rmsnorm(norm)(h)
     assert torch.equal(fused, ref)
+
+
+def test_pair_split_schedule_equals_one_sm_rows():
+    """Schedule 5 (the SM pair over each expert's whole 256-row blocks, one SM
+    past them) computes every output row with the same per-row arithmetic as
+    the one-SM rows schedule: the prefill block's outputs are identical."""
+    wl = WORKLOADS["c3"]
+    inp = make_moe_inputs(wl, device="cuda", tokens=4096)
+    x = inp["x"].to(torch.bfloat16)
+    pe = ops.packed_experts(inp["gate_up"].to(torch.bfloat16), inp["down"].to(torch.bfloat16), "nxd")
+    outs = []
+    for sched in (1, 5):
+        _lib.set_option("gemm_schedule", sched)
+        try:
+            outs.append(ops.moe_block(x, inp["router"], pe, wl.top_k))
+        finally:
+            _lib.set_option("gemm_schedule", 0)
+    assert torch.equal(outs[0], outs[1]), f"max diff {(outs[0].float() - outs[1].float()).abs().max().item()}"
