@@ -76,6 +76,8 @@ def parse():
     ap.add_argument("--ep-side-ctas", type=int, default=0,
                     help="N > 1, overlapped schedule: CTAs of the send / return kernels beside the GEMMs (0: library "
                          "default)")
+    ap.add_argument("--gemm-schedule", type=int, default=None,
+                    help="expert GEMM tile schedule (library option gemm_schedule; default: the library's)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: exchange over peer memory (library kernels) or NCCL all-to-all")
     return ap.parse_args()
@@ -478,6 +480,8 @@ def run_b200(args):
     _lib.load()
     _lib.set_option("ep_overlap", args.ep_overlap)
     _lib.set_option("ep_groups", args.ep_groups)
+    if args.gemm_schedule is not None:
+        _lib.set_option("gemm_schedule", args.gemm_schedule)
     if args.ep_side_ctas:
         _lib.set_option("ep_side_ctas", args.ep_side_ctas)
     if args.profile_once and args.stack_profile_layers > 0:
