@@ -178,7 +178,7 @@ def test_from_safetensors_equals_from_hf(tmp_path, fp8):
     assert torch.equal(a.prefill(ids, all_logits=True), b.prefill(ids, all_logits=True))
 
 
-def _ep_stack_worker(rank, world, port, out_dir):
+def _ep_stack_worker(rank, world, port, out_dir, overlap=-1):
     """One rank of an expert-parallel decoder stack (each rank: its own two
     sequences, E / P experts) next to a single-GPU stack with the same seed on
     the same GPU (all experts)."""
@@ -189,10 +189,12 @@ def _ep_stack_worker(rank, world, port, out_dir):
     import torch.distributed as dist
 
     from nki_moe_b200.qwen_stack import Qwen3MoEConfig, Qwen3MoEStack
+    from nki_moe_b200 import _lib
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
+    _lib.set_option("ep_overlap", overlap)
     cfg = Qwen3MoEConfig(vocab_size=1024, hidden_size=256, num_hidden_layers=2, num_attention_heads=4,
                          num_key_value_heads=2, head_dim=128, moe_intermediate_size=128, num_experts=8,
                          num_experts_per_tok=2)
@@ -217,12 +219,15 @@ def _ep_stack_worker(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_expert_parallel_stack_two_gpus(tmp_path):
+@pytest.mark.parametrize("overlap", [-1, 2])
+def test_expert_parallel_stack_two_gpus(tmp_path, overlap):
     """Expert-parallel decoder stack on 2 GPUs (peer-memory exchange in every
     layer, decode step captured in one CUDA graph with device-side epochs)
     against the single-GPU stack of the same weights: logits within the bars
     above (the exchange rounds each rank's partial sum to bf16), graph decode
-    bit-identical to eager decode."""
+    bit-identical to eager decode.  With the default schedule (one block at
+    these sizes) and with the copy-engine schedule forced, whose side-stream
+    copies are then captured into the decode graph."""
     import socket
 
     import numpy as np
@@ -232,7 +237,7 @@ def test_expert_parallel_stack_two_gpus(tmp_path):
     port = sock.getsockname()[1]
     sock.close()
     world = 2
-    mp.start_processes(_ep_stack_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_ep_stack_worker, args=(world, port, str(tmp_path), overlap), nprocs=world, join=True,
                        start_method="spawn")
     for r in range(world):
         ld = lambda k: torch.from_numpy(np.load(tmp_path / f"{k}_{r}.npy"))  # noqa: E731
