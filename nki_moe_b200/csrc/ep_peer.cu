@@ -255,8 +255,12 @@ __global__ void __launch_bounds__(256) ep_peer_combine_kernel(const __nv_bfloat1
   const int chunks = H >> 3;
   const long long rows = static_cast<long long>(nq) * Tm;
   const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long r = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
-       r += nw) {
+  // when the rows include region 0 (this rank's own, no NVLink), it is taken
+  // last, so the remote regions' stores start at once
+  const long long shift = (q0 == 0 && nq > 1) ? Tm : 0;
+  for (long long i = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); i < rows;
+       i += nw) {
+    const long long r = i + shift < rows ? i + shift : i + shift - rows;
     const int my_yr = lane < K ? slot_row[r * K + lane] : -1;
     const unsigned present = __ballot_sync(0xffffffffu, my_yr >= 0);
     if (present == 0u) continue;
