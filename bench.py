@@ -260,6 +260,27 @@ def cpu_inputs(inp, torch):
             else v.float().cpu().numpy() for k, v in inp.items()}
 
 
+def bind_to_gpu_cpus(gpu_index: int):
+    """Run this process on the CPUs next to its GPU (NVML's affinity mask for
+    the device), so that its page-locked host buffers are allocated in that
+    socket's memory and its host<->device copies do not cross sockets.
+    Returns the previous affinity (restored for the CPU legs), or None."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+        ncpu = os.cpu_count() or 1
+        masks = pynvml.nvmlDeviceGetCpuAffinity(h, (ncpu + 63) // 64)
+        cpus = {64 * i + b for i, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1 and 64 * i + b < ncpu}
+        before = os.sched_getaffinity(0)
+        if cpus and cpus != before:
+            os.sched_setaffinity(0, cpus)
+            return before
+    except Exception:  # noqa: BLE001 - no NVML or no affinity support: leave the process where it is
+        pass
+    return None
+
+
 def pin_cpu_threads():
     """Use every host core for the CPU legs, whatever the launcher set
     (torchrun exports OMP_NUM_THREADS=1): torch's intra-op pool and the BLAS
@@ -501,6 +522,7 @@ def run_b200(args):
         torch.cuda.nvtx.range_pop()
         return
     hbm_gbs, tf_burst, tf_sus, peak_src = peaks()
+    all_cpus = bind_to_gpu_cpus(local) if world > 1 else None
     sampler = ClockSampler(local)
     sampler.start()
     ep_peer = world > 1 and args.ep == "peer"
@@ -734,6 +756,8 @@ def run_b200(args):
         if not args.no_cpu_baseline and rank == 0:
             # the oracle on this rank's whole batch, repeated to about 10 s of
             # CPU work (3 s for the sub-workloads), on every host core
+            if all_cpus:
+                os.sched_setaffinity(0, all_cpus)
             pin_cpu_threads()
             cin = cpu_inputs(inp, torch)
             cin["x"] = x.float().cpu().numpy()
@@ -745,7 +769,18 @@ def run_b200(args):
                                  "sample": f"the {T_local}-token {wl.name} batch"
                                            f"{' of rank 0' if world > 1 else ''} x {rep} (numpy oracle, fp32), "
                                            f"{dt * rep:.1f} s"}
+            if all_cpus:
+                bind_to_gpu_cpus(local)
         if world > 1:
+            # the other ranks wait for rank 0's CPU leg on the rendezvous store
+            # (a blocking socket read), not in a collective whose host threads
+            # spin and would take cores from the CPU baseline
+            store = torch.distributed.distributed_c10d._get_default_store()
+            key = f"bench_cpu_leg_done_{which}"
+            if rank == 0:
+                store.set(key, "1")
+            else:
+                store.wait([key])
             torch.distributed.barrier()
         result[which] = r
         if block is not None and hasattr(block, "close"):
