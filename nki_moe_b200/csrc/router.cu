@@ -2,6 +2,9 @@
 //   logits = x . Wr^T in fp32 (router dtype fp32, qwen_with_nki.py:276),
 //   p = softmax(logits), (w, idx) = topk(p, K) descending, w /= sum(w).
 #include <algorithm>
+#include <mutex>
+#include <set>
+#include <utility>
 
 #include "kernels.h"
 #include "permute_small.cuh"
@@ -909,27 +912,30 @@ cudaError_t router_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_
     return cudaErrorInvalidValue;
   const size_t smem = router_tc_smem_bytes();
   const unsigned grid = static_cast<unsigned>((T + kRtRows - 1) / kRtRows);
-  if (norm) {
-    static bool attr = false;
-    if (!attr) {
-      cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
+  // the dynamic shared-memory opt-in, once per kernel and device (not per
+  // launch, so launches can be captured into CUDA graphs)
+  static std::mutex mu;
+  static std::set<std::pair<int, int>> done;  // (norm, device)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done.count({norm ? 1 : 0, dev})) {
+      e = norm ? cudaFuncSetAttribute(router_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem))
+               : cudaFuncSetAttribute(router_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem));
       if (e != cudaSuccess) return e;
-      attr = true;
+      done.insert({norm ? 1 : 0, dev});
     }
+  }
+  if (norm)
     router_tc_kernel<true><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out, bias,
                                                            logits_out, static_cast<int>(T), H, status);
-  } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      attr = true;
-    }
+  else
     router_tc_kernel<false><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr, bias,
                                                             logits_out, static_cast<int>(T), H, status);
-  }
   return cudaGetLastError();
 }
 }  // namespace nkimoe
