@@ -517,6 +517,31 @@ def test_programmatic_dependent_launch_off_is_bit_identical(c1_inputs):
         assert torch.equal(a, b)
 
 
+def test_back_to_back_decode_blocks_read_their_own_offsets(c1_inputs):
+    """Decode blocks launched back to back on one stream (no synchronisation
+    between calls, the workspace and its expert offsets reused by every call,
+    the routing different each time) equal the same blocks run one at a time
+    without programmatic dependent launch, bit for bit.  The decode GEMMs read
+    the offsets and start their weight loads before their dependency wait, so
+    a GEMM that saw the previous call's offsets would show here."""
+    g = torch.Generator().manual_seed(91)
+    rw = c1_inputs["router"].cuda()
+    pe = ops.packed_experts(*[bf(c1_inputs[k])[0] for k in ("gate_up", "down")], "nxd")
+    xs = [torch.randn((8, 8, 64)[i % 3], 2048, generator=g).bfloat16().cuda() for i in range(24)]
+    _lib.set_option("pdl", 0)
+    try:
+        ref = []
+        for x in xs:
+            ref.append(ops.moe_block(x, rw, pe, 8))
+            torch.cuda.synchronize()
+    finally:
+        _lib.set_option("pdl", 1)
+    outs = [ops.moe_block(x, rw, pe, 8) for x in xs]
+    torch.cuda.synchronize()
+    for a, b in zip(outs, ref):
+        assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("T,chunk,pinned", [(2048, 0, True), (2048, 1000, False), (3000, 769, True),
                                             (300, 0, True), (5, 0, True), (0, 0, True)])
 def test_moe_block_host_equals_device_block(c1_inputs, T, chunk, pinned):
