@@ -78,6 +78,9 @@ def parse():
                          "default)")
     ap.add_argument("--gemm-schedule", type=int, default=None,
                     help="expert GEMM tile schedule (library option gemm_schedule; default: the library's)")
+    ap.add_argument("--ep-replicas", type=int, default=-1,
+                    help="N > 1, peer exchange: extra expert slots per rank for copies of hot experts, planned from "
+                         "the routing of a calibration batch (-1: 2 for the skewed workload, 0 otherwise)")
     ap.add_argument("--ep", default="peer", choices=["peer", "nccl"],
                     help="N > 1: exchange over peer memory (library kernels) or NCCL all-to-all")
     return ap.parse_args()
@@ -443,14 +446,21 @@ def measure_stack(torch, world=1, rank=0):
             "data": "synthetic"}
 
 
-def ep_exchange_counts(torch, idx, world, rank, experts):
+def ep_exchange_counts(torch, idx, world, rank, experts, block=None):
     """(token, rank) rows and (token, slot) pairs between the ranks of an
     expert-parallel step, from every rank's routing: rows[s][d] = tokens of
     rank s with an expert on rank d (each sent once), pairs[s][d] = their
-    (token, slot) pairs."""
+    (token, slot) pairs.  With a peer block holding hot-expert replicas, slot
+    (t, k) goes to the rank of holder t mod n_e of its expert, as the
+    exchange sends it."""
     import torch.distributed as dist
-    el = experts // world
-    dr = idx.long() // el
+    if block is not None and getattr(block, "replicas", None) is not None:
+        il = idx.long()
+        t = torch.arange(idx.shape[0], device=idx.device).unsqueeze(1)
+        v = block.expert_slots.long()[il, t % block.slot_counts.long()[il]]
+        dr = v // block.local_slots
+    else:
+        dr = idx.long() // (experts // world)
     hit = torch.zeros(idx.shape[0], world, dtype=torch.bool, device=idx.device)
     hit.scatter_(1, dr, True)
     mine = torch.stack([hit.sum(0), torch.bincount(dr.flatten(), minlength=world)]).to(torch.int64)
@@ -593,9 +603,20 @@ def run_b200(args):
         block = None
         if world > 1:
             if ep_peer:
-                from nki_moe_b200.ep_peer import PeerExpertParallelMoE
+                from nki_moe_b200.ep_peer import PeerExpertParallelMoE, expert_load
+                extra = args.ep_replicas if args.ep_replicas >= 0 else (2 if which == "skewed" else 0)
+                load = None
+                if extra > 0:
+                    # the plan comes from another batch of the same distribution
+                    # (its routing summed over the ranks), not the timed one
+                    g_cal = torch.Generator(device="cuda").manual_seed(wl.seed * 7919 + 17 + rank)
+                    x_cal = torch.randn(T_local, wl.hidden, generator=g_cal, device="cuda").to(torch.bfloat16)
+                    _, idx_cal, _ = ops.moe_block(x_cal, rw, pe, wl.top_k, bias=rb, return_routing=True)
+                    load = expert_load(idx_cal, wl.experts)
+                    del x_cal, idx_cal
                 # epochs counted on the device: the step replays as a CUDA graph
-                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=T_local, device_epochs=True)
+                block = PeerExpertParallelMoE.from_dense(moe, max_tokens=T_local, device_epochs=True,
+                                                         extra_slots=extra, expected_load=load)
             else:
                 from nki_moe_b200.ep import ExpertParallelMoE
                 block = ExpertParallelMoE.from_dense(moe, torch.distributed.group.WORLD)
@@ -652,7 +673,17 @@ def run_b200(args):
                                    "GEMMs); stages_ms_one_block: the one-block schedule, whose stages isolate the "
                                    "kernels (the roofline and exchange figures come from it)")
         if world > 1:
-            rows, pairs = ep_exchange_counts(torch, idx_one, world, rank, wl.experts)
+            rows, pairs = ep_exchange_counts(torch, idx_one, world, rank, wl.experts,
+                                             block if ep_peer else None)
+            if ep_peer and block.replicas is not None:
+                _, pairs0 = ep_exchange_counts(torch, idx_one, world, rank, wl.experts)
+                r["replicas"] = {
+                    "extra_slots_per_rank": block.local_slots - wl.experts // world,
+                    "copies": sum(len(h) - 1 for h in block.replicas[1]),
+                    "max_holders": block.max_holders,
+                    "rank_rows_max_over_mean_without": float(pairs0.sum(0).max() / pairs0.sum(0).float().mean()),
+                    "plan": "greedy copies of the busiest rank's heaviest expert onto the least loaded rank, from "
+                            "the routing of a separate calibration batch of the same distribution"}
             pairs_in = int(pairs[:, rank].sum())
             rows_out_remote = int(rows[rank].sum() - rows[rank, rank])
             rows_in_remote = int(rows[:, rank].sum() - rows[rank, rank])
@@ -846,7 +877,7 @@ def run_b200(args):
                                                            d.get("rank_rows_max_over_mean_at_8")),
                           "roofline": d.get("roofline"), "stages_ms": d["stages_ms"],
                           "stages_ms_one_block": d.get("stages_ms_one_block"), "ep_schedule": d.get("ep_schedule"),
-                          "parity": d.get("parity"),
+                          "parity": d.get("parity"), "replicas": d.get("replicas"),
                           "exchange": d.get("exchange"), "e2e": d.get("e2e"), "cpu_baseline": d.get("cpu_baseline")}
     if not args.no_stack and (world == 1 or 8 % world == 0):
         line["stack"] = measure_stack(torch, world, rank)

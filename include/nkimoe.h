@@ -440,6 +440,12 @@ NKIMOE_API int nkimoe_peer_free(void* ptr);
 NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
                                                  int64_t num_ranks, int64_t max_tokens);
 
+/* The schedule nkimoe_ep_peer_forward takes for num_ranks ranks and buffers of
+ * max_tokens rows under the current "ep_overlap" option: 0 one block, 1
+ * overlapped with SM stores, 2 overlapped with copy engines.  Host-only; no
+ * reference counterpart. */
+NKIMOE_API int nkimoe_ep_peer_schedule(int64_t num_ranks, int64_t max_tokens);
+
 /* The expert-parallel MoE block for this rank's T <= max_tokens tokens, one
  * stream-ordered call with no host synchronisation: route (as
  * nkimoe_moe_block) -> each token's row sent once to every rank owning one of
@@ -465,17 +471,40 @@ NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I
  * (nkimoe_read_status) after a bounded wait (~10 s; option
  * "peer_wait_cycles").  topk_idx_out / topk_w_out (device, [T, K], may be
  * NULL): the routing of this rank's tokens, as nkimoe_moe_block returns it. */
-/* The schedule nkimoe_ep_peer_forward takes for num_ranks ranks and buffers of
- * max_tokens rows under the current "ep_overlap" option: 0 one block, 1
- * overlapped with SM stores, 2 overlapped with copy engines.  Host-only; no
- * reference counterpart. */
-NKIMOE_API int nkimoe_ep_peer_schedule(int64_t num_ranks, int64_t max_tokens);
 NKIMOE_API int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias,
                                       const void* router_w_split, const void* w13_local, const void* w2_local,
                                       void* out, int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H,
                                       int64_t I, int64_t E, int64_t K,
                                       int64_t num_ranks, int64_t rank, int64_t max_tokens, void* const* peer_buffers,
                                       uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
+
+/* nkimoe_ep_peer_forward with hot-expert replicas: every rank holds
+ * local_slots expert slots (its own experts and copies of other ranks' hot
+ * experts; slot v is local expert v % local_slots of rank v / local_slots;
+ * w13_local / w2_local hold this rank's local_slots packed experts).
+ * expert_slots (device int32 [E, max_holders]) lists, for expert e, the
+ * slot_counts[e] (device int32 [E], 1..max_holders) slots that hold its
+ * weights; slot k of token t with expert e goes to slot expert_slots[e *
+ * max_holders + t mod slot_counts[e]], so an expert's tokens are split evenly
+ * over its holders.  With every slot_counts[e] = 1 and expert e at slot e
+ * (local_slots = E / P) this is nkimoe_ep_peer_forward.  Every rank passes
+ * the same tables.  The partial sums a token gets back come from the ranks
+ * its slots went to, so the output meets the block tolerance against the
+ * single-GPU block (as without replicas); the returned routing is the real
+ * expert ids.  An entry outside [0, num_ranks * local_slots) drops its slot
+ * and sets NKIMOE_DEV_BAD_INDEX.  The reference has no counterpart (NxDI's
+ * moe_ep_degree partitions experts statically, qwen.py:272, :515). */
+NKIMOE_API size_t nkimoe_ep_peer_workspace_bytes_mapped(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                                        int64_t num_ranks, int64_t max_tokens, int64_t local_slots);
+NKIMOE_API int nkimoe_ep_peer_forward_mapped(const void* x, const float* router_w, const float* router_bias,
+                                             const void* router_w_split, const void* w13_local,
+                                             const void* w2_local, void* out, int32_t* topk_idx_out,
+                                             float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
+                                             int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
+                                             void* const* peer_buffers, uint32_t epoch, void* workspace,
+                                             size_t workspace_bytes, void* stream, int64_t local_slots,
+                                             const int32_t* expert_slots, const int32_t* slot_counts,
+                                             int64_t max_holders);
 
 /* ---------------------------------------------------------------- pieces */
 

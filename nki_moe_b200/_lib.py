@@ -82,6 +82,10 @@ SIGNATURES = {
     "nkimoe_ep_peer_schedule": (_i, [_i64, _i64]),
     "nkimoe_ep_peer_forward": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _c.POINTER(_vp), _c.c_uint32, _vp, _sz, _vp]),
+    "nkimoe_ep_peer_workspace_bytes_mapped": (_sz, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+    "nkimoe_ep_peer_forward_mapped": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                           _i64, _i64, _i64, _c.POINTER(_vp), _c.c_uint32, _vp, _sz, _vp, _i64, _vp,
+                                           _vp, _i64]),
     "nkimoe_ep_dispatch_workspace_bytes": (_sz, [_i64, _i64]),
     "nkimoe_ep_dispatch": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _sz,
                                 _vp]),

@@ -445,7 +445,7 @@ int experts_impl(const void* x, const void* w13, const void* w2, const void* idx
 // the rank's own tokens (their own-expert slots in self_idx / self_w) and one
 // per group of remote regions.  The workspace holds the larger of the two.
 struct PeerWs {
-  size_t route, disp, slot_in, slot_out, counters, self_idx, self_w, recv;
+  size_t route, disp, slot_in, slot_out, counters, self_idx, self_w, idx_v, recv;
   // copy-engine schedule: outgoing rows per destination and returned sums per region
   size_t stage_x, stage_slots, stage_w, stage_counts, ret_stage, total;
 };
@@ -469,7 +469,9 @@ size_t overlapped_recv_bytes(long long T, long long H, long long I, long long El
   return o;
 }
 
-PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, long long P, long long Tm) {
+// El: expert slots per rank (E / P, or more with hot-expert replicas).
+PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, long long P, long long Tm,
+               long long El) {
   PeerWs W{};
   size_t o = 0;
   W.route = o; o += round256(ws_layout(T, H, I, E, K).offsets);  // status, logits, partials, idx, w
@@ -479,9 +481,10 @@ PeerWs peer_ws(long long T, long long H, long long I, long long E, long long K, 
   W.counters = o; o += 256;
   W.self_idx = o; o += round256(sizeof(int32_t) * T * K);
   W.self_w = o; o += round256(sizeof(float) * T * K);
+  W.idx_v = o; o += round256(sizeof(int32_t) * T * K);
   W.recv = o;
-  size_t recv = ws_layout(P * Tm, H, I, E / P, K).total;
-  for (long long g = 1; g < P; ++g) recv = std::max(recv, overlapped_recv_bytes(T, H, I, E / P, K, P, Tm, g));
+  size_t recv = ws_layout(P * Tm, H, I, El, K).total;
+  for (long long g = 1; g < P; ++g) recv = std::max(recv, overlapped_recv_bytes(T, H, I, El, K, P, Tm, g));
   o += round256(recv);
   W.stage_x = o; o += round256(sizeof(uint16_t) * P * Tm * H);
   W.stage_slots = o; o += round256(sizeof(int32_t) * P * Tm * K);
@@ -1382,7 +1385,13 @@ int nkimoe_peer_free(void* ptr) {
 size_t nkimoe_ep_peer_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K, int64_t num_ranks,
                                       int64_t max_tokens) {
   if (num_ranks <= 0 || E % num_ranks != 0) return 0;
-  return peer_ws(T, H, I, E, K, num_ranks, max_tokens).total;
+  return peer_ws(T, H, I, E, K, num_ranks, max_tokens, E / num_ranks).total;
+}
+
+size_t nkimoe_ep_peer_workspace_bytes_mapped(int64_t T, int64_t H, int64_t I, int64_t E, int64_t K,
+                                             int64_t num_ranks, int64_t max_tokens, int64_t local_slots) {
+  if (num_ranks <= 0 || local_slots <= 0 || local_slots > kMaxExperts) return 0;
+  return peer_ws(T, H, I, E, K, num_ranks, max_tokens, local_slots).total;
 }
 
 int nkimoe_ep_peer_schedule(int64_t num_ranks, int64_t max_tokens) {
@@ -1391,21 +1400,31 @@ int nkimoe_ep_peer_schedule(int64_t num_ranks, int64_t max_tokens) {
   return (num_ranks > 1 && num_ranks <= 4 && max_tokens >= 1024) ? 2 : 0;
 }
 
-int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
-                           const void* w13_local, const void* w2_local, void* out, int32_t* topk_idx_out,
-                           float* topk_w_out, int64_t T, int64_t H, int64_t I,
-                           int64_t E, int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
-                           void* const* peer_buffers, uint32_t epoch, void* workspace, size_t workspace_bytes,
-                           void* stream) {
+// The expert-parallel block; El expert slots per rank, slot v on rank
+// v / El.  Without expert_slots slot v is expert v (El = E / P); with them
+// slot (t, k) of expert e goes to slot expert_slots[e * max_holders + t mod
+// slot_counts[e]] (hot-expert replicas).
+static int ep_peer_forward_impl(const void* x, const float* router_w, const float* router_bias,
+                                const void* router_w_split, const void* w13_local, const void* w2_local, void* out,
+                                int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I, int64_t E,
+                                int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
+                                void* const* peer_buffers, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                                void* stream, long long El, const int32_t* expert_slots, const int32_t* slot_counts,
+                                long long max_holders) {
   const long long P = num_ranks, Tm = max_tokens;
   int rc = check_moe_shapes(std::max<long long>(T, 1), H, I, E, K);
   if (rc != NKIMOE_OK) return rc;
-  NKI_REQUIRE(P >= 1 && P <= kMaxPeers && E % P == 0 && rank >= 0 && rank < P, NKIMOE_ERR_UNSUPPORTED,
+  NKI_REQUIRE(P >= 1 && P <= kMaxPeers && rank >= 0 && rank < P && (expert_slots || E % P == 0),
+              NKIMOE_ERR_UNSUPPORTED,
               "ep peer: need 1 <= ranks <= %d dividing the experts, 0 <= rank < ranks", kMaxPeers);
+  NKI_REQUIRE(El >= 1 && El <= kMaxExperts && (!expert_slots || (slot_counts && max_holders >= 1 &&
+                                                                  max_holders <= kMaxExperts)),
+              NKIMOE_ERR_INVALID_ARG, "ep peer: bad expert slot map (%lld slots per rank, %lld holders)", El,
+              max_holders);
   NKI_REQUIRE(T >= 0 && T <= Tm && P * Tm * K < (1LL << 31) && P * Tm * (H / 8) < (1LL << 31) && E <= 256,
               NKIMOE_ERR_UNSUPPORTED, "ep peer: tokens %lld exceed max_tokens %lld or the buffers are too large",
               static_cast<long long>(T), Tm);
-  const PeerWs W = peer_ws(T, H, I, E, K, P, Tm);
+  const PeerWs W = peer_ws(T, H, I, E, K, P, Tm, El);
   NKI_REQUIRE(workspace && workspace_bytes >= W.total && aligned16(workspace), NKIMOE_ERR_WORKSPACE,
               "workspace %zu < %zu", workspace_bytes, W.total);
   NKI_REQUIRE(peer_buffers && router_w && w13_local && w2_local && (T == 0 || (x && out)), NKIMOE_ERR_INVALID_ARG,
@@ -1419,7 +1438,6 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   NKI_REQUIRE(T == 0 || (aligned16(x) && aligned16(out)), NKIMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
   const cudaStream_t s = as_stream(stream);
   const EpPeerLayout PL = ep_peer_layout(P, Tm, H, K);
-  const long long El = E / P;
   const int me = static_cast<int>(rank);
   char* b = static_cast<char*>(workspace);
   // routing of the local tokens (its status word is the call's status word)
@@ -1439,6 +1457,14 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     rc = router_impl(x, router_w, router_bias, router_w_split, idx, w, T, H, E, K, rb, R, status, s);
     if (rc != NKIMOE_OK) return rc;
   }
+  // the expert slots the (token, slot) pairs go to
+  const int32_t* route = idx;
+  if (expert_slots && T > 0) {
+    int32_t* idx_v = reinterpret_cast<int32_t*>(b + W.idx_v);
+    NKI_CUDA(ep_remap_launch(idx, static_cast<int>(T), static_cast<int>(K), static_cast<int>(E), expert_slots,
+                             slot_counts, static_cast<int>(max_holders), static_cast<int>(P * El), idx_v, status, s));
+    route = idx_v;
+  }
   // (token, rank) pairs grouped by rank, tokens ascending
   mark(kStagePermute, s);
   char* db = b + W.disp;
@@ -1450,7 +1476,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   int32_t* slot_in = reinterpret_cast<int32_t*>(b + W.slot_in);
   int32_t* slot_out = reinterpret_cast<int32_t*>(b + W.slot_out);
   if (T > 0)
-    NKI_CUDA(ep_dest_launch(idx, static_cast<int>(T), static_cast<int>(K), static_cast<int>(P), static_cast<int>(El),
+    NKI_CUDA(ep_dest_launch(route, static_cast<int>(T), static_cast<int>(K), static_cast<int>(P), static_cast<int>(El),
                             dest, s));
   NKI_CUDA(permute_launch(dest, NKIMOE_I32, static_cast<int>(T), static_cast<int>(P), static_cast<int>(P), row_token,
                           row_slot, slot_in, offsets, scratch, status, s));
@@ -1475,11 +1501,11 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
   if (!overlapped) {
     // ---- one block: every row (own included) through the buffers, then all
     // of this rank's experts over all P regions
-    NKI_CUDA(ep_peer_local_launch(idx, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
+    NKI_CUDA(ep_peer_local_launch(route, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
                                   static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), me, false, slot_out,
                                   nullptr, nullptr, s));
     mark(kStageEpSend, s);
-    NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+    NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), route, w, row_token, row_slot, offsets,
                                  static_cast<int>(T), static_cast<int>(H), static_cast<int>(K), static_cast<int>(P),
                                  static_cast<int>(El), static_cast<int>(Tm), me, 0, static_cast<int>(P), peers, PL,
                                  counters, epoch_p, 0, s));
@@ -1508,7 +1534,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     const bool copy_engines = schedule == 2;
     int32_t* self_idx = reinterpret_cast<int32_t*>(b + W.self_idx);
     float* self_w = reinterpret_cast<float*>(b + W.self_w);
-    NKI_CUDA(ep_peer_local_launch(idx, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
+    NKI_CUDA(ep_peer_local_launch(route, w, slot_in, offsets, static_cast<int>(T), static_cast<int>(K),
                                   static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), me, true, slot_out,
                                   self_idx, self_w, s));
     int dev = 0;
@@ -1528,7 +1554,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
     __nv_bfloat16* ret_stage = reinterpret_cast<__nv_bfloat16*>(b + W.ret_stage);
     const size_t region_x = sizeof(uint16_t) * Tm * H, region_k = sizeof(int32_t) * Tm * K;
     if (copy_engines)
-      NKI_CUDA(ep_peer_stage_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+      NKI_CUDA(ep_peer_stage_launch(static_cast<const __nv_bfloat16*>(x), route, w, row_token, row_slot, offsets,
                                     static_cast<int>(T), static_cast<int>(H), static_cast<int>(K), static_cast<int>(P),
                                     static_cast<int>(El), static_cast<int>(Tm), me, stage_x, stage_slots, stage_w,
                                     stage_counts, s));
@@ -1549,7 +1575,7 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
         NKI_CUDA(ep_peer_publish_launch(reinterpret_cast<int32_t*>(pd + PL.counts) + q, stage_counts + d,
                                         reinterpret_cast<uint32_t*>(pd + PL.disp_flag) + q, epoch_p, es.side));
       } else {
-        NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), idx, w, row_token, row_slot, offsets,
+        NKI_CUDA(ep_peer_send_launch(static_cast<const __nv_bfloat16*>(x), route, w, row_token, row_slot, offsets,
                                      static_cast<int>(T), static_cast<int>(H), static_cast<int>(K),
                                      static_cast<int>(P), static_cast<int>(El), static_cast<int>(Tm), me, d, 1, peers,
                                      PL, counters + q, epoch_p, side_ctas, es.side));
@@ -1621,6 +1647,31 @@ int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* ro
                             static_cast<int>(H), s));
   mark(kStageEpEnd, s);
   return NKIMOE_OK;
+}
+
+int nkimoe_ep_peer_forward(const void* x, const float* router_w, const float* router_bias, const void* router_w_split,
+                           const void* w13_local, const void* w2_local, void* out, int32_t* topk_idx_out,
+                           float* topk_w_out, int64_t T, int64_t H, int64_t I,
+                           int64_t E, int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
+                           void* const* peer_buffers, uint32_t epoch, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  NKI_REQUIRE(num_ranks >= 1 && E % num_ranks == 0, NKIMOE_ERR_UNSUPPORTED, "ep peer: ranks must divide the experts");
+  return ep_peer_forward_impl(x, router_w, router_bias, router_w_split, w13_local, w2_local, out, topk_idx_out,
+                              topk_w_out, T, H, I, E, K, num_ranks, rank, max_tokens, peer_buffers, epoch, workspace,
+                              workspace_bytes, stream, E / num_ranks, nullptr, nullptr, 0);
+}
+
+int nkimoe_ep_peer_forward_mapped(const void* x, const float* router_w, const float* router_bias,
+                                  const void* router_w_split, const void* w13_local, const void* w2_local, void* out,
+                                  int32_t* topk_idx_out, float* topk_w_out, int64_t T, int64_t H, int64_t I,
+                                  int64_t E, int64_t K, int64_t num_ranks, int64_t rank, int64_t max_tokens,
+                                  void* const* peer_buffers, uint32_t epoch, void* workspace,
+                                  size_t workspace_bytes, void* stream, int64_t local_slots,
+                                  const int32_t* expert_slots, const int32_t* slot_counts, int64_t max_holders) {
+  NKI_REQUIRE(expert_slots && slot_counts, NKIMOE_ERR_INVALID_ARG, "ep peer: null expert slot map");
+  return ep_peer_forward_impl(x, router_w, router_bias, router_w_split, w13_local, w2_local, out, topk_idx_out,
+                              topk_w_out, T, H, I, E, K, num_ranks, rank, max_tokens, peer_buffers, epoch, workspace,
+                              workspace_bytes, stream, local_slots, expert_slots, slot_counts, max_holders);
 }
 
 int nkimoe_combine(const void* y, const int32_t* slot_row, const float* slot_weight, void* out, int64_t T, int64_t K,

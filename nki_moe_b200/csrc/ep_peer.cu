@@ -81,6 +81,31 @@ __device__ __forceinline__ bool last_block_done(unsigned* counter) {
   return last;
 }
 
+// Hot-expert replicas: slot (t, k) of expert e goes to holder t mod
+// counts[e] of e, i.e. to the expert slot slots[e * max_holders + t mod
+// counts[e]] (slot v lives on rank v / local_slots as its local expert
+// v % local_slots), which splits an expert's tokens evenly over the ranks
+// that hold a copy of its weights.  An id outside [0, E), or a table entry
+// outside [0, num_slots), maps to -1 (no rank takes the slot) and is flagged.
+__global__ void ep_remap_kernel(const int32_t* __restrict__ idx, int T, int K, int E,
+                                const int32_t* __restrict__ slots, const int32_t* __restrict__ counts,
+                                int max_holders, int num_slots, int32_t* __restrict__ idx_v, int* status) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(T) * K) return;
+  const int t = static_cast<int>(i / K);
+  const int e = idx[i];
+  int v = -1;
+  if (e >= 0 && e < E) {
+    const int n = counts[e];
+    if (n >= 1 && n <= max_holders) v = slots[static_cast<long long>(e) * max_holders + t % n];
+  }
+  if (v < 0 || v >= num_slots) {
+    v = -1;
+    if (status) atomicOr(status, kDevErrBadIndex);
+  }
+  idx_v[i] = v;
+}
+
 // Source side: send row r (token row_token[r], destination d = row_slot[r] % P,
 // j = r - rank_offsets[d]) of destinations [d_first, d_first + d_count) to
 // region (d - src) mod P of d's buffer: the token row, its K slots as d sees
@@ -426,6 +451,16 @@ cudaError_t ep_peer_local_launch(const int32_t* idx, const float* w, const int32
 
 cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s) {
   ep_peer_step_kernel<<<1, 1, 0, s>>>(step, value);
+  return cudaGetLastError();
+}
+
+cudaError_t ep_remap_launch(const int32_t* idx, int T, int K, int E, const int32_t* slots, const int32_t* counts,
+                            int max_holders, int num_slots, int32_t* idx_v, int* status, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (max_holders < 1) return cudaErrorInvalidValue;
+  const long long n = static_cast<long long>(T) * K;
+  ep_remap_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(idx, T, K, E, slots, counts, max_holders,
+                                                                         num_slots, idx_v, status);
   return cudaGetLastError();
 }
 

@@ -209,6 +209,11 @@ cudaError_t ep_peer_publish_launch(int32_t* count_dst, const int32_t* count_src,
 // epoch := value when nonzero, else epoch + 1 (device-side step count)
 cudaError_t ep_peer_step_launch(uint32_t* step, uint32_t value, cudaStream_t s);
 // Waits (bounded by budget_cycles) until flags[0 .. n) all hold the epoch.
+// Hot-expert replicas: idx_v[t, k] = slots[idx[t, k] * max_holders +
+// t mod counts[idx[t, k]]], the expert slot (rank * local_slots + local
+// expert) that takes slot (t, k); -1 and a status flag for bad entries.
+cudaError_t ep_remap_launch(const int32_t* idx, int T, int K, int E, const int32_t* slots, const int32_t* counts,
+                            int max_holders, int num_slots, int32_t* idx_v, int* status, cudaStream_t s);
 cudaError_t ep_peer_wait_launch(const uint32_t* flags, int n, const uint32_t* epoch_p, int* status,
                                 long long budget_cycles, cudaStream_t s);
 // Regions q0 .. q0 + nq - 1 (slots from region q0 on): rows past counts[q] get empty slots.

@@ -145,6 +145,53 @@ def test_peer_ep_single_rank_equals_block(overlap):
         _lib.set_option("ep_overlap", -1)
 
 
+@pytest.mark.parametrize("overlap", [0, 2])
+def test_peer_ep_single_rank_with_replica_slots_equals_block(overlap):
+    """Hot-expert replica slots through the mapped exchange on a single rank:
+    the rank holds two extra slots with copies of the two busiest experts of a
+    routing sample, and the remap sends every other token of those experts to
+    the copy (t mod 2).  Each (token, slot) row is the same arithmetic whichever
+    slot computes it and the rank's sum runs over a token's slots in k order,
+    so the output equals the single-GPU block bit for bit."""
+    _lib.set_option("ep_overlap", overlap)
+    from nki_moe_b200.ep_peer import PeerExpertParallelMoE, expert_load
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+
+    wl = WORKLOADS["c3"]
+    inp = make_moe_inputs(wl, device="cuda", tokens=1024)
+    moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        moe.router.weight.copy_(inp["router"])
+        moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
+        moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+    E = wl.experts
+    _, idx0, _ = ops.moe_block(inp["x"].to(torch.bfloat16), moe.router.weight, moe.packed(), wl.top_k,
+                               return_routing=True)
+    load = expert_load(idx0, E)
+    hot = sorted(range(E), key=lambda e: (-load[e], e))[:2]
+    slot_experts = [list(range(E)) + hot]
+    holders = [[e] for e in range(E)]
+    holders[hot[0]].append(E)
+    holders[hot[1]].append(E + 1)
+    sel = torch.tensor(slot_experts[0], dtype=torch.long, device="cuda")
+    peer = PeerExpertParallelMoE(moe.router.weight, moe.gate_up_proj.detach().index_select(0, sel).contiguous(),
+                                 moe.down_proj.detach().index_select(0, sel).contiguous(), E, wl.top_k, 1024,
+                                 replicas=(slot_experts, holders))
+    try:
+        for step, T in enumerate((1024, 600)):
+            x = torch.randn(T, wl.hidden, generator=torch.Generator(device="cuda").manual_seed(80 + step),
+                            device="cuda").to(torch.bfloat16)
+            y, idx, _ = peer(x, return_routing=True)
+            assert ops.read_status(ops.workspace(x.device, 1)) == 0
+            ref, ridx, _ = ops.moe_block(x, moe.router.weight, moe.packed(), wl.top_k, return_routing=True)
+            assert torch.equal(idx, ridx)  # the real expert ids come back
+            assert bool((idx == hot[0]).any()) and bool((idx == hot[1]).any())
+            assert torch.equal(y, ref), f"step {step}: max diff {(y.float() - ref.float()).abs().max().item()}"
+    finally:
+        peer.close()
+        _lib.set_option("ep_overlap", -1)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -258,6 +305,73 @@ def test_expert_parallel_two_gpus_matches_single_gpu(tmp_path):
         # after rank 1 left a step and the ranks resynchronised
         assert np.array_equal(np.load(tmp_path / f"peer3_{r}.npy"), np.load(tmp_path / f"dedup2_{r}.npy"))
     assert int(np.load(tmp_path / "timeout0.npy")[0]) == 1  # rank 0's step raised the wait timeout
+
+
+def _replica_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    from nki_moe_b200.ep_peer import PeerExpertParallelMoE, expert_load
+    from nki_moe_b200.nki_moe_integrated import NKIMoESimple
+    from nki_moe_b200.workloads import WORKLOADS, make_moe_inputs
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    wl = WORKLOADS["c4"]  # Zipf(1.2) router bias: a few experts take most rows
+    inp = make_moe_inputs(wl, device="cuda", tokens=2048)
+    moe = NKIMoESimple(wl.hidden, wl.intermediate, wl.experts, wl.top_k, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        moe.router.weight.copy_(inp["router"])
+        moe.gate_up_proj.copy_(inp["gate_up"].to(torch.bfloat16))
+        moe.down_proj.copy_(inp["down"].to(torch.bfloat16))
+    moe.router_bias = inp["router_bias"]
+    rw, rb, pe = moe.router.weight, moe.router_bias, moe.packed()
+    x_cal = torch.randn(1024, wl.hidden, generator=torch.Generator(device="cuda").manual_seed(90 + rank),
+                        device="cuda").to(torch.bfloat16)
+    _, idx_cal, _ = ops.moe_block(x_cal, rw, pe, wl.top_k, bias=rb, return_routing=True)
+    load = expert_load(idx_cal, wl.experts)
+    peer = PeerExpertParallelMoE.from_dense(moe, max_tokens=1024, extra_slots=2, expected_load=load)
+    x = inp["x"].to(torch.bfloat16).view(world, 1024, wl.hidden)[rank].contiguous()
+    ref, ridx, _ = ops.moe_block(x, rw, pe, wl.top_k, bias=rb, return_routing=True)
+    outs = []
+    for overlap in (0, 2, -1):
+        _lib.set_option("ep_overlap", overlap)
+        y, idx, _ = peer(x, return_routing=True)
+        outs.append(y)
+        assert torch.equal(idx, ridx)
+    _lib.set_option("ep_overlap", -1)
+    status = ops.read_status(ops.workspace(x.device, 1))
+    torch.cuda.synchronize()
+    np.save(os.path.join(out_dir, f"rep_ref{rank}.npy"), ref.float().cpu().numpy())
+    for i, y in enumerate(outs):
+        np.save(os.path.join(out_dir, f"rep{i}_{rank}.npy"), y.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"rep_meta{rank}.npy"),
+            np.array([status, sum(len(h) - 1 for h in peer.replicas[1]), peer.local_slots]))
+    peer.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_two_gpus_with_hot_expert_replicas(tmp_path):
+    """Skewed routing (Zipf router bias) over two ranks with two replica slots
+    each, planned from a calibration batch: the one-block and copy-engine
+    schedules give the same output, which meets the block bar against the
+    single-GPU block with identical routing (the real expert ids)."""
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_replica_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    for r in range(world):
+        status, copies, local_slots = np.load(tmp_path / f"rep_meta{r}.npy")
+        assert status == 0 and copies >= 1 and local_slots == 64 + 2
+        ref = np.load(tmp_path / f"rep_ref{r}.npy")
+        ys = [np.load(tmp_path / f"rep{i}_{r}.npy") for i in range(3)]
+        for y in ys:
+            assert oracle.normwise_rel_err(y, ref) < 2e-2 and oracle.cosine(y, ref) > 0.999
+            assert np.array_equal(y, ys[0])  # every schedule computes the same sums
 
 
 def test_peer_wait_runs_out_when_a_peer_never_joins():
