@@ -63,7 +63,10 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * 2 weights, 3 rows on an SM pair, 4 features x rows on an SM pair, 5 rows
  * on an SM pair over each expert's whole 256-row blocks and on one SM past
  * them),
- * "weights_rows" (16, 32 or 64 rows per decode tile), "router" (0 auto,
+ * "weights_rows" (16, 32 or 64 rows per decode tile), "weights_balance"
+ * (1, the default: a decode GEMM deals its tiles evenly to as many CTAs as
+ * its waves need, so the weight stream does not end with a few CTAs reading
+ * alone; 0: every CTA strides over the tiles), "router" (0 auto,
  * 1 CUDA-core fp32, 2 tensor-core split-fp32), "prefetch" (64-wide K blocks
  * of a prefill GEMM CTA's next tile pulled into L2 when it starts a tile;
  * 0 = off),

@@ -63,6 +63,7 @@ inline void mark(int stage, cudaStream_t s) {
     cudaEventRecord(g_stage_events[stage], s);
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
+std::atomic<int> g_weights_balance{1};  // weights-schedule GEMMs: tiles dealt evenly over the waves
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
 std::atomic<int> g_router_fused{1};  // tensor-core router: summed logits in one kernel (0: GEMM partials)
 std::atomic<int> g_stage_stores{3};  // rows-schedule epilogue staging: bit 0 SwiGLU, bit 1 scaled bf16
@@ -192,6 +193,7 @@ int run_gemm(const void* act, long long act_rows, const void* w, long long E, lo
   p.tma_gather4 = gather4 ? 1 : 0;
   p.row_weight = row_weight;
   p.prefetch = g_prefetch.load();
+  p.balance_waves = g_weights_balance.load();
   p.stage_stores = g_stage_stores.load();
   p.epilogue = epilogue;
   p.out = out;
@@ -737,6 +739,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "weights_rows" && (value == 0 || value == 16 || value == 32 || value == 64)) {
     g_weights_rows = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "weights_balance" && (value == 0 || value == 1)) {
+    g_weights_balance = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "epilogue_staging" && value >= 0 && value <= 3) {

@@ -1011,6 +1011,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tcgen05_fence_after();
   const uint32_t tmem_base = ctl.tmem_base;
   const int total_tiles = ctl.tile_start[E];
+  // balance_waves: the tiles dealt to as many CTAs as their waves need
+  // (ceil(tiles / ceil(tiles / grid))), so the weight stream does not end with
+  // a few CTAs reading alone; the other CTAs take no tile
+  int ncta = static_cast<int>(gridDim.x);
+  if (p.balance_waves && total_tiles > 0) {
+    const int waves = (total_tiles + ncta - 1) / ncta;
+    ncta = (total_tiles + waves - 1) / waves;
+  }
+  const int first_tile = static_cast<int>(blockIdx.x) < ncta ? static_cast<int>(blockIdx.x) : total_tiles;
 
   if (warp == 0) {
     // TMA mode: lane 0 alone runs the loop; gather mode: the whole warp
@@ -1020,7 +1029,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t issued_mask = 0, last_phase_mask = 0;
       bool ok = true;
       const uint64_t pol_w = policy_evict_first();
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x) {
+      for (int tile = first_tile; ok && tile < total_tiles; tile += ncta) {
         const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
         const int row0 = ctl.seg[tc.e] + tc.rblk * BT;
         const int arow0 = p.shared_a ? tc.rblk * BT : row0;
@@ -1098,7 +1107,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true, issued = false;
       int t_local = 0;
-      for (int tile = blockIdx.x; ok && tile < total_tiles; tile += gridDim.x, ++t_local) {
+      for (int tile = first_tile; ok && tile < total_tiles; tile += ncta, ++t_local) {
         const int acc = t_local & 1;
         const uint32_t acc_phase = (t_local >> 1) & 1;
         if (!mbar_wait(&ctl.acc_empty[acc], acc_phase ^ 1u, &ctl.abort_flag, p.status)) {
@@ -1138,7 +1147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int feat = quarter * 32 + lane;  // TMEM lane = feature row of the tile
     int t_local = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++t_local) {
+    for (int tile = first_tile; tile < total_tiles; tile += ncta, ++t_local) {
       const TileCoord tc = decode_tile(ctl, E, tile, BT, feat_tiles);
       const int acc = t_local & 1;
       const uint32_t acc_phase = (t_local >> 1) & 1;

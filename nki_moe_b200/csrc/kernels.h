@@ -291,6 +291,7 @@ struct GroupedGemmParams {
   int* status;
   int row_split;              // rows schedules: 0 every row; 1 each expert's whole blocks of 256 rows
                               // (the SM-pair kernel); 2 the rows past them (the 1-SM kernel)
+  int balance_waves;          // weights schedule: tiles dealt evenly to ceil(tiles / waves) CTAs
 };
 
 // Tile shape choices exposed to the host.

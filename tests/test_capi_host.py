@@ -43,6 +43,10 @@ def test_version_and_options():
     _lib.set_option("pdl", 1)
     with pytest.raises(_lib.NKIMoEError):
         _lib.set_option("pdl", 2)
+    _lib.set_option("weights_balance", 0)
+    _lib.set_option("weights_balance", 1)
+    with pytest.raises(_lib.NKIMoEError):
+        _lib.set_option("weights_balance", 2)
 
 
 def test_workspace_sizes_are_host_functions():
