@@ -76,6 +76,8 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * "epilogue_staging" (prefill GEMM bf16 outputs written through a per-warp
  * shared-memory tile as whole-sector row stores: bit 0 the SwiGLU output,
  * bit 1 the routing-weight-scaled output; default 3),
+ * "router_halves" (1, the default: the tensor-core router runs two CTAs per
+ * 128-row block, one per half of the experts; 0: one CTA over all 128),
  * "router_fused" (1, the default: the tensor-core router forms the summed
  * fp32 logits of its three weight planes in one kernel before the top-k;
  * 0: the grouped GEMM writes the three planes' partials, which the top-k

@@ -63,6 +63,7 @@ inline void mark(int stage, cudaStream_t s) {
     cudaEventRecord(g_stage_events[stage], s);
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
+std::atomic<int> g_router_halves{1};   // tensor-core router: two CTAs per row block (experts split)
 std::atomic<int> g_weights_balance{1};  // weights-schedule GEMMs: tiles dealt evenly over the waves
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
 std::atomic<int> g_router_fused{1};  // tensor-core router: summed logits in one kernel (0: GEMM partials)
@@ -253,10 +254,11 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
     // the three planes' logits summed in one tensor-core kernel (the same MMAs
     // and sums as the router GEMM + partials form below), then the top-k
     CUtensorMap tx, tw;
-    NKI_REQUIRE(make_tmap_bf16(&tx, x, T, H, 128) && make_tmap_bf16(&tw, router_w_split, 3 * E, H, 128),
+    const int ept = g_router_halves.load() ? 64 : 128;  // experts per CTA = rows of a plane's TMA box
+    NKI_REQUIRE(make_tmap_bf16(&tx, x, T, H, 128) && make_tmap_bf16(&tw, router_w_split, 3 * E, H, ept),
                 NKIMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the router operands");
     NKI_CUDA(router_tc_launch(tx, tw, nullptr, nullptr, 0, 0.f, nullptr, router_bias, logits, T, static_cast<int>(H),
-                              status, s));
+                              status, s, ept));
     mark(kStageTopk, s);
     NKI_CUDA(topk_softmax_partials_launch(logits, 1, nullptr, nullptr, static_cast<int>(T), static_cast<int>(E),
                                           static_cast<int>(K), idx, w, s));
@@ -741,6 +743,10 @@ int nkimoe_set_option(const char* name, long long value) {
     g_weights_rows = static_cast<int>(value);
     return NKIMOE_OK;
   }
+  if (n == "router_halves" && (value == 0 || value == 1)) {
+    g_router_halves = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
   if (n == "weights_balance" && (value == 0 || value == 1)) {
     g_weights_balance = static_cast<int>(value);
     return NKIMOE_OK;
@@ -1048,12 +1054,14 @@ int nkimoe_moe_block_rmsnorm(const void* h, const void* norm_w, int norm_w_dtype
                      router_tc_supported(T, static_cast<int>(H), static_cast<int>(E), true);
   if (fused) {
     CUtensorMap tw;
-    NKI_REQUIRE(make_tmap_bf16(&tw, router_w_split, 3 * E, H, 128), NKIMOE_ERR_CUDA,
+    const int ept = g_router_halves.load() ? 64 : 128;  // experts per CTA = rows of a plane's TMA box
+    NKI_REQUIRE(make_tmap_bf16(&tw, router_w_split, 3 * E, H, ept), NKIMOE_ERR_CUDA,
                 "cuTensorMapEncodeTiled failed for the router planes");
     float* logits = reinterpret_cast<float*>(base + L.logits);
     mark(kStageRouter, s);
     NKI_CUDA(router_tc_launch(tw, tw, static_cast<const __nv_bfloat16*>(h), norm_w, norm_w_dtype, eps,
-                              static_cast<__nv_bfloat16*>(x), router_bias, logits, T, static_cast<int>(H), status, s));
+                              static_cast<__nv_bfloat16*>(x), router_bias, logits, T, static_cast<int>(H), status, s,
+                              ept));
     mark(kStageTopk, s);
     NKI_CUDA(topk_softmax_partials_launch(logits, 1, nullptr, nullptr, static_cast<int>(T), static_cast<int>(E),
                                           static_cast<int>(K), idx, w, s));

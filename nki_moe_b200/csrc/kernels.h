@@ -133,7 +133,9 @@ cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, co
 // Same on logits given as `splits` fp32 partial sums [split][T][E] (+ bias[E]);
 // logits_out (nullable) receives the summed logits.
 // Router logits of a prefill batch on the tensor cores in one kernel (E ==
-// 128, the weights as three bf16 planes; tmap_w over [3 E, H], box 64 x 128):
+// 128, the weights as three bf16 planes; tmap_w over [3 E, H], box 64 x
+// experts_per_cta (64: two CTAs per 128-row block, one per half of the
+// experts; or 128)):
 // logits_out [T, E] = ((hi + mid) + lo) + bias, the values topk_softmax
 // forms from the router GEMM's three partials, so its top-k is bit for bit the
 // two-kernel one.  With h non-null the CTA normalises the rows first (RMSNorm,
@@ -142,7 +144,8 @@ cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, co
 bool router_tc_supported(long long T, int H, int E, bool norm);
 cudaError_t router_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
                              const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out, const float* bias,
-                             float* logits_out, long long T, int H, int* status, cudaStream_t s);
+                             float* logits_out, long long T, int H, int* status, cudaStream_t s,
+                             int experts_per_cta);
 cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const float* bias, float* logits_out,
                                          int tokens, int experts, int top_k, int32_t* idx, float* w, cudaStream_t s);
 

@@ -278,11 +278,13 @@ __global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restri
 }
 
 // Router logits of a prefill batch in one tensor-core kernel, with an
-// optional RMSNorm of the rows in front of it.  CTA = 128 rows; the fp32
-// router weights are three exact bf16 planes (hi, mid, lo; router_split_kernel)
-// and each plane has its own TMEM accumulator (3 x 128 columns).  The MMAs are
-// the ones of the router GEMM (M128 N128 K16, K ascending, one accumulator per
-// plane) and the epilogue adds the planes as topk_softmax_kernel adds split
+// optional RMSNorm of the rows in front of it.  CTA = 128 rows x one half of
+// the experts (two CTAs per row block, so a batch fills twice as many SMs);
+// the fp32 router weights are three exact bf16 planes (hi, mid, lo;
+// router_split_kernel) and each plane has its own TMEM accumulator (3 x 64
+// columns).  The MMAs are
+// those of the router GEMM (M128 K16, K ascending, one accumulator per plane;
+// N = 64 experts here, 128 there: each logit is the same sum) and the epilogue adds the planes as topk_softmax_kernel adds split
 // partials, ((hi + mid) + lo) + bias, so the logits it writes give the same
 // top-k bit for bit; the top-k itself stays a separate kernel (spread over the
 // whole GPU it is several times faster than in these 64-128 CTAs' epilogues).
@@ -297,13 +299,19 @@ __global__ void __launch_bounds__(256) topk_softmax_kernel(const float* __restri
 //              32 w .. 32 w + 31 = rows; fp32 logits rows to global memory)
 //   warp 4:    TMA producer (router planes; the x block without the norm)
 //   warp 5:    MMA issuer, TMEM owner
-constexpr int kRtRows = 128, kRtBK = 64, kRtE = 128, kRtStages = 3, kRtThreads = 192;
+constexpr int kRtRows = 128, kRtBK = 64, kRtE = 128, kRtThreads = 192, kRtMaxStages = 5;
 constexpr uint32_t kRtABytes = kRtRows * kRtBK * 2;      // 16 KB
-constexpr uint32_t kRtBBytes = 3 * kRtE * kRtBK * 2;     // 48 KB: three planes
-constexpr uint32_t kRtStageBytes = kRtABytes + kRtBBytes;
+// EH experts per CTA (64: two CTAs per row block, the default; 128: one)
+template <int EH>
+struct RtShape {
+  static constexpr int kStages = EH == 128 ? 3 : 5;
+  static constexpr uint32_t kBBytes = 3 * EH * kRtBK * 2;  // three planes of the CTA's experts
+  static constexpr uint32_t kStageBytes = kRtABytes + kBBytes;
+  static constexpr uint32_t kTmemCols = EH == 128 ? 512 : 256;
+};
 
 struct RtCtl {
-  uint64_t full[kRtStages], empty[kRtStages], afull[kRtStages];
+  uint64_t full[kRtMaxStages], empty[kRtMaxStages], afull[kRtMaxStages];
   uint64_t acc_full, drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -314,7 +322,7 @@ __device__ __forceinline__ float rt_weight(const void* w, int w_dtype, int k) {
   return w_dtype == 0 ? static_cast<const float*>(w)[k] : __bfloat162float(static_cast<const __nv_bfloat16*>(w)[k]);
 }
 
-template <bool kNorm>
+template <bool kNorm, int EH>
 __global__ void __launch_bounds__(kRtThreads, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                      const __nv_bfloat16* __restrict__ h, const void* __restrict__ norm_w, int norm_w_dtype,
@@ -325,10 +333,12 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(rt_smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long row0 = static_cast<long long>(blockIdx.x) * kRtRows;
+  using S = RtShape<EH>;
+  const long long row0 = static_cast<long long>(blockIdx.x / (kRtE / EH)) * kRtRows;
+  const int eh = static_cast<int>(blockIdx.x % (kRtE / EH));  // experts [EH eh, EH eh + EH)
   const int kblocks = H / kRtBK;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRtStages; ++s) {
+    for (int s = 0; s < S::kStages; ++s) {
       mbar_init(&ctl.full[s], 1);
       mbar_init(&ctl.empty[s], 1);
       mbar_init(&ctl.afull[s], 4 * 32);
@@ -342,7 +352,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
     prefetch_tmap(&tmap_w);
     if (!kNorm) prefetch_tmap(&tmap_x);
   }
-  if (warp == 5) tmem_alloc(&ctl.tmem_base, 512);
+  if (warp == 5) tmem_alloc(&ctl.tmem_base, S::kTmemCols);
   if (kNorm && warp < 4) {
     // sum of squares of each row as rmsnorm_kernel forms it: lane l adds the
     // squares of chunks l + 32 i (8 bf16 each) in order, then a butterfly
@@ -392,21 +402,22 @@ __global__ void __launch_bounds__(kRtThreads, 1)
           ok = false;
           break;
         }
-        uint8_t* st = smem + stage * kRtStageBytes;
-        mbar_arrive_expect_tx(&ctl.full[stage], kNorm ? kRtBBytes : kRtStageBytes);
+        uint8_t* st = smem + stage * S::kStageBytes;
+        mbar_arrive_expect_tx(&ctl.full[stage], kNorm ? S::kBBytes : S::kStageBytes);
         if (!kNorm) tma_load_2d(st, &tmap_x, &ctl.full[stage], kb * kRtBK, static_cast<int>(row0));
 #pragma unroll
         for (int p = 0; p < 3; ++p)
-          tma_load_2d(st + kRtABytes + p * (kRtE * kRtBK * 2), &tmap_w, &ctl.full[stage], kb * kRtBK, p * kRtE);
+          tma_load_2d(st + kRtABytes + p * (EH * kRtBK * 2), &tmap_w, &ctl.full[stage], kb * kRtBK,
+                      p * kRtE + eh * EH);
         issued |= 1u << stage;
         last = (last & ~(1u << stage)) | (phase << stage);
-        if (++stage == kRtStages) {
+        if (++stage == S::kStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
       if (!ok)  // let copies in flight land before the CTA exits
-        for (int s = 0; s < kRtStages; ++s)
+        for (int s = 0; s < S::kStages; ++s)
           if ((issued >> s) & 1u) {
             const long long t0 = clock64();
             while (!mbar_try_wait(&ctl.full[s], (last >> s) & 1u))
@@ -417,7 +428,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16_f32(kRtRows, kRtE);
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(kRtRows, EH);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, any = false;
@@ -428,18 +439,18 @@ __global__ void __launch_bounds__(kRtThreads, 1)
           break;
         }
         tcgen05_fence_after();
-        uint8_t* st = smem + stage * kRtStageBytes;
+        uint8_t* st = smem + stage * S::kStageBytes;
         const uint64_t da = umma_desc_sw128(smem_u32(st));
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
-          const uint64_t db = umma_desc_sw128(smem_u32(st + kRtABytes + p * (kRtE * kRtBK * 2)));
+          const uint64_t db = umma_desc_sw128(smem_u32(st + kRtABytes + p * (EH * kRtBK * 2)));
 #pragma unroll
           for (int kk = 0; kk < kRtBK / 16; ++kk)
-            umma_bf16(tmem_base + p * kRtE, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_bf16(tmem_base + p * EH, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0 ? 1u : 0u);
         }
         umma_commit(&ctl.empty[stage]);
         any = true;
-        if (++stage == kRtStages) {
+        if (++stage == S::kStages) {
           stage = 0;
           phase ^= 1u;
         }
@@ -469,7 +480,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
           ok = false;
           break;
         }
-        uint8_t* sa = smem + stage * kRtStageBytes;
+        uint8_t* sa = smem + stage * S::kStageBytes;
         const int k0 = kb * kRtBK + c * 8;
         float wv[8];
 #pragma unroll
@@ -494,13 +505,13 @@ __global__ void __launch_bounds__(kRtThreads, 1)
             o.y = pack_bf16x2(b.x * r * wv[2], b.y * r * wv[3]);
             o.z = pack_bf16x2(cc.x * r * wv[4], cc.y * r * wv[5]);
             o.w = pack_bf16x2(d.x * r * wv[6], d.y * r * wv[7]);
-            *reinterpret_cast<uint4*>(x_out + row * H + k0) = o;
+            if (eh == 0) *reinterpret_cast<uint4*>(x_out + row * H + k0) = o;
           }
           *reinterpret_cast<uint4*>(sa + rl * 128 + ((c ^ (rl & 7)) << 4)) = o;
         }
         fence_proxy_async_shared();  // generic-proxy writes -> tensor-core reads
         mbar_arrive(&ctl.afull[stage]);
-        if (++stage == kRtStages) {
+        if (++stage == S::kStages) {
           stage = 0;
           phase ^= 1u;
         }
@@ -515,11 +526,11 @@ __global__ void __launch_bounds__(kRtThreads, 1)
       const long long row = row0 + warp * 32 + lane;
       const uint32_t tl = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll 1
-      for (int c0 = 0; c0 < kRtE; c0 += 32) {
+      for (int c0 = 0; c0 < EH; c0 += 32) {
         uint32_t a[32], b[32], d[32];
         tmem_ld_32x32b_x32(tl + c0, a);
-        tmem_ld_32x32b_x32(tl + kRtE + c0, b);
-        tmem_ld_32x32b_x32(tl + 2 * kRtE + c0, d);
+        tmem_ld_32x32b_x32(tl + EH + c0, b);
+        tmem_ld_32x32b_x32(tl + 2 * EH + c0, d);
         tmem_ld_wait();
         float lg[32];
 #pragma unroll
@@ -527,11 +538,11 @@ __global__ void __launch_bounds__(kRtThreads, 1)
           float acc = __uint_as_float(a[j]);
           acc += __uint_as_float(b[j]);
           acc += __uint_as_float(d[j]);
-          if (bias) acc += bias[c0 + j];
+          if (bias) acc += bias[eh * EH + c0 + j];
           lg[j] = acc;
         }
         if (row < T) {
-          float4* dst = reinterpret_cast<float4*>(logits_out + row * kRtE + c0);
+          float4* dst = reinterpret_cast<float4*>(logits_out + row * kRtE + eh * EH + c0);
 #pragma unroll
           for (int q = 0; q < 8; ++q) dst[q] = make_float4(lg[4 * q], lg[4 * q + 1], lg[4 * q + 2], lg[4 * q + 3]);
         }
@@ -542,7 +553,7 @@ __global__ void __launch_bounds__(kRtThreads, 1)
   __syncthreads();
   if (warp == 5) {
     tcgen05_fence_after();
-    tmem_dealloc(tmem_base, 512);
+    tmem_dealloc(tmem_base, S::kTmemCols);
   }
 }
 
@@ -898,44 +909,64 @@ cudaError_t topk_softmax_partials_launch(const float* partial, int splits, const
 }
 
 
-size_t router_tc_smem_bytes() { return static_cast<size_t>(kRtStages) * kRtStageBytes + 1024; }
+size_t router_tc_smem_bytes(int eh) {
+  return eh == 128 ? static_cast<size_t>(RtShape<128>::kStages) * RtShape<128>::kStageBytes + 1024
+                   : static_cast<size_t>(RtShape<64>::kStages) * RtShape<64>::kStageBytes + 1024;
+}
 
 bool router_tc_supported(long long T, int H, int E, bool norm) {
   return E == kRtE && H % kRtBK == 0 && H >= kRtBK && T > 0 && (!norm || H <= 8 * 32 * 8);
 }
 
-cudaError_t router_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
-                             const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out, const float* bias,
-                             float* logits_out, long long T, int H, int* status, cudaStream_t s) {
-  const bool norm = h != nullptr;
-  if (!router_tc_supported(T, H, kRtE, norm) || !logits_out || (norm && (!norm_w || !x_out)))
-    return cudaErrorInvalidValue;
-  const size_t smem = router_tc_smem_bytes();
-  const unsigned grid = static_cast<unsigned>((T + kRtRows - 1) / kRtRows);
-  // the dynamic shared-memory opt-in, once per kernel and device (not per
-  // launch, so launches can be captured into CUDA graphs)
+namespace {
+// the dynamic shared-memory opt-in, once per kernel and device (not per
+// launch, so launches can be captured into CUDA graphs)
+template <bool kNorm, int EH>
+cudaError_t router_tc_opt_in(size_t smem) {
   static std::mutex mu;
-  static std::set<std::pair<int, int>> done;  // (norm, device)
+  static std::set<int> done;  // devices
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (!done.count({norm ? 1 : 0, dev})) {
-      e = norm ? cudaFuncSetAttribute(router_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem))
-               : cudaFuncSetAttribute(router_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      done.insert({norm ? 1 : 0, dev});
-    }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done.count(dev)) {
+    e = cudaFuncSetAttribute(router_tc_kernel<kNorm, EH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    done.insert(dev);
   }
-  if (norm)
-    router_tc_kernel<true><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out, bias,
-                                                           logits_out, static_cast<int>(T), H, status);
-  else
-    router_tc_kernel<false><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr, bias,
-                                                            logits_out, static_cast<int>(T), H, status);
+  return cudaSuccess;
+}
+
+template <bool kNorm, int EH>
+cudaError_t router_tc_run(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
+                          const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out, const float* bias,
+                          float* logits_out, long long T, int H, int* status, cudaStream_t s) {
+  const size_t smem = router_tc_smem_bytes(EH);
+  const cudaError_t e = router_tc_opt_in<kNorm, EH>(smem);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = static_cast<unsigned>((kRtE / EH) * ((T + kRtRows - 1) / kRtRows));
+  router_tc_kernel<kNorm, EH><<<grid, kRtThreads, smem, s>>>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out,
+                                                              bias, logits_out, static_cast<int>(T), H, status);
   return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t router_tc_launch(const CUtensorMap& tmap_x, const CUtensorMap& tmap_w, const __nv_bfloat16* h,
+                             const void* norm_w, int norm_w_dtype, float eps, __nv_bfloat16* x_out, const float* bias,
+                             float* logits_out, long long T, int H, int* status, cudaStream_t s, int experts_per_cta) {
+  const bool norm = h != nullptr;
+  if (!router_tc_supported(T, H, kRtE, norm) || !logits_out || (norm && (!norm_w || !x_out)) ||
+      (experts_per_cta != 64 && experts_per_cta != 128))
+    return cudaErrorInvalidValue;
+  if (experts_per_cta == 64)
+    return norm ? router_tc_run<true, 64>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out, bias, logits_out, T,
+                                          H, status, s)
+                : router_tc_run<false, 64>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr, bias, logits_out, T,
+                                           H, status, s);
+  return norm ? router_tc_run<true, 128>(tmap_x, tmap_w, h, norm_w, norm_w_dtype, eps, x_out, bias, logits_out, T, H,
+                                         status, s)
+              : router_tc_run<false, 128>(tmap_x, tmap_w, nullptr, nullptr, 0, 0.f, nullptr, bias, logits_out, T, H,
+                                          status, s);
 }
 }  // namespace nkimoe

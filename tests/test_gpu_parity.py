@@ -734,22 +734,26 @@ def test_fused_tensor_core_router_equals_two_kernels(T):
     """The one-kernel tensor-core router logits (the three weight planes
     summed in the epilogue) issue the same MMAs and sums as the router GEMM's
     partials added by the top-k kernel: routing indices and weights identical
-    bit for bit, with and without a router bias, on full and ragged row tiles."""
+    bit for bit, with and without a router bias, on full and ragged row tiles,
+    with 64 experts per CTA (two CTAs per row block, the default) and 128."""
     g = torch.Generator().manual_seed(T)
     x = torch.randn(T, 2048, generator=g).bfloat16().cuda()
     rw = (torch.randn(128, 2048, generator=g) * 0.02).cuda()
     bias = (torch.randn(128, generator=g) * 0.1).cuda()
     for b in (None, bias):
         outs = []
-        for fused in (1, 0):
+        for fused, halves in ((1, 1), (1, 0), (0, 1)):
             _lib.set_option("router_fused", fused)
+            _lib.set_option("router_halves", halves)
             try:
                 outs.append(ops.route(x, rw, 8, bias=b))
             finally:
                 _lib.set_option("router_fused", 1)
-        (i1, w1), (i0, w0) = outs
-        assert torch.equal(i1, i0)
-        assert torch.equal(w1.view(torch.int32), w0.view(torch.int32))
+                _lib.set_option("router_halves", 1)
+        i0, w0 = outs[-1]
+        for i1, w1 in outs[:-1]:
+            assert torch.equal(i1, i0)
+            assert torch.equal(w1.view(torch.int32), w0.view(torch.int32))
 
 
 @pytest.mark.parametrize("T", [300, 2048, 8192])
