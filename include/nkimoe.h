@@ -76,6 +76,9 @@ NKIMOE_API const char* nkimoe_last_error(void);
  * "epilogue_staging" (prefill GEMM bf16 outputs written through a per-warp
  * shared-memory tile as whole-sector row stores: bit 0 the SwiGLU output,
  * bit 1 the routing-weight-scaled output; default 3),
+ * "router_permutes" (1, the default: a decode router of 9 to 255 tokens
+ * also writes the expert permutation in its last CTA; 0: a separate
+ * permutation launch),
  * "router_halves" (1, the default: the tensor-core router runs two CTAs per
  * 128-row block, one per half of the experts; 0: one CTA over all 128),
  * "router_fused" (1, the default: the tensor-core router forms the summed

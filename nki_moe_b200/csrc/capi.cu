@@ -63,6 +63,7 @@ inline void mark(int stage, cudaStream_t s) {
     cudaEventRecord(g_stage_events[stage], s);
 }
 std::atomic<int> g_weights_rows{0};  // 0 auto, else 16/32/64
+std::atomic<int> g_router_permutes{1};  // decode routers of 9-255 tokens also write the permutation
 std::atomic<int> g_router_halves{1};   // tensor-core router: two CTAs per row block (experts split)
 std::atomic<int> g_weights_balance{1};  // weights-schedule GEMMs: tiles dealt evenly over the waves
 std::atomic<int> g_router{0};        // 0 auto, 1 CUDA-core split-K, 2 tensor-core split-fp32
@@ -274,10 +275,16 @@ int router_impl(const void* x, const float* router_w, const float* router_bias, 
                                           static_cast<int>(K), idx, w, s));
   } else if (router_topk_fused_supported(static_cast<int>(H), static_cast<int>(E), static_cast<int>(K)) && T > 8 &&
              T < 256) {
-    // several token groups: 8-CTA clusters (faster than the split router there)
+    // several token groups: 8-CTA clusters (faster than the split router
+    // there); the grid's last CTA writes the permutation too (one counter in
+    // the status block after the status word, cleared by every caller)
+    const bool fuse_perm = perm && permuted && g_router_permutes.load() &&
+                           router_topk_cluster_permutes(static_cast<int>(T), static_cast<int>(K));
     NKI_CUDA(router_topk_cluster_launch(static_cast<const __nv_bfloat16*>(x), router_w, router_bias, logits,
                                         static_cast<int>(T), static_cast<int>(H), static_cast<int>(E),
-                                        static_cast<int>(K), idx, w, s));
+                                        static_cast<int>(K), idx, w, s, reinterpret_cast<int*>(base + L.status + 64),
+                                        fuse_perm ? perm : nullptr));
+    if (fuse_perm) *permuted = true;
     mark(kStageTopk, s);
   } else if (router_topk_fused_supported(static_cast<int>(H), static_cast<int>(E), static_cast<int>(K)) &&
              (T + 7) / 8 <= router_topk_max_groups()) {
@@ -741,6 +748,10 @@ int nkimoe_set_option(const char* name, long long value) {
   }
   if (n == "weights_rows" && (value == 0 || value == 16 || value == 32 || value == 64)) {
     g_weights_rows = static_cast<int>(value);
+    return NKIMOE_OK;
+  }
+  if (n == "router_permutes" && (value == 0 || value == 1)) {
+    g_router_permutes = static_cast<int>(value);
     return NKIMOE_OK;
   }
   if (n == "router_halves" && (value == 0 || value == 1)) {

@@ -122,10 +122,15 @@ struct RouterPermOut {
 bool router_topk_fused_permutes(int tokens);
 // The same result for more than one token group (measured faster there):
 // 8-CTA clusters of 8 tokens, the expert logits of a token gathered over
-// distributed shared memory.  Same support conditions; no partials, no counters.
+// distributed shared memory.  Same support conditions; no partials.  With
+// `perm` (tokens * top_k <= kPermuteSmall) the last CTA of the grid to finish
+// (`counter`: one int, zero on entry, left at zero) also writes the
+// permutation, as permute_launch would.
+bool router_topk_cluster_permutes(int tokens, int top_k);
 cudaError_t router_topk_cluster_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                        int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
-                                       cudaStream_t s);
+                                       cudaStream_t s, int* counter = nullptr,
+                                       const RouterPermOut* perm = nullptr);
 cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                      int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
                                      float* partial, int* counters, cudaStream_t s,

@@ -694,7 +694,8 @@ template <int EG>
 __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(256)
     router_topk_cluster_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wr,
                                const float* __restrict__ bias, float* __restrict__ logits_out, int T, int H, int E,
-                               int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+                               int K, int32_t* __restrict__ idx_out, float* __restrict__ w_out, int* counter,
+                               RouterPermOut perm) {
   extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [8][H]: the cluster's token rows
   __shared__ float lg[kRouterCluster][EG];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -773,6 +774,21 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(256)
     topk_select_warp<VPT>(v, E, K, lane, idx_out + t * K, w_out + t * K);
   }
   cluster_sync();  // no CTA leaves while another still reads its logits
+  if (perm.row_token != nullptr) {
+    // the last CTA of the grid to finish (device-scope counter, no spinning)
+    // holds every token's routing: it writes the permutation
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1;
+      if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    if (threadIdx.x == 0) *counter = 0;
+    permute_small_cta<int32_t>(idx_out, T, K, E, perm.row_token, perm.row_slot, perm.slot_row, perm.expert_offsets,
+                               w_out, perm.row_weight, perm.status);
+  }
 }
 
 }  // namespace
@@ -859,22 +875,46 @@ cudaError_t router_topk_fused_launch(const __nv_bfloat16* x, const float* wr, co
   return e;
 }
 
+bool router_topk_cluster_permutes(int tokens, int top_k) {
+  return tokens >= 1 && static_cast<long long>(tokens) * top_k <= kPermuteSmall;
+}
+
 cudaError_t router_topk_cluster_launch(const __nv_bfloat16* x, const float* wr, const float* bias, float* logits_out,
                                      int tokens, int hidden, int experts, int top_k, int32_t* idx, float* w,
-                                     cudaStream_t s) {
+                                     cudaStream_t s, int* counter, const RouterPermOut* perm) {
   if (tokens == 0) return cudaSuccess;
   if (!router_topk_fused_supported(hidden, experts, top_k)) return cudaErrorInvalidValue;
+  if (perm && (!counter || !router_topk_cluster_permutes(tokens, top_k))) return cudaErrorInvalidValue;
+  const RouterPermOut po = perm ? *perm : RouterPermOut{};
   const size_t smem = static_cast<size_t>(kRouterCluster) * hidden * sizeof(__nv_bfloat16);
   const unsigned grid = static_cast<unsigned>((tokens + kRouterCluster - 1) / kRouterCluster) * kRouterCluster;
   const int eg = (experts + kRouterCluster - 1) / kRouterCluster;
+  // the dynamic shared-memory opt-in (the row staging plus the permutation's
+  // static tables pass 48 KB), once per kernel and device so that launches
+  // can be captured into CUDA graphs
+  static std::mutex mu;
+  static std::set<std::pair<int, int>> done;  // (EG, device)
+  int dev = 0;
+  cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) return e0;
 #define NKI_RTC(EGV)                                                                                         \
   do {                                                                                                      \
     auto k = router_topk_cluster_kernel<EGV>;                                                               \
-    if (smem > 48 * 1024) {                                                                                 \
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-      if (e != cudaSuccess) return e;                                                                       \
+    {                                                                                                       \
+      std::lock_guard<std::mutex> lock(mu);                                                                 \
+      if (!done.count({EGV, dev})) {                                                                        \
+        cudaFuncAttributes fa{};                                                                            \
+        int optin = 0;                                                                                      \
+        cudaError_t e = cudaFuncGetAttributes(&fa, k);                                                      \
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev); \
+        if (e == cudaSuccess)                                                                               \
+          e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,                          \
+                                   optin - static_cast<int>(fa.sharedSizeBytes));                           \
+        if (e != cudaSuccess) return e;                                                                     \
+        done.insert({EGV, dev});                                                                            \
+      }                                                                                                     \
     }                                                                                                       \
-    k<<<grid, 256, smem, s>>>(x, wr, bias, logits_out, tokens, hidden, experts, top_k, idx, w);              \
+    k<<<grid, 256, smem, s>>>(x, wr, bias, logits_out, tokens, hidden, experts, top_k, idx, w, counter, po);  \
   } while (0)
   if (eg <= 4) NKI_RTC(4);
   else if (eg <= 8) NKI_RTC(8);

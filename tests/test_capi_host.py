@@ -43,6 +43,8 @@ def test_version_and_options():
     _lib.set_option("pdl", 1)
     with pytest.raises(_lib.NKIMoEError):
         _lib.set_option("pdl", 2)
+    _lib.set_option("router_permutes", 0)
+    _lib.set_option("router_permutes", 1)
     _lib.set_option("router_halves", 0)
     _lib.set_option("router_halves", 1)
     _lib.set_option("weights_balance", 0)

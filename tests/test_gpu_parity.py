@@ -481,12 +481,13 @@ def test_moe_block_add_rmsnorm_equals_unfused(c1_inputs, T, in_place, w_dtype):
     assert torch.equal(xn, ref_xn)
 
 
-@pytest.mark.parametrize("T", [1, 5, 8, 9])
+@pytest.mark.parametrize("T", [1, 5, 8, 9, 64, 255])
 def test_router_permutation_equals_permute_kernel(c1_inputs, T):
-    """Up to 8 tokens the decode router's last CTA also writes the expert
-    permutation (no separate permutation launch): the block's output equals,
+    """Decode routers also write the expert permutation (no separate
+    permutation launch): up to 8 tokens the split router's last CTA, from 9
+    to 255 tokens the cluster router's last CTA.  The block's output equals,
     bit for bit, the experts stage run on the same routing with the
-    permutation kernel (9 tokens: two token groups, the separate kernel)."""
+    permutation kernel."""
     g = torch.Generator().manual_seed(40 + T)
     xb = torch.randn(T, 2048, generator=g).bfloat16().cuda()
     rw = c1_inputs["router"].cuda()
